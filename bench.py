@@ -1,0 +1,399 @@
+"""Benchmark of the B200 Q8 GQA decode attention (the reference's attend_q8 +
+store_kv hot path) on BASELINE.json's headline configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+Default workload (config 2, Llama-3-8B-shaped decode): 32 layers, 32 q / 8 kv
+heads, head_dim 128, Q8 KV cache of 4096 positions plus the token appended each
+step (n = 4097), q ~ N(0,1) rotated by RoPE (theta 500000) at position 4096.
+One step = one token: for every layer the fused kernel appends the new K/V row
+(bit-exact Q8) and attends -- a single multi-layer launch of libtqk.so's
+tqk_decode_q8.  K/V per step is 302 MB, larger than the 126 MB L2, so no flush
+is needed between steps.
+
+For N > 1 (torchrun, one process per GPU) every rank decodes its own sequence
+(batch sharding, no collective): weak scaling, value = all ranks' tokens / the
+slowest rank's time.  Other configs: --config 1 (1 layer, n = 1024),
+3 (ragged batch 64), 4 (context 131072, sequence split across ranks with an
+NCCL all-gather of log-sum-exp partials), 5 (chunked causal prefill).
+
+Rank 0 prints one JSON line.  --impl reference times the reference's own CPU
+code for the same workload (oracle/_ref/libtqref_avx2.so: the reference's AVX2
+attention composed as its attend_q8, all host threads) and prints the same line
+with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q8 GQA decode attention tokens/s and HBM GB/s (% peak) at 1/2/4/8 B200"
+QK, BB = 32, 36
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _traffic_from_profile(name: str):
+    """dram bytes per launch recorded from an ncu capture (profiles/<name>.txt)."""
+    path = os.path.join(ROOT, "profiles", name + ".txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """Samples nvidia-smi every 200 ms while running (the driver's clock rule)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+        return False
+
+    def summary(self):
+        rows = [l.split(", ") for l in (getattr(self, "out", "") or "").strip().splitlines() if l.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if n_gpus > 1 and world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} needs torchrun with {n_gpus} processes (WORLD_SIZE={world})")
+    return rank, local, world
+
+
+def pg_init(world, local):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist if world > 1 else None
+
+
+def max_over_ranks(dist, value: float) -> float:
+    import torch
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    import torch
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+class Config2:
+    """Llama-3-8B-shaped decode: L layers of one sequence, fused append + attention."""
+    name = "config2"
+
+    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096):
+        import torch
+        from tailorquantkernel_b200 import tqk
+        self.tqk = tqk
+        self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
+        self.mt = pos + 1
+        self.nb = hd // QK
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        shape = (layers, n_kv, self.mt, hd)
+        # setup (untimed): N(0,1) K/V quantised by the device quantiser into the cache
+        self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+        self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+        rng = np.random.default_rng(seed)
+        q = rope_np(rng.standard_normal((layers, n_q * hd), dtype=np.float32), hd, pos, 500000.0)
+        self.q = torch.from_numpy(q).cuda()
+        self.k_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
+        self.v_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
+        self.out = torch.empty(layers, n_q * hd, device="cuda")
+        self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
+                                    item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
+                                    q_item_stride=n_q * hd, out_item_stride=n_q * hd, k_new=self.k_new,
+                                    v_new=self.v_new, kv_new_item_stride=n_kv * hd)
+        # algorithmic bytes of one step: K/V rows read + the appended Q8 rows written
+        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * self.nb * BB
+        self.append_bytes = 2 * layers * n_kv * self.nb * BB
+        self.bytes_per_step = self.kv_bytes + self.append_bytes
+        self.tokens_per_step = 1
+        self.launches_per_step = 1
+        # pinned host buffers of the end-to-end leg
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_k = self.k_new.cpu().pin_memory()
+        self.h_v = self.v_new.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_q.numel() * 4 + self.h_k.numel() * 4 + self.h_v.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+
+    def step(self):
+        self.tqk.decode(self.args)
+
+    def step_e2e(self):
+        import torch
+        s = torch.cuda.current_stream()
+        self.q.copy_(self.h_q, non_blocking=True)
+        self.k_new.copy_(self.h_k, non_blocking=True)
+        self.v_new.copy_(self.h_v, non_blocking=True)
+        self.tqk.decode(self.args)
+        self.h_out.copy_(self.out, non_blocking=True)
+        s.synchronize()
+
+    def describe(self):
+        return {"workload": "config2: Llama-3-8B-shaped Q8 GQA decode, all 32 layers, 32 q / 8 kv heads, "
+                            "head_dim 128, context 4096 + 1 appended token (n=4097), RoPE(500000) q",
+                "layers": self.L, "seq_len": self.pos + 1, "kv_bytes_per_token": self.kv_bytes,
+                "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
+
+    # the reference's CPU path on the same workload (host planes)
+    def host_planes(self):
+        return self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), \
+            self.k_new.cpu().numpy(), self.v_new.cpu().numpy()
+
+
+def rope_np(x, hd, pos, theta):
+    """Half-split RoPE of the reference (model/rope.c:4-22) on every head of x [..., heads*hd]."""
+    i = np.arange(hd // 2, dtype=np.float64)
+    a = pos * np.power(theta, -2.0 * i / hd)
+    c, s = np.cos(a), np.sin(a)
+    h = x.reshape(-1, hd).astype(np.float64)
+    x0, x1 = h[:, : hd // 2].copy(), h[:, hd // 2:].copy()
+    h[:, : hd // 2] = x0 * c - x1 * s
+    h[:, hd // 2:] = x0 * s + x1 * c
+    return h.astype(np.float32).reshape(x.shape)
+
+
+class HostConfig2:
+    """Config 2 built on the host only, for the reference arm: K/V ~ N(0,1) per
+    layer quantised by the reference's own quantize_row_q8."""
+
+    def __init__(self, orc, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096):
+        self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
+        self.mt = pos + 1
+        self.nb = hd // QK
+        rng = np.random.default_rng(seed)
+        row = self.nb * BB
+        self.kp = np.empty((layers, n_kv, self.mt, row), np.uint8)
+        self.vp = np.empty((layers, n_kv, self.mt, row), np.uint8)
+        for layer in range(layers):
+            self.kp[layer] = orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
+            self.vp[layer] = orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
+        self.q = rope_np(rng.standard_normal((layers, n_q * hd), dtype=np.float32), hd, pos, 500000.0)
+        self.k_new = rng.standard_normal((layers, n_kv * hd), dtype=np.float32)
+        self.v_new = rng.standard_normal((layers, n_kv * hd), dtype=np.float32)
+        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * row
+        self.bytes_per_step = self.kv_bytes + 2 * layers * n_kv * row
+
+    def host_planes(self):
+        return self.kp, self.vp, self.q, self.k_new, self.v_new
+
+    def describe(self):
+        return Config2.describe(self)
+
+
+# ---------------------------------------------------------------------------
+# reference CPU path (oracle/_ref: the reference's AVX2 build) -- baseline only
+# ---------------------------------------------------------------------------
+def reference_oracle():
+    """The reference's AVX2 build when it was compiled here, else the restatement."""
+    import oracle
+    kind = "reference" if oracle.available("ref_avx2") else "port"
+    return oracle.Oracle("ref_avx2" if kind == "reference" else "port"), kind
+
+
+def reference_token_seconds(orc, wl, budget_s: float, max_tokens: int | None = None, min_tokens: int = 2):
+    """Times the reference's CPU store_kv + attend_q8 for whole tokens (all
+    layers), with all host threads, until `budget_s` passes (at least
+    min_tokens).  Returns (median seconds per token, tokens, threads)."""
+    threads = os.cpu_count() or 1
+    kp, vp, q, kn, vn = wl.host_planes()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end or len(times) < min_tokens) and (max_tokens is None or len(times) < max_tokens):
+        t0 = time.perf_counter()
+        for layer in range(wl.L):
+            orc.store_kv(kp[layer], vp[layer], wl.nkv, wl.hd, wl.mt, wl.pos, kn[layer], vn[layer])
+            orc.attend(kp[layer], vp[layer], wl.nq, wl.nkv, wl.hd, wl.mt, wl.pos, q[layer], threads=threads)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times), threads
+
+
+def run_reference(args):
+    rank, local, world = dist_init(args.gpus)
+    if rank != 0:
+        return 0  # the reference is a single-process CPU library: rank 0 alone runs it
+    orc, kind = reference_oracle()
+    wl = HostConfig2(orc, seed=1000)
+    reference_token_seconds(orc, wl, 0.0, max_tokens=args.warmup, min_tokens=args.warmup)
+    sec, n, threads = reference_token_seconds(orc, wl, 0.0, max_tokens=args.steps, min_tokens=args.steps)
+    value = 1.0 / sec
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
+            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "impl": "reference",
+            "config": {**wl.describe(), "global_batch": 1, "parallelism": "reference CPU (OpenMP over kv heads)"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                             "sample": f"{n} whole tokens of config 2 (32 layers of store_kv + attend_q8), median"},
+            "hbm_gbs_equivalent": wl.bytes_per_step / sec / 1e9,
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    rank, local, world = dist_init(args.gpus)
+    torch.cuda.set_device(local)
+    dist = pg_init(world, local)
+    from tailorquantkernel_b200 import tqk
+    peak, peak_kind = _peaks()
+
+    wl = Config2(seed=1000 + rank)
+    stream = torch.cuda.current_stream()
+    for _ in range(max(args.warmup, 3)):
+        wl.step()
+    barrier(dist)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        barrier(dist)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            wl.step()
+        ev1.record(stream)
+        barrier(dist)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    t = max_over_ranks(dist, t_local)
+    status = tqk.device_status()
+
+    # end to end through the C ABI with host buffers (pinned H2D of q/k/v, D2H of out)
+    for _ in range(2):
+        wl.step_e2e()
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        wl.step_e2e()
+    t_e2e = max_over_ranks(dist, time.perf_counter() - t0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        orc, kind = reference_oracle()
+        sec, n, threads = reference_token_seconds(orc, wl, args.cpu_seconds)
+        cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{n} whole tokens of config 2 (32 layers of store_kv + attend_q8), "
+                         f"~{args.cpu_seconds:.0f} s budget, median per token"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        per_launch = t_local / (args.steps * wl.launches_per_step)
+        achieved = wl.bytes_per_step / per_launch / 1e9
+        traffic = _traffic_from_profile("decode_q8_config2")
+        line = {
+            "metric": METRIC,
+            "value": world * args.steps * wl.tokens_per_step / t,
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8+fp32",
+            "data": "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q",
+            "config": {**wl.describe(), "global_batch": world, "parallelism":
+                       "batch-sharded: one sequence per GPU, no collective" if world > 1 else "single GPU"},
+            "hbm_gbs": achieved,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": wl.bytes_per_step,
+                         "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * args.steps / t_e2e, "unit": "tokens/s",
+                    "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
+                    "api": "tqk_decode_q8 (C ABI) with pinned host q/k/v in and attention output out, "
+                           "stream-synchronised every step"},
+            "gpu_launches": args.steps * wl.launches_per_step,
+            "clocks": clk.summary(),
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=2, choices=[2])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,188 @@
+/*
+ * tqk.h -- C ABI of the B200 (sm_100a) Q8 GQA attention kernels.
+ *
+ * This is the boundary the reference's plain-C attention layer binds to.  All
+ * entry points take plain device pointers and sizes, run asynchronously on the
+ * given CUDA stream (NULL = the legacy default stream), and return an int
+ * status: 0 on success, a negative TQK_E* code otherwise (never abort).  Device
+ * pointers to Q8 planes must be 16-byte aligned (cudaMalloc memory is).
+ *
+ * Data format (identical bytes to the reference):
+ *   block_q8 = { float d; int8_t q[32]; }, 36 bytes, no padding
+ *       (reference packer/packer.h:7-11);
+ *   a cache plane is [n_kv_heads][max_tokens][head_dim/32] blocks and the row
+ *       of kv head h at position t is slot h*max_tokens + t
+ *       (reference model/attention_layer.c:62-64, model/kv_cache.c:33-39);
+ *   q / out are head-major fp32 [n_q_heads][head_dim]; query head h reads kv
+ *       head h / (n_q_heads/n_kv_heads) (reference model/attention_layer.c:130-137).
+ */
+#ifndef TQK_H
+#define TQK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Exported symbols; the library is built with hidden default visibility. */
+#if defined(__GNUC__)
+#define TQK_API __attribute__((visibility("default")))
+#else
+#define TQK_API
+#endif
+
+#define TQK_QK 32
+typedef struct { float d; int8_t q[TQK_QK]; } tqk_block_q8;
+
+typedef void *tqk_stream_t; /* a cudaStream_t */
+
+/* Status codes.  -1 keeps the reference's meaning "position out of range"
+ * (reference model/attention_layer.c:172 and :203-204). */
+#define TQK_OK               0
+#define TQK_EPOS            -1
+#define TQK_EINVAL         -20  /* bad shape or NULL pointer */
+#define TQK_EALIGN         -21  /* a device pointer is not 16-byte aligned */
+#define TQK_EWORKSPACE     -22  /* caller workspace smaller than tqk_decode_workspace_size() */
+#define TQK_ECUDA          -23  /* CUDA runtime error; tqk_last_error() has the text */
+#define TQK_ENODEV         -24  /* no usable CUDA device */
+#define TQK_ETIMEOUT       -25  /* a device-side bounded wait gave up (see tqk_device_status) */
+#define TQK_EUNSUPPORTED   -26  /* head_dim > 256 or another shape outside the kernels' range */
+
+TQK_API const char *tqk_status_string(int status);
+/* Text of the last failure on the calling host thread ("" if none). */
+TQK_API const char *tqk_last_error(void);
+/* Library version string, e.g. "tqk 0.1 sm_100a". */
+TQK_API const char *tqk_version(void);
+
+/* Reads (and with clear != 0 resets) the sticky device-side error word of the
+ * current device: 0 when no kernel reported a timeout or bad input.  Synchronises
+ * the device.  The kernels set it instead of trapping. */
+TQK_API int tqk_device_status(int *device_error, int clear);
+
+/* ---------------------------------------------------------------------------
+ * Quantiser.  Replaces quantize_row_q8 (reference kernel/quant_x.c:12-34) for
+ * rows resident in device memory: rows x n floats -> rows x n/32 blocks, n a
+ * multiple of 32.  Bit-exact with the reference (int8 values and fp32 scales),
+ * including zero, denormal, Inf and NaN inputs.
+ */
+TQK_API int tqk_quantize_rows_q8(const float *x, tqk_block_q8 *out, int rows, int n, tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * KV append.  Replaces the Q8 branch of store_kv (reference
+ * model/attention_layer.c:66-90): quantises the n_kv rows of k and v (fp32
+ * [n_kv][head_dim], device) into slot h*max_tokens+pos of each plane.
+ * Returns TQK_EPOS without touching the planes when pos is outside [0, max_tokens).
+ */
+TQK_API int tqk_store_kv_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_kv_heads, int head_dim,
+                    int max_tokens, int pos, const float *k, const float *v, tqk_stream_t stream);
+
+/* Batched append of n consecutive positions pos0..pos0+n-1 (the append half of
+ * attention_layer_batch, reference model/attention_layer.c:221-236): k, v are
+ * [n][n_kv][head_dim] fp32 (token-major, as the reference's ws->k / ws->v). */
+TQK_API int tqk_store_kv_q8_batch(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_kv_heads, int head_dim,
+                          int max_tokens, int pos0, int n, const float *k, const float *v,
+                          tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Reference-shaped single kernels (model/attn_q8.c:56-76 dispatchers and
+ * model/softmax.c:4).  These keep the reference's per-op contract (strided score
+ * rows, strided outputs, nothing written past n or head_dim) so the reference's
+ * kernel tests can drive them; the fused decode below is the fast path.
+ */
+/* scores[h*stride + t] = scale * sum_b (float)dot_int(q[h][b], k[t][b]) * (qd*kd),
+ * bit-exact with attn_scores_q8_scalar (model/attn_q8.c:17-34). */
+TQK_API int tqk_attn_scores_q8(const tqk_block_q8 *q, int g, const tqk_block_q8 *k, int n, int nb, float scale,
+                       float *scores, size_t stride, tqk_stream_t stream);
+/* out[h*out_stride + j] = sum_t (w[h*w_stride+t] * vd) * vq, token order, bit-exact
+ * with attn_accum_q8_scalar (model/attn_q8.c:36-54). */
+TQK_API int tqk_attn_accum_q8(const float *w, size_t w_stride, int g, const tqk_block_q8 *v, int n, int nb,
+                      float *out, size_t out_stride, tqk_stream_t stream);
+/* In-place softmax of `rows` rows of n floats, row r at x + r*stride (model/softmax.c:4-23). */
+TQK_API int tqk_softmax_rows(float *x, int rows, int n, size_t stride, tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused decode attention (the hot path).  Replaces attend_q8 (reference
+ * model/attention_layer.c:125-150) -- quantise the group's q heads, int8 scores,
+ * softmax, Q8 V accumulation -- as one split-sequence (flash-decoding) kernel
+ * with an online FP32 softmax and a log-sum-exp merge of the splits, and
+ * optionally fuses the KV append of store_kv (model/attention_layer.c:66-90).
+ *
+ * One call covers n_items independent items (layers of one token, sequences of
+ * a batch, or both), each with its own planes, q, out and length:
+ *   item i reads planes k + i*item_stride, v + i*item_stride (in blocks),
+ *   q + i*q_item_stride, writes out + i*out_item_stride (in floats), and attends
+ *   to its first len_i positions, where
+ *     len_i = lens[i]                       if lens != NULL (device int32 array)
+ *     len_i = len0 + i*len_step             otherwise.
+ * With k_new/v_new non-NULL, item i first appends k_new + i*kv_new_item_stride
+ * (fp32 [n_kv][head_dim]) at position len_i - 1, bit-exact with store_kv, and
+ * the attention includes it, exactly as store_kv followed by attend_q8.
+ * len_i == 0 writes zeros (the reference's empty softmax leaves accum's zeros).
+ *
+ * out_mode TQK_OUT_NORMALIZED writes the attention output; TQK_OUT_PARTIAL
+ * writes per (item, q head) the unnormalised partial {acc[head_dim], m, l}
+ * (layout: out + i*out_item_stride + h*(head_dim+2)) for a cross-device
+ * log-sum-exp merge with tqk_merge_partials().
+ */
+#define TQK_OUT_NORMALIZED 0
+#define TQK_OUT_PARTIAL    1
+
+typedef struct {
+    tqk_block_q8 *k, *v;          /* planes of item 0 (device) */
+    int64_t item_stride;          /* blocks between consecutive items' planes (0 = shared planes) */
+    int n_items;
+    int n_q_heads, n_kv_heads, head_dim, max_tokens;
+    const int32_t *lens;          /* device [n_items], or NULL */
+    int len0, len_step;           /* used when lens == NULL */
+    int max_len;                  /* upper bound of len_i; sizes the grid */
+    const float *q;  int64_t q_item_stride;
+    float *out;      int64_t out_item_stride;
+    const float *k_new, *v_new;   /* optional fused append (device), or NULL */
+    int64_t kv_new_item_stride;
+    int out_mode;                 /* TQK_OUT_NORMALIZED or TQK_OUT_PARTIAL */
+    int split_tokens;             /* tokens per split (multiple of 64); 0 = choose automatically */
+} tqk_decode_args;
+
+/* Bytes of device workspace tqk_decode_q8 needs for these arguments. */
+TQK_API int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes);
+/* A caller workspace must be zeroed once before first use (tqk_workspace_init);
+ * every call leaves it zeroed again.  Calls that share a workspace must be
+ * ordered on one stream.  workspace == NULL uses a library-owned workspace per
+ * (device, stream), allocated on first use. */
+TQK_API int tqk_workspace_init(void *workspace, size_t bytes, tqk_stream_t stream);
+TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes, tqk_stream_t stream);
+
+/* attend_q8 for one layer of one sequence: n = pos + 1 positions
+ * (reference model/attention_layer.c:125-150); TQK_EPOS if pos is out of range. */
+TQK_API int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                  int head_dim, int max_tokens, int pos, const float *q, float *out, tqk_stream_t stream);
+
+/* store_kv + attend_q8 of one decode step for one layer, fused in one launch. */
+TQK_API int tqk_append_attend_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                         int head_dim, int max_tokens, int pos, const float *q, const float *k,
+                         const float *v, float *out, tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Chunked causal prefill (attention_layer_batch's append+attend loop, reference
+ * model/attention_layer.c:221-236): appends n tokens at pos0..pos0+n-1, then
+ * token i attends over positions <= pos0+i.  q/out [n][n_q][hd], k/v [n][n_kv][hd].
+ */
+TQK_API int tqk_prefill_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                   int head_dim, int max_tokens, int pos0, int n, const float *q, const float *k,
+                   const float *v, float *out, tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Log-sum-exp merge of n_parts partials written with TQK_OUT_PARTIAL (e.g. one
+ * per GPU of a sequence split, gathered into one buffer): parts is
+ * [n_parts][n_heads][head_dim+2], part p at parts + p*part_stride floats.
+ * out[h][j] = sum_p acc_p e^{m_p-M} / sum_p l_p e^{m_p-M}, M = max_p m_p.
+ */
+TQK_API int tqk_merge_partials(const float *parts, int n_parts, int64_t part_stride, int n_heads, int head_dim,
+                       float *out, tqk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TQK_H */

@@ -1,0 +1,195 @@
+"""CPU checkers for the Q8 attention path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference leg
+may import this package.  It binds, with ctypes and numpy:
+
+* ``port``       -- oracle/libtq_oracle.so, the scalar restatement (tq_oracle.c);
+* ``ref_scalar`` -- oracle/_ref/libtqref_scalar.so, the reference's own sources
+                    compiled without TQ_HAVE_AVX2 (its scalar path), plus
+                    ref_attend.c composing attend_q8 from its exported functions;
+* ``ref_avx2``   -- oracle/_ref/libtqref_avx2.so, the reference's AVX2/FMA build.
+
+All three expose the same methods.  Planes are numpy uint8 arrays of shape
+[n_kv, max_tokens, nb*36] (the reference layout, model/kv_cache.c:33-39).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+QK = 32
+BLOCK_BYTES = 36
+
+_LIBS = {
+    "port": os.path.join(HERE, "libtq_oracle.so"),
+    "ref_scalar": os.path.join(HERE, "_ref", "libtqref_scalar.so"),
+    "ref_avx2": os.path.join(HERE, "_ref", "libtqref_avx2.so"),
+}
+
+# symbol names per build: (port name, reference name)
+_NAMES = {
+    "quantize_row": ("tqo_quantize_row_q8", "quantize_row_q8"),
+    "softmax": ("tqo_softmax", "softmax"),
+    "scores": ("tqo_attn_scores_q8", "attn_scores_q8_scalar"),
+    "accum": ("tqo_attn_accum_q8", "attn_accum_q8_scalar"),
+    "scores_dispatch": ("tqo_attn_scores_q8", "attn_scores_q8"),
+    "accum_dispatch": ("tqo_attn_accum_q8", "attn_accum_q8"),
+    "head": ("tqo_attention_head_q8", "attention_head_q8"),
+    "store_kv": ("tqo_store_kv_q8", "refdrv_store_kv_q8"),
+    "attend": ("tqo_attend_q8", "refdrv_attend_q8"),
+    "prefill": ("tqo_prefill_q8", "refdrv_prefill_q8"),
+}
+
+
+def available(kind: str) -> bool:
+    return os.path.exists(_LIBS[kind])
+
+
+def build(reference: str | None = None) -> None:
+    """make -C oracle [ref]: the restatement always, the reference builds when its tree exists."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    ref = reference or os.environ.get("TQK_REFERENCE", "/root/reference")
+    if os.path.isdir(ref):
+        subprocess.run(["make", "-s", "-C", HERE, f"REF={ref}", "ref"], check=True)
+
+
+def _f32p(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def _vp(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class Oracle:
+    def __init__(self, kind: str = "port"):
+        path = _LIBS[kind]
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (run `make -C oracle` / `make -C oracle ref`)")
+        self.kind = kind
+        self.lib = ctypes.CDLL(path)
+        idx = 0 if kind == "port" else 1
+        self._fn = {k: getattr(self.lib, v[idx]) for k, v in _NAMES.items()}
+        for f in self._fn.values():
+            f.restype = None
+        for k in ("store_kv", "prefill"):
+            self._fn[k].restype = ctypes.c_int
+        vp, i, f, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+        self._fn["quantize_row"].argtypes = [vp, vp, i]
+        self._fn["softmax"].argtypes = [vp, i]
+        for k in ("scores", "scores_dispatch"):
+            self._fn[k].argtypes = [vp, i, vp, i, i, f, vp, sz]
+        for k in ("accum", "accum_dispatch"):
+            self._fn[k].argtypes = [vp, sz, i, vp, i, i, vp, sz]
+        self._fn["head"].argtypes = [vp, vp, vp, vp, i, i, vp, vp]
+        self._fn["store_kv"].argtypes = [vp, vp, i, i, i, i, vp, vp]
+        self._fn["attend"].argtypes = [vp, vp, i, i, i, i, i, vp, vp, vp, i]
+        self._fn["prefill"].argtypes = [vp, vp, i, i, i, i, i, i, vp, vp, vp, vp, vp, i]
+        if kind != "port":
+            self.lib.refdrv_max_threads.restype = i
+            self.lib.refdrv_quantize_rows.argtypes = [vp, vp, i, i]
+            self.lib.refdrv_quantize_rows.restype = None
+        else:
+            self.lib.tqo_quantize_rows_q8.argtypes = [vp, vp, i, i]
+            self.lib.tqo_quantize_rows_q8.restype = None
+
+    # --- quantiser -------------------------------------------------------
+    def quantize_rows(self, x: np.ndarray) -> np.ndarray:
+        """quantize_row_q8 per row of x [..., n] -> uint8 [..., n/32*36]."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = x.shape[-1]
+        rows = x.reshape(-1, n)
+        out = np.zeros((rows.shape[0], n // QK * BLOCK_BYTES), dtype=np.uint8)
+        if self.kind == "port":  # one C call for all rows
+            self.lib.tqo_quantize_rows_q8(_vp(rows), _vp(out), ctypes.c_int(rows.shape[0]), ctypes.c_int(n))
+            return out.reshape(*x.shape[:-1], n // QK * BLOCK_BYTES)
+        for r in range(rows.shape[0]):
+            self._fn["quantize_row"](ctypes.c_void_p(rows[r:].ctypes.data), ctypes.c_void_p(out[r:].ctypes.data), n)
+        return out.reshape(*x.shape[:-1], n // QK * BLOCK_BYTES)
+
+    def quantize_rows_bulk(self, x: np.ndarray) -> np.ndarray:
+        """Same as quantize_rows, with the row loop in C for both builds."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n = x.shape[-1]
+        rows = x.reshape(-1, n)
+        out = np.empty((rows.shape[0], n // QK * BLOCK_BYTES), dtype=np.uint8)
+        fn = self.lib.tqo_quantize_rows_q8 if self.kind == "port" else self.lib.refdrv_quantize_rows
+        fn(_vp(rows), _vp(out), ctypes.c_int(rows.shape[0]), ctypes.c_int(n))
+        return out.reshape(*x.shape[:-1], n // QK * BLOCK_BYTES)
+
+    def softmax(self, x: np.ndarray) -> np.ndarray:
+        y = np.ascontiguousarray(x, dtype=np.float32).copy()
+        self._fn["softmax"](_vp(y), y.shape[-1])
+        return y
+
+    # --- per-op kernels ----------------------------------------------------
+    def attn_scores(self, qb, g, kb, n, nb, scale, stride, dispatched=False, fill=np.nan):
+        sc = np.full(g * stride, fill, dtype=np.float32)
+        self._fn["scores_dispatch" if dispatched else "scores"](_vp(np.ascontiguousarray(qb)), g,
+                                                               _vp(np.ascontiguousarray(kb)), n, nb,
+                                                               ctypes.c_float(scale), _vp(sc), stride)
+        return sc
+
+    def attn_accum(self, w, w_stride, g, vb, n, nb, out_stride, dispatched=False, fill=np.nan):
+        out = np.full(g * out_stride, fill, dtype=np.float32)
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self._fn["accum_dispatch" if dispatched else "accum"](_vp(w), w_stride, g, _vp(np.ascontiguousarray(vb)), n,
+                                                             nb, _vp(out), out_stride)
+        return out
+
+    def attention_head(self, q, kb, vb, n, head_dim):
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        qq = np.zeros(head_dim // QK * BLOCK_BYTES, dtype=np.uint8)
+        sc = np.zeros(max(n, 1), dtype=np.float32)
+        out = np.zeros(head_dim, dtype=np.float32)
+        self._fn["head"](_vp(q), _vp(qq), _vp(np.ascontiguousarray(kb)), _vp(np.ascontiguousarray(vb)), n, head_dim,
+                         _vp(sc), _vp(out))
+        return out, qq, sc[:n]
+
+    # --- cache + attention ---------------------------------------------------
+    def store_kv(self, kp, vp, n_kv, head_dim, max_tokens, pos, k, v) -> int:
+        return self._fn["store_kv"](_vp(kp), _vp(vp), n_kv, head_dim, max_tokens, pos,
+                                    _vp(np.ascontiguousarray(k, dtype=np.float32)),
+                                    _vp(np.ascontiguousarray(v, dtype=np.float32)))
+
+    def attend(self, kp, vp, n_q, n_kv, head_dim, max_tokens, pos, q, threads=1) -> np.ndarray:
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        scores = np.zeros(n_q * max_tokens, dtype=np.float32)
+        out = np.zeros(n_q * head_dim, dtype=np.float32)
+        self._fn["attend"](_vp(kp), _vp(vp), n_q, n_kv, head_dim, max_tokens, pos, _vp(q), _vp(scores), _vp(out),
+                           threads)
+        return out
+
+    def prefill(self, kp, vp, n_q, n_kv, head_dim, max_tokens, pos0, n, q, k, v, threads=1) -> np.ndarray:
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        scores = np.zeros(n_q * max_tokens, dtype=np.float32)
+        out = np.zeros(n * n_q * head_dim, dtype=np.float32)
+        rc = self._fn["prefill"](_vp(kp), _vp(vp), n_q, n_kv, head_dim, max_tokens, pos0, n, _vp(q),
+                                 _vp(np.ascontiguousarray(k, dtype=np.float32)),
+                                 _vp(np.ascontiguousarray(v, dtype=np.float32)), _vp(scores), _vp(out), threads)
+        if rc != 0:
+            raise ValueError(f"prefill returned {rc}")
+        return out
+
+    def max_threads(self) -> int:
+        return self.lib.refdrv_max_threads() if self.kind != "port" else os.cpu_count() or 1
+
+
+def dequantize(blocks: np.ndarray) -> np.ndarray:
+    """uint8 [..., nb*36] -> float32 [..., nb*32]: d * q per block."""
+    b = np.ascontiguousarray(blocks).reshape(*blocks.shape[:-1], -1, BLOCK_BYTES)
+    d = b[..., :4].copy().view(np.float32)
+    q = b[..., 4:].view(np.int8).astype(np.float32)
+    return (d * q).reshape(*blocks.shape[:-1], -1)
+
+
+def attention_f64(q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:
+    """float64 softmax attention of one head (tools/test_model.c:424-454 semantics)."""
+    q = q.astype(np.float64)
+    s = (k.astype(np.float64) @ q) / np.sqrt(q.shape[-1])
+    p = np.exp(s - s.max())
+    return (p[:, None] * v.astype(np.float64)).sum(0) / p.sum()

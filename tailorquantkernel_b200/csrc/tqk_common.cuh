@@ -1,0 +1,146 @@
+// tqk_common.cuh -- device helpers shared by the sm_100a Q8 attention kernels.
+//
+// * The Q8 block format (36 bytes: fp32 scale + 32 int8) and the bit-exact
+//   device quantiser of reference kernel/quant_x.c:5-34.
+// * Thin inline-PTX wrappers for the 1-D TMA bulk copy (cp.async.bulk, never the
+//   .multicast form) and mbarriers, with time-bounded waits that record an error
+//   instead of hanging.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/tqk.h"
+
+namespace tqk {
+
+constexpr int QK = 32;
+constexpr int BLOCK_BYTES = 36;
+static_assert(sizeof(tqk_block_q8) == BLOCK_BYTES, "tqk_block_q8 must be 36 bytes");
+
+// Device error codes written to the sticky error word (tqk_device_status).
+enum : int { DEVERR_NONE = 0, DEVERR_TIMEOUT = 1, DEVERR_BADLEN = 2 };
+
+// Kernels report failures into a sticky per-device error word that the runtime
+// allocates (tqk_device_status reads it) and passes to every launch.
+__device__ __forceinline__ void record_error(int *err, int code) {
+    if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// ----------------------------------------------------------------------------
+// Quantiser (reference kernel/quant_x.c:5-34).  Every float operation is an
+// explicitly rounded intrinsic so nvcc cannot contract or reorder it:
+//   d   = amax / 127.0f           (IEEE division)
+//   inv = d != 0 ? 1.0f / d : 0   (IEEE division)
+//   q   = low byte of bits(x*inv + 1.5*2^23) - 0x4B400000
+// which reproduces the reference's magic-number rounding for every input,
+// including Inf/NaN (where a cvt.rni would differ).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float q8_scale(float amax) { return __fdiv_rn(amax, 127.0f); }
+__device__ __forceinline__ float q8_inverse(float d) { return d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f; }
+__device__ __forceinline__ int8_t q8_round(float x, float inv) {
+    const float shifted = __fadd_rn(__fmul_rn(x, inv), 12582912.0f);
+    return (int8_t)(__float_as_int(shifted) - 0x4B400000);
+}
+// |x| as the reference's max loop sees it: NaN never exceeds the running max.
+__device__ __forceinline__ float q8_absmax(float a, float x) {
+    const float ax = fabsf(x);
+    return ax > a ? ax : a;
+}
+
+// Quantise one 32-float block held one element per lane of a full warp.
+// Returns this lane's int8; *d receives the block scale (all lanes).
+__device__ __forceinline__ int8_t warp_quantize_block(float x, float *d) {
+    float m = q8_absmax(0.0f, x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, m, o);
+        m = other > m ? other : m;
+    }
+    const float s = q8_scale(m);
+    *d = s;
+    return q8_round(x, q8_inverse(s));
+}
+
+// ----------------------------------------------------------------------------
+// PTX wrappers: mbarrier + 1-D bulk async copy global -> shared.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: spins on try_wait (which itself suspends for a short while)
+// until the phase completes or `limit_ns` of wall time pass.  Returns false on
+// timeout and records DEVERR_TIMEOUT; never waits forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns, int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            record_error(err, DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// 1-D TMA bulk copy (non-multicast).  dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_copy_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ----------------------------------------------------------------------------
+// int8 helpers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Four signed bytes of w -> four exact floats, via the 2^23 exponent trick:
+// bias each byte to unsigned (xor 0x80), place it in the low mantissa byte of
+// 2^23 (0x4B000000) and subtract 2^23 + 128.  All integer ALU + one FADD each.
+__device__ __forceinline__ void s8x4_to_f32(uint32_t w, float &f0, float &f1, float &f2, float &f3) {
+    const uint32_t u = w ^ 0x80808080u;
+    const float bias = 8388736.0f;  // 2^23 + 128
+    f0 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)), bias);
+    f1 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)), bias);
+    f2 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)), bias);
+    f3 = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)), bias);
+}
+
+}  // namespace tqk

@@ -1,0 +1,778 @@
+// tqk_decode.cu -- fused Q8 GQA decode attention for sm_100a (the hot path).
+//
+// Replaces attend_q8 (reference model/attention_layer.c:125-150) and, fused,
+// store_kv's Q8 branch (:66-90).  Design (one CTA = one contiguous token range
+// of one kv head of one item, serving all q heads of the group):
+//
+//   * K/V rows (144 B for head_dim 128 = 4 blocks of 36 B, 16-byte aligned) of
+//     a 64-token tile are one contiguous byte range per plane; thread 0 streams
+//     them into a STAGES-deep shared-memory ring with 1-D TMA bulk copies
+//     (cp.async.bulk, no multicast) completing on mbarriers, so each K/V byte
+//     leaves HBM exactly once per launch.
+//   * q is quantised in-kernel with the bit-exact device quantiser; scores use
+//     dp4a on int8 (exact int32 block sums) and then the reference's rounding
+//     sequence acc += (float)sum * (qd*kd), acc * scale with explicitly rounded
+//     intrinsics, so every score equals attn_scores_q8_scalar's bit for bit.
+//   * online softmax in FP32 per q head; V accumulation o += (p*vd) * (float)q
+//     with threads owning 4-column slices and warps owning token subsets.
+//   * splits write (m, l, acc) partials; the last CTA of an (item, kv head)
+//     (atomic ticket, no waiting) merges them by log-sum-exp in split order, so
+//     results are deterministic.
+#include "tqk_internal.h"
+
+#include <cmath>
+#include <mutex>
+
+namespace tqk {
+
+constexpr int DEC_THREADS = 128;
+constexpr int DEC_WARPS = DEC_THREADS / 32;
+constexpr int DEC_T = 64;          // tokens per tile
+constexpr int MAX_SPLITS = 256;    // bound on splits per (item, kv head)
+constexpr uint64_t WAIT_NS = 1000000000ull;   // 1 s bound on any mbarrier wait
+constexpr uint64_t DRAIN_NS = 20000000ull;    // 20 ms bound when draining after a timeout
+
+struct DecodeParams {
+    const uint8_t *k, *v;        // planes of item 0 (bytes)
+    uint8_t *kw, *vw;            // the same planes, writable (fused append)
+    long long item_stride;       // bytes between items' planes
+    int n_items, n_kv, group, max_tokens;
+    int heads_per_cta, head_slices, pairs;  // pairs = n_kv * head_slices
+    const int *lens;
+    int len0, len_step;
+    const float *q;
+    long long q_item_stride;     // floats
+    float *out;
+    long long out_item_stride;   // floats
+    const float *k_new, *v_new;
+    long long kv_new_item_stride;  // floats
+    int out_mode;
+    int split_tokens;            // multiple of DEC_T
+    int max_splits;
+    float scale;
+    float *part;                 // [n_items][pairs][max_splits][GMAX][HD+2]
+    int *counters;               // [n_items][pairs]
+    int *err;
+};
+
+template <int NB>
+constexpr int stages_for() { return NB >= 8 ? 2 : 3; }
+
+// Shared-memory layout of one CTA (bytes; every region 16-byte aligned).
+template <int NB, int GMAX>
+struct DecLayout {
+    static constexpr int HD = NB * QK;
+    static constexpr int ROW = NB * BLOCK_BYTES;
+    static constexpr int TILE = DEC_T * ROW;   // one plane's tile
+    static constexpr int STAGES = stages_for<NB>();
+    static constexpr int STAGE_BYTES = 2 * TILE;
+    static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+    static constexpr int OFF_QQ = OFF_BAR + 64;
+    static constexpr int OFF_QD = OFF_QQ + GMAX * HD;
+    static constexpr int OFF_SC = OFF_QD + ((GMAX * NB * 4 + 15) / 16) * 16;
+    static constexpr int OFF_PV = OFF_SC + GMAX * DEC_T * 4;
+    static constexpr int OFF_STATE = OFF_PV + DEC_T * NB * GMAX * 4;  // m, l, corr
+    static constexpr int OFF_NEW = OFF_STATE + ((3 * GMAX * 4 + 15) / 16) * 16;
+    static constexpr int OFF_FLAG = OFF_NEW + ((2 * ROW + 15) / 16) * 16;
+    static constexpr int BYTES = OFF_FLAG + 16;
+    // after the pipeline drains, the stage ring is reused for the cross-warp
+    // reduction and the merge weights
+    static constexpr int RED_BYTES = DEC_WARPS * GMAX * HD * 4;
+    static constexpr int WTS_BYTES = MAX_SPLITS * GMAX * 4;
+    static_assert(RED_BYTES + WTS_BYTES <= OFF_BAR, "stage ring too small for the epilogue scratch");
+    static_assert(TILE % 16 == 0, "tiles must be whole 16-byte units");
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Score of one cached K row against one quantised q head, with the rounding
+// sequence of attn_scores_q8_scalar (reference model/attn_q8.c:24-31).
+template <int NB>
+__device__ __forceinline__ float score_row(const uint8_t *row, const uint32_t (&qw)[NB * 8], const float (&qds)[NB],
+                                           float scale) {
+    float acc = 0.0f;
+    if constexpr (NB % 4 == 0) {
+#pragma unroll
+        for (int b4 = 0; b4 < NB / 4; b4++) {
+            uint32_t w[36];
+            const uint4 *r4 = reinterpret_cast<const uint4 *>(row + b4 * 4 * BLOCK_BYTES);
+#pragma unroll
+            for (int i = 0; i < 9; i++) {
+                const uint4 u = r4[i];
+                w[4 * i + 0] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+            }
+#pragma unroll
+            for (int bb = 0; bb < 4; bb++) {
+                const int b = b4 * 4 + bb;
+                int sum = 0;
+#pragma unroll
+                for (int k = 0; k < 8; k++) sum = __dp4a((int)w[bb * 9 + 1 + k], (int)qw[b * 8 + k], sum);
+                const float kd = __uint_as_float(w[bb * 9]);
+                acc = __fadd_rn(acc, __fmul_rn(__int2float_rn(sum), __fmul_rn(qds[b], kd)));
+            }
+        }
+    } else {
+        const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            int sum = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) sum = __dp4a((int)rw[b * 9 + 1 + k], (int)qw[b * 8 + k], sum);
+            const float kd = __uint_as_float(rw[b * 9]);
+            acc = __fadd_rn(acc, __fmul_rn(__int2float_rn(sum), __fmul_rn(qds[b], kd)));
+        }
+    }
+    return __fmul_rn(acc, scale);
+}
+
+template <int NB, int GMAX>
+__global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodeParams p) {
+    using L = DecLayout<NB, GMAX>;
+    constexpr int HD = L::HD, ROW = L::ROW, STAGES = L::STAGES;
+    constexpr bool kTma = (NB % 4 == 0);  // 144-byte rows: every tile is 16-byte aligned
+    constexpr int CPL = (HD / 32 < 4) ? 4 : HD / 32;  // V columns per lane
+    constexpr int LPT = HD / CPL;                     // lanes per token row
+    constexpr int TPW = 32 / LPT;                     // token rows per warp pass
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    const int item = blockIdx.z;
+    const int pair = blockIdx.y;
+    const int kvh = pair / p.head_slices;
+    const int slice = pair - kvh * p.head_slices;
+    const int g0 = slice * p.heads_per_cta;
+    const int G = min(p.heads_per_cta, p.group - g0);
+    int len = p.lens ? p.lens[item] : p.len0 + item * p.len_step;
+    if (len < 0 || len > p.max_tokens) {
+        if (tid == 0) record_error(p.err, DEVERR_BADLEN);
+        len = len < 0 ? 0 : p.max_tokens;
+    }
+    int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
+    if (n_splits > p.max_splits) {  // a device length above the max_len the grid was sized for
+        if (tid == 0) record_error(p.err, DEVERR_BADLEN);
+        n_splits = p.max_splits;
+        len = p.max_splits * p.split_tokens;
+    }
+    const int s = blockIdx.x;
+    if (s >= (n_splits > 0 ? n_splits : 1)) return;
+    const int qh0 = kvh * p.group + g0;
+    float *out_item = p.out + (long long)item * p.out_item_stride;
+
+    if (len == 0) {  // empty context: zeros, like the reference's accum over no tokens
+        for (int i = tid; i < G * HD; i += DEC_THREADS) {
+            const int g = i / HD, c = i - g * HD;
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                out_item[(long long)(qh0 + g) * HD + c] = 0.0f;
+            } else {
+                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+                o[c] = 0.0f;
+                if (c == 0) { o[HD] = -INFINITY; o[HD + 1] = 0.0f; }
+            }
+        }
+        return;
+    }
+
+    const int t_begin = s * p.split_tokens;
+    const int t_end = min(len, t_begin + p.split_tokens);
+    const int n_tiles = (t_end - t_begin + DEC_T - 1) / DEC_T;
+    const long long head_off = (long long)kvh * p.max_tokens * ROW;
+    const uint8_t *kbase = p.k + (long long)item * p.item_stride + head_off;
+    const uint8_t *vbase = p.v + (long long)item * p.item_stride + head_off;
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    int8_t *qq = reinterpret_cast<int8_t *>(smem + L::OFF_QQ);
+    float *qd = reinterpret_cast<float *>(smem + L::OFF_QD);
+    float *sc = reinterpret_cast<float *>(smem + L::OFF_SC);
+    float *pv = reinterpret_cast<float *>(smem + L::OFF_PV);
+    float *m_s = reinterpret_cast<float *>(smem + L::OFF_STATE);
+    float *l_s = m_s + GMAX;
+    float *corr_s = l_s + GMAX;
+    uint8_t *newrow = smem + L::OFF_NEW;
+    int *flag = reinterpret_cast<int *>(smem + L::OFF_FLAG);
+
+    auto issue = [&](int j) {
+        const int slot = j % STAGES;
+        const int t0 = t_begin + j * DEC_T;
+        const int rows = min(DEC_T, t_end - t0);
+        const uint32_t bytes = (uint32_t)(rows * ROW);
+        uint8_t *ks = smem + slot * L::STAGE_BYTES;
+        mbar_arrive_expect_tx(&bars[slot], 2 * bytes);
+        bulk_copy_g2s(ks, kbase + (long long)t0 * ROW, bytes, &bars[slot]);
+        bulk_copy_g2s(ks + L::TILE, vbase + (long long)t0 * ROW, bytes, &bars[slot]);
+    };
+
+    if (kTma && tid == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+        for (int j = 0; j < min(STAGES - 1, n_tiles); j++) issue(j);
+    }
+    for (int i = tid; i < GMAX; i += DEC_THREADS) {
+        m_s[i] = -INFINITY;
+        l_s[i] = 0.0f;
+        corr_s[i] = 1.0f;
+    }
+    for (int i = tid; i < DEC_T * NB * GMAX; i += DEC_THREADS) pv[i] = 0.0f;
+
+    // quantise this CTA's q heads: one warp per 32-float block (quant_x.c:12-34)
+    const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
+    for (int blk = warp; blk < GMAX * NB; blk += DEC_WARPS) {
+        const int g = blk / NB, b = blk - g * NB;
+        const float x = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
+        float d;
+        const int8_t v8 = warp_quantize_block(x, &d);
+        qq[g * HD + b * QK + lane] = v8;
+        if (lane == 0) qd[g * NB + b] = d;
+    }
+
+    // fused append (store_kv, attention_layer.c:66-90): the split holding
+    // position len-1 quantises the new K/V rows, writes them to the cache and
+    // substitutes them for that row of its staged tile
+    const bool do_append = p.k_new != nullptr && s == n_splits - 1;
+    const int pos = len - 1;
+    if (do_append && warp < 2) {
+        const float *src = (warp == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride +
+                           (long long)kvh * HD;
+        uint8_t *nrow = newrow + warp * ROW;
+        uint8_t *grow = (warp == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + head_off + (long long)pos * ROW;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float d;
+            const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+            nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+            if (lane == 0) *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
+            if (slice == 0) {
+                grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+                if (lane == 0) *reinterpret_cast<float *>(grow + b * BLOCK_BYTES) = d;
+            }
+        }
+    }
+    __syncthreads();
+
+    // this thread's q head for the score phase (DEC_THREADS % GMAX == 0, so it is fixed)
+    const int gq = tid % GMAX;
+    uint32_t qw[NB * 8];
+    float qds[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        qds[b] = qd[gq * NB + b];
+#pragma unroll
+        for (int k = 0; k < 8; k++) qw[b * 8 + k] = reinterpret_cast<const uint32_t *>(qq + gq * HD + b * QK)[k];
+    }
+
+    const int sub_t = lane / LPT;
+    const int c0 = (lane % LPT) * CPL;
+    const int vb = c0 / QK;
+    float acc[GMAX][CPL];
+#pragma unroll
+    for (int g = 0; g < GMAX; g++)
+#pragma unroll
+        for (int c = 0; c < CPL; c++) acc[g][c] = 0.0f;
+
+    for (int j = 0; j < n_tiles; j++) {
+        const int slot = j % STAGES;
+        const int t0 = t_begin + j * DEC_T;
+        const int rows = min(DEC_T, t_end - t0);
+        uint8_t *ks = smem + slot * L::STAGE_BYTES;
+        uint8_t *vs = ks + L::TILE;
+        bool ok = true;
+        if constexpr (kTma) {
+            // slot (j-1)%STAGES was released by the trailing barrier of iteration j-1
+            if (tid == 0 && j + STAGES - 1 < n_tiles) issue(j + STAGES - 1);
+            ok = mbar_wait_bounded(&bars[slot], (uint32_t)((j / STAGES) & 1), WAIT_NS, p.err);
+        } else {
+            // rows of 36 or 72 bytes are only 4-byte aligned: cooperative word copy
+            const uint32_t *gk = reinterpret_cast<const uint32_t *>(kbase + (long long)t0 * ROW);
+            const uint32_t *gv = reinterpret_cast<const uint32_t *>(vbase + (long long)t0 * ROW);
+            uint32_t *sk = reinterpret_cast<uint32_t *>(ks);
+            uint32_t *sv = reinterpret_cast<uint32_t *>(vs);
+            const int words = rows * ROW / 4;
+            for (int i = tid; i < words; i += DEC_THREADS) {
+                sk[i] = __ldg(gk + i);
+                sv[i] = __ldg(gv + i);
+            }
+        }
+        const bool has_new = do_append && pos >= t0 && pos < t0 + rows;  // CTA-uniform
+        if (!kTma || has_new) {
+            if (has_new) {
+                __syncthreads();  // every thread has seen the tile land before it is patched
+                const int r = pos - t0;
+                for (int i = tid; i < ROW / 4; i += DEC_THREADS) {
+                    reinterpret_cast<uint32_t *>(ks + r * ROW)[i] = reinterpret_cast<const uint32_t *>(newrow)[i];
+                    reinterpret_cast<uint32_t *>(vs + r * ROW)[i] =
+                        reinterpret_cast<const uint32_t *>(newrow + ROW)[i];
+                }
+            }
+            __syncthreads();
+        }
+
+        // scores: thread -> (q head gq, tokens tid/GMAX + k*DEC_THREADS/GMAX)
+        for (int it = tid; it < DEC_T * GMAX; it += DEC_THREADS) {
+            const int tt = it / GMAX;
+            float sv = -INFINITY;
+            if (gq < G && tt < rows) sv = score_row<NB>(ks + tt * ROW, qw, qds, p.scale);
+            sc[gq * DEC_T + tt] = sv;
+        }
+        if (!__syncthreads_and(ok)) {
+            // a tile never arrived: drain our outstanding copies (bounded) and leave
+            if (kTma && tid == 0) {
+                for (int jj = j; jj < min(j + STAGES - 1, n_tiles); jj++)
+                    mbar_wait_bounded(&bars[jj % STAGES], (uint32_t)((jj / STAGES) & 1), DRAIN_NS, p.err);
+            }
+            return;
+        }
+
+        // online softmax (one warp per q head) and pv[t][b][g] = p * vd
+        for (int g = warp; g < G; g += DEC_WARPS) {
+            const float s0 = sc[g * DEC_T + lane], s1 = sc[g * DEC_T + lane + 32];
+            const float m_old = m_s[g];
+            const float m_new = fmaxf(m_old, warp_max(fmaxf(s0, s1)));
+            const float corr = expf(m_old - m_new);
+            const float p0 = expf(s0 - m_new), p1 = expf(s1 - m_new);
+            const float psum = warp_sum(p0 + p1);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int t = lane + 32 * h;
+                const float pt = h ? p1 : p0;
+                if (t < rows) {
+#pragma unroll
+                    for (int b = 0; b < NB; b++) {
+                        const float vd = *reinterpret_cast<const float *>(vs + t * ROW + b * BLOCK_BYTES);
+                        pv[(t * NB + b) * GMAX + g] = pt * vd;
+                    }
+                }
+            }
+            if (lane == 0) {
+                l_s[g] = l_s[g] * corr + psum;
+                m_s[g] = m_new;
+                corr_s[g] = corr;
+            }
+        }
+        __syncthreads();
+
+        // V accumulation: lane owns CPL columns, warp owns a token subset
+        {
+            float cr[GMAX];
+#pragma unroll
+            for (int g = 0; g < GMAX; g++) cr[g] = corr_s[g];
+#pragma unroll
+            for (int g = 0; g < GMAX; g++)
+#pragma unroll
+                for (int c = 0; c < CPL; c++) acc[g][c] *= cr[g];
+            for (int tt = warp * TPW + sub_t; tt < rows; tt += DEC_WARPS * TPW) {
+                const uint8_t *vrow = vs + tt * ROW + vb * BLOCK_BYTES + 4 + (c0 % QK);
+                float pvv[GMAX];
+                const float *pvt = pv + (tt * NB + vb) * GMAX;
+                if constexpr (GMAX >= 4) {
+#pragma unroll
+                    for (int g = 0; g < GMAX; g += 4) {
+                        const float4 f = *reinterpret_cast<const float4 *>(pvt + g);
+                        pvv[g] = f.x; pvv[g + 1] = f.y; pvv[g + 2] = f.z; pvv[g + 3] = f.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int g = 0; g < GMAX; g++) pvv[g] = pvt[g];
+                }
+#pragma unroll
+                for (int w = 0; w < CPL / 4; w++) {
+                    const uint32_t word = *reinterpret_cast<const uint32_t *>(vrow + 4 * w);
+                    float f[4];
+                    s8x4_to_f32(word, f[0], f[1], f[2], f[3]);
+#pragma unroll
+                    for (int g = 0; g < GMAX; g++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) acc[g][4 * w + c] = fmaf(pvv[g], f[c], acc[g][4 * w + c]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- epilogue: reduce the token subsets, then finish or hand off the split
+#pragma unroll
+    for (int o = LPT; o < 32; o <<= 1)
+#pragma unroll
+        for (int g = 0; g < GMAX; g++)
+#pragma unroll
+            for (int c = 0; c < CPL; c++) acc[g][c] += __shfl_xor_sync(0xffffffffu, acc[g][c], o);
+    float *red = reinterpret_cast<float *>(smem);  // stage ring is idle now
+    if (sub_t == 0) {
+#pragma unroll
+        for (int g = 0; g < GMAX; g++)
+#pragma unroll
+            for (int c = 0; c < CPL; c++) red[(warp * GMAX + g) * HD + c0 + c] = acc[g][c];
+    }
+    __syncthreads();
+
+    const bool single = n_splits == 1;
+    const long long pair_base = ((long long)item * p.pairs + pair) * p.max_splits;
+    for (int i = tid; i < G * HD; i += DEC_THREADS) {
+        const int g = i / HD, c = i - g * HD;
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; w++) a += red[(w * GMAX + g) * HD + c];
+        if (single) {
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                out_item[(long long)(qh0 + g) * HD + c] = a / l_s[g];
+            } else {
+                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+                o[c] = a;
+                if (c == 0) { o[HD] = m_s[g]; o[HD + 1] = l_s[g]; }
+            }
+        } else {
+            float *pp = p.part + ((pair_base + s) * GMAX + g) * (HD + 2);
+            pp[c] = a;
+            if (c == 0) { pp[HD] = m_s[g]; pp[HD + 1] = l_s[g]; }
+        }
+    }
+    if (single) return;
+
+    // last-arriving split merges (threadFenceReduction pattern: no waiting)
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int prev = atomicAdd(&p.counters[(long long)item * p.pairs + pair], 1);
+        *flag = (prev == n_splits - 1);
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+
+    float *wts = red + DEC_WARPS * GMAX * HD;
+    const float *pb = p.part + pair_base * GMAX * (HD + 2);
+    for (int g = warp; g < G; g += DEC_WARPS) {
+        float M = -INFINITY;
+        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD));
+        M = warp_max(M);
+        float Lsum = 0.0f;
+        for (int sp = lane; sp < n_splits; sp += 32) {
+            const float w = expf(__ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD) - M);
+            wts[sp * GMAX + g] = w;
+            Lsum += __ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD + 1) * w;
+        }
+        Lsum = warp_sum(Lsum);
+        if (lane == 0) { m_s[g] = M; l_s[g] = Lsum; }
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += DEC_THREADS) {
+        const int g = i / HD, c = i - g * HD;
+        float a = 0.0f;
+        for (int sp = 0; sp < n_splits; sp++) a = fmaf(wts[sp * GMAX + g], __ldcg(pb + (sp * GMAX + g) * (HD + 2) + c), a);
+        if (p.out_mode == TQK_OUT_NORMALIZED) {
+            out_item[(long long)(qh0 + g) * HD + c] = a / l_s[g];
+        } else {
+            float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+            o[c] = a;
+            if (c == 0) { o[HD] = m_s[g]; o[HD + 1] = l_s[g]; }
+        }
+    }
+    if (tid == 0) p.counters[(long long)item * p.pairs + pair] = 0;  // ready for the next launch
+}
+
+// Cross-part log-sum-exp merge (tqk_merge_partials): one CTA per head.
+__global__ void merge_partials_kernel(const float *__restrict__ parts, int n_parts, long long part_stride,
+                                      int head_dim, float *__restrict__ out) {
+    const int h = blockIdx.x;
+    const int stride = head_dim + 2;
+    __shared__ float s_m, s_l;
+    if (threadIdx.x < 32) {
+        float M = -INFINITY;
+        for (int pi = threadIdx.x; pi < n_parts; pi += 32) M = fmaxf(M, parts[pi * part_stride + (long long)h * stride + head_dim]);
+        M = warp_max(M);
+        float Lsum = 0.0f;
+        for (int pi = threadIdx.x; pi < n_parts; pi += 32) {
+            const float *pp = parts + pi * part_stride + (long long)h * stride;
+            if (pp[head_dim + 1] > 0.0f) Lsum += pp[head_dim + 1] * expf(pp[head_dim] - M);
+        }
+        Lsum = warp_sum(Lsum);
+        if (threadIdx.x == 0) { s_m = M; s_l = Lsum; }
+    }
+    __syncthreads();
+    const float M = s_m, Lsum = s_l;
+    for (int c = threadIdx.x; c < head_dim; c += blockDim.x) {
+        float a = 0.0f;
+        for (int pi = 0; pi < n_parts; pi++) {
+            const float *pp = parts + pi * part_stride + (long long)h * stride;
+            if (pp[head_dim + 1] > 0.0f) a = fmaf(expf(pp[head_dim] - M), pp[c], a);
+        }
+        out[(long long)h * head_dim + c] = Lsum > 0.0f ? a / Lsum : 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+int gmax_for(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
+
+template <int NB, int GMAX>
+int launch_decode(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
+    using L = DecLayout<NB, GMAX>;
+    // the dynamic shared-memory opt-in is a per-device function attribute
+    static std::mutex mu;
+    static int occ_by_dev[64];  // 0 = not yet set up on that device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail_cuda(e, "decode: cudaGetDevice");
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ_by_dev[dev] == 0) {
+            e = cudaFuncSetAttribute(decode_q8_kernel<NB, GMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+            int o = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_q8_kernel<NB, GMAX>, DEC_THREADS, L::BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "decode_q8_kernel attributes");
+            occ_by_dev[dev] = o > 0 ? o : -1;
+        }
+        occ = occ_by_dev[dev] > 0 ? occ_by_dev[dev] : 0;
+    }
+    if (ctas_per_sm) {
+        *ctas_per_sm = occ;
+        return TQK_OK;
+    }
+    decode_q8_kernel<NB, GMAX><<<grid, DEC_THREADS, L::BYTES, stream>>>(p);
+    return check_launch("decode_q8_kernel");
+}
+
+template <int NB>
+int dispatch_gmax(int gmax, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
+    switch (gmax) {
+        case 1: return launch_decode<NB, 1>(p, grid, stream, occ);
+        case 2: return launch_decode<NB, 2>(p, grid, stream, occ);
+        case 4: return launch_decode<NB, 4>(p, grid, stream, occ);
+        default: return launch_decode<NB, 8>(p, grid, stream, occ);
+    }
+}
+
+int dispatch(int nb, int gmax, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
+    switch (nb) {
+        case 1: return dispatch_gmax<1>(gmax, p, grid, stream, occ);
+        case 2: return dispatch_gmax<2>(gmax, p, grid, stream, occ);
+        case 4: return dispatch_gmax<4>(gmax, p, grid, stream, occ);
+        case 8: return dispatch_gmax<8>(gmax, p, grid, stream, occ);
+        default: return fail(TQK_EUNSUPPORTED, "decode: head_dim must be 32, 64, 128 or 256");
+    }
+}
+
+struct Plan {
+    int nb, gmax, heads_per_cta, head_slices, pairs, split_tokens, max_splits, max_len;
+    size_t counters_bytes, part_bytes;
+};
+
+int make_plan(const tqk_decode_args *a, Plan *pl) {
+    if (!a) return fail(TQK_EINVAL, "decode: NULL args");
+    if (a->n_items <= 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0 || a->head_dim <= 0 || a->max_tokens <= 0)
+        return fail(TQK_EINVAL, "decode: non-positive shape");
+    if (a->n_q_heads % a->n_kv_heads) return fail(TQK_EINVAL, "decode: n_q_heads % n_kv_heads != 0");
+    if (a->head_dim % QK) return fail(TQK_EINVAL, "decode: head_dim % 32 != 0");
+    const int nb = a->head_dim / QK;
+    if (nb != 1 && nb != 2 && nb != 4 && nb != 8) return fail(TQK_EUNSUPPORTED, "decode: head_dim must be 32, 64, 128 or 256");
+    if (!a->k || !a->v || !a->q || !a->out) return fail(TQK_EINVAL, "decode: NULL pointer");
+    if ((a->k_new == nullptr) != (a->v_new == nullptr)) return fail(TQK_EINVAL, "decode: k_new and v_new go together");
+    if (a->out_mode != TQK_OUT_NORMALIZED && a->out_mode != TQK_OUT_PARTIAL) return fail(TQK_EINVAL, "decode: out_mode");
+    if (a->n_items > 65535) return fail(TQK_EINVAL, "decode: n_items > 65535");
+    int max_len;
+    if (a->lens) {
+        max_len = a->max_len;
+        if (max_len < 0 || max_len > a->max_tokens) return fail(TQK_EINVAL, "decode: max_len outside [0, max_tokens]");
+    } else {
+        const long long first = a->len0, last = a->len0 + (long long)(a->n_items - 1) * a->len_step;
+        const long long lo = first < last ? first : last, hi = first < last ? last : first;
+        if (lo < 0 || hi > a->max_tokens) return fail(TQK_EPOS, "decode: length outside [0, max_tokens]");
+        if (a->k_new && lo < 1) return fail(TQK_EPOS, "decode: append needs length >= 1");
+        max_len = (int)hi;
+    }
+    if (nb % 4 == 0) {
+        if ((reinterpret_cast<uintptr_t>(a->k) & 15) || (reinterpret_cast<uintptr_t>(a->v) & 15) ||
+            ((a->item_stride * BLOCK_BYTES) & 15))
+            return fail(TQK_EALIGN, "decode: planes and item stride must be 16-byte aligned");
+    } else if ((reinterpret_cast<uintptr_t>(a->k) & 3) || (reinterpret_cast<uintptr_t>(a->v) & 3)) {
+        return fail(TQK_EALIGN, "decode: planes must be 4-byte aligned");
+    }
+    const int group = a->n_q_heads / a->n_kv_heads;
+    pl->nb = nb;
+    pl->gmax = gmax_for(group);
+    pl->heads_per_cta = group < pl->gmax ? group : pl->gmax;
+    pl->head_slices = (group + pl->heads_per_cta - 1) / pl->heads_per_cta;
+    pl->pairs = a->n_kv_heads * pl->head_slices;
+    pl->max_len = max_len;
+
+    int split = a->split_tokens;
+    if (split <= 0) {
+        const int rc = ensure_device();
+        if (rc) return rc;
+        const DeviceInfo *d = device_info();
+        int occ = 0;
+        DecodeParams dummy{};
+        const int orc = dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
+        if (orc) return orc;
+        const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
+        const long long pairs_total = (long long)a->n_items * pl->pairs;
+        long long want = (2 * slots + pairs_total - 1) / pairs_total;
+        if (want < 1) want = 1;
+        split = (int)((max_len + want - 1) / want);
+    }
+    split = ((split + DEC_T - 1) / DEC_T) * DEC_T;
+    if (split < DEC_T) split = DEC_T;
+    while ((max_len + split - 1) / split > MAX_SPLITS) split += DEC_T;
+    pl->split_tokens = split;
+    pl->max_splits = max_len > 0 ? (max_len + split - 1) / split : 1;
+    if (pl->max_splits > 1) {
+        pl->counters_bytes = (((size_t)a->n_items * pl->pairs * sizeof(int)) + 255) / 256 * 256;
+        pl->part_bytes = (size_t)a->n_items * pl->pairs * pl->max_splits * pl->gmax * (a->head_dim + 2) * sizeof(float);
+    } else {
+        pl->counters_bytes = 0;
+        pl->part_bytes = 0;
+    }
+    return TQK_OK;
+}
+
+}  // namespace
+}  // namespace tqk
+
+using namespace tqk;
+
+extern "C" int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes) {
+    Plan pl;
+    int rc = make_plan(a, &pl);
+    if (rc) return rc;
+    if (bytes) *bytes = pl.counters_bytes + pl.part_bytes;
+    return TQK_OK;
+}
+
+extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes,
+                             tqk_stream_t stream) {
+    Plan pl;
+    int rc = make_plan(a, &pl);  // validates before touching the device
+    if (rc) return rc;
+    rc = ensure_device();
+    if (rc) return rc;
+    const size_t need = pl.counters_bytes + pl.part_bytes;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (need) {
+        if (!workspace) {
+            workspace = library_workspace(st, need);
+            if (!workspace) return fail(TQK_ECUDA, "decode: cannot allocate the library workspace");
+        } else if (workspace_bytes < need) {
+            return fail(TQK_EWORKSPACE, "decode: workspace smaller than tqk_decode_workspace_size()");
+        }
+    }
+    DecodeParams p{};
+    p.k = reinterpret_cast<const uint8_t *>(a->k);
+    p.v = reinterpret_cast<const uint8_t *>(a->v);
+    p.kw = reinterpret_cast<uint8_t *>(a->k);
+    p.vw = reinterpret_cast<uint8_t *>(a->v);
+    p.item_stride = a->item_stride * BLOCK_BYTES;
+    p.n_items = a->n_items;
+    p.n_kv = a->n_kv_heads;
+    p.group = a->n_q_heads / a->n_kv_heads;
+    p.max_tokens = a->max_tokens;
+    p.heads_per_cta = pl.heads_per_cta;
+    p.head_slices = pl.head_slices;
+    p.pairs = pl.pairs;
+    p.lens = a->lens;
+    p.len0 = a->len0;
+    p.len_step = a->len_step;
+    p.q = a->q;
+    p.q_item_stride = a->q_item_stride;
+    p.out = a->out;
+    p.out_item_stride = a->out_item_stride;
+    p.k_new = a->k_new;
+    p.v_new = a->v_new;
+    p.kv_new_item_stride = a->kv_new_item_stride;
+    p.out_mode = a->out_mode;
+    p.split_tokens = pl.split_tokens;
+    p.max_splits = pl.max_splits;
+    p.scale = 1.0f / sqrtf((float)a->head_dim);  // as attend_q8 computes it (attention_layer.c:131)
+    p.counters = need ? reinterpret_cast<int *>(workspace) : nullptr;
+    p.part = need ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes) : nullptr;
+    p.err = device_info()->err_word;
+    const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
+    return dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
+}
+
+extern "C" int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads,
+                             int n_kv_heads, int head_dim, int max_tokens, int pos, const float *q, float *out,
+                             tqk_stream_t stream) {
+    if (pos < 0 || pos >= max_tokens) return fail(TQK_EPOS, "tqk_attend_q8: position out of range");
+    tqk_decode_args a{};
+    a.k = const_cast<tqk_block_q8 *>(k_plane);
+    a.v = const_cast<tqk_block_q8 *>(v_plane);
+    a.n_items = 1;
+    a.n_q_heads = n_q_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.head_dim = head_dim;
+    a.max_tokens = max_tokens;
+    a.len0 = pos + 1;
+    a.q = q;
+    a.out = out;
+    return tqk_decode_q8(&a, nullptr, 0, stream);
+}
+
+extern "C" int tqk_append_attend_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                                    int head_dim, int max_tokens, int pos, const float *q, const float *k,
+                                    const float *v, float *out, tqk_stream_t stream) {
+    if (pos < 0 || pos >= max_tokens) return fail(TQK_EPOS, "tqk_append_attend_q8: position out of range");
+    if (!k || !v) return fail(TQK_EINVAL, "tqk_append_attend_q8: NULL k/v");
+    tqk_decode_args a{};
+    a.k = k_plane;
+    a.v = v_plane;
+    a.n_items = 1;
+    a.n_q_heads = n_q_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.head_dim = head_dim;
+    a.max_tokens = max_tokens;
+    a.len0 = pos + 1;
+    a.q = q;
+    a.out = out;
+    a.k_new = k;
+    a.v_new = v;
+    return tqk_decode_q8(&a, nullptr, 0, stream);
+}
+
+extern "C" int tqk_prefill_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                              int head_dim, int max_tokens, int pos0, int n, const float *q, const float *k,
+                              const float *v, float *out, tqk_stream_t stream) {
+    if (n <= 0) return fail(TQK_EINVAL, "tqk_prefill_q8: n must be positive");
+    if (pos0 < 0 || (long long)pos0 + n > max_tokens) return fail(TQK_EPOS, "tqk_prefill_q8: range out of cache");
+    int rc = tqk_store_kv_q8_batch(k_plane, v_plane, n_kv_heads, head_dim, max_tokens, pos0, n, k, v, stream);
+    if (rc) return rc;
+    tqk_decode_args a{};
+    a.k = k_plane;
+    a.v = v_plane;
+    a.item_stride = 0;
+    a.n_items = n;
+    a.n_q_heads = n_q_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.head_dim = head_dim;
+    a.max_tokens = max_tokens;
+    a.len0 = pos0 + 1;
+    a.len_step = 1;
+    a.q = q;
+    a.q_item_stride = (int64_t)n_q_heads * head_dim;
+    a.out = out;
+    a.out_item_stride = (int64_t)n_q_heads * head_dim;
+    return tqk_decode_q8(&a, nullptr, 0, stream);
+}
+
+extern "C" int tqk_merge_partials(const float *parts, int n_parts, int64_t part_stride, int n_heads, int head_dim,
+                                  float *out, tqk_stream_t stream) {
+    if (!parts || !out || n_parts <= 0 || n_heads <= 0 || head_dim <= 0)
+        return fail(TQK_EINVAL, "tqk_merge_partials: bad arguments");
+    int rc = ensure_device();
+    if (rc) return rc;
+    merge_partials_kernel<<<n_heads, 128, 0, (cudaStream_t)stream>>>(parts, n_parts, part_stride, head_dim, out);
+    return check_launch("merge_partials_kernel");
+}

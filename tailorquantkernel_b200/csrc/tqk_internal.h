@@ -1,0 +1,35 @@
+// tqk_internal.h -- host-side runtime shared by the tqk_*.cu translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "tqk_common.cuh"
+
+namespace tqk {
+
+// Records `msg` as the calling thread's last error and returns `status`.
+int fail(int status, const char *msg);
+// Maps a CUDA error to TQK_ECUDA with a message naming `what`.
+int fail_cuda(cudaError_t e, const char *what);
+// Checks the launch that was just issued (configuration errors only; async).
+int check_launch(const char *what);
+// Makes sure a CUDA device is usable from this thread; TQK_ENODEV otherwise.
+int ensure_device();
+
+struct DeviceInfo {
+    int device = -1;
+    int sm_count = 0;
+    size_t smem_optin = 0;  // max dynamic shared memory per block
+    int *err_word = nullptr;  // sticky device error word (device memory)
+};
+// Cached properties of the current device (initialised on first use).
+const DeviceInfo *device_info();
+
+// Library-owned decode workspace for (current device, stream), grown on demand
+// and zeroed when (re)allocated.  Returns nullptr on allocation failure.
+void *library_workspace(cudaStream_t stream, size_t bytes);
+
+}  // namespace tqk

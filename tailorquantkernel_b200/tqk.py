@@ -1,0 +1,240 @@
+"""ctypes binding of libtqk.so (the C ABI in include/tqk.h).
+
+All functions take torch CUDA tensors (or raw device addresses) and launch on the
+current torch stream unless a stream is given.  Nothing here computes on the
+CPU: a missing libtqk.so raises at import time and a failing call raises
+:class:`TQKError` carrying the library's status code and message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libtqk.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"{LIB_PATH} is missing: build it with `python -m tailorquantkernel_b200.build` "
+        "(there is no CPU fallback)")
+
+_lib = ctypes.CDLL(LIB_PATH)
+
+QK = 32
+BLOCK_BYTES = 36
+
+OK = 0
+EPOS = -1
+EINVAL = -20
+EALIGN = -21
+EWORKSPACE = -22
+ECUDA = -23
+ENODEV = -24
+ETIMEOUT = -25
+EUNSUPPORTED = -26
+
+OUT_NORMALIZED = 0
+OUT_PARTIAL = 1
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+
+class DecodeArgs(ctypes.Structure):
+    """Mirror of tqk_decode_args (include/tqk.h)."""
+    _fields_ = [
+        ("k", _vp), ("v", _vp),
+        ("item_stride", _i64),
+        ("n_items", _i),
+        ("n_q_heads", _i), ("n_kv_heads", _i), ("head_dim", _i), ("max_tokens", _i),
+        ("lens", _vp),
+        ("len0", _i), ("len_step", _i),
+        ("max_len", _i),
+        ("q", _vp), ("q_item_stride", _i64),
+        ("out", _vp), ("out_item_stride", _i64),
+        ("k_new", _vp), ("v_new", _vp),
+        ("kv_new_item_stride", _i64),
+        ("out_mode", _i),
+        ("split_tokens", _i),
+    ]
+
+
+def _sig(name, argtypes, restype=_i):
+    fn = getattr(_lib, name)
+    fn.argtypes = argtypes
+    fn.restype = restype
+    return fn
+
+
+tqk_status_string = _sig("tqk_status_string", [_i], ctypes.c_char_p)
+tqk_last_error = _sig("tqk_last_error", [], ctypes.c_char_p)
+tqk_version = _sig("tqk_version", [], ctypes.c_char_p)
+tqk_device_status = _sig("tqk_device_status", [ctypes.POINTER(_i), _i])
+tqk_quantize_rows_q8 = _sig("tqk_quantize_rows_q8", [_vp, _vp, _i, _i, _vp])
+tqk_store_kv_q8 = _sig("tqk_store_kv_q8", [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp])
+tqk_store_kv_q8_batch = _sig("tqk_store_kv_q8_batch", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
+tqk_attn_scores_q8 = _sig("tqk_attn_scores_q8", [_vp, _i, _vp, _i, _i, _f, _vp, _sz, _vp])
+tqk_attn_accum_q8 = _sig("tqk_attn_accum_q8", [_vp, _sz, _i, _vp, _i, _i, _vp, _sz, _vp])
+tqk_softmax_rows = _sig("tqk_softmax_rows", [_vp, _i, _i, _sz, _vp])
+tqk_decode_workspace_size = _sig("tqk_decode_workspace_size", [ctypes.POINTER(DecodeArgs), ctypes.POINTER(_sz)])
+tqk_workspace_init = _sig("tqk_workspace_init", [_vp, _sz, _vp])
+tqk_decode_q8 = _sig("tqk_decode_q8", [ctypes.POINTER(DecodeArgs), _vp, _sz, _vp])
+tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
+tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
+tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
+tqk_merge_partials = _sig("tqk_merge_partials", [_vp, _i, _i64, _i, _i, _vp, _vp])
+
+EXPORTED = [
+    "tqk_status_string", "tqk_last_error", "tqk_version", "tqk_device_status",
+    "tqk_quantize_rows_q8", "tqk_store_kv_q8", "tqk_store_kv_q8_batch",
+    "tqk_attn_scores_q8", "tqk_attn_accum_q8", "tqk_softmax_rows",
+    "tqk_decode_workspace_size", "tqk_workspace_init", "tqk_decode_q8",
+    "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
+]
+
+
+class TQKError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        self.status = status
+        msg = tqk_last_error().decode(errors="replace")
+        super().__init__(f"{where}: {tqk_status_string(status).decode()} ({status}): {msg}")
+
+
+def check(status: int, where: str) -> None:
+    if status != OK:
+        raise TQKError(status, where)
+
+
+# ---------------------------------------------------------------------------
+# torch helpers (torch is imported lazily: the library itself does not need it)
+# ---------------------------------------------------------------------------
+def _ptr(t) -> Optional[int]:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if not t.is_cuda:
+        raise ValueError("tensor must live on a CUDA device")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream) -> int:
+    import torch
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def q8_bytes(rows: int, n: int) -> int:
+    return rows * (n // QK) * BLOCK_BYTES
+
+
+def empty_planes(n_kv: int, max_tokens: int, head_dim: int, device="cuda", leading=()):
+    """Uninitialised uint8 tensor for a Q8 plane [*leading, n_kv, max_tokens, nb*36]."""
+    import torch
+    return torch.empty((*leading, n_kv, max_tokens, head_dim // QK * BLOCK_BYTES), dtype=torch.uint8, device=device)
+
+
+def quantize_rows(x, out=None, stream=None):
+    """quantize_row_q8 over the rows of a CUDA fp32 tensor [..., n] -> uint8 [..., n/32*36]."""
+    import torch
+    n = x.shape[-1]
+    rows = x.numel() // n if n else 0
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n // QK * BLOCK_BYTES), dtype=torch.uint8, device=x.device)
+    check(tqk_quantize_rows_q8(_ptr(x), _ptr(out), rows, n, _stream(stream)), "tqk_quantize_rows_q8")
+    return out
+
+
+def store_kv(k_plane, v_plane, n_kv, head_dim, max_tokens, pos, k, v, stream=None):
+    check(tqk_store_kv_q8(_ptr(k_plane), _ptr(v_plane), n_kv, head_dim, max_tokens, pos, _ptr(k), _ptr(v),
+                          _stream(stream)), "tqk_store_kv_q8")
+
+
+def store_kv_batch(k_plane, v_plane, n_kv, head_dim, max_tokens, pos0, n, k, v, stream=None):
+    check(tqk_store_kv_q8_batch(_ptr(k_plane), _ptr(v_plane), n_kv, head_dim, max_tokens, pos0, n, _ptr(k),
+                                _ptr(v), _stream(stream)), "tqk_store_kv_q8_batch")
+
+
+def attend(k_plane, v_plane, n_q, n_kv, head_dim, max_tokens, pos, q, out, stream=None):
+    check(tqk_attend_q8(_ptr(k_plane), _ptr(v_plane), n_q, n_kv, head_dim, max_tokens, pos, _ptr(q), _ptr(out),
+                        _stream(stream)), "tqk_attend_q8")
+
+
+def append_attend(k_plane, v_plane, n_q, n_kv, head_dim, max_tokens, pos, q, k, v, out, stream=None):
+    check(tqk_append_attend_q8(_ptr(k_plane), _ptr(v_plane), n_q, n_kv, head_dim, max_tokens, pos, _ptr(q),
+                               _ptr(k), _ptr(v), _ptr(out), _stream(stream)), "tqk_append_attend_q8")
+
+
+def prefill(k_plane, v_plane, n_q, n_kv, head_dim, max_tokens, pos0, n, q, k, v, out, stream=None):
+    check(tqk_prefill_q8(_ptr(k_plane), _ptr(v_plane), n_q, n_kv, head_dim, max_tokens, pos0, n, _ptr(q), _ptr(k),
+                         _ptr(v), _ptr(out), _stream(stream)), "tqk_prefill_q8")
+
+
+def attn_scores(q_blocks, g, k_blocks, n, nb, scale, scores, stride, stream=None):
+    check(tqk_attn_scores_q8(_ptr(q_blocks), g, _ptr(k_blocks), n, nb, scale, _ptr(scores), stride,
+                             _stream(stream)), "tqk_attn_scores_q8")
+
+
+def attn_accum(w, w_stride, g, v_blocks, n, nb, out, out_stride, stream=None):
+    check(tqk_attn_accum_q8(_ptr(w), w_stride, g, _ptr(v_blocks), n, nb, _ptr(out), out_stride, _stream(stream)),
+          "tqk_attn_accum_q8")
+
+
+def softmax_rows(x, rows, n, stride, stream=None):
+    check(tqk_softmax_rows(_ptr(x), rows, n, stride, _stream(stream)), "tqk_softmax_rows")
+
+
+def decode_args(k, v, n_q, n_kv, head_dim, max_tokens, q, out, *, n_items=1, item_stride_blocks=0, lens=None,
+                len0=0, len_step=0, max_len=0, q_item_stride=0, out_item_stride=0, k_new=None, v_new=None,
+                kv_new_item_stride=0, out_mode=OUT_NORMALIZED, split_tokens=0) -> DecodeArgs:
+    a = DecodeArgs()
+    a.k, a.v = _ptr(k), _ptr(v)
+    a.item_stride = item_stride_blocks
+    a.n_items = n_items
+    a.n_q_heads, a.n_kv_heads, a.head_dim, a.max_tokens = n_q, n_kv, head_dim, max_tokens
+    a.lens = _ptr(lens)
+    a.len0, a.len_step, a.max_len = len0, len_step, max_len
+    a.q, a.q_item_stride = _ptr(q), q_item_stride
+    a.out, a.out_item_stride = _ptr(out), out_item_stride
+    a.k_new, a.v_new = _ptr(k_new), _ptr(v_new)
+    a.kv_new_item_stride = kv_new_item_stride
+    a.out_mode = out_mode
+    a.split_tokens = split_tokens
+    return a
+
+
+def decode(args: DecodeArgs, workspace=None, stream=None) -> None:
+    ws = _ptr(workspace) if workspace is not None else None
+    nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(tqk_decode_q8(ctypes.byref(args), ws, nbytes, _stream(stream)), "tqk_decode_q8")
+
+
+def decode_workspace_size(args: DecodeArgs) -> int:
+    out = _sz(0)
+    check(tqk_decode_workspace_size(ctypes.byref(args), ctypes.byref(out)), "tqk_decode_workspace_size")
+    return out.value
+
+
+def workspace_init(workspace, stream=None) -> None:
+    check(tqk_workspace_init(_ptr(workspace), workspace.numel() * workspace.element_size(), _stream(stream)),
+          "tqk_workspace_init")
+
+
+def merge_partials(parts, n_parts, part_stride, n_heads, head_dim, out, stream=None):
+    check(tqk_merge_partials(_ptr(parts), n_parts, part_stride, n_heads, head_dim, _ptr(out), _stream(stream)),
+          "tqk_merge_partials")
+
+
+def device_status(clear: bool = False) -> int:
+    v = _i(0)
+    check(tqk_device_status(ctypes.byref(v), int(clear)), "tqk_device_status")
+    return v.value

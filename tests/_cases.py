@@ -1,0 +1,124 @@
+"""Seeded synthetic inputs for the parity tests and the golden fixtures.
+
+The reference publishes no dataset for this path; its configs
+define shapes and distributions: q, K, V ~ N(0,1) fp32, K/V quantised to Q8 by
+the reference quantiser, config 2's q rotated by RoPE (theta 500000) at its
+position, config 3's K/V with 1% of entries scaled x8.  numpy's PCG64 stream
+stands in for the reference benches' xorshift64 Box-Muller stream; every
+fixture stores a SHA-256 of its generated inputs so a changed stream is caught.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+QK = 32
+BLOCK_BYTES = 36
+
+
+def normal(rng: np.random.Generator, shape, outlier_frac: float = 0.0) -> np.ndarray:
+    x = rng.standard_normal(shape, dtype=np.float32)
+    if outlier_frac > 0:
+        mask = rng.random(shape, dtype=np.float32) < outlier_frac
+        x[mask] *= 8.0
+    return x
+
+
+def rope(x: np.ndarray, head_dim: int, pos: int, theta: float) -> np.ndarray:
+    """Half-split rotation of model/rope.c:4-22 applied to every head of x [..., heads*hd]."""
+    i = np.arange(head_dim // 2, dtype=np.float64)
+    freq = np.power(theta, -2.0 * i / head_dim)
+    a = pos * freq
+    c, s = np.cos(a), np.sin(a)
+    h = x.reshape(-1, head_dim).astype(np.float64)
+    x0, x1 = h[:, : head_dim // 2].copy(), h[:, head_dim // 2:].copy()
+    h[:, : head_dim // 2] = x0 * c - x1 * s
+    h[:, head_dim // 2:] = x0 * s + x1 * c
+    return h.astype(np.float32).reshape(x.shape)
+
+
+def digest(*arrays: np.ndarray) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def quant_edge_rows(rng: np.random.Generator, n: int = 128) -> np.ndarray:
+    """Rows exercising the quantiser's corners (kernel/quant_x.c:5-34)."""
+    rows = []
+    rows.append(rng.standard_normal(n, dtype=np.float32))
+    rows.append(np.zeros(n, np.float32))                                  # zero scale
+    rows.append(np.full(n, 3.25, np.float32))                             # constant
+    r = rng.standard_normal(n, dtype=np.float32); r[::17] *= 8; rows.append(r)  # outliers
+    # exact ties after scaling: max 127 -> inv 1, values k + 0.5 round half to even
+    r = np.concatenate([np.array([127.0], np.float32), (np.arange(n - 1) % 9 - 4 + 0.5).astype(np.float32)])
+    rows.append(r)
+    r = rng.standard_normal(n, dtype=np.float32) * 1e-39; rows.append(r.astype(np.float32))  # denormals
+    r = np.clip(rng.standard_normal(n), -1, 1).astype(np.float32) * np.float32(3e38); rows.append(r)  # near overflow
+    r = rng.standard_normal(n, dtype=np.float32); r[5] = np.inf; rows.append(r)
+    r = rng.standard_normal(n, dtype=np.float32); r[40] = -np.inf; r[41] = np.nan; rows.append(r)
+    r = rng.standard_normal(n, dtype=np.float32); r[70] = np.nan; rows.append(r)
+    rows.append(np.full(n, np.nan, np.float32))
+    r = np.zeros(n, np.float32); r[3] = 1e-45; rows.append(r)             # smallest denormal
+    r = rng.standard_normal(n, dtype=np.float32); r[:32] = -0.0; rows.append(r)
+    for k in range(8):
+        rows.append((rng.standard_normal(n, dtype=np.float32) * (10.0 ** rng.uniform(-6, 6))).astype(np.float32))
+    return np.stack(rows).astype(np.float32)
+
+
+def decode_case(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, n: int, *, outlier_frac: float = 0.0,
+                rope_pos: int | None = None, rope_theta: float = 500000.0, q_scale: float = 1.0):
+    """fp32 K/V [n_kv, max_tokens, hd] (rows >= n left zero), q [n_q*hd]."""
+    rng = np.random.default_rng(seed)
+    kf = np.zeros((n_kv, max_tokens, hd), np.float32)
+    vf = np.zeros((n_kv, max_tokens, hd), np.float32)
+    kf[:, :n] = normal(rng, (n_kv, n, hd), outlier_frac)
+    vf[:, :n] = normal(rng, (n_kv, n, hd), outlier_frac)
+    q = normal(rng, (n_q * hd,)) * np.float32(q_scale)
+    if rope_pos is not None:
+        q = rope(q, hd, rope_pos, rope_theta)
+    return kf, vf, q.astype(np.float32)
+
+
+def tolerance_ok(got: np.ndarray, ref: np.ndarray, atol: float = 1e-3, rtol: float = 1e-3):
+    """The attention tolerance of the north star: max abs error <= 1e-3 and
+    relative error (max |diff| / max |ref|) <= 1e-3, in FP32."""
+    diff = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    max_abs = float(diff.max()) if diff.size else 0.0
+    scale = float(np.abs(ref).max()) if ref.size else 0.0
+    rel = max_abs / scale if scale > 0 else max_abs
+    return (max_abs <= atol and rel <= rtol and bool(np.isfinite(got).all())), max_abs, rel
+
+
+def sweep_inputs(g: int, n: int, hd: int):
+    """Inputs of one per-op sweep case (the shape grid of tools/test_model.c:1677-1697)."""
+    rng = np.random.default_rng(900 + g * 100 + n * 10 + hd)
+    qf = rng.standard_normal((g, hd), dtype=np.float32)
+    kf = rng.standard_normal((n, hd), dtype=np.float32)
+    vf = rng.standard_normal((n, hd), dtype=np.float32)
+    w = rng.standard_normal((g, n + 4), dtype=np.float32)
+    return qf, kf, vf, w
+
+
+def head_inputs(hd: int, n: int, seed: int):
+    """Inputs of one attention_head_q8 case (tools/test_model.c:584-728 style; seed 90 = x30 scores)."""
+    rng = np.random.default_rng(seed)
+    s = np.float32(30.0 if seed == 90 else 1.0)
+    q = rng.standard_normal(hd, dtype=np.float32) * s
+    kf = rng.standard_normal((n, hd), dtype=np.float32) * s
+    vf = rng.standard_normal((n, hd), dtype=np.float32)
+    return q, kf, vf
+
+
+def prefill_inputs(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, pos0: int, n: int):
+    rng = np.random.default_rng(seed)
+    kf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
+    vf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
+    kf[:, pos0:] = 0
+    vf[:, pos0:] = 0
+    qn = rng.standard_normal((n, n_q * hd), dtype=np.float32)
+    kn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+    vn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+    return kf, vf, qn, kn, vn

@@ -1,0 +1,26 @@
+"""pytest configuration: the `gpu` marker and import paths.
+
+`-m "not gpu"` runs on any machine (oracle pins, golden fixtures, host logic,
+C-ABI exports); `-m gpu` needs a CUDA device and calls the kernels through the
+C ABI of tailorquantkernel_b200/libtqk.so.
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")

@@ -1,0 +1,280 @@
+"""GPU parity of the fused decode attention (attend_q8 + store_kv,
+model/attention_layer.c:62-150) through the C ABI, against the oracle.
+
+Tolerance (the north star's): max abs error <= 1e-3 and relative error
+(max |diff| / max |ref|) <= 1e-3 in FP32 (tests/_cases.py:tolerance_ok); the Q8
+append is bit-exact.  Small cases compare with the golden fixtures made by the
+reference itself; BASELINE.json's full configurations compare with the oracle
+restatement on GPU-generated inputs.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from _cases import decode_case, digest, tolerance_ok
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def tqk(cuda):
+    from tailorquantkernel_b200 import tqk as t
+    return t
+
+
+@pytest.fixture(scope="module")
+def port():
+    return oracle.Oracle("port")
+
+
+def _golden_names():
+    g = np.load(os.path.join(GOLDEN, "decode.npz"))
+    return sorted({k.split("__")[0] for k in g.files})
+
+
+def _golden(name):
+    g = np.load(os.path.join(GOLDEN, "decode.npz"))
+    seed, nq, nkv, hd, mt, pos, of, rp = (int(v) for v in g[f"{name}__params"])
+    kf, vf, q = decode_case(seed, nq, nkv, hd, mt, pos + 1, outlier_frac=of / 1e6, rope_pos=None if rp < 0 else rp)
+    assert digest(kf, vf, q) == str(g[f"{name}__in_sha"])
+    return (nq, nkv, hd, mt, pos), kf, vf, q, g[f"{name}__out"], str(g[f"{name}__planes_sha"])
+
+
+@pytest.mark.parametrize("name", _golden_names())
+def test_attend_matches_golden(tqk, cuda, name):
+    import torch
+    (nq, nkv, hd, mt, pos), kf, vf, q, ref, planes_sha = _golden(name)
+    kp = tqk.quantize_rows(torch.from_numpy(kf).to(cuda))
+    vp = tqk.quantize_rows(torch.from_numpy(vf).to(cuda))
+    assert digest(kp.cpu().numpy(), vp.cpu().numpy()) == planes_sha  # device quantiser == reference
+    out = torch.empty(nq * hd, device=cuda)
+    tqk.attend(kp, vp, nq, nkv, hd, mt, pos, torch.from_numpy(q).to(cuda), out)
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), ref)
+    assert ok, f"{name}: max abs {max_abs:.3g} rel {rel:.3g}"
+
+
+@pytest.mark.parametrize("name", _golden_names())
+def test_fused_append_attend_matches_golden(tqk, cuda, name):
+    """store_kv + attend_q8 in one launch: the appended row is bit-exact and the
+    attention sees it."""
+    import torch
+    (nq, nkv, hd, mt, pos), kf, vf, q, ref, planes_sha = _golden(name)
+    k_new = np.ascontiguousarray(kf[:, pos])
+    v_new = np.ascontiguousarray(vf[:, pos])
+    kf2, vf2 = kf.copy(), vf.copy()
+    kf2[:, pos] = 0
+    vf2[:, pos] = 0
+    kp = tqk.quantize_rows(torch.from_numpy(kf2).to(cuda))
+    vp = tqk.quantize_rows(torch.from_numpy(vf2).to(cuda))
+    out = torch.empty(nq * hd, device=cuda)
+    tqk.append_attend(kp, vp, nq, nkv, hd, mt, pos, torch.from_numpy(q).to(cuda), torch.from_numpy(k_new).to(cuda),
+                      torch.from_numpy(v_new).to(cuda), out)
+    assert digest(kp.cpu().numpy(), vp.cpu().numpy()) == planes_sha
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), ref)
+    assert ok, f"{name}: max abs {max_abs:.3g} rel {rel:.3g}"
+
+
+def _gpu_planes(gen, shape_f32, tqk, outlier_frac=0.0):
+    """N(0,1) fp32 on the device (optionally 1% x8 outliers), quantised to Q8 by the device quantiser."""
+    import torch
+    x = torch.randn(shape_f32, device="cuda", generator=gen)
+    if outlier_frac:
+        x = torch.where(torch.rand(shape_f32, device="cuda", generator=gen) < outlier_frac, x * 8, x)
+    return tqk.quantize_rows(x)
+
+
+def test_config2_all_layers_fused_append(tqk, port, cuda):
+    """Config 2: 32 layers, 32 q / 8 kv heads, context 4096 + the appended token
+    at position 4096, q with RoPE at 4096 -- one multi-item launch."""
+    import torch
+    from _cases import rope
+    L, nq, nkv, hd, pos = 32, 32, 8, 128, 4096
+    mt = pos + 1
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    kp = _gpu_planes(gen, (L, nkv, mt, hd), tqk)
+    vp = _gpu_planes(gen, (L, nkv, mt, hd), tqk)
+    rng = np.random.default_rng(2)
+    q = rope(rng.standard_normal((L, nq * hd), dtype=np.float32), hd, pos, 500000.0)
+    k_new = rng.standard_normal((L, nkv * hd), dtype=np.float32)
+    v_new = rng.standard_normal((L, nkv * hd), dtype=np.float32)
+    out = torch.empty(L, nq * hd, device=cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=L,
+                           item_stride_blocks=nkv * mt * (hd // 32), len0=pos + 1, q_item_stride=nq * hd,
+                           out_item_stride=nq * hd, k_new=torch.from_numpy(k_new).to(cuda),
+                           v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    for layer in range(L):
+        # the oracle appends from fp32 itself; the device's append must be bit-exact
+        kref, vref = kh[layer].copy(), vh[layer].copy()
+        assert port.store_kv(kref, vref, nkv, hd, mt, pos, k_new[layer], v_new[layer]) == 0
+        assert np.array_equal(kref, kh[layer]) and np.array_equal(vref, vh[layer]), f"append layer {layer}"
+        ref = port.attend(kref, vref, nq, nkv, hd, mt, pos, q[layer])
+        ok, max_abs, rel = tolerance_ok(got[layer], ref)
+        assert ok, f"layer {layer}: max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
+def test_config3_ragged_batch_device_lens(tqk, port, cuda):
+    """Config 3: batch 64, lengths ~U[512, 8192], 1% x8 outliers, device lens array."""
+    import torch
+    B, nq, nkv, hd, mt = 64, 32, 8, 128, 8192
+    rng = np.random.default_rng(3)
+    lens = rng.integers(512, 8193, B).astype(np.int32)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    kp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    vp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    q = rng.standard_normal((B, nq * hd), dtype=np.float32)
+    out = torch.empty(B, nq * hd, device=cuda)
+    lens_d = torch.from_numpy(lens).to(cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=B,
+                           item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
+                           q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=1024)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    for b in range(B):
+        ref = port.attend(kh[b], vh[b], nq, nkv, hd, mt, int(lens[b]) - 1, q[b])
+        ok, max_abs, rel = tolerance_ok(got[b], ref)
+        assert ok, f"seq {b} (len {lens[b]}): max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
+def test_config4_long_context_and_sequence_split_merge(tqk, port, cuda):
+    """Config 4: 64 q / 8 kv heads, context 131072.  Also the sequence-split path
+    of the multi-GPU version emulated on one device: 4 disjoint token ranges
+    written as partials, then the log-sum-exp merge."""
+    import torch
+    nq, nkv, hd, n = 64, 8, 128, 131072
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    kp = _gpu_planes(gen, (nkv, n, hd), tqk)
+    vp = _gpu_planes(gen, (nkv, n, hd), tqk)
+    q = np.random.default_rng(4).standard_normal(nq * hd, dtype=np.float32)
+    qd = torch.from_numpy(q).to(cuda)
+    out = torch.empty(nq * hd, device=cuda)
+    tqk.attend(kp, vp, nq, nkv, hd, n, n - 1, qd, out)
+    ref = port.attend(kp.cpu().numpy(), vp.cpu().numpy(), nq, nkv, hd, n, n - 1, q)
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), ref)
+    assert ok, f"max abs {max_abs:.3g} rel {rel:.3g}"
+
+    parts_n = 4
+    shard = n // parts_n
+    parts = torch.empty(parts_n, nq * (hd + 2), device=cuda)
+    for r in range(parts_n):
+        kr = kp[:, r * shard:(r + 1) * shard].contiguous()
+        vr = vp[:, r * shard:(r + 1) * shard].contiguous()
+        args = tqk.decode_args(kr, vr, nq, nkv, hd, shard, qd, parts[r], len0=shard, out_mode=tqk.OUT_PARTIAL)
+        tqk.decode(args)
+    merged = torch.empty(nq * hd, device=cuda)
+    tqk.merge_partials(parts, parts_n, nq * (hd + 2), nq, hd, merged)
+    ok, max_abs, rel = tolerance_ok(merged.cpu().numpy(), ref)
+    assert ok, f"merged: max abs {max_abs:.3g} rel {rel:.3g}"
+
+
+def test_split_invariance_and_caller_workspace(tqk, cuda):
+    """The result does not depend on how the sequence is split, and a caller
+    workspace gives the same bytes as the library's."""
+    import torch
+    nq, nkv, hd, n = 32, 8, 128, 5000
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    kp = _gpu_planes(gen, (nkv, n, hd), tqk)
+    vp = _gpu_planes(gen, (nkv, n, hd), tqk)
+    q = torch.randn(nq * hd, device=cuda, generator=gen)
+    outs = []
+    for split in (0, 64, 192, 1024, 4096, 5056):
+        out = torch.empty(nq * hd, device=cuda)
+        tqk.decode(tqk.decode_args(kp, vp, nq, nkv, hd, n, q, out, len0=n, split_tokens=split))
+        outs.append(out.cpu().numpy())
+    for o in outs[1:]:
+        assert np.abs(o - outs[0]).max() <= 2e-6 * max(1.0, np.abs(outs[0]).max())
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, n, q, torch.empty(1, device=cuda), len0=n, split_tokens=64)
+    ws = torch.empty(tqk.decode_workspace_size(args), dtype=torch.uint8, device=cuda)
+    tqk.workspace_init(ws)
+    for _ in range(2):  # the workspace is left reusable
+        out = torch.empty(nq * hd, device=cuda)
+        args.out = out.data_ptr()
+        tqk.decode(args, workspace=ws)
+        assert np.array_equal(out.cpu().numpy(), outs[1])
+
+
+def test_zero_length_items_and_partial_output(tqk, port, cuda):
+    import torch
+    nq, nkv, hd, mt = 8, 2, 64, 300
+    kf, vf, q = decode_case(6, nq, nkv, hd, mt, mt)
+    kp = tqk.quantize_rows(torch.from_numpy(kf).to(cuda)).unsqueeze(0).repeat(3, 1, 1, 1).contiguous()
+    vp = tqk.quantize_rows(torch.from_numpy(vf).to(cuda)).unsqueeze(0).repeat(3, 1, 1, 1).contiguous()
+    lens = torch.tensor([0, 1, 257], dtype=torch.int32, device=cuda)
+    qd = torch.from_numpy(q).to(cuda).repeat(3)
+    out = torch.full((3, nq * hd), 5.0, device=cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, qd, out, n_items=3, item_stride_blocks=nkv * mt * hd // 32,
+                           lens=lens, max_len=257, q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=64)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    assert (got[0] == 0).all()
+    kh, vh = kp[0].cpu().numpy(), vp[0].cpu().numpy()
+    for i, n in ((1, 1), (2, 257)):
+        ok, max_abs, rel = tolerance_ok(got[i], port.attend(kh, vh, nq, nkv, hd, mt, n - 1, q))
+        assert ok, (n, max_abs, rel)
+
+
+def test_prefill_matches_golden_and_sequential(tqk, port, cuda):
+    import torch
+    from _cases import prefill_inputs
+    g = np.load(os.path.join(GOLDEN, "prefill.npz"))
+    seed, nq, nkv, hd, mt, pos0, n = (int(v) for v in g["params"])
+    kf, vf, qn, kn, vn = prefill_inputs(seed, nq, nkv, hd, mt, pos0, n)
+    kp = tqk.quantize_rows(torch.from_numpy(kf).to(cuda))
+    vp = tqk.quantize_rows(torch.from_numpy(vf).to(cuda))
+    out = torch.empty(n * nq * hd, device=cuda)
+    tqk.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, torch.from_numpy(qn).to(cuda), torch.from_numpy(kn).to(cuda),
+                torch.from_numpy(vn).to(cuda), out)
+    assert np.array_equal(kp.cpu().numpy()[:, pos0:pos0 + n], g["kp"])
+    assert np.array_equal(vp.cpu().numpy()[:, pos0:pos0 + n], g["vp"])
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), g["out"])
+    assert ok, (max_abs, rel)
+
+
+def test_config5_prefill_full(tqk, port, cuda):
+    """Config 5: 2048 new tokens at positions 2048..4095 over a 2048-token Q8
+    cache, 32 q / 8 kv heads, causal -- checked on a spread of query tokens."""
+    import torch
+    nq, nkv, hd, pos0, n = 32, 8, 128, 2048, 2048
+    mt = pos0 + n
+    gen = torch.Generator(device="cuda").manual_seed(55)
+    kfull = torch.zeros(nkv, mt, hd, device=cuda)
+    vfull = torch.zeros(nkv, mt, hd, device=cuda)
+    kfull[:, :pos0] = torch.randn(nkv, pos0, hd, device=cuda, generator=gen)
+    vfull[:, :pos0] = torch.randn(nkv, pos0, hd, device=cuda, generator=gen)
+    kp, vp = tqk.quantize_rows(kfull), tqk.quantize_rows(vfull)
+    qn = torch.randn(n, nq * hd, device=cuda, generator=gen)
+    kn = torch.randn(n, nkv * hd, device=cuda, generator=gen)
+    vn = torch.randn(n, nkv * hd, device=cuda, generator=gen)
+    out = torch.empty(n, nq * hd, device=cuda)
+    tqk.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, qn, kn, vn, out)
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    # the appended rows are the reference quantiser's
+    assert np.array_equal(kh[:, pos0:], port.quantize_rows(kn.cpu().numpy().reshape(n, nkv, hd).transpose(1, 0, 2)))
+    got, qh = out.cpu().numpy(), qn.cpu().numpy()
+    for i in (0, 1, 17, 511, 1024, 2046, 2047):
+        ref = port.attend(kh, vh, nq, nkv, hd, mt, pos0 + i, qh[i])
+        ok, max_abs, rel = tolerance_ok(got[i], ref)
+        assert ok, f"token {i}: max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
+def test_bad_arguments_are_rejected(tqk, cuda):
+    import torch
+    kp = torch.zeros(8, 16, 144, dtype=torch.uint8, device=cuda)
+    q = torch.zeros(32 * 128, device=cuda)
+    out = torch.zeros(32 * 128, device=cuda)
+    with pytest.raises(tqk.TQKError) as e:
+        tqk.attend(kp, kp, 32, 8, 128, 16, 16, q, out)
+    assert e.value.status == tqk.EPOS
+    args = tqk.decode_args(kp.view(-1)[4:], kp, 32, 8, 128, 15, q, out, len0=3)  # 4-byte offset planes
+    with pytest.raises(tqk.TQKError) as e:
+        tqk.decode(args)
+    assert e.value.status == tqk.EALIGN

@@ -1,0 +1,155 @@
+"""Pins the oracle (CPU, no GPU needed).
+
+The scalar restatement oracle/tq_oracle.c must reproduce, bit for bit, the
+golden fixtures that tests/golden/make_golden.py generated from the reference's
+own scalar build, and -- where oracle/_ref was built from the reference tree --
+the reference build itself on fresh inputs.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from _cases import (decode_case, digest, head_inputs, prefill_inputs, quant_edge_rows, sweep_inputs,
+                    tolerance_ok)
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def port():
+    if not oracle.available("port"):
+        oracle.build()
+    return oracle.Oracle("port")
+
+
+def _load(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def test_quantiser_golden(port):
+    g = _load("quant_edge.npz")
+    x = quant_edge_rows(np.random.default_rng(1))
+    assert np.array_equal(x.view(np.uint32), g["x"].view(np.uint32))
+    assert np.array_equal(port.quantize_rows(x), g["blocks"])
+
+
+def _decode_cases():
+    g = _load("decode.npz")
+    return sorted({k.split("__")[0] for k in g.files})
+
+
+@pytest.mark.parametrize("name", _decode_cases())
+def test_decode_golden(port, name):
+    g = _load("decode.npz")
+    seed, nq, nkv, hd, mt, pos, of, rp = (int(v) for v in g[f"{name}__params"])
+    kf, vf, q = decode_case(seed, nq, nkv, hd, mt, pos + 1, outlier_frac=of / 1e6, rope_pos=None if rp < 0 else rp)
+    assert digest(kf, vf, q) == str(g[f"{name}__in_sha"]), "input stream changed"
+    kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+    assert digest(kp, vp) == str(g[f"{name}__planes_sha"])
+    out = port.attend(kp, vp, nq, nkv, hd, mt, pos, q)
+    assert np.array_equal(out, g[f"{name}__out"])
+
+
+def test_prefill_golden(port):
+    g = _load("prefill.npz")
+    seed, nq, nkv, hd, mt, pos0, n = (int(v) for v in g["params"])
+    kf, vf, qn, kn, vn = prefill_inputs(seed, nq, nkv, hd, mt, pos0, n)
+    assert digest(kf, vf, qn, kn, vn) == str(g["in_sha"])
+    kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+    out = port.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, qn, kn, vn)
+    assert np.array_equal(out, g["out"])
+    assert np.array_equal(kp[:, pos0:pos0 + n], g["kp"]) and np.array_equal(vp[:, pos0:pos0 + n], g["vp"])
+
+
+def test_ops_sweep_golden(port):
+    g = _load("ops_sweep.npz")
+    keys = sorted({k.split("__")[0] for k in g.files})
+    assert len(keys) == 24
+    for key in keys:
+        gg, n, hd = (int(p[1:] if p[0] == "g" or p[0] == "n" else p[2:]) for p in key.split("_"))
+        nb = hd // 32
+        qf, kf, vf, w = sweep_inputs(gg, n, hd)
+        qb, kb, vb = port.quantize_rows(qf), port.quantize_rows(kf), port.quantize_rows(vf)
+        assert digest(qb, kb, vb, w) == str(g[key + "__in_sha"])
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+        sc = port.attn_scores(qb, gg, kb, n, nb, scale, n + 4).reshape(gg, n + 4)
+        assert np.array_equal(sc[:, :n], g[key + "__scores"]), key
+        assert np.isnan(sc[:, n:]).all(), "scores written past n"
+        acc = port.attn_accum(w, n + 4, gg, vb, n, nb, hd + 8).reshape(gg, hd + 8)
+        assert np.array_equal(acc[:, :hd], g[key + "__accum"]), key
+        assert np.isnan(acc[:, hd:]).all(), "accum written past head_dim"
+
+
+def test_head_q8_golden(port):
+    g = _load("head_q8.npz")
+    for hd, n, seed in ((32, 1, 60), (128, 100, 70), (128, 16, 90)):
+        q, kf, vf = head_inputs(hd, n, seed)
+        kb, vb = port.quantize_rows(kf), port.quantize_rows(vf)
+        key = f"hd{hd}_n{n}_s{seed}"
+        assert digest(q, kb, vb) == str(g[key + "__in_sha"])
+        o, qq, sc = port.attention_head(q, kb, vb, n, hd)
+        assert np.array_equal(o, g[key + "__out"])
+        assert np.array_equal(qq, g[key + "__qq"])
+        assert np.array_equal(sc, g[key + "__scores"])
+
+
+def test_quantiser_against_reference_build(port):
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    ref = oracle.Oracle("ref_scalar")
+    rng = np.random.default_rng(123)
+    x = np.concatenate([quant_edge_rows(rng, 256),
+                        rng.standard_normal((200, 256), dtype=np.float32) * np.float32(1e-3),
+                        (rng.integers(-300, 300, (64, 256)) / 2).astype(np.float32)])
+    assert np.array_equal(port.quantize_rows(x), ref.quantize_rows(x))
+
+
+@pytest.mark.parametrize("shape", [(32, 8, 128, 300, 257), (16, 2, 64, 90, 33), (12, 4, 32, 40, 1)])
+def test_attend_against_reference_build(port, shape):
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    ref = oracle.Oracle("ref_scalar")
+    nq, nkv, hd, mt, n = shape
+    kf, vf, q = decode_case(7 + n, nq, nkv, hd, mt, n)
+    kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+    a = port.attend(kp, vp, nq, nkv, hd, mt, n - 1, q)
+    b = ref.attend(kp, vp, nq, nkv, hd, mt, n - 1, q)
+    assert np.array_equal(a, b)
+
+
+def test_avx2_baseline_matches_oracle():
+    """The timed CPU baseline (reference AVX2 build) computes the same attention."""
+    if not oracle.available("ref_avx2"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    avx = oracle.Oracle("ref_avx2")
+    g = np.load(os.path.join(GOLDEN, "decode.npz"))
+    seed, nq, nkv, hd, mt, pos, _, _ = (int(v) for v in g["cfg1__params"])
+    kf, vf, q = decode_case(seed, nq, nkv, hd, mt, pos + 1)
+    kp, vp = avx.quantize_rows(kf), avx.quantize_rows(vf)
+    out = avx.attend(kp, vp, nq, nkv, hd, mt, pos, q, threads=4)
+    ok, max_abs, rel = tolerance_ok(out, g["cfg1__out"], 1e-5, 1e-5)
+    assert ok, (max_abs, rel)
+
+
+def test_prefill_equals_sequential_decode(port):
+    """attention_layer_batch semantics: a chunk equals per-token store + attend."""
+    nq, nkv, hd, mt, pos0, n = 8, 2, 64, 48, 20, 7
+    kf, vf, qn, kn, vn = prefill_inputs(5, nq, nkv, hd, mt, pos0, n)
+    kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+    kp2, vp2 = kp.copy(), vp.copy()
+    out = port.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, qn, kn, vn).reshape(n, -1)
+    for i in range(n):
+        assert port.store_kv(kp2, vp2, nkv, hd, mt, pos0 + i, kn[i], vn[i]) == 0
+        assert np.array_equal(port.attend(kp2, vp2, nq, nkv, hd, mt, pos0 + i, qn[i]), out[i])
+    assert np.array_equal(kp, kp2) and np.array_equal(vp, vp2)
+
+
+def test_store_kv_rejects_bad_pos(port):
+    kp = np.full((2, 4, 36), 7, np.uint8)
+    vp = kp.copy()
+    k = np.ones(64, np.float32)
+    for pos in (-1, 4, 9):
+        assert port.store_kv(kp, vp, 2, 32, 4, pos, k, k) == -1
+    assert (kp == 7).all() and (vp == 7).all()
