@@ -38,8 +38,15 @@ __device__ __forceinline__ void record_error(int *err, int code) {
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float q8_scale(float amax) { return __fdiv_rn(amax, 127.0f); }
 __device__ __forceinline__ float q8_inverse(float d) { return d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f; }
+// NaN: the reference runs on x86, where x*inv returns x itself (quieted) when
+// x is NaN and the "default NaN" 0xFFC00000 for Inf*0 or 0*Inf, and the add
+// passes that NaN through; its int8 is the low byte of those bits (0x4B400000
+// has a zero low byte).  The GPU would return its canonical 0x7FFFFFFF instead,
+// so NaN products are mapped explicitly.
 __device__ __forceinline__ int8_t q8_round(float x, float inv) {
-    const float shifted = __fadd_rn(__fmul_rn(x, inv), 12582912.0f);
+    const float v = __fmul_rn(x, inv);
+    if (isnan(v)) return isnan(x) ? (int8_t)(__float_as_uint(x) & 0xFFu) : (int8_t)0;
+    const float shifted = __fadd_rn(v, 12582912.0f);
     return (int8_t)(__float_as_int(shifted) - 0x4B400000);
 }
 // |x| as the reference's max loop sees it: NaN never exceeds the running max.
@@ -82,6 +89,12 @@ __device__ __forceinline__ void fence_barrier_init() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
+}
+
+// Plain arrive (count 1) with release semantics: the arriving warp's reads of
+// the slot happen before the producer's next copy into it.
+__device__ __forceinline__ void mbar_arrive_release(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {

@@ -134,6 +134,91 @@ __device__ __forceinline__ float score_row(const uint8_t *row, const uint32_t (&
     return __fmul_rn(acc, scale);
 }
 
+// Barrier over the first NT threads of the CTA: bar 0 with the whole CTA, or a
+// named barrier when only the consumer warps take part.
+template <int BAR, int NT>
+__device__ __forceinline__ void cta_sync() {
+    if constexpr (BAR == 0) {
+        __syncthreads();
+    } else {
+        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    }
+}
+
+// Finishes one split of one (item, kv-head slice).  acc(g, c) is the CTA's
+// unnormalised sum for its q head g and column c, relative to the running max
+// ms[g], with softmax denominator ls[g].  A single split writes the output (or
+// the partial, in TQK_OUT_PARTIAL mode); otherwise the split's partial goes to
+// the workspace and the last-arriving split (atomic ticket, never a wait)
+// merges all splits by log-sum-exp, in split order, so results are
+// deterministic.  ms/ls are overwritten by the merge.
+template <int HD, int GROWS, int NT, int BAR, typename AccFn>
+__device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int item, int pair, int s, int n_splits,
+                                             int qh0, int G, float *out_item, AccFn acc, float *ms, float *ls,
+                                             float *wts, int *flag) {
+    const bool single = n_splits == 1;
+    const long long pair_base = ((long long)item * p.pairs + pair) * p.max_splits;
+    for (int i = tid; i < G * HD; i += NT) {
+        const int g = i / HD, c = i - g * HD;
+        const float a = acc(g, c);
+        if (single) {
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                out_item[(long long)(qh0 + g) * HD + c] = a / ls[g];
+            } else {
+                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+                o[c] = a;
+                if (c == 0) { o[HD] = ms[g]; o[HD + 1] = ls[g]; }
+            }
+        } else {
+            float *pp = p.part + ((pair_base + s) * GROWS + g) * (HD + 2);
+            pp[c] = a;
+            if (c == 0) { pp[HD] = ms[g]; pp[HD + 1] = ls[g]; }
+        }
+    }
+    if (single) return;
+
+    __threadfence();
+    cta_sync<BAR, NT>();
+    if (tid == 0) {
+        const int prev = atomicAdd(&p.counters[(long long)item * p.pairs + pair], 1);
+        *flag = (prev == n_splits - 1);
+    }
+    cta_sync<BAR, NT>();
+    if (!*flag) return;
+    __threadfence();
+
+    const int lane = tid & 31, warp = tid >> 5;
+    const float *pb = p.part + pair_base * GROWS * (HD + 2);
+    for (int g = warp; g < G; g += NT / 32) {
+        float M = -INFINITY;
+        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD));
+        M = warp_max(M);
+        float Lsum = 0.0f;
+        for (int sp = lane; sp < n_splits; sp += 32) {
+            const float w = expf(__ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD) - M);
+            wts[sp * GROWS + g] = w;
+            Lsum += __ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD + 1) * w;
+        }
+        Lsum = warp_sum(Lsum);
+        if (lane == 0) { ms[g] = M; ls[g] = Lsum; }
+    }
+    cta_sync<BAR, NT>();
+    for (int i = tid; i < G * HD; i += NT) {
+        const int g = i / HD, c = i - g * HD;
+        float a = 0.0f;
+        for (int sp = 0; sp < n_splits; sp++)
+            a = fmaf(wts[sp * GROWS + g], __ldcg(pb + (sp * GROWS + g) * (HD + 2) + c), a);
+        if (p.out_mode == TQK_OUT_NORMALIZED) {
+            out_item[(long long)(qh0 + g) * HD + c] = a / ls[g];
+        } else {
+            float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+            o[c] = a;
+            if (c == 0) { o[HD] = ms[g]; o[HD + 1] = ls[g]; }
+        }
+    }
+    if (tid == 0) p.counters[(long long)item * p.pairs + pair] = 0;  // ready for the next launch
+}
+
 template <int NB, int GMAX>
 __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodeParams p) {
     using L = DecLayout<NB, GMAX>;
@@ -413,71 +498,21 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
             for (int c = 0; c < CPL; c++) red[(warp * GMAX + g) * HD + c0 + c] = acc[g][c];
     }
     __syncthreads();
-
-    const bool single = n_splits == 1;
-    const long long pair_base = ((long long)item * p.pairs + pair) * p.max_splits;
-    for (int i = tid; i < G * HD; i += DEC_THREADS) {
-        const int g = i / HD, c = i - g * HD;
+    auto acc_of = [&](int g, int c) {
         float a = 0.0f;
 #pragma unroll
         for (int w = 0; w < DEC_WARPS; w++) a += red[(w * GMAX + g) * HD + c];
-        if (single) {
-            if (p.out_mode == TQK_OUT_NORMALIZED) {
-                out_item[(long long)(qh0 + g) * HD + c] = a / l_s[g];
-            } else {
-                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
-                o[c] = a;
-                if (c == 0) { o[HD] = m_s[g]; o[HD + 1] = l_s[g]; }
-            }
-        } else {
-            float *pp = p.part + ((pair_base + s) * GMAX + g) * (HD + 2);
-            pp[c] = a;
-            if (c == 0) { pp[HD] = m_s[g]; pp[HD + 1] = l_s[g]; }
-        }
-    }
-    if (single) return;
-
-    // last-arriving split merges (threadFenceReduction pattern: no waiting)
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const int prev = atomicAdd(&p.counters[(long long)item * p.pairs + pair], 1);
-        *flag = (prev == n_splits - 1);
-    }
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
-
-    float *wts = red + DEC_WARPS * GMAX * HD;
-    const float *pb = p.part + pair_base * GMAX * (HD + 2);
-    for (int g = warp; g < G; g += DEC_WARPS) {
-        float M = -INFINITY;
-        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD));
-        M = warp_max(M);
-        float Lsum = 0.0f;
-        for (int sp = lane; sp < n_splits; sp += 32) {
-            const float w = expf(__ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD) - M);
-            wts[sp * GMAX + g] = w;
-            Lsum += __ldcg(pb + (sp * GMAX + g) * (HD + 2) + HD + 1) * w;
-        }
-        Lsum = warp_sum(Lsum);
-        if (lane == 0) { m_s[g] = M; l_s[g] = Lsum; }
-    }
-    __syncthreads();
-    for (int i = tid; i < G * HD; i += DEC_THREADS) {
-        const int g = i / HD, c = i - g * HD;
-        float a = 0.0f;
-        for (int sp = 0; sp < n_splits; sp++) a = fmaf(wts[sp * GMAX + g], __ldcg(pb + (sp * GMAX + g) * (HD + 2) + c), a);
-        if (p.out_mode == TQK_OUT_NORMALIZED) {
-            out_item[(long long)(qh0 + g) * HD + c] = a / l_s[g];
-        } else {
-            float *o = out_item + (long long)(qh0 + g) * (HD + 2);
-            o[c] = a;
-            if (c == 0) { o[HD] = m_s[g]; o[HD + 1] = l_s[g]; }
-        }
-    }
-    if (tid == 0) p.counters[(long long)item * p.pairs + pair] = 0;  // ready for the next launch
+        return a;
+    };
+    finish_split<HD, GMAX, DEC_THREADS, 0>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, m_s, l_s,
+                                          red + DEC_WARPS * GMAX * HD, flag);
 }
+
+}  // namespace tqk
+
+#include "tqk_decode_mma.cuh"
+
+namespace tqk {
 
 // Cross-part log-sum-exp merge (tqk_merge_partials): one CTA per head.
 __global__ void merge_partials_kernel(const float *__restrict__ parts, int n_parts, long long part_stride,
@@ -515,6 +550,44 @@ __global__ void merge_partials_kernel(const float *__restrict__ parts, int n_par
 namespace {
 
 int gmax_for(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
+
+// Tensor-core kernel (head_dim 128 / 256): up to 16 q heads per CTA.
+template <int NB, int GPAD>
+int launch_mma(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
+    using L = MmaLayout<NB, GPAD>;
+    static std::mutex mu;
+    static int occ_by_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail_cuda(e, "decode: cudaGetDevice");
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ_by_dev[dev] == 0) {
+            e = cudaFuncSetAttribute(decode_q8_mma_kernel<NB, GPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     L::BYTES);
+            int o = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_q8_mma_kernel<NB, GPAD>, MMA_THREADS,
+                                                                  L::BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "decode_q8_mma_kernel attributes");
+            occ_by_dev[dev] = o > 0 ? o : -1;
+        }
+        occ = occ_by_dev[dev] > 0 ? occ_by_dev[dev] : 0;
+    }
+    if (ctas_per_sm) {
+        *ctas_per_sm = occ;
+        return TQK_OK;
+    }
+    decode_q8_mma_kernel<NB, GPAD><<<grid, MMA_THREADS, L::BYTES, stream>>>(p);
+    return check_launch("decode_q8_mma_kernel");
+}
+
+int dispatch_mma(int nb, int gpad, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
+    if (nb == 4) return gpad > 8 ? launch_mma<4, 16>(p, grid, stream, occ) : launch_mma<4, 8>(p, grid, stream, occ);
+    if (nb == 8) return gpad > 8 ? launch_mma<8, 16>(p, grid, stream, occ) : launch_mma<8, 8>(p, grid, stream, occ);
+    return fail(TQK_EUNSUPPORTED, "decode: tensor-core kernel needs head_dim 128 or 256");
+}
 
 template <int NB, int GMAX>
 int launch_decode(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
@@ -568,6 +641,7 @@ int dispatch(int nb, int gmax, const DecodeParams &p, dim3 grid, cudaStream_t st
 
 struct Plan {
     int nb, gmax, heads_per_cta, head_slices, pairs, split_tokens, max_splits, max_len;
+    bool mma;  // tensor-core kernel (head_dim 128/256) or the CUDA-core one (32/64)
     size_t counters_bytes, part_bytes;
 };
 
@@ -603,7 +677,8 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     }
     const int group = a->n_q_heads / a->n_kv_heads;
     pl->nb = nb;
-    pl->gmax = gmax_for(group);
+    pl->mma = nb % 4 == 0;
+    pl->gmax = pl->mma ? (group <= 8 ? 8 : 16) : gmax_for(group);
     pl->heads_per_cta = group < pl->gmax ? group : pl->gmax;
     pl->head_slices = (group + pl->heads_per_cta - 1) / pl->heads_per_cta;
     pl->pairs = a->n_kv_heads * pl->head_slices;
@@ -616,7 +691,8 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
         const DeviceInfo *d = device_info();
         int occ = 0;
         DecodeParams dummy{};
-        const int orc = dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
+        const int orc = pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
+                                : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
         if (orc) return orc;
         const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
         const long long pairs_total = (long long)a->n_items * pl->pairs;
@@ -700,7 +776,7 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     p.part = need ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes) : nullptr;
     p.err = device_info()->err_word;
     const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
-    return dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
+    return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
 }
 
 extern "C" int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads,

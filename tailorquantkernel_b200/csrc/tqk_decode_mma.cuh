@@ -1,0 +1,503 @@
+// tqk_decode_mma.cuh -- tensor-core Q8 decode attention for head_dim 128/256
+// (included by tqk_decode.cu, which defines DecodeParams, finish_split and the
+// warp helpers).
+//
+// One CTA = one token range of one kv head of one item, serving up to 16 q
+// heads.  Warp roles:
+//   * warp 4 (producer): one thread streams 64-token K/V tiles (144-byte rows,
+//     contiguous per plane) into a STAGES-deep ring with 1-D TMA bulk copies,
+//     paced by "empty" mbarriers the consumers release;
+//   * warps 0-3 (consumers): warp w owns rows 16w..16w+15 of every tile and runs
+//     its own online softmax, so there is no CTA-wide barrier per tile.
+// Per 16-token slice a consumer warp does:
+//   QK  mma.m16n8k32 s8*s8->s32, one per Q8 block (q heads = M rows, tokens =
+//       N columns): exact int32 block dots, combined with the reference's
+//       rounding sequence acc += (float)dot * (qd*kd) (model/attn_q8.c:24-31),
+//       so every score equals attn_scores_q8_scalar's bit for bit;
+//   softmax: per q-head row, max/sum over the quad of lanes holding the row;
+//   PV  mma.m16n8k16 f16->f32 per (block, 8-column n-tile): A = p*vd*2^-K
+//       split into fp16 hi + lo (two MMAs, ~22-bit precision), B = the int8 V
+//       values converted exactly to fp16.  V columns are taken in a permuted
+//       order inside each 32-column block (n-tile jj, column n -> 4n + jj) so
+//       each lane's B fragment is one aligned word per token row (bank
+//       conflict free); the output store undoes the permutation.
+// K (a power-of-two scale that keeps p*vd inside fp16 range) only grows, and
+// the accumulators are rescaled exactly when it or a row max changes.
+#pragma once
+
+namespace tqk {
+
+constexpr int MMA_WARPS = 4;                    // consumer warps
+constexpr int MMA_THREADS = (MMA_WARPS + 1) * 32;
+constexpr int MMA_T = 16 * MMA_WARPS;           // tokens per tile
+template <int NB>
+constexpr int mma_stages() { return 3; }  // 3 x 18 KB ring: 3 CTAs/SM for head_dim 128
+
+template <int NB, int GPAD>
+struct MmaLayout {
+    static constexpr int HD = NB * QK;
+    static constexpr int ROW = NB * BLOCK_BYTES;
+    static constexpr int TILE = MMA_T * ROW;
+    static constexpr int STAGES = mma_stages<NB>();
+    static constexpr int STAGE_BYTES = 2 * TILE;
+    static constexpr int OFF_BAR = STAGES * STAGE_BYTES;           // full[STAGES], empty[STAGES]
+    static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [16][HD]
+    static constexpr int OFF_QD = OFF_QQ + 16 * HD;                // float [16][NB]
+    static constexpr int OFF_NEW = OFF_QD + ((16 * NB * 4 + 15) / 16) * 16;   // appended K, V rows
+    static constexpr int OFF_FLAG = OFF_NEW + ((2 * ROW + 15) / 16) * 16;     // int flag, int timeout
+    static constexpr int BYTES = OFF_FLAG + 16;
+    // epilogue scratch, in the idle stage ring
+    static constexpr int RED_FLOATS = MMA_WARPS * GPAD * HD;
+    static constexpr int SCRATCH_FLOATS = RED_FLOATS + 3 * MMA_WARPS * GPAD + 2 * GPAD + MAX_SPLITS * GPAD;
+    static_assert(SCRATCH_FLOATS * 4 <= OFF_BAR, "stage ring too small for the epilogue scratch");
+    static_assert(TILE % 16 == 0, "tiles must be whole 16-byte units");
+};
+
+// D = A(16x32 s8, row) * B(32x8 s8, col), int32, C = 0.
+__device__ __forceinline__ void mma_s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32.
+__device__ __forceinline__ void mma_f16_k16(float &d0, float &d1, float &d2, float &d3, uint32_t a0, uint32_t a1,
+                                            uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Same, for at most 8 q heads: rows 8-15 of A are zero, so only d0/d1 are kept
+// (the other two outputs are dead temporaries).
+__device__ __forceinline__ void mma_f16_k16_lo(float &d0, float &d1, uint32_t a0, uint32_t a2, uint32_t b0,
+                                               uint32_t b1) {
+    float x2, x3;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%5}, {%7,%8}, {%0,%1,%9,%9};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// Two fp32 -> packed f16x2 (x0 in the low half), round to nearest.
+__device__ __forceinline__ uint32_t pack_f16x2(float x0, float x1) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+__device__ __forceinline__ void unpack_f16x2(uint32_t h, float &x0, float &x1) {
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(x0), "=f"(x1)
+        : "r"(h));
+}
+// hi + lo fp16 split of (x0, x1): hi = f16(x), lo = f16(x - hi).
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    hi = pack_f16x2(x0, x1);
+    float h0, h1;
+    unpack_f16x2(hi, h0, h1);
+    lo = pack_f16x2(x0 - h0, x1 - h1);
+}
+
+// Byte jj of a and of b (signed int8) -> exact f16x2 {a_jj, b_jj}: bias to
+// unsigned (xor 0x80), drop into the mantissa of 1024.0 (0x6400) and subtract 1152.
+template <int JJ>
+__device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t a, uint32_t b) {
+    const uint32_t t = __byte_perm(a, b, JJ | ((4 + JJ) << 8));
+    const uint32_t h = (t & 0x00FF00FFu) ^ 0x64806480u;
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    return r;
+}
+
+__device__ __forceinline__ float exp2_int(int k) {  // 2^k, k in [-126, 127]
+    return __int_as_float((k + 127) << 23);
+}
+
+template <int NB, int GPAD>
+__global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const DecodeParams p) {
+    using L = MmaLayout<NB, GPAD>;
+    constexpr int HD = L::HD, ROW = L::ROW, STAGES = L::STAGES;
+    constexpr bool HI = GPAD > 8;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    const int item = blockIdx.z;
+    const int pair = blockIdx.y;
+    const int kvh = pair / p.head_slices;
+    const int slice = pair - kvh * p.head_slices;
+    const int g0 = slice * p.heads_per_cta;
+    const int G = min(p.heads_per_cta, p.group - g0);
+    int len = p.lens ? p.lens[item] : p.len0 + item * p.len_step;
+    if (len < 0 || len > p.max_tokens) {
+        if (tid == 0) record_error(p.err, DEVERR_BADLEN);
+        len = len < 0 ? 0 : p.max_tokens;
+    }
+    int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
+    if (n_splits > p.max_splits) {
+        if (tid == 0) record_error(p.err, DEVERR_BADLEN);
+        n_splits = p.max_splits;
+        len = p.max_splits * p.split_tokens;
+    }
+    const int s = blockIdx.x;
+    if (s >= (n_splits > 0 ? n_splits : 1)) return;
+    const int qh0 = kvh * p.group + g0;
+    float *out_item = p.out + (long long)item * p.out_item_stride;
+
+    if (len == 0) {  // empty context: zeros, like the reference's accum over no tokens
+        for (int i = tid; i < G * HD; i += MMA_THREADS) {
+            const int g = i / HD, c = i - g * HD;
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                out_item[(long long)(qh0 + g) * HD + c] = 0.0f;
+            } else {
+                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+                o[c] = 0.0f;
+                if (c == 0) { o[HD] = -INFINITY; o[HD + 1] = 0.0f; }
+            }
+        }
+        return;
+    }
+
+    const int t_begin = s * p.split_tokens;
+    const int t_end = min(len, t_begin + p.split_tokens);
+    const int n_tiles = (t_end - t_begin + MMA_T - 1) / MMA_T;
+    const long long head_off = (long long)kvh * p.max_tokens * ROW;
+    const uint8_t *kbase = p.k + (long long)item * p.item_stride + head_off;
+    const uint8_t *vbase = p.v + (long long)item * p.item_stride + head_off;
+
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint64_t *empty = full + STAGES;
+    int8_t *qq = reinterpret_cast<int8_t *>(smem + L::OFF_QQ);
+    float *qd = reinterpret_cast<float *>(smem + L::OFF_QD);
+    uint8_t *newrow = smem + L::OFF_NEW;
+    int *flag = reinterpret_cast<int *>(smem + L::OFF_FLAG);
+    int *timeout = flag + 1;
+
+    auto issue = [&](int j) {
+        const int slot = j % STAGES;
+        const int t0 = t_begin + j * MMA_T;
+        const int rows = min(MMA_T, t_end - t0);
+        const uint32_t bytes = (uint32_t)(rows * ROW);
+        uint8_t *ks = smem + slot * L::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[slot], 2 * bytes);
+        bulk_copy_g2s(ks, kbase + (long long)t0 * ROW, bytes, &full[slot]);
+        bulk_copy_g2s(ks + L::TILE, vbase + (long long)t0 * ROW, bytes, &full[slot]);
+    };
+
+    const int producer = MMA_WARPS * 32;
+    if (tid == producer) {
+#pragma unroll
+        for (int st = 0; st < STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], MMA_WARPS);
+        }
+        fence_barrier_init();
+        for (int j = 0; j < min(STAGES, n_tiles); j++) issue(j);
+        *timeout = 0;
+    }
+
+    const bool do_append = p.k_new != nullptr && s == n_splits - 1;
+    const int pos = len - 1;
+    if (warp < MMA_WARPS) {
+        // quantise this CTA's q heads (quant_x.c:12-34): 16 rows, rows >= G are zero
+        const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
+        for (int blk = warp; blk < 16 * NB; blk += MMA_WARPS) {
+            const int g = blk / NB, b = blk - g * NB;
+            const float x = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
+            float d;
+            const int8_t v8 = warp_quantize_block(x, &d);
+            qq[g * HD + b * QK + lane] = v8;
+            if (lane == 0) qd[g * NB + b] = d;
+        }
+        // fused append (store_kv, attention_layer.c:66-90) by the split holding len-1
+        if (do_append && warp < 2) {
+            const float *src = (warp == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride +
+                               (long long)kvh * HD;
+            uint8_t *nrow = newrow + warp * ROW;
+            uint8_t *grow = (warp == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + head_off +
+                            (long long)pos * ROW;
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float d;
+                const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+                nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+                if (lane == 0) *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
+                if (slice == 0) {
+                    grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+                    if (lane == 0) *reinterpret_cast<float *>(grow + b * BLOCK_BYTES) = d;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    if (warp == MMA_WARPS) {
+        // producer: the rest of the tiles, each once its slot has been released
+        if (lane == 0) {
+            for (int j = STAGES; j < n_tiles; j++) {
+                const int slot = j % STAGES;
+                if (!mbar_wait_bounded(&empty[slot], (uint32_t)(((j / STAGES) - 1) & 1), WAIT_NS, p.err)) {
+                    *timeout = 1;
+                    break;
+                }
+                issue(j);
+            }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------------ consumers
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t qa[NB][4];
+    float qd_lo[NB], qd_hi[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        qa[b][0] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 4 * t);
+        qa[b][2] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 16 + 4 * t);
+        qa[b][1] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 4 * t) : 0u;
+        qa[b][3] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 16 + 4 * t) : 0u;
+        qd_lo[b] = qd[g * NB + b];
+        qd_hi[b] = HI ? qd[(g + 8) * NB + b] : 0.0f;
+    }
+
+    float m_lo = -INFINITY, l_lo = 0.0f, m_hi = -INFINITY, l_hi = 0.0f;
+    int kscale = -125;  // running power-of-two exponent of the PV operand scale, in [-125, 126]
+    constexpr int NACC = HI ? 4 : 2;  // d0,d1 (rows g) [+ d2,d3 (rows g+8)]
+    float acc[NB][4][NACC];
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+            for (int e = 0; e < NACC; e++) acc[b][jj][e] = 0.0f;
+
+    const int r0 = warp * 16;
+    bool timed_out = false;
+    for (int j = 0; j < n_tiles; j++) {
+        const int slot = j % STAGES;
+        const int t0 = t_begin + j * MMA_T;
+        const int rows = min(MMA_T, t_end - t0);
+        const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((j / STAGES) & 1), WAIT_NS, p.err);
+        if (!__all_sync(0xffffffffu, ok)) {
+            timed_out = true;
+            break;
+        }
+        const int nvalid = rows - r0;  // tokens of this warp's slice present in the tile
+        if (nvalid > 0) {
+            uint8_t *ks = smem + slot * L::STAGE_BYTES + r0 * ROW;
+            uint8_t *vs = ks + L::TILE;
+            if (do_append && pos >= t0 + r0 && pos < t0 + r0 + 16) {
+                // substitute the freshly quantised row for the cache row at len-1
+                const int r = pos - t0 - r0;
+                for (int i = lane; i < ROW / 4; i += 32) {
+                    reinterpret_cast<uint32_t *>(ks + r * ROW)[i] = reinterpret_cast<const uint32_t *>(newrow)[i];
+                    reinterpret_cast<uint32_t *>(vs + r * ROW)[i] = reinterpret_cast<const uint32_t *>(newrow + ROW)[i];
+                }
+                __syncwarp();
+            }
+
+            // ---- scores: two 8-token n-tiles; lane holds tokens nt*8 + 2t + {0,1}
+            float sc[2][4];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                const uint8_t *kb = ks + (nt * 8 + g) * ROW;             // B fragment row (token nt*8+g)
+                const uint8_t *kda = ks + (nt * 8 + 2 * t) * ROW;        // scale rows of the lane's tokens
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+                for (int b = 0; b < NB; b++) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 4 + 4 * t);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 20 + 4 * t);
+                    int c[4];
+                    mma_s8_k32(c, qa[b], b0, b1);
+                    const float kd0 = *reinterpret_cast<const float *>(kda + b * BLOCK_BYTES);
+                    const float kd1 = *reinterpret_cast<const float *>(kda + ROW + b * BLOCK_BYTES);
+                    a0 = __fadd_rn(a0, __fmul_rn(__int2float_rn(c[0]), __fmul_rn(qd_lo[b], kd0)));
+                    a1 = __fadd_rn(a1, __fmul_rn(__int2float_rn(c[1]), __fmul_rn(qd_lo[b], kd1)));
+                    if (HI) {
+                        a2 = __fadd_rn(a2, __fmul_rn(__int2float_rn(c[2]), __fmul_rn(qd_hi[b], kd0)));
+                        a3 = __fadd_rn(a3, __fmul_rn(__int2float_rn(c[3]), __fmul_rn(qd_hi[b], kd1)));
+                    }
+                }
+                const int tk = nt * 8 + 2 * t;
+                const bool v0 = tk < nvalid, v1 = tk + 1 < nvalid;
+                sc[nt][0] = v0 ? __fmul_rn(a0, p.scale) : -INFINITY;
+                sc[nt][1] = v1 ? __fmul_rn(a1, p.scale) : -INFINITY;
+                sc[nt][2] = v0 ? __fmul_rn(a2, p.scale) : -INFINITY;
+                sc[nt][3] = v1 ? __fmul_rn(a3, p.scale) : -INFINITY;
+            }
+
+            // ---- online softmax per q-head row (the quad of lanes sharing g)
+            float pr[2][4];
+            float corr_lo, corr_hi = 1.0f;
+            {
+                float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(m_lo, mx);
+                corr_lo = expf(m_lo - mn);
+                pr[0][0] = expf(sc[0][0] - mn);
+                pr[0][1] = expf(sc[0][1] - mn);
+                pr[1][0] = expf(sc[1][0] - mn);
+                pr[1][1] = expf(sc[1][1] - mn);
+                float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                l_lo = l_lo * corr_lo + sum;
+                m_lo = mn;
+            }
+            if (HI) {
+                float mx = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(m_hi, mx);
+                corr_hi = expf(m_hi - mn);
+                pr[0][2] = expf(sc[0][2] - mn);
+                pr[0][3] = expf(sc[0][3] - mn);
+                pr[1][2] = expf(sc[1][2] - mn);
+                pr[1][3] = expf(sc[1][3] - mn);
+                float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                l_hi = l_hi * corr_hi + sum;
+                m_hi = mn;
+            } else {
+                pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.0f;
+            }
+
+            // ---- V scales of the lane's tokens (2t, 2t+1, 8+2t, 9+2t); masked rows are 0
+            float vd[4][NB];
+            float vmax = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int tk = (q >> 1) * 8 + 2 * t + (q & 1);
+#pragma unroll
+                for (int b = 0; b < NB; b++) {
+                    const float d = tk < nvalid ? *reinterpret_cast<const float *>(vs + tk * ROW + b * BLOCK_BYTES) : 0.0f;
+                    vd[q][b] = d;
+                    vmax = fmaxf(vmax, d);
+                }
+            }
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+            // exponent of the slice's largest scale (warp-uniform); zero/denormal -> keep the running one
+            const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
+            const int knew = max(kscale, min(kt, 126));
+            const bool rescale = __any_sync(0xffffffffu, corr_lo != 1.0f || corr_hi != 1.0f || knew != kscale);
+            if (rescale) {
+                const int df = kscale - knew;                 // <= 0
+                const float f = df < -126 ? 0.0f : exp2_int(df);  // exact power of two <= 1
+                const float flo = corr_lo * f, fhi = corr_hi * f;
+#pragma unroll
+                for (int b = 0; b < NB; b++)
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) {
+                        acc[b][jj][0] *= flo;
+                        acc[b][jj][1] *= flo;
+                        if constexpr (HI) {
+                            acc[b][jj][NACC - 2] *= fhi;
+                            acc[b][jj][NACC - 1] *= fhi;
+                        }
+                    }
+                kscale = knew;
+            }
+            const float inv_k = exp2_int(-kscale);
+
+            // ---- P·V per block: A = p*vd*2^-K (hi+lo fp16), B = int8 V -> fp16
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                uint32_t ah0, al0, ah2, al2, ah1 = 0, al1 = 0, ah3 = 0, al3 = 0;
+                split_f16x2(pr[0][0] * inv_k * vd[0][b], pr[0][1] * inv_k * vd[1][b], ah0, al0);
+                split_f16x2(pr[1][0] * inv_k * vd[2][b], pr[1][1] * inv_k * vd[3][b], ah2, al2);
+                if (HI) {
+                    split_f16x2(pr[0][2] * inv_k * vd[0][b], pr[0][3] * inv_k * vd[1][b], ah1, al1);
+                    split_f16x2(pr[1][2] * inv_k * vd[2][b], pr[1][3] * inv_k * vd[3][b], ah3, al3);
+                }
+                const uint8_t *vw = vs + b * BLOCK_BYTES + 4 + 4 * g;
+                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vw + (2 * t) * ROW);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 1) * ROW);
+                const uint32_t w8 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 8) * ROW);
+                const uint32_t w9 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 9) * ROW);
+#define TQK_PV_NTILE(JJ)                                                                                   \
+    {                                                                                                      \
+        const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);               \
+        float *a = acc[b][JJ];                                                                             \
+        if constexpr (HI) {                                                                                \
+            mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                             \
+            mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                             \
+        } else {                                                                                           \
+            mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                                \
+            mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                                \
+        }                                                                                                  \
+    }
+                TQK_PV_NTILE(0)
+                TQK_PV_NTILE(1)
+                TQK_PV_NTILE(2)
+                TQK_PV_NTILE(3)
+#undef TQK_PV_NTILE
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_release(&empty[slot]);
+    }
+
+    // ------------------------------------------------------------------ epilogue
+    if (timed_out) *timeout = 1;
+    cta_sync<1, MMA_WARPS * 32>();
+    if (*timeout) return;  // a tile never arrived (DEVERR_TIMEOUT recorded): leave without output
+
+    float *red = reinterpret_cast<float *>(smem);          // [W][GPAD][HD]
+    float *wm = red + L::RED_FLOATS;                       // [W][GPAD] row max
+    float *wl = wm + MMA_WARPS * GPAD;                     // [W][GPAD] row sum
+    float *wsc = wl + MMA_WARPS * GPAD;                    // [W][GPAD] merge weight
+    float *fm = wsc + MMA_WARPS * GPAD;                    // [GPAD]
+    float *fl = fm + GPAD;                                 // [GPAD]
+    float *wts = fl + GPAD;                                // [MAX_SPLITS][GPAD]
+    const float unscale = exp2_int(kscale);
+    if (t == 0) {
+        wm[warp * GPAD + g] = m_lo;
+        wl[warp * GPAD + g] = l_lo;
+        if (HI) {
+            wm[warp * GPAD + g + 8] = m_hi;
+            wl[warp * GPAD + g + 8] = l_hi;
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            // permuted n-tile column n holds block column 4n + jj; this lane's d0/d1 are n = 2t, 2t+1
+            const int c = b * QK + 8 * t + jj;
+            red[(warp * GPAD + g) * HD + c] = acc[b][jj][0] * unscale;
+            red[(warp * GPAD + g) * HD + c + 4] = acc[b][jj][1] * unscale;
+            if constexpr (HI) {
+                red[(warp * GPAD + g + 8) * HD + c] = acc[b][jj][NACC - 2] * unscale;
+                red[(warp * GPAD + g + 8) * HD + c + 4] = acc[b][jj][NACC - 1] * unscale;
+            }
+        }
+    cta_sync<1, MMA_WARPS * 32>();
+    if (tid < GPAD) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; w++) M = fmaxf(M, wm[w * GPAD + tid]);
+        float Lsum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; w++) {
+            const float mw = wm[w * GPAD + tid];
+            const float e = mw == -INFINITY ? 0.0f : expf(mw - M);
+            wsc[w * GPAD + tid] = e;
+            Lsum += wl[w * GPAD + tid] * e;
+        }
+        fm[tid] = M;
+        fl[tid] = Lsum;
+    }
+    cta_sync<1, MMA_WARPS * 32>();
+    auto acc_of = [&](int gg, int c) {
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < MMA_WARPS; w++) a = fmaf(red[(w * GPAD + gg) * HD + c], wsc[w * GPAD + gg], a);
+        return a;
+    };
+    finish_split<HD, GPAD, MMA_WARPS * 32, 1>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, fm, fl, wts,
+                                              flag);
+}
+
+}  // namespace tqk

@@ -62,6 +62,9 @@ def quant_edge_rows(rng: np.random.Generator, n: int = 128) -> np.ndarray:
     r = rng.standard_normal(n, dtype=np.float32); r[70] = np.nan; rows.append(r)
     rows.append(np.full(n, np.nan, np.float32))
     r = np.zeros(n, np.float32); r[3] = 1e-45; rows.append(r)             # smallest denormal
+    r = rng.standard_normal(n, dtype=np.float32)                           # NaN payloads: quiet and signalling
+    r[[2, 33, 70, 101]] = np.array([0x7FC000AB, 0xFFC00012, 0x7F8000CD, 0xFF800001], np.uint32).view(np.float32)
+    rows.append(r)
     r = rng.standard_normal(n, dtype=np.float32); r[:32] = -0.0; rows.append(r)
     for k in range(8):
         rows.append((rng.standard_normal(n, dtype=np.float32) * (10.0 ** rng.uniform(-6, 6))).astype(np.float32))
