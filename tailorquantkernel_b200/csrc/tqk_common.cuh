@@ -115,14 +115,28 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-// Bounded wait: spins on try_wait (which itself suspends for a short while)
-// until the phase completes or `limit_ns` of wall time pass.  Returns false on
-// timeout and records DEVERR_TIMEOUT; never waits forever.
+// try_wait that suspends the thread until the phase completes or about
+// `hint_ns` pass, so a waiting warp does not spin on the issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: sleeps in try_wait until the phase completes or `limit_ns` of
+// wall time pass.  Returns false on timeout and records DEVERR_TIMEOUT; never
+// waits forever.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns, int *err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
         if (globaltimer_ns() - t0 > limit_ns) {
             record_error(err, DEVERR_TIMEOUT);
             return false;

@@ -28,7 +28,7 @@ namespace tqk {
 constexpr int DEC_THREADS = 128;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_T = 64;          // tokens per tile
-constexpr int MAX_SPLITS = 256;    // bound on splits per (item, kv head)
+constexpr int MAX_SPLITS = 128;    // bound on splits per (item, kv head)
 constexpr uint64_t WAIT_NS = 1000000000ull;   // 1 s bound on any mbarrier wait
 constexpr uint64_t DRAIN_NS = 20000000ull;    // 20 ms bound when draining after a timeout
 
@@ -78,7 +78,7 @@ struct DecLayout {
     // after the pipeline drains, the stage ring is reused for the cross-warp
     // reduction and the merge weights
     static constexpr int RED_BYTES = DEC_WARPS * GMAX * HD * 4;
-    static constexpr int WTS_BYTES = MAX_SPLITS * GMAX * 4;
+    static constexpr int WTS_BYTES = 2 * MAX_SPLITS * GMAX * 4;  // merge weights + split sums
     static_assert(RED_BYTES + WTS_BYTES <= OFF_BAR, "stage ring too small for the epilogue scratch");
     static_assert(TILE % 16 == 0, "tiles must be whole 16-byte units");
 };
@@ -189,15 +189,24 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
 
     const int lane = tid & 31, warp = tid >> 5;
     const float *pb = p.part + pair_base * GROWS * (HD + 2);
+    // every split's (m, l) in one round trip (wts holds m, ls_all holds l)
+    float *lall = wts + MAX_SPLITS * GROWS;
+    for (int i = tid; i < n_splits * G; i += NT) {
+        const int sp = i / G, g = i - sp * G;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pb + (sp * GROWS + g) * (HD + 2) + HD));
+        wts[sp * GROWS + g] = ml.x;
+        lall[sp * GROWS + g] = ml.y;
+    }
+    cta_sync<BAR, NT>();
     for (int g = warp; g < G; g += NT / 32) {
         float M = -INFINITY;
-        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, __ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD));
+        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, wts[sp * GROWS + g]);
         M = warp_max(M);
         float Lsum = 0.0f;
         for (int sp = lane; sp < n_splits; sp += 32) {
-            const float w = expf(__ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD) - M);
+            const float w = expf(wts[sp * GROWS + g] - M);
             wts[sp * GROWS + g] = w;
-            Lsum += __ldcg(pb + (sp * GROWS + g) * (HD + 2) + HD + 1) * w;
+            Lsum += lall[sp * GROWS + g] * w;
         }
         Lsum = warp_sum(Lsum);
         if (lane == 0) { ms[g] = M; ls[g] = Lsum; }
@@ -206,8 +215,18 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
     for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, c = i - g * HD;
         float a = 0.0f;
-        for (int sp = 0; sp < n_splits; sp++)
-            a = fmaf(wts[sp * GROWS + g], __ldcg(pb + (sp * GROWS + g) * (HD + 2) + c), a);
+        int sp = 0;
+        for (; sp + 4 <= n_splits; sp += 4) {  // four independent loads in flight
+            const float x0 = __ldcg(pb + ((sp + 0) * GROWS + g) * (HD + 2) + c);
+            const float x1 = __ldcg(pb + ((sp + 1) * GROWS + g) * (HD + 2) + c);
+            const float x2 = __ldcg(pb + ((sp + 2) * GROWS + g) * (HD + 2) + c);
+            const float x3 = __ldcg(pb + ((sp + 3) * GROWS + g) * (HD + 2) + c);
+            a = fmaf(wts[(sp + 0) * GROWS + g], x0, a);
+            a = fmaf(wts[(sp + 1) * GROWS + g], x1, a);
+            a = fmaf(wts[(sp + 2) * GROWS + g], x2, a);
+            a = fmaf(wts[(sp + 3) * GROWS + g], x3, a);
+        }
+        for (; sp < n_splits; sp++) a = fmaf(wts[sp * GROWS + g], __ldcg(pb + (sp * GROWS + g) * (HD + 2) + c), a);
         if (p.out_mode == TQK_OUT_NORMALIZED) {
             out_item[(long long)(qh0 + g) * HD + c] = a / ls[g];
         } else {

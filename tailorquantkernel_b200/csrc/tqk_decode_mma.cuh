@@ -25,13 +25,21 @@
 // the accumulators are rescaled exactly when it or a row max changes.
 #pragma once
 
+#include <type_traits>
+
 namespace tqk {
 
-constexpr int MMA_WARPS = 4;                    // consumer warps
+#ifndef TQK_MMA_WARPS
+#define TQK_MMA_WARPS 4
+#endif
+#ifndef TQK_MMA_STAGES
+#define TQK_MMA_STAGES 3
+#endif
+constexpr int MMA_WARPS = TQK_MMA_WARPS;        // consumer warps (16 tokens of each tile apiece)
 constexpr int MMA_THREADS = (MMA_WARPS + 1) * 32;
 constexpr int MMA_T = 16 * MMA_WARPS;           // tokens per tile
 template <int NB>
-constexpr int mma_stages() { return 3; }  // 3 x 18 KB ring: 3 CTAs/SM for head_dim 128
+constexpr int mma_stages() { return TQK_MMA_STAGES; }  // default 3 x 18 KB ring: 3 CTAs/SM at head_dim 128
 
 template <int NB, int GPAD>
 struct MmaLayout {
@@ -48,7 +56,7 @@ struct MmaLayout {
     static constexpr int BYTES = OFF_FLAG + 16;
     // epilogue scratch, in the idle stage ring
     static constexpr int RED_FLOATS = MMA_WARPS * GPAD * HD;
-    static constexpr int SCRATCH_FLOATS = RED_FLOATS + 3 * MMA_WARPS * GPAD + 2 * GPAD + MAX_SPLITS * GPAD;
+    static constexpr int SCRATCH_FLOATS = RED_FLOATS + 3 * MMA_WARPS * GPAD + 2 * GPAD + 2 * MAX_SPLITS * GPAD;
     static_assert(SCRATCH_FLOATS * 4 <= OFF_BAR, "stage ring too small for the epilogue scratch");
     static_assert(TILE % 16 == 0, "tiles must be whole 16-byte units");
 };
@@ -78,6 +86,31 @@ __device__ __forceinline__ void mma_f16_k16_lo(float &d0, float &d1, uint32_t a0
         : "r"(a0), "r"(0u), "r"(a2), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
+// Packed fp32 pairs (Blackwell f32x2 ALU ops, each lane of the pair rounded
+// like the scalar instruction).
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float x, float y) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ void upk2(f32x2 v, float &x, float &y) { asm("mov.b64 {%0,%1}, %2;" : "=f"(x), "=f"(y) : "l"(v)); }
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 // Two fp32 -> packed f16x2 (x0 in the low half), round to nearest.
 __device__ __forceinline__ uint32_t pack_f16x2(float x0, float x1) {
     uint32_t r;
@@ -89,12 +122,18 @@ __device__ __forceinline__ void unpack_f16x2(uint32_t h, float &x0, float &x1) {
         : "=f"(x0), "=f"(x1)
         : "r"(h));
 }
-// hi + lo fp16 split of (x0, x1): hi = f16(x), lo = f16(x - hi).
-__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
-    hi = pack_f16x2(x0, x1);
-    float h0, h1;
-    unpack_f16x2(hi, h0, h1);
-    lo = pack_f16x2(x0 - h0, x1 - h1);
+// hi + lo fp16 split of a pair x (values in [0, 1]): hi = x truncated to 10
+// mantissa bits (exact in fp16 for normal values), lo = f16(x - hi) with
+// |x - hi| < 2^-10 |x|, so hi + lo carries ~21 bits of x.
+__device__ __forceinline__ void split_f16x2(f32x2 x, uint32_t &hi, uint32_t &lo) {
+    float x0, x1;
+    upk2(x, x0, x1);
+    const float h0 = __uint_as_float(__float_as_uint(x0) & 0xFFFFE000u);
+    const float h1 = __uint_as_float(__float_as_uint(x1) & 0xFFFFE000u);
+    float r0, r1;
+    upk2(sub2(x, pk2(h0, h1)), r0, r1);
+    hi = pack_f16x2(h0, h1);
+    lo = pack_f16x2(r0, r1);
 }
 
 // Byte jj of a and of b (signed int8) -> exact f16x2 {a_jj, b_jj}: bias to
@@ -198,15 +237,26 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
     const bool do_append = p.k_new != nullptr && s == n_splits - 1;
     const int pos = len - 1;
     if (warp < MMA_WARPS) {
-        // quantise this CTA's q heads (quant_x.c:12-34): 16 rows, rows >= G are zero
+        // quantise this CTA's G q heads (quant_x.c:12-34), one row per warp with
+        // the row's loads issued together; the padding rows G..15 are zero
         const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
-        for (int blk = warp; blk < 16 * NB; blk += MMA_WARPS) {
-            const int g = blk / NB, b = blk - g * NB;
-            const float x = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
-            float d;
-            const int8_t v8 = warp_quantize_block(x, &d);
-            qq[g * HD + b * QK + lane] = v8;
-            if (lane == 0) qd[g * NB + b] = d;
+        for (int g = warp; g < 16; g += MMA_WARPS) {
+            if (g < G) {
+                float x[NB];
+#pragma unroll
+                for (int b = 0; b < NB; b++) x[b] = __ldg(qsrc + g * HD + b * QK + lane);
+#pragma unroll
+                for (int b = 0; b < NB; b++) {
+                    float d;
+                    const int8_t v8 = warp_quantize_block(x[b], &d);
+                    qq[g * HD + b * QK + lane] = v8;
+                    if (lane == 0) qd[g * NB + b] = d;
+                }
+            } else {
+#pragma unroll
+                for (int b = 0; b < NB; b++) qq[g * HD + b * QK + lane] = 0;
+                if (lane < NB) qd[g * NB + lane] = 0.0f;
+            }
         }
         // fused append (store_kv, attention_layer.c:66-90) by the split holding len-1
         if (do_append && warp < 2) {
@@ -259,6 +309,12 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         qd_hi[b] = HI ? qd[(g + 8) * NB + b] : 0.0f;
     }
 
+    f32x2 qdl2[NB], qdh2[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        qdl2[b] = pk2(qd_lo[b], qd_lo[b]);
+        qdh2[b] = pk2(qd_hi[b], qd_hi[b]);
+    }
     float m_lo = -INFINITY, l_lo = 0.0f, m_hi = -INFINITY, l_hi = 0.0f;
     int kscale = -125;  // running power-of-two exponent of the PV operand scale, in [-125, 126]
     constexpr int NACC = HI ? 4 : 2;  // d0,d1 (rows g) [+ d2,d3 (rows g+8)]
@@ -269,6 +325,161 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         for (int jj = 0; jj < 4; jj++)
 #pragma unroll
             for (int e = 0; e < NACC; e++) acc[b][jj][e] = 0.0f;
+
+    // One 16-token slice of a tile: scores, online softmax (log2 domain), P*V.
+    // FULL slices skip all masking; partial ones mask tokens >= nvalid.
+    auto run_slice = [&](auto full_tag, const uint8_t *ks, const uint8_t *vs, int nvalid) {
+        constexpr bool FULL = decltype(full_tag)::value;
+        const f32x2 scale2 = pk2(p.scale, p.scale);
+        const f32x2 log2e2 = pk2(1.4426950408889634f, 1.4426950408889634f);
+        // ---- scores: two 8-token n-tiles; lane holds tokens nt*8 + 2t + {0,1}
+        float sc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            const uint8_t *kb = ks + (nt * 8 + g) * ROW;       // B fragment row (token nt*8+g)
+            const uint8_t *kda = ks + (nt * 8 + 2 * t) * ROW;  // scale rows of the lane's tokens
+            // acc += (float)dot * (qd*kd) per block, for the lane's token pair,
+            // with separately rounded products and sums as in the reference
+            f32x2 alo = pk2(0.0f, 0.0f), ahi = pk2(0.0f, 0.0f);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 4 + 4 * t);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 20 + 4 * t);
+                int c[4];
+                mma_s8_k32(c, qa[b], b0, b1);
+                const f32x2 kd = pk2(*reinterpret_cast<const float *>(kda + b * BLOCK_BYTES),
+                                     *reinterpret_cast<const float *>(kda + ROW + b * BLOCK_BYTES));
+                alo = add2(alo, mul2(pk2(__int2float_rn(c[0]), __int2float_rn(c[1])), mul2(qdl2[b], kd)));
+                if constexpr (HI)
+                    ahi = add2(ahi, mul2(pk2(__int2float_rn(c[2]), __int2float_rn(c[3])), mul2(qdh2[b], kd)));
+            }
+            // the reference's score (acc * scale, bit-exact), then to log2 units
+            upk2(mul2(mul2(alo, scale2), log2e2), sc[nt][0], sc[nt][1]);
+            if constexpr (HI) upk2(mul2(mul2(ahi, scale2), log2e2), sc[nt][2], sc[nt][3]);
+            else sc[nt][2] = sc[nt][3] = 0.0f;
+            if constexpr (!FULL) {
+                const int tk = nt * 8 + 2 * t;
+                if (tk >= nvalid) sc[nt][0] = sc[nt][2] = -INFINITY;
+                if (tk + 1 >= nvalid) sc[nt][1] = sc[nt][3] = -INFINITY;
+            }
+        }
+
+        // ---- online softmax per q-head row (the quad of lanes sharing g), base 2
+        float pr[2][4];
+        float corr_lo, corr_hi = 1.0f;
+        {
+            float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m_lo, mx);
+            corr_lo = exp2f(m_lo - mn);
+            pr[0][0] = exp2f(sc[0][0] - mn);
+            pr[0][1] = exp2f(sc[0][1] - mn);
+            pr[1][0] = exp2f(sc[1][0] - mn);
+            pr[1][1] = exp2f(sc[1][1] - mn);
+            float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l_lo = l_lo * corr_lo + sum;
+            m_lo = mn;
+        }
+        if constexpr (HI) {
+            float mx = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const float mn = fmaxf(m_hi, mx);
+            corr_hi = exp2f(m_hi - mn);
+            pr[0][2] = exp2f(sc[0][2] - mn);
+            pr[0][3] = exp2f(sc[0][3] - mn);
+            pr[1][2] = exp2f(sc[1][2] - mn);
+            pr[1][3] = exp2f(sc[1][3] - mn);
+            float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            l_hi = l_hi * corr_hi + sum;
+            m_hi = mn;
+        } else {
+            pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.0f;
+        }
+
+        // ---- V scales of the lane's tokens (2t, 2t+1, 8+2t, 9+2t); masked rows are 0
+        float vd[4][NB];
+        float vmax = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int tk = (q >> 1) * 8 + 2 * t + (q & 1);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float d = *reinterpret_cast<const float *>(vs + tk * ROW + b * BLOCK_BYTES);
+                if constexpr (!FULL) d = tk < nvalid ? d : 0.0f;
+                vd[q][b] = d;
+                vmax = fmaxf(vmax, d);
+            }
+        }
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+        // exponent of the slice's largest scale (warp-uniform); zero/denormal -> keep the running one
+        const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
+        const int knew = max(kscale, min(kt, 126));
+        const bool rescale = __any_sync(0xffffffffu, corr_lo != 1.0f || corr_hi != 1.0f || knew != kscale);
+        if (rescale) {
+            const int df = kscale - knew;                     // <= 0
+            const float f = df < -126 ? 0.0f : exp2_int(df);  // exact power of two <= 1
+            const float flo = corr_lo * f, fhi = corr_hi * f;
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    acc[b][jj][0] *= flo;
+                    acc[b][jj][1] *= flo;
+                    if constexpr (HI) {
+                        acc[b][jj][NACC - 2] *= fhi;
+                        acc[b][jj][NACC - 1] *= fhi;
+                    }
+                }
+            kscale = knew;
+        }
+        const float inv_k = exp2_int(-kscale);
+        const f32x2 ik2 = pk2(inv_k, inv_k);
+        const f32x2 p00 = mul2(pk2(pr[0][0], pr[0][1]), ik2), p10 = mul2(pk2(pr[1][0], pr[1][1]), ik2);
+        const f32x2 p02 = HI ? mul2(pk2(pr[0][2], pr[0][3]), ik2) : 0ull;
+        const f32x2 p12 = HI ? mul2(pk2(pr[1][2], pr[1][3]), ik2) : 0ull;
+
+        // ---- P*V per block: A = p*vd*2^-K (hi+lo fp16), B = int8 V -> fp16
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            uint32_t ah0, al0, ah2, al2, ah1 = 0, al1 = 0, ah3 = 0, al3 = 0;
+            const f32x2 vd01 = pk2(vd[0][b], vd[1][b]), vd23 = pk2(vd[2][b], vd[3][b]);
+            split_f16x2(mul2(p00, vd01), ah0, al0);
+            split_f16x2(mul2(p10, vd23), ah2, al2);
+            if constexpr (HI) {
+                split_f16x2(mul2(p02, vd01), ah1, al1);
+                split_f16x2(mul2(p12, vd23), ah3, al3);
+            }
+            const uint8_t *vw = vs + b * BLOCK_BYTES + 4 + 4 * g;
+            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vw + (2 * t) * ROW);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 1) * ROW);
+            const uint32_t w8 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 8) * ROW);
+            const uint32_t w9 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 9) * ROW);
+#define TQK_PV_NTILE(JJ)                                                                               \
+    {                                                                                                  \
+        const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);           \
+        float *a = acc[b][JJ];                                                                         \
+        if constexpr (HI) {                                                                            \
+            mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                         \
+            mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                         \
+        } else {                                                                                       \
+            mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                            \
+            mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                            \
+        }                                                                                              \
+    }
+            TQK_PV_NTILE(0)
+            TQK_PV_NTILE(1)
+            TQK_PV_NTILE(2)
+            TQK_PV_NTILE(3)
+#undef TQK_PV_NTILE
+        }
+    };
 
     const int r0 = warp * 16;
     bool timed_out = false;
@@ -294,146 +505,10 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
                 }
                 __syncwarp();
             }
-
-            // ---- scores: two 8-token n-tiles; lane holds tokens nt*8 + 2t + {0,1}
-            float sc[2][4];
-#pragma unroll
-            for (int nt = 0; nt < 2; nt++) {
-                const uint8_t *kb = ks + (nt * 8 + g) * ROW;             // B fragment row (token nt*8+g)
-                const uint8_t *kda = ks + (nt * 8 + 2 * t) * ROW;        // scale rows of the lane's tokens
-                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll
-                for (int b = 0; b < NB; b++) {
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 4 + 4 * t);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 20 + 4 * t);
-                    int c[4];
-                    mma_s8_k32(c, qa[b], b0, b1);
-                    const float kd0 = *reinterpret_cast<const float *>(kda + b * BLOCK_BYTES);
-                    const float kd1 = *reinterpret_cast<const float *>(kda + ROW + b * BLOCK_BYTES);
-                    a0 = __fadd_rn(a0, __fmul_rn(__int2float_rn(c[0]), __fmul_rn(qd_lo[b], kd0)));
-                    a1 = __fadd_rn(a1, __fmul_rn(__int2float_rn(c[1]), __fmul_rn(qd_lo[b], kd1)));
-                    if (HI) {
-                        a2 = __fadd_rn(a2, __fmul_rn(__int2float_rn(c[2]), __fmul_rn(qd_hi[b], kd0)));
-                        a3 = __fadd_rn(a3, __fmul_rn(__int2float_rn(c[3]), __fmul_rn(qd_hi[b], kd1)));
-                    }
-                }
-                const int tk = nt * 8 + 2 * t;
-                const bool v0 = tk < nvalid, v1 = tk + 1 < nvalid;
-                sc[nt][0] = v0 ? __fmul_rn(a0, p.scale) : -INFINITY;
-                sc[nt][1] = v1 ? __fmul_rn(a1, p.scale) : -INFINITY;
-                sc[nt][2] = v0 ? __fmul_rn(a2, p.scale) : -INFINITY;
-                sc[nt][3] = v1 ? __fmul_rn(a3, p.scale) : -INFINITY;
-            }
-
-            // ---- online softmax per q-head row (the quad of lanes sharing g)
-            float pr[2][4];
-            float corr_lo, corr_hi = 1.0f;
-            {
-                float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float mn = fmaxf(m_lo, mx);
-                corr_lo = expf(m_lo - mn);
-                pr[0][0] = expf(sc[0][0] - mn);
-                pr[0][1] = expf(sc[0][1] - mn);
-                pr[1][0] = expf(sc[1][0] - mn);
-                pr[1][1] = expf(sc[1][1] - mn);
-                float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                l_lo = l_lo * corr_lo + sum;
-                m_lo = mn;
-            }
-            if (HI) {
-                float mx = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float mn = fmaxf(m_hi, mx);
-                corr_hi = expf(m_hi - mn);
-                pr[0][2] = expf(sc[0][2] - mn);
-                pr[0][3] = expf(sc[0][3] - mn);
-                pr[1][2] = expf(sc[1][2] - mn);
-                pr[1][3] = expf(sc[1][3] - mn);
-                float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                l_hi = l_hi * corr_hi + sum;
-                m_hi = mn;
-            } else {
-                pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.0f;
-            }
-
-            // ---- V scales of the lane's tokens (2t, 2t+1, 8+2t, 9+2t); masked rows are 0
-            float vd[4][NB];
-            float vmax = 0.0f;
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int tk = (q >> 1) * 8 + 2 * t + (q & 1);
-#pragma unroll
-                for (int b = 0; b < NB; b++) {
-                    const float d = tk < nvalid ? *reinterpret_cast<const float *>(vs + tk * ROW + b * BLOCK_BYTES) : 0.0f;
-                    vd[q][b] = d;
-                    vmax = fmaxf(vmax, d);
-                }
-            }
-            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-            vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-            // exponent of the slice's largest scale (warp-uniform); zero/denormal -> keep the running one
-            const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
-            const int knew = max(kscale, min(kt, 126));
-            const bool rescale = __any_sync(0xffffffffu, corr_lo != 1.0f || corr_hi != 1.0f || knew != kscale);
-            if (rescale) {
-                const int df = kscale - knew;                 // <= 0
-                const float f = df < -126 ? 0.0f : exp2_int(df);  // exact power of two <= 1
-                const float flo = corr_lo * f, fhi = corr_hi * f;
-#pragma unroll
-                for (int b = 0; b < NB; b++)
-#pragma unroll
-                    for (int jj = 0; jj < 4; jj++) {
-                        acc[b][jj][0] *= flo;
-                        acc[b][jj][1] *= flo;
-                        if constexpr (HI) {
-                            acc[b][jj][NACC - 2] *= fhi;
-                            acc[b][jj][NACC - 1] *= fhi;
-                        }
-                    }
-                kscale = knew;
-            }
-            const float inv_k = exp2_int(-kscale);
-
-            // ---- P·V per block: A = p*vd*2^-K (hi+lo fp16), B = int8 V -> fp16
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                uint32_t ah0, al0, ah2, al2, ah1 = 0, al1 = 0, ah3 = 0, al3 = 0;
-                split_f16x2(pr[0][0] * inv_k * vd[0][b], pr[0][1] * inv_k * vd[1][b], ah0, al0);
-                split_f16x2(pr[1][0] * inv_k * vd[2][b], pr[1][1] * inv_k * vd[3][b], ah2, al2);
-                if (HI) {
-                    split_f16x2(pr[0][2] * inv_k * vd[0][b], pr[0][3] * inv_k * vd[1][b], ah1, al1);
-                    split_f16x2(pr[1][2] * inv_k * vd[2][b], pr[1][3] * inv_k * vd[3][b], ah3, al3);
-                }
-                const uint8_t *vw = vs + b * BLOCK_BYTES + 4 + 4 * g;
-                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vw + (2 * t) * ROW);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 1) * ROW);
-                const uint32_t w8 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 8) * ROW);
-                const uint32_t w9 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 9) * ROW);
-#define TQK_PV_NTILE(JJ)                                                                                   \
-    {                                                                                                      \
-        const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);               \
-        float *a = acc[b][JJ];                                                                             \
-        if constexpr (HI) {                                                                                \
-            mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                             \
-            mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                             \
-        } else {                                                                                           \
-            mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                                \
-            mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                                \
-        }                                                                                                  \
-    }
-                TQK_PV_NTILE(0)
-                TQK_PV_NTILE(1)
-                TQK_PV_NTILE(2)
-                TQK_PV_NTILE(3)
-#undef TQK_PV_NTILE
-            }
+            if (nvalid >= 16)
+                run_slice(std::true_type{}, ks, vs, 16);
+            else
+                run_slice(std::false_type{}, ks, vs, nvalid);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_release(&empty[slot]);
@@ -481,12 +556,12 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         float Lsum = 0.0f;
 #pragma unroll
         for (int w = 0; w < MMA_WARPS; w++) {
-            const float mw = wm[w * GPAD + tid];
-            const float e = mw == -INFINITY ? 0.0f : expf(mw - M);
+            const float mw = wm[w * GPAD + tid];  // base-2 units
+            const float e = mw == -INFINITY ? 0.0f : exp2f(mw - M);
             wsc[w * GPAD + tid] = e;
             Lsum += wl[w * GPAD + tid] * e;
         }
-        fm[tid] = M;
+        fm[tid] = M * 0.6931471805599453f;  // back to natural-log units for partials / merges
         fl[tid] = Lsum;
     }
     cta_sync<1, MMA_WARPS * 32>();
