@@ -136,7 +136,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (globaltimer_ns() - t0 > limit_ns) {
             record_error(err, DEVERR_TIMEOUT);
             return false;

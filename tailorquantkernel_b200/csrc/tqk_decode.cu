@@ -20,6 +20,7 @@
 //     results are deterministic.
 #include "tqk_internal.h"
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 
@@ -530,6 +531,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
 }  // namespace tqk
 
 #include "tqk_decode_mma.cuh"
+#include "tqk_decode_pack.cuh"
 
 namespace tqk {
 
@@ -602,6 +604,42 @@ int launch_mma(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_
     return check_launch("decode_q8_mma_kernel");
 }
 
+// Two-kv-heads-per-CTA kernel for 4 q heads per kv head.
+template <int NB>
+int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
+    using L = PackLayout<NB>;
+    static std::mutex mu;
+    static int occ_by_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail_cuda(e, "decode: cudaGetDevice");
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ_by_dev[dev] == 0) {
+            e = cudaFuncSetAttribute(decode_q8_pack_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+            int o = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_q8_pack_kernel<NB>, PK_THREADS, L::BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "decode_q8_pack_kernel attributes");
+            occ_by_dev[dev] = o > 0 ? o : -1;
+        }
+        occ = occ_by_dev[dev] > 0 ? occ_by_dev[dev] : 0;
+    }
+    if (ctas_per_sm) {
+        *ctas_per_sm = occ;
+        return TQK_OK;
+    }
+    decode_q8_pack_kernel<NB><<<grid, PK_THREADS, L::BYTES, stream>>>(p);
+    return check_launch("decode_q8_pack_kernel");
+}
+
+int dispatch_pack(int nb, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
+    if (nb == 4) return launch_pack<4>(p, grid, stream, occ);
+    if (nb == 8) return launch_pack<8>(p, grid, stream, occ);
+    return fail(TQK_EUNSUPPORTED, "decode: packed kernel needs head_dim 128 or 256");
+}
+
 int dispatch_mma(int nb, int gpad, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
     if (nb == 4) return gpad > 8 ? launch_mma<4, 16>(p, grid, stream, occ) : launch_mma<4, 8>(p, grid, stream, occ);
     if (nb == 8) return gpad > 8 ? launch_mma<8, 16>(p, grid, stream, occ) : launch_mma<8, 8>(p, grid, stream, occ);
@@ -660,7 +698,8 @@ int dispatch(int nb, int gmax, const DecodeParams &p, dim3 grid, cudaStream_t st
 
 struct Plan {
     int nb, gmax, heads_per_cta, head_slices, pairs, split_tokens, max_splits, max_len;
-    bool mma;  // tensor-core kernel (head_dim 128/256) or the CUDA-core one (32/64)
+    bool mma;   // tensor-core kernel (head_dim 128/256) or the CUDA-core one (32/64)
+    bool pack;  // tensor-core kernel with two kv heads per CTA (4 q heads per kv head)
     size_t counters_bytes, part_bytes;
 };
 
@@ -697,10 +736,11 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     const int group = a->n_q_heads / a->n_kv_heads;
     pl->nb = nb;
     pl->mma = nb % 4 == 0;
-    pl->gmax = pl->mma ? (group <= 8 ? 8 : 16) : gmax_for(group);
-    pl->heads_per_cta = group < pl->gmax ? group : pl->gmax;
-    pl->head_slices = (group + pl->heads_per_cta - 1) / pl->heads_per_cta;
-    pl->pairs = a->n_kv_heads * pl->head_slices;
+    pl->pack = pl->mma && group == 4 && a->n_kv_heads % 2 == 0;
+    pl->gmax = pl->pack ? 8 : pl->mma ? (group <= 8 ? 8 : 16) : gmax_for(group);
+    pl->heads_per_cta = pl->pack ? 8 : (group < pl->gmax ? group : pl->gmax);
+    pl->head_slices = pl->pack ? 1 : (group + pl->heads_per_cta - 1) / pl->heads_per_cta;
+    pl->pairs = pl->pack ? a->n_kv_heads / 2 : a->n_kv_heads * pl->head_slices;
     pl->max_len = max_len;
 
     int split = a->split_tokens;
@@ -710,8 +750,9 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
         const DeviceInfo *d = device_info();
         int occ = 0;
         DecodeParams dummy{};
-        const int orc = pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
-                                : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
+        const int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ)
+                        : pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
+                                  : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
         if (orc) return orc;
         const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
         const long long pairs_total = (long long)a->n_items * pl->pairs;
@@ -795,6 +836,7 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     p.part = need ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes) : nullptr;
     p.err = device_info()->err_word;
     const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
+    if (pl.pack) return dispatch_pack(pl.nb, p, grid, st, nullptr);
     return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
 }
 

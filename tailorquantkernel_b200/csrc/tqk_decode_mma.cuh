@@ -151,6 +151,203 @@ __device__ __forceinline__ float exp2_int(int k) {  // 2^k, k in [-126, 127]
     return __int_as_float((k + 127) << 23);
 }
 
+// Per-warp state of the tensor-core decode for one (item, kv-head slice) run:
+// q fragments, running row max / sum (base 2) and the P*V accumulators.
+template <int NB, bool HI>
+struct SliceState {
+    static constexpr int NACC = HI ? 4 : 2;  // d0,d1 (rows g) [+ d2,d3 (rows g+8)]
+    uint32_t qa[NB][4];
+    f32x2 qdl2[NB], qdh2[NB];
+    float m_lo, l_lo, m_hi, l_hi;
+    int kscale;  // running power-of-two exponent of the PV operand scale, in [-125, 126]
+    float acc[NB][4][NACC];
+
+    // Loads this lane's q fragments (rows g, g+8) from a quantised [16][HD] int8
+    // tile with scales [16][NB], and clears the softmax / accumulator state.
+    __device__ __forceinline__ void begin(const int8_t *qq, const float *qd, int g, int t) {
+        constexpr int HD = NB * QK;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            qa[b][0] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 4 * t);
+            qa[b][2] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 16 + 4 * t);
+            qa[b][1] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 4 * t) : 0u;
+            qa[b][3] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 16 + 4 * t) : 0u;
+            const float lo = qd[g * NB + b];
+            const float hi = HI ? qd[(g + 8) * NB + b] : 0.0f;
+            qdl2[b] = pk2(lo, lo);
+            qdh2[b] = pk2(hi, hi);
+        }
+        m_lo = m_hi = -INFINITY;
+        l_lo = l_hi = 0.0f;
+        kscale = -125;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+                for (int e = 0; e < NACC; e++) acc[b][jj][e] = 0.0f;
+    }
+};
+
+// One 16-token slice (K rows at ks, V rows at vs, 144*NB/4-byte rows): scores,
+// online softmax (log2 domain), P*V into st.  FULL slices skip all masking;
+// partial ones mask tokens >= nvalid.  g = lane/4, t = lane%4.
+template <int NB, bool HI, bool FULL>
+__device__ __forceinline__ void mma_slice(SliceState<NB, HI> &st, const uint8_t *ks, const uint8_t *vs, int nvalid,
+                                          float scale, int g, int t) {
+    constexpr int ROW = NB * BLOCK_BYTES;
+    constexpr int NACC = SliceState<NB, HI>::NACC;
+    const f32x2 scale2 = pk2(scale, scale);
+    const f32x2 log2e2 = pk2(1.4426950408889634f, 1.4426950408889634f);
+    // ---- scores: two 8-token n-tiles; lane holds tokens nt*8 + 2t + {0,1}
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++) {
+        const uint8_t *kb = ks + (nt * 8 + g) * ROW;       // B fragment row (token nt*8+g)
+        const uint8_t *kda = ks + (nt * 8 + 2 * t) * ROW;  // scale rows of the lane's tokens
+        // st.acc += (float)dot * (qd*kd) per block, for the lane's token pair,
+        // with separately rounded products and sums as in the reference
+        f32x2 alo = pk2(0.0f, 0.0f), ahi = pk2(0.0f, 0.0f);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 4 + 4 * t);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 20 + 4 * t);
+            int c[4];
+            mma_s8_k32(c, st.qa[b], b0, b1);
+            const f32x2 kd = pk2(*reinterpret_cast<const float *>(kda + b * BLOCK_BYTES),
+                                 *reinterpret_cast<const float *>(kda + ROW + b * BLOCK_BYTES));
+            alo = add2(alo, mul2(pk2(__int2float_rn(c[0]), __int2float_rn(c[1])), mul2(st.qdl2[b], kd)));
+            if constexpr (HI)
+                ahi = add2(ahi, mul2(pk2(__int2float_rn(c[2]), __int2float_rn(c[3])), mul2(st.qdh2[b], kd)));
+        }
+        // the reference's score (st.acc * scale, bit-exact), then to log2 units
+        upk2(mul2(mul2(alo, scale2), log2e2), sc[nt][0], sc[nt][1]);
+        if constexpr (HI) upk2(mul2(mul2(ahi, scale2), log2e2), sc[nt][2], sc[nt][3]);
+        else sc[nt][2] = sc[nt][3] = 0.0f;
+        if constexpr (!FULL) {
+            const int tk = nt * 8 + 2 * t;
+            if (tk >= nvalid) sc[nt][0] = sc[nt][2] = -INFINITY;
+            if (tk + 1 >= nvalid) sc[nt][1] = sc[nt][3] = -INFINITY;
+        }
+    }
+
+    // ---- online softmax per q-head row (the quad of lanes sharing g), base 2
+    float pr[2][4];
+    float corr_lo, corr_hi = 1.0f;
+    {
+        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(st.m_lo, mx);
+        corr_lo = exp2f(st.m_lo - mn);
+        pr[0][0] = exp2f(sc[0][0] - mn);
+        pr[0][1] = exp2f(sc[0][1] - mn);
+        pr[1][0] = exp2f(sc[1][0] - mn);
+        pr[1][1] = exp2f(sc[1][1] - mn);
+        float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        st.l_lo = st.l_lo * corr_lo + sum;
+        st.m_lo = mn;
+    }
+    if constexpr (HI) {
+        float mx = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(st.m_hi, mx);
+        corr_hi = exp2f(st.m_hi - mn);
+        pr[0][2] = exp2f(sc[0][2] - mn);
+        pr[0][3] = exp2f(sc[0][3] - mn);
+        pr[1][2] = exp2f(sc[1][2] - mn);
+        pr[1][3] = exp2f(sc[1][3] - mn);
+        float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        st.l_hi = st.l_hi * corr_hi + sum;
+        st.m_hi = mn;
+    } else {
+        pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.0f;
+    }
+
+    // ---- V scales of the lane's tokens (2t, 2t+1, 8+2t, 9+2t); masked rows are 0
+    float vd[4][NB];
+    float vmax = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int tk = (q >> 1) * 8 + 2 * t + (q & 1);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float d = *reinterpret_cast<const float *>(vs + tk * ROW + b * BLOCK_BYTES);
+            if constexpr (!FULL) d = tk < nvalid ? d : 0.0f;
+            vd[q][b] = d;
+            vmax = fmaxf(vmax, d);
+        }
+    }
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+    // exponent of the slice's largest scale (warp-uniform); zero/denormal -> keep the running one
+    const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
+    const int knew = max(st.kscale, min(kt, 126));
+    const bool rescale = __any_sync(0xffffffffu, corr_lo != 1.0f || corr_hi != 1.0f || knew != st.kscale);
+    if (rescale) {
+        const int df = st.kscale - knew;                     // <= 0
+        const float f = df < -126 ? 0.0f : exp2_int(df);  // exact power of two <= 1
+        const float flo = corr_lo * f, fhi = corr_hi * f;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                st.acc[b][jj][0] *= flo;
+                st.acc[b][jj][1] *= flo;
+                if constexpr (HI) {
+                    st.acc[b][jj][NACC - 2] *= fhi;
+                    st.acc[b][jj][NACC - 1] *= fhi;
+                }
+            }
+        st.kscale = knew;
+    }
+    const float inv_k = exp2_int(-st.kscale);
+    const f32x2 ik2 = pk2(inv_k, inv_k);
+    const f32x2 p00 = mul2(pk2(pr[0][0], pr[0][1]), ik2), p10 = mul2(pk2(pr[1][0], pr[1][1]), ik2);
+    const f32x2 p02 = HI ? mul2(pk2(pr[0][2], pr[0][3]), ik2) : 0ull;
+    const f32x2 p12 = HI ? mul2(pk2(pr[1][2], pr[1][3]), ik2) : 0ull;
+
+    // ---- P*V per block: A = p*vd*2^-K (hi+lo fp16), B = int8 V -> fp16
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        uint32_t ah0, al0, ah2, al2, ah1 = 0, al1 = 0, ah3 = 0, al3 = 0;
+        const f32x2 vd01 = pk2(vd[0][b], vd[1][b]), vd23 = pk2(vd[2][b], vd[3][b]);
+        split_f16x2(mul2(p00, vd01), ah0, al0);
+        split_f16x2(mul2(p10, vd23), ah2, al2);
+        if constexpr (HI) {
+            split_f16x2(mul2(p02, vd01), ah1, al1);
+            split_f16x2(mul2(p12, vd23), ah3, al3);
+        }
+        const uint8_t *vw = vs + b * BLOCK_BYTES + 4 + 4 * g;
+        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vw + (2 * t) * ROW);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 1) * ROW);
+        const uint32_t w8 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 8) * ROW);
+        const uint32_t w9 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 9) * ROW);
+#define TQK_PV_NTILE(JJ)                                                                               \
+{                                                                                                  \
+    const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);           \
+    float *a = st.acc[b][JJ];                                                                         \
+    if constexpr (HI) {                                                                            \
+        mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                         \
+        mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                         \
+    } else {                                                                                       \
+        mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                            \
+        mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                            \
+    }                                                                                              \
+}
+        TQK_PV_NTILE(0)
+        TQK_PV_NTILE(1)
+        TQK_PV_NTILE(2)
+        TQK_PV_NTILE(3)
+#undef TQK_PV_NTILE
+    }
+}
+
 template <int NB, int GPAD>
 __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const DecodeParams p) {
     using L = MmaLayout<NB, GPAD>;
@@ -297,189 +494,9 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
 
     // ------------------------------------------------------------------ consumers
     const int g = lane >> 2, t = lane & 3;
-    uint32_t qa[NB][4];
-    float qd_lo[NB], qd_hi[NB];
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-        qa[b][0] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 4 * t);
-        qa[b][2] = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 16 + 4 * t);
-        qa[b][1] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 4 * t) : 0u;
-        qa[b][3] = HI ? *reinterpret_cast<const uint32_t *>(qq + (g + 8) * HD + b * QK + 16 + 4 * t) : 0u;
-        qd_lo[b] = qd[g * NB + b];
-        qd_hi[b] = HI ? qd[(g + 8) * NB + b] : 0.0f;
-    }
-
-    f32x2 qdl2[NB], qdh2[NB];
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-        qdl2[b] = pk2(qd_lo[b], qd_lo[b]);
-        qdh2[b] = pk2(qd_hi[b], qd_hi[b]);
-    }
-    float m_lo = -INFINITY, l_lo = 0.0f, m_hi = -INFINITY, l_hi = 0.0f;
-    int kscale = -125;  // running power-of-two exponent of the PV operand scale, in [-125, 126]
-    constexpr int NACC = HI ? 4 : 2;  // d0,d1 (rows g) [+ d2,d3 (rows g+8)]
-    float acc[NB][4][NACC];
-#pragma unroll
-    for (int b = 0; b < NB; b++)
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++)
-#pragma unroll
-            for (int e = 0; e < NACC; e++) acc[b][jj][e] = 0.0f;
-
-    // One 16-token slice of a tile: scores, online softmax (log2 domain), P*V.
-    // FULL slices skip all masking; partial ones mask tokens >= nvalid.
-    auto run_slice = [&](auto full_tag, const uint8_t *ks, const uint8_t *vs, int nvalid) {
-        constexpr bool FULL = decltype(full_tag)::value;
-        const f32x2 scale2 = pk2(p.scale, p.scale);
-        const f32x2 log2e2 = pk2(1.4426950408889634f, 1.4426950408889634f);
-        // ---- scores: two 8-token n-tiles; lane holds tokens nt*8 + 2t + {0,1}
-        float sc[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; nt++) {
-            const uint8_t *kb = ks + (nt * 8 + g) * ROW;       // B fragment row (token nt*8+g)
-            const uint8_t *kda = ks + (nt * 8 + 2 * t) * ROW;  // scale rows of the lane's tokens
-            // acc += (float)dot * (qd*kd) per block, for the lane's token pair,
-            // with separately rounded products and sums as in the reference
-            f32x2 alo = pk2(0.0f, 0.0f), ahi = pk2(0.0f, 0.0f);
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 4 + 4 * t);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kb + b * BLOCK_BYTES + 20 + 4 * t);
-                int c[4];
-                mma_s8_k32(c, qa[b], b0, b1);
-                const f32x2 kd = pk2(*reinterpret_cast<const float *>(kda + b * BLOCK_BYTES),
-                                     *reinterpret_cast<const float *>(kda + ROW + b * BLOCK_BYTES));
-                alo = add2(alo, mul2(pk2(__int2float_rn(c[0]), __int2float_rn(c[1])), mul2(qdl2[b], kd)));
-                if constexpr (HI)
-                    ahi = add2(ahi, mul2(pk2(__int2float_rn(c[2]), __int2float_rn(c[3])), mul2(qdh2[b], kd)));
-            }
-            // the reference's score (acc * scale, bit-exact), then to log2 units
-            upk2(mul2(mul2(alo, scale2), log2e2), sc[nt][0], sc[nt][1]);
-            if constexpr (HI) upk2(mul2(mul2(ahi, scale2), log2e2), sc[nt][2], sc[nt][3]);
-            else sc[nt][2] = sc[nt][3] = 0.0f;
-            if constexpr (!FULL) {
-                const int tk = nt * 8 + 2 * t;
-                if (tk >= nvalid) sc[nt][0] = sc[nt][2] = -INFINITY;
-                if (tk + 1 >= nvalid) sc[nt][1] = sc[nt][3] = -INFINITY;
-            }
-        }
-
-        // ---- online softmax per q-head row (the quad of lanes sharing g), base 2
-        float pr[2][4];
-        float corr_lo, corr_hi = 1.0f;
-        {
-            float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mn = fmaxf(m_lo, mx);
-            corr_lo = exp2f(m_lo - mn);
-            pr[0][0] = exp2f(sc[0][0] - mn);
-            pr[0][1] = exp2f(sc[0][1] - mn);
-            pr[1][0] = exp2f(sc[1][0] - mn);
-            pr[1][1] = exp2f(sc[1][1] - mn);
-            float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            l_lo = l_lo * corr_lo + sum;
-            m_lo = mn;
-        }
-        if constexpr (HI) {
-            float mx = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mn = fmaxf(m_hi, mx);
-            corr_hi = exp2f(m_hi - mn);
-            pr[0][2] = exp2f(sc[0][2] - mn);
-            pr[0][3] = exp2f(sc[0][3] - mn);
-            pr[1][2] = exp2f(sc[1][2] - mn);
-            pr[1][3] = exp2f(sc[1][3] - mn);
-            float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            l_hi = l_hi * corr_hi + sum;
-            m_hi = mn;
-        } else {
-            pr[0][2] = pr[0][3] = pr[1][2] = pr[1][3] = 0.0f;
-        }
-
-        // ---- V scales of the lane's tokens (2t, 2t+1, 8+2t, 9+2t); masked rows are 0
-        float vd[4][NB];
-        float vmax = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int tk = (q >> 1) * 8 + 2 * t + (q & 1);
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float d = *reinterpret_cast<const float *>(vs + tk * ROW + b * BLOCK_BYTES);
-                if constexpr (!FULL) d = tk < nvalid ? d : 0.0f;
-                vd[q][b] = d;
-                vmax = fmaxf(vmax, d);
-            }
-        }
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-        // exponent of the slice's largest scale (warp-uniform); zero/denormal -> keep the running one
-        const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
-        const int knew = max(kscale, min(kt, 126));
-        const bool rescale = __any_sync(0xffffffffu, corr_lo != 1.0f || corr_hi != 1.0f || knew != kscale);
-        if (rescale) {
-            const int df = kscale - knew;                     // <= 0
-            const float f = df < -126 ? 0.0f : exp2_int(df);  // exact power of two <= 1
-            const float flo = corr_lo * f, fhi = corr_hi * f;
-#pragma unroll
-            for (int b = 0; b < NB; b++)
-#pragma unroll
-                for (int jj = 0; jj < 4; jj++) {
-                    acc[b][jj][0] *= flo;
-                    acc[b][jj][1] *= flo;
-                    if constexpr (HI) {
-                        acc[b][jj][NACC - 2] *= fhi;
-                        acc[b][jj][NACC - 1] *= fhi;
-                    }
-                }
-            kscale = knew;
-        }
-        const float inv_k = exp2_int(-kscale);
-        const f32x2 ik2 = pk2(inv_k, inv_k);
-        const f32x2 p00 = mul2(pk2(pr[0][0], pr[0][1]), ik2), p10 = mul2(pk2(pr[1][0], pr[1][1]), ik2);
-        const f32x2 p02 = HI ? mul2(pk2(pr[0][2], pr[0][3]), ik2) : 0ull;
-        const f32x2 p12 = HI ? mul2(pk2(pr[1][2], pr[1][3]), ik2) : 0ull;
-
-        // ---- P*V per block: A = p*vd*2^-K (hi+lo fp16), B = int8 V -> fp16
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-            uint32_t ah0, al0, ah2, al2, ah1 = 0, al1 = 0, ah3 = 0, al3 = 0;
-            const f32x2 vd01 = pk2(vd[0][b], vd[1][b]), vd23 = pk2(vd[2][b], vd[3][b]);
-            split_f16x2(mul2(p00, vd01), ah0, al0);
-            split_f16x2(mul2(p10, vd23), ah2, al2);
-            if constexpr (HI) {
-                split_f16x2(mul2(p02, vd01), ah1, al1);
-                split_f16x2(mul2(p12, vd23), ah3, al3);
-            }
-            const uint8_t *vw = vs + b * BLOCK_BYTES + 4 + 4 * g;
-            const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vw + (2 * t) * ROW);
-            const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 1) * ROW);
-            const uint32_t w8 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 8) * ROW);
-            const uint32_t w9 = *reinterpret_cast<const uint32_t *>(vw + (2 * t + 9) * ROW);
-#define TQK_PV_NTILE(JJ)                                                                               \
-    {                                                                                                  \
-        const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);           \
-        float *a = acc[b][JJ];                                                                         \
-        if constexpr (HI) {                                                                            \
-            mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                         \
-            mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                         \
-        } else {                                                                                       \
-            mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                            \
-            mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                            \
-        }                                                                                              \
-    }
-            TQK_PV_NTILE(0)
-            TQK_PV_NTILE(1)
-            TQK_PV_NTILE(2)
-            TQK_PV_NTILE(3)
-#undef TQK_PV_NTILE
-        }
-    };
+    SliceState<NB, HI> st;
+    st.begin(qq, qd, g, t);
+    constexpr int NACC = SliceState<NB, HI>::NACC;
 
     const int r0 = warp * 16;
     bool timed_out = false;
@@ -506,9 +523,9 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
                 __syncwarp();
             }
             if (nvalid >= 16)
-                run_slice(std::true_type{}, ks, vs, 16);
+                mma_slice<NB, HI, true>(st, ks, vs, 16, p.scale, g, t);
             else
-                run_slice(std::false_type{}, ks, vs, nvalid);
+                mma_slice<NB, HI, false>(st, ks, vs, nvalid, p.scale, g, t);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_release(&empty[slot]);
@@ -526,13 +543,13 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
     float *fm = wsc + MMA_WARPS * GPAD;                    // [GPAD]
     float *fl = fm + GPAD;                                 // [GPAD]
     float *wts = fl + GPAD;                                // [MAX_SPLITS][GPAD]
-    const float unscale = exp2_int(kscale);
+    const float unscale = exp2_int(st.kscale);
     if (t == 0) {
-        wm[warp * GPAD + g] = m_lo;
-        wl[warp * GPAD + g] = l_lo;
+        wm[warp * GPAD + g] = st.m_lo;
+        wl[warp * GPAD + g] = st.l_lo;
         if (HI) {
-            wm[warp * GPAD + g + 8] = m_hi;
-            wl[warp * GPAD + g + 8] = l_hi;
+            wm[warp * GPAD + g + 8] = st.m_hi;
+            wl[warp * GPAD + g + 8] = st.l_hi;
         }
     }
 #pragma unroll
@@ -541,11 +558,11 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         for (int jj = 0; jj < 4; jj++) {
             // permuted n-tile column n holds block column 4n + jj; this lane's d0/d1 are n = 2t, 2t+1
             const int c = b * QK + 8 * t + jj;
-            red[(warp * GPAD + g) * HD + c] = acc[b][jj][0] * unscale;
-            red[(warp * GPAD + g) * HD + c + 4] = acc[b][jj][1] * unscale;
+            red[(warp * GPAD + g) * HD + c] = st.acc[b][jj][0] * unscale;
+            red[(warp * GPAD + g) * HD + c + 4] = st.acc[b][jj][1] * unscale;
             if constexpr (HI) {
-                red[(warp * GPAD + g + 8) * HD + c] = acc[b][jj][NACC - 2] * unscale;
-                red[(warp * GPAD + g + 8) * HD + c + 4] = acc[b][jj][NACC - 1] * unscale;
+                red[(warp * GPAD + g + 8) * HD + c] = st.acc[b][jj][NACC - 2] * unscale;
+                red[(warp * GPAD + g + 8) * HD + c + 4] = st.acc[b][jj][NACC - 1] * unscale;
             }
         }
     cta_sync<1, MMA_WARPS * 32>();
