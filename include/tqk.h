@@ -147,10 +147,15 @@ typedef struct {
 
 /* Bytes of device workspace tqk_decode_q8 needs for these arguments. */
 TQK_API int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes);
-/* A caller workspace must be zeroed once before first use (tqk_workspace_init);
- * every call leaves it zeroed again.  Calls that share a workspace must be
- * ordered on one stream.  workspace == NULL uses a library-owned workspace per
- * (device, stream), allocated on first use. */
+/* A caller workspace starts with the split-merge tickets (one int per item and
+ * head unit, at least 64 KiB) followed by the partials.  It must be zeroed once
+ * before first use (tqk_workspace_init); every completed call leaves the
+ * tickets at zero again, so calls of up to 16384 units (n_items x kv-head
+ * units) can reuse it without re-initialising.  Zero it again before a call
+ * with more units than any earlier one, and after a call that reported
+ * TQK_ETIMEOUT.  Calls that share a workspace must be ordered on one stream.
+ * workspace == NULL uses a library-owned workspace per (device, stream),
+ * allocated on first use, whose tickets live apart from the partials. */
 TQK_API int tqk_workspace_init(void *workspace, size_t bytes, tqk_stream_t stream);
 TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes, tqk_stream_t stream);
 

@@ -636,8 +636,7 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
 
 int dispatch_pack(int nb, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
     if (nb == 4) return launch_pack<4>(p, grid, stream, occ);
-    if (nb == 8) return launch_pack<8>(p, grid, stream, occ);
-    return fail(TQK_EUNSUPPORTED, "decode: packed kernel needs head_dim 128 or 256");
+    return fail(TQK_EUNSUPPORTED, "decode: packed kernel needs head_dim 128");
 }
 
 int dispatch_mma(int nb, int gpad, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
@@ -703,6 +702,16 @@ struct Plan {
     size_t counters_bytes, part_bytes;
 };
 
+// Tickets of the split merge: one int per (item, head unit), at the start of a
+// caller workspace, followed by the partials.  Every completed call leaves its
+// tickets at zero but writes partials right after them, so the region has a
+// fixed floor of 64 KiB: calls of up to 16384 units all use the same ticket
+// bytes and can share a workspace without re-initialisation.
+size_t counters_region(int n_items, int units) {
+    const size_t b = (((size_t)n_items * units * sizeof(int)) + 255) / 256 * 256;
+    return b < 65536 ? 65536 : b;
+}
+
 int make_plan(const tqk_decode_args *a, Plan *pl) {
     if (!a) return fail(TQK_EINVAL, "decode: NULL args");
     if (a->n_items <= 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0 || a->head_dim <= 0 || a->max_tokens <= 0)
@@ -736,7 +745,7 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     const int group = a->n_q_heads / a->n_kv_heads;
     pl->nb = nb;
     pl->mma = nb % 4 == 0;
-    pl->pack = pl->mma && group == 4 && a->n_kv_heads % 2 == 0;
+    pl->pack = nb == 4 && group == 4 && a->n_kv_heads % 2 == 0;  // head_dim 128 only (register budget)
     pl->gmax = pl->pack ? 8 : pl->mma ? (group <= 8 ? 8 : 16) : gmax_for(group);
     pl->heads_per_cta = pl->pack ? 8 : (group < pl->gmax ? group : pl->gmax);
     pl->head_slices = pl->pack ? 1 : (group + pl->heads_per_cta - 1) / pl->heads_per_cta;
@@ -756,7 +765,11 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
         if (orc) return orc;
         const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
         const long long pairs_total = (long long)a->n_items * pl->pairs;
-        long long want = (2 * slots + pairs_total - 1) / pairs_total;
+        // equal lengths: as many splits as keep every CTA in one wave (a second,
+        // partly filled wave costs more than the shorter splits save); unequal
+        // lengths: about two CTAs per slot, so short and long items even out
+        const bool uniform = !a->lens && a->len_step == 0;
+        long long want = uniform ? slots / pairs_total : (2 * slots + pairs_total - 1) / pairs_total;
         if (want < 1) want = 1;
         split = (int)((max_len + want - 1) / want);
     }
@@ -766,7 +779,7 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     pl->split_tokens = split;
     pl->max_splits = max_len > 0 ? (max_len + split - 1) / split : 1;
     if (pl->max_splits > 1) {
-        pl->counters_bytes = (((size_t)a->n_items * pl->pairs * sizeof(int)) + 255) / 256 * 256;
+        pl->counters_bytes = counters_region(a->n_items, pl->pairs);
         pl->part_bytes = (size_t)a->n_items * pl->pairs * pl->max_splits * pl->gmax * (a->head_dim + 2) * sizeof(float);
     } else {
         pl->counters_bytes = 0;
@@ -797,12 +810,19 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     if (rc) return rc;
     const size_t need = pl.counters_bytes + pl.part_bytes;
     cudaStream_t st = (cudaStream_t)stream;
+    int *counters = nullptr;
+    float *part = nullptr;
     if (need) {
         if (!workspace) {
-            workspace = library_workspace(st, need);
-            if (!workspace) return fail(TQK_ECUDA, "decode: cannot allocate the library workspace");
+            // library-owned: tickets in a buffer of their own, which partials never touch
+            counters = library_counters(st, pl.counters_bytes);
+            part = reinterpret_cast<float *>(library_workspace(st, pl.part_bytes));
+            if (!counters || !part) return fail(TQK_ECUDA, "decode: cannot allocate the library workspace");
         } else if (workspace_bytes < need) {
             return fail(TQK_EWORKSPACE, "decode: workspace smaller than tqk_decode_workspace_size()");
+        } else {
+            counters = reinterpret_cast<int *>(workspace);
+            part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes);
         }
     }
     DecodeParams p{};
@@ -832,8 +852,8 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     p.split_tokens = pl.split_tokens;
     p.max_splits = pl.max_splits;
     p.scale = 1.0f / sqrtf((float)a->head_dim);  // as attend_q8 computes it (attention_layer.c:131)
-    p.counters = need ? reinterpret_cast<int *>(workspace) : nullptr;
-    p.part = need ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes) : nullptr;
+    p.counters = counters;
+    p.part = part;
     p.err = device_info()->err_word;
     const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
     if (pl.pack) return dispatch_pack(pl.nb, p, grid, st, nullptr);

@@ -5,35 +5,48 @@
 // With 4 q heads per kv head, the m16n8 fragments of tqk_decode_mma.cuh leave
 // q rows 4-7 empty, so half of every lane's scalar work (score combine,
 // softmax, P*vd) is spent on padding.  Here a CTA serves kv heads A = 2h and
-// B = 2h+1 and a warp step covers 8 tokens of each:
-//   QK  rows 0-3 = A's q heads, rows 4-7 = B's; one m16n8k32 against A's 8
-//       K rows and one against B's, each lane keeping the one that matches its
-//       row (lanes g < 4: A, g >= 4: B) -- every lane holds useful scores;
+// B = 2h+1 and a warp step covers 16 tokens of each, as two 8-token n-tiles:
+//   QK  rows 0-3 = A's q heads, rows 4-7 = B's.  Per n-tile and Q8 block two
+//       accumulating m16n8k32 MMAs: A operand {A's q rows, zeros} against A's
+//       K rows, then {zeros, B's q rows} against B's, so every lane's D
+//       fragment holds the exact int32 dots of its own row and head;
 //   PV  the k = 16 dimension of m16n8k16 is A's 8 tokens then B's 8 tokens:
 //       rows 0-3 carry P_A*vd in k 0-7 and zeros in k 8-15, rows 4-7 the
 //       opposite, and the B operand stacks V_A over V_B, so one MMA (hi + lo)
 //       accumulates both heads without wasted products.
-// Everything else -- TMA ring, exact scores, base-2 online softmax, hi/lo fp16
-// split, power-of-two PV scale, split merge -- is as in tqk_decode_mma.cuh.
+// The online softmax updates once per 16 tokens, and the power-of-two PV scale
+// K is kept per q-head row (a quad of lanes), so neither needs a warp-wide
+// reduction.  Everything else -- TMA ring, exact scores, base-2 softmax, hi/lo
+// fp16 split, split merge -- is as in tqk_decode_mma.cuh.
 #pragma once
 
 namespace tqk {
 
-constexpr int PK_WARPS = 4;                    // consumer warps
+#ifndef TQK_PK_WARPS
+#define TQK_PK_WARPS 4
+#endif
+#ifndef TQK_PK_STAGES
+#define TQK_PK_STAGES 2
+#endif
+#ifndef TQK_PK_MINB
+#define TQK_PK_MINB 2  // CTAs per SM the register budget is sized for
+#endif
+constexpr int PK_WARPS = TQK_PK_WARPS;         // consumer warps
 constexpr int PK_THREADS = (PK_WARPS + 1) * 32;
-constexpr int PK_T = 8 * PK_WARPS;             // tokens per tile, per kv head
+constexpr int PK_ROWS = 16;                    // tokens of each kv head per warp step
+constexpr int PK_T = PK_ROWS * PK_WARPS;       // tokens per tile, per kv head
 
 template <int NB>
 struct PackLayout {
     static constexpr int HD = NB * QK;
     static constexpr int ROW = NB * BLOCK_BYTES;
     static constexpr int TILE = PK_T * ROW;       // one plane of one kv head
-    static constexpr int STAGES = 3;
+    static constexpr int STAGES = TQK_PK_STAGES;
     static constexpr int STAGE_BYTES = 4 * TILE;  // K_A, K_B, V_A, V_B
     static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-    static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [16][HD] (rows 8-15 zero)
-    static constexpr int OFF_QD = OFF_QQ + 16 * HD;                             // float [16][NB]
-    static constexpr int OFF_NEW = OFF_QD + ((16 * NB * 4 + 15) / 16) * 16;    // appended rows [head][K,V][ROW]
+    static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [8][HD]
+    static constexpr int OFF_QD = OFF_QQ + 8 * HD;                              // float [8][NB]
+    static constexpr int OFF_NEW = OFF_QD + ((8 * NB * 4 + 15) / 16) * 16;     // appended rows [head][K,V][ROW]
     static constexpr int OFF_FLAG = OFF_NEW + ((4 * ROW + 15) / 16) * 16;
     static constexpr int BYTES = OFF_FLAG + 16;
     static constexpr int RED_FLOATS = PK_WARPS * 8 * HD;
@@ -41,8 +54,259 @@ struct PackLayout {
     static_assert(SCRATCH_FLOATS * 4 <= OFF_BAR, "stage ring too small for the epilogue scratch");
 };
 
+// D(rows 0-7) += A(16x32 s8, rows 8-15 zero) * B(32x8 s8), int32.
+__device__ __forceinline__ void mma_s8_k32_lo(int &d0, int &d1, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    int x2, x3;
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%5}, {%7,%8}, {%0,%1,%9,%9};"
+        : "+r"(d0), "+r"(d1), "=r"(x2), "=r"(x3)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// Per-warp state of the packed decode: q operands, running row max / sum
+// (base 2), the row's PV scale exponent and the P*V accumulators.  Lane
+// (g, t) owns q-head row g (head A for g < 4, head B otherwise).
 template <int NB>
-__global__ void __launch_bounds__(PK_THREADS) decode_q8_pack_kernel(const DecodeParams p) {
+struct PackState {
+    uint32_t qa[NB][2], qb[NB][2];  // score A operands {k 4t.., k 16+4t..}: own row in qa (head A) or qb (head B)
+    f32x2 qd2[NB];
+    float m, l;
+    int kscale;  // exponent of the row's PV operand scale, in [-125, 126]
+    float acc[NB][4][2];
+
+    __device__ __forceinline__ void begin(const int8_t *qq, const float *qd, int g, int t, bool hb) {
+        constexpr int HD = NB * QK;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const uint32_t x0 = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 4 * t);
+            const uint32_t x2 = *reinterpret_cast<const uint32_t *>(qq + g * HD + b * QK + 16 + 4 * t);
+            qa[b][0] = hb ? 0u : x0;
+            qa[b][1] = hb ? 0u : x2;
+            qb[b][0] = hb ? x0 : 0u;
+            qb[b][1] = hb ? x2 : 0u;
+            const float d = qd[g * NB + b];
+            qd2[b] = pk2(d, d);
+        }
+        m = -INFINITY;
+        l = 0.0f;
+        kscale = -125;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) acc[b][jj][0] = acc[b][jj][1] = 0.0f;
+    }
+};
+
+// One warp step: tokens 0-15 of kv head A (k_a, v_a) and of kv head B (k_b,
+// v_b), 144*NB/4-byte rows; FULL steps skip the masking of tokens >= nvalid.
+// g = lane/4, t = lane%4, hb = g >= 4; mask_a / mask_b = f16x2 1.0 for the
+// lane's own head's k half of the PV operand, 0 for the other.
+template <int NB, bool FULL>
+__device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a, const uint8_t *k_b,
+                                          const uint8_t *v_a, const uint8_t *v_b, int nvalid, float scale, int g,
+                                          int t, bool hb, uint32_t mask_a, uint32_t mask_b) {
+    constexpr int ROW = NB * BLOCK_BYTES;
+    const uint8_t *kmine = hb ? k_b : k_a;  // the lane's own head for scales
+    const uint8_t *vmine = hb ? v_b : v_a;
+
+    // ---- scores of row g for tokens 2t, 2t+1 (n-tile 0) and 8+2t, 9+2t (n-tile 1),
+    //      rounded exactly as the reference: acc += (float)dot * (qd*kd) per block
+    f32x2 sc0 = pk2(0.0f, 0.0f), sc1 = pk2(0.0f, 0.0f);
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const int kb = b * BLOCK_BYTES + 4 + 4 * t;
+        int c00 = 0, c01 = 0, c10 = 0, c11 = 0;
+        mma_s8_k32_lo(c00, c01, st.qa[b][0], st.qa[b][1], *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb + 16));
+        mma_s8_k32_lo(c10, c11, st.qa[b][0], st.qa[b][1],
+                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb + 16));
+        mma_s8_k32_lo(c00, c01, st.qb[b][0], st.qb[b][1], *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb + 16));
+        mma_s8_k32_lo(c10, c11, st.qb[b][0], st.qb[b][1],
+                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb + 16));
+        const uint8_t *kd = kmine + (2 * t) * ROW + b * BLOCK_BYTES;
+        const f32x2 kd0 = pk2(*reinterpret_cast<const float *>(kd), *reinterpret_cast<const float *>(kd + ROW));
+        const f32x2 kd1 =
+            pk2(*reinterpret_cast<const float *>(kd + 8 * ROW), *reinterpret_cast<const float *>(kd + 9 * ROW));
+        sc0 = add2(sc0, mul2(pk2(__int2float_rn(c00), __int2float_rn(c01)), mul2(st.qd2[b], kd0)));
+        sc1 = add2(sc1, mul2(pk2(__int2float_rn(c10), __int2float_rn(c11)), mul2(st.qd2[b], kd1)));
+    }
+    const f32x2 sl2 = pk2(scale, scale), l2e = pk2(1.4426950408889634f, 1.4426950408889634f);
+    float s0, s1, s2, s3;  // the reference's scores (acc * scale), then in log2 units
+    upk2(mul2(mul2(sc0, sl2), l2e), s0, s1);
+    upk2(mul2(mul2(sc1, sl2), l2e), s2, s3);
+    if constexpr (!FULL) {
+        if (2 * t >= nvalid) s0 = -INFINITY;
+        if (2 * t + 1 >= nvalid) s1 = -INFINITY;
+        if (8 + 2 * t >= nvalid) s2 = -INFINITY;
+        if (9 + 2 * t >= nvalid) s3 = -INFINITY;
+    }
+
+    // ---- online softmax of the row over its 16 tokens (the quad)
+    float mx = fmaxf(fmaxf(s0, s1), fmaxf(s2, s3));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(st.m, mx);
+    const float corr = exp2f(st.m - mn);
+    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn), p2 = exp2f(s2 - mn), p3 = exp2f(s3 - mn);
+    float sum = (p0 + p1) + (p2 + p3);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    st.l = st.l * corr + sum;
+    st.m = mn;
+
+    // ---- V scales of the lane's tokens (own head); the row's largest picks K
+    float vd[4][NB];
+    float vmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int tk = (i >> 1) * 8 + 2 * t + (i & 1);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float d = *reinterpret_cast<const float *>(vmine + tk * ROW + b * BLOCK_BYTES);
+            if constexpr (!FULL) d = tk < nvalid ? d : 0.0f;
+            vd[i][b] = d;
+            vmax = fmaxf(vmax, d);
+        }
+    }
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+    const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
+    const int knew = max(st.kscale, min(kt, 126));
+    if (__any_sync(0xffffffffu, corr != 1.0f || knew != st.kscale)) {
+        const int df = st.kscale - knew;  // <= 0
+        const float f = (df < -126 ? 0.0f : exp2_int(df)) * corr;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                st.acc[b][jj][0] *= f;
+                st.acc[b][jj][1] *= f;
+            }
+        st.kscale = knew;
+    }
+    const float inv_k = exp2_int(-st.kscale);
+    const f32x2 ik2 = pk2(inv_k, inv_k);
+    const f32x2 pp0 = mul2(pk2(p0, p1), ik2), pp1 = mul2(pk2(p2, p3), ik2);
+
+    // ---- P*V: per n-tile, k 0-7 = head A's tokens, k 8-15 = head B's
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        uint32_t h0, l0, h1, l1;
+        split_f16x2(mul2(pp0, pk2(vd[0][b], vd[1][b])), h0, l0);
+        split_f16x2(mul2(pp1, pk2(vd[2][b], vd[3][b])), h1, l1);
+        const uint32_t h0a = hmul2(h0, mask_a), h0b = hmul2(h0, mask_b);
+        const uint32_t l0a = hmul2(l0, mask_a), l0b = hmul2(l0, mask_b);
+        const uint32_t h1a = hmul2(h1, mask_a), h1b = hmul2(h1, mask_b);
+        const uint32_t l1a = hmul2(l1, mask_a), l1b = hmul2(l1, mask_b);
+        const int wo = b * BLOCK_BYTES + 4 + 4 * g;
+        const uint32_t wa0 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t) * ROW + wo);
+        const uint32_t wa1 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t + 1) * ROW + wo);
+        const uint32_t wa8 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t + 8) * ROW + wo);
+        const uint32_t wa9 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t + 9) * ROW + wo);
+        const uint32_t wb0 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t) * ROW + wo);
+        const uint32_t wb1 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t + 1) * ROW + wo);
+        const uint32_t wb8 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t + 8) * ROW + wo);
+        const uint32_t wb9 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t + 9) * ROW + wo);
+#define TQK_PK_NTILE(JJ)                                                                        \
+    {                                                                                           \
+        float *a = st.acc[b][JJ];                                                               \
+        const uint32_t x0 = s8pair_to_f16x2<JJ>(wa0, wa1), y0 = s8pair_to_f16x2<JJ>(wb0, wb1);  \
+        mma_f16_k16_lo(a[0], a[1], h0a, h0b, x0, y0);                                           \
+        mma_f16_k16_lo(a[0], a[1], l0a, l0b, x0, y0);                                           \
+        const uint32_t x1 = s8pair_to_f16x2<JJ>(wa8, wa9), y1 = s8pair_to_f16x2<JJ>(wb8, wb9);  \
+        mma_f16_k16_lo(a[0], a[1], h1a, h1b, x1, y1);                                           \
+        mma_f16_k16_lo(a[0], a[1], l1a, l1b, x1, y1);                                           \
+    }
+        TQK_PK_NTILE(0)
+        TQK_PK_NTILE(1)
+        TQK_PK_NTILE(2)
+        TQK_PK_NTILE(3)
+#undef TQK_PK_NTILE
+    }
+}
+
+// Quantises the 8 q heads qh0..qh0+7 of `item` (quant_x.c:12-34) into qq
+// [8][HD] / qd [8][NB]; consumer warp `warp` does rows warp, warp+PK_WARPS, ...
+template <int NB>
+__device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int qh0, int warp, int lane, int8_t *qq,
+                                            float *qd) {
+    constexpr int HD = NB * QK, QR = 8 / PK_WARPS;
+    const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
+    float x[QR][NB];  // loads first
+#pragma unroll
+    for (int r = 0; r < QR; r++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) x[r][b] = __ldg(qsrc + (warp + PK_WARPS * r) * HD + b * QK + lane);
+#pragma unroll
+    for (int r = 0; r < QR; r++) {
+        const int g = warp + PK_WARPS * r;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float d;
+            const int8_t v8 = warp_quantize_block(x[r][b], &d);
+            qq[g * HD + b * QK + lane] = v8;
+            if (lane == 0) qd[g * NB + b] = d;
+        }
+    }
+}
+
+// Fused append (store_kv, attention_layer.c:66-90): quantises the new K and V
+// rows of kv heads kvh_a, kvh_a+1 of `item`, writes them to the cache at
+// position pos and to newrow [head][K,V][ROW] for patching the staged tile.
+// Jobs 0/1 = K/V of head A, 2/3 = K/V of head B, one per consumer warp.
+template <int NB>
+__device__ __forceinline__ void pack_append(const DecodeParams &p, int item, int kvh_a, int pos, int warp, int lane,
+                                            uint8_t *newrow) {
+    constexpr int HD = NB * QK, ROW = NB * BLOCK_BYTES;
+    const long long head_bytes = (long long)p.max_tokens * ROW;
+    for (int job = warp; job < 4; job += PK_WARPS) {
+        const int hsel = job >> 1, plane = job & 1;
+        const int kvh = kvh_a + hsel;
+        const float *src =
+            (plane == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride + (long long)kvh * HD;
+        uint8_t *nrow = newrow + (hsel * 2 + plane) * ROW;
+        uint8_t *grow = (plane == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + (long long)kvh * head_bytes +
+                        (long long)pos * ROW;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float d;
+            const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+            nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+            grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+            if (lane == 0) {
+                *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
+                *reinterpret_cast<float *>(grow + b * BLOCK_BYTES) = d;
+            }
+        }
+    }
+}
+
+// Copies the appended rows into the staged tile when position pos falls in the
+// warp's rows [row0, row0 + PK_ROWS) of tile rows starting at token t0.
+template <int NB>
+__device__ __forceinline__ void pack_patch(int pos, int t0, int r0, int lane, uint8_t *k_a, uint8_t *k_b, uint8_t *v_a,
+                                           uint8_t *v_b, const uint8_t *newrow) {
+    constexpr int ROW = NB * BLOCK_BYTES;
+    if (pos < t0 + r0 || pos >= t0 + r0 + PK_ROWS) return;
+    const int r = pos - t0 - r0;
+    uint8_t *dsts[4] = {k_a + r * ROW, v_a + r * ROW, k_b + r * ROW, v_b + r * ROW};
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        for (int i = lane; i < ROW / 4; i += 32)
+            reinterpret_cast<uint32_t *>(dsts[q])[i] = reinterpret_cast<const uint32_t *>(newrow + q * ROW)[i];
+    __syncwarp();
+}
+
+template <int NB>
+__global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel(const DecodeParams p) {
     using L = PackLayout<NB>;
     constexpr int HD = L::HD, ROW = L::ROW, STAGES = L::STAGES;
 
@@ -127,49 +391,8 @@ __global__ void __launch_bounds__(PK_THREADS) decode_q8_pack_kernel(const Decode
     const bool do_append = p.k_new != nullptr && s == n_splits - 1;
     const int pos = len - 1;
     if (warp < PK_WARPS) {
-        // quantise the 8 q heads (quant_x.c:12-34), two rows per warp, loads first; rows 8-15 zero
-        const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
-        float x[2][NB];
-#pragma unroll
-        for (int r = 0; r < 2; r++)
-#pragma unroll
-            for (int b = 0; b < NB; b++) x[r][b] = __ldg(qsrc + (warp + 4 * r) * HD + b * QK + lane);
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const int g = warp + 4 * r;
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float d;
-                const int8_t v8 = warp_quantize_block(x[r][b], &d);
-                qq[g * HD + b * QK + lane] = v8;
-                qq[(g + 8) * HD + b * QK + lane] = 0;
-                if (lane == 0) {
-                    qd[g * NB + b] = d;
-                    qd[(g + 8) * NB + b] = 0.0f;
-                }
-            }
-        }
-        // fused append (store_kv, attention_layer.c:66-90): warp 0/1 K/V of head A, 2/3 of head B
-        if (do_append) {
-            const int hb = warp >> 1, plane = warp & 1;
-            const int kvh = kvh_a + hb;
-            const float *src = (plane == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride +
-                               (long long)kvh * HD;
-            uint8_t *nrow = newrow + (hb * 2 + plane) * ROW;
-            uint8_t *grow = (plane == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + (long long)kvh * head_bytes +
-                            (long long)pos * ROW;
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float d;
-                const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
-                nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
-                grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
-                if (lane == 0) {
-                    *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
-                    *reinterpret_cast<float *>(grow + b * BLOCK_BYTES) = d;
-                }
-            }
-        }
+        pack_load_q<NB>(p, item, qh0, warp, lane, qq, qd);
+        if (do_append) pack_append<NB>(p, item, kvh_a, pos, warp, lane, newrow);
     }
     __syncthreads();
 
@@ -190,10 +413,11 @@ __global__ void __launch_bounds__(PK_THREADS) decode_q8_pack_kernel(const Decode
     // ------------------------------------------------------------------ consumers
     const int g = lane >> 2, t = lane & 3;
     const bool hb = g >= 4;  // this lane's row belongs to kv head B
-    SliceState<NB, false> st;
-    st.begin(qq, qd, g, t);
+    PackState<NB> st;
+    st.begin(qq, qd, g, t, hb);
+    const uint32_t mask_a = hb ? 0u : 0x3C003C00u, mask_b = hb ? 0x3C003C00u : 0u;  // f16x2 {1, 1} or 0
 
-    const int r0 = warp * 8;  // this warp's 8 tokens of each head in a tile
+    const int r0 = warp * PK_ROWS;  // this warp's tokens of each head in a tile
     bool timed_out = false;
     for (int j = 0; j < n_tiles; j++) {
         const int slot = j % STAGES;
@@ -209,109 +433,11 @@ __global__ void __launch_bounds__(PK_THREADS) decode_q8_pack_kernel(const Decode
             uint8_t *stg = smem + slot * L::STAGE_BYTES;
             uint8_t *k_a = stg + r0 * ROW, *k_b = stg + L::TILE + r0 * ROW;
             uint8_t *v_a = stg + 2 * L::TILE + r0 * ROW, *v_b = stg + 3 * L::TILE + r0 * ROW;
-            if (do_append && pos >= t0 + r0 && pos < t0 + r0 + 8) {
-                const int r = pos - t0 - r0;
-                uint8_t *dsts[4] = {k_a + r * ROW, v_a + r * ROW, k_b + r * ROW, v_b + r * ROW};
-#pragma unroll
-                for (int q = 0; q < 4; q++)
-                    for (int i = lane; i < ROW / 4; i += 32)
-                        reinterpret_cast<uint32_t *>(dsts[q])[i] = reinterpret_cast<const uint32_t *>(newrow + q * ROW)[i];
-                __syncwarp();
-            }
-            const uint8_t *kmine = hb ? k_b : k_a;  // the lane's own head for scales
-            const uint8_t *vmine = hb ? v_b : v_a;
-
-            // ---- scores of the lane's row g for tokens 2t, 2t+1 (exact reference rounding)
-            f32x2 acc2 = pk2(0.0f, 0.0f);
-            {
-                const uint8_t *kba = k_a + g * ROW, *kbb = k_b + g * ROW;  // B fragment token g of each head
-#pragma unroll
-                for (int b = 0; b < NB; b++) {
-                    int ca[4], cb[4];
-                    mma_s8_k32(ca, st.qa[b], *reinterpret_cast<const uint32_t *>(kba + b * BLOCK_BYTES + 4 + 4 * t),
-                               *reinterpret_cast<const uint32_t *>(kba + b * BLOCK_BYTES + 20 + 4 * t));
-                    mma_s8_k32(cb, st.qa[b], *reinterpret_cast<const uint32_t *>(kbb + b * BLOCK_BYTES + 4 + 4 * t),
-                               *reinterpret_cast<const uint32_t *>(kbb + b * BLOCK_BYTES + 20 + 4 * t));
-                    const int c0 = hb ? cb[0] : ca[0], c1 = hb ? cb[1] : ca[1];
-                    const f32x2 kd = pk2(*reinterpret_cast<const float *>(kmine + (2 * t) * ROW + b * BLOCK_BYTES),
-                                         *reinterpret_cast<const float *>(kmine + (2 * t + 1) * ROW + b * BLOCK_BYTES));
-                    acc2 = add2(acc2, mul2(pk2(__int2float_rn(c0), __int2float_rn(c1)), mul2(st.qdl2[b], kd)));
-                }
-            }
-            float s0, s1;
-            upk2(mul2(mul2(acc2, pk2(p.scale, p.scale)), pk2(1.4426950408889634f, 1.4426950408889634f)), s0, s1);
-            if (2 * t >= nvalid) s0 = -INFINITY;
-            if (2 * t + 1 >= nvalid) s1 = -INFINITY;
-
-            // ---- online softmax of the row over its 8 tokens (the quad)
-            float mx = fmaxf(s0, s1);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-            const float mn = fmaxf(st.m_lo, mx);
-            const float corr = exp2f(st.m_lo - mn);
-            const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn);
-            float sum = p0 + p1;
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            st.l_lo = st.l_lo * corr + sum;
-            st.m_lo = mn;
-
-            // ---- V scales of the lane's tokens (own head); slice max over both heads
-            float vd0[NB], vd1[NB];
-            float vmax = 0.0f;
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float d0 = *reinterpret_cast<const float *>(vmine + (2 * t) * ROW + b * BLOCK_BYTES);
-                float d1 = *reinterpret_cast<const float *>(vmine + (2 * t + 1) * ROW + b * BLOCK_BYTES);
-                if (2 * t >= nvalid) d0 = 0.0f;
-                if (2 * t + 1 >= nvalid) d1 = 0.0f;
-                vd0[b] = d0;
-                vd1[b] = d1;
-                vmax = fmaxf(vmax, fmaxf(d0, d1));
-            }
-            vmax = warp_max(vmax);
-            const int kt = vmax >= 1.17549435e-38f ? ((__float_as_int(vmax) >> 23) & 0xFF) - 127 + 1 : -125;
-            const int knew = max(st.kscale, min(kt, 126));
-            if (__any_sync(0xffffffffu, corr != 1.0f || knew != st.kscale)) {
-                const int df = st.kscale - knew;
-                const float f = (df < -126 ? 0.0f : exp2_int(df)) * corr;
-#pragma unroll
-                for (int b = 0; b < NB; b++)
-#pragma unroll
-                    for (int jj = 0; jj < 4; jj++) {
-                        st.acc[b][jj][0] *= f;
-                        st.acc[b][jj][1] *= f;
-                    }
-                st.kscale = knew;
-            }
-            const float inv_k = exp2_int(-st.kscale);
-            const f32x2 pp = mul2(pk2(p0, p1), pk2(inv_k, inv_k));
-
-            // ---- P*V: k 0-7 = head A's tokens, k 8-15 = head B's; lanes fill their own half
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                uint32_t ah, al;
-                split_f16x2(mul2(pp, pk2(vd0[b], vd1[b])), ah, al);
-                const uint32_t ah0 = hb ? 0u : ah, ah2 = hb ? ah : 0u;
-                const uint32_t al0 = hb ? 0u : al, al2 = hb ? al : 0u;
-                const int wo = b * BLOCK_BYTES + 4 + 4 * g;
-                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t) * ROW + wo);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(v_a + (2 * t + 1) * ROW + wo);
-                const uint32_t w8 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t) * ROW + wo);
-                const uint32_t w9 = *reinterpret_cast<const uint32_t *>(v_b + (2 * t + 1) * ROW + wo);
-#define TQK_PK_NTILE(JJ)                                                                        \
-    {                                                                                           \
-        const uint32_t bb0 = s8pair_to_f16x2<JJ>(w0, w1), bb1 = s8pair_to_f16x2<JJ>(w8, w9);    \
-        float *a = st.acc[b][JJ];                                                               \
-        mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                         \
-        mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                         \
-    }
-                TQK_PK_NTILE(0)
-                TQK_PK_NTILE(1)
-                TQK_PK_NTILE(2)
-                TQK_PK_NTILE(3)
-#undef TQK_PK_NTILE
-            }
+            if (do_append) pack_patch<NB>(pos, t0, r0, lane, k_a, k_b, v_a, v_b, newrow);
+            if (nvalid >= PK_ROWS)
+                pack_step<NB, true>(st, k_a, k_b, v_a, v_b, nvalid, p.scale, g, t, hb, mask_a, mask_b);
+            else
+                pack_step<NB, false>(st, k_a, k_b, v_a, v_b, nvalid, p.scale, g, t, hb, mask_a, mask_b);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_release(&empty[slot]);
@@ -331,8 +457,8 @@ __global__ void __launch_bounds__(PK_THREADS) decode_q8_pack_kernel(const Decode
     float *wts = fl + 8;                           // [2][MAX_SPLITS][8]
     const float unscale = exp2_int(st.kscale);
     if (t == 0) {
-        wm[warp * 8 + g] = st.m_lo;
-        wl[warp * 8 + g] = st.l_lo;
+        wm[warp * 8 + g] = st.m;
+        wl[warp * 8 + g] = st.l;
     }
 #pragma unroll
     for (int b = 0; b < NB; b++)

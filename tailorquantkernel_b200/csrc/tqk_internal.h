@@ -28,8 +28,12 @@ struct DeviceInfo {
 // Cached properties of the current device (initialised on first use).
 const DeviceInfo *device_info();
 
-// Library-owned decode workspace for (current device, stream), grown on demand
-// and zeroed when (re)allocated.  Returns nullptr on allocation failure.
+// Library-owned decode partials buffer for (current device, stream), grown on
+// demand and zeroed when (re)allocated.  Returns nullptr on allocation failure.
 void *library_workspace(cudaStream_t stream, size_t bytes);
+// Library-owned split-merge tickets for (current device, stream): a buffer that
+// holds nothing but tickets, zeroed when (re)allocated; every completed decode
+// leaves its tickets at zero, so the buffer stays zero between calls.
+int *library_counters(cudaStream_t stream, size_t bytes);
 
 }  // namespace tqk

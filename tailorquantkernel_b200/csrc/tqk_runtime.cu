@@ -21,6 +21,27 @@ struct Workspace {
     size_t bytes = 0;
 };
 std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
+std::map<std::pair<int, cudaStream_t>, Workspace> g_counters;
+
+// Grows `w` to at least `bytes` (minimum 1 MiB), zeroing the new buffer on `stream`.
+void *grow_zeroed(Workspace &w, cudaStream_t stream, size_t bytes) {
+    if (w.bytes >= bytes && w.ptr) return w.ptr;
+    if (w.ptr) {
+        // the old buffer may still be in use by work queued on `stream`
+        cudaStreamSynchronize(stream);
+        cudaFree(w.ptr);
+        w.ptr = nullptr;
+        w.bytes = 0;
+    }
+    size_t grow = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
+    if (cudaMalloc(&w.ptr, grow) != cudaSuccess) {
+        w.ptr = nullptr;
+        return nullptr;
+    }
+    if (cudaMemsetAsync(w.ptr, 0, grow, stream) != cudaSuccess) return nullptr;
+    w.bytes = grow;
+    return w.ptr;
+}
 }  // namespace
 
 int fail(int status, const char *msg) {
@@ -71,23 +92,14 @@ void *library_workspace(cudaStream_t stream, size_t bytes) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lock(g_mutex);
-    Workspace &w = g_workspaces[{dev, stream}];
-    if (w.bytes >= bytes && w.ptr) return w.ptr;
-    if (w.ptr) {
-        // the old buffer may still be in use by work queued on `stream`
-        cudaStreamSynchronize(stream);
-        cudaFree(w.ptr);
-        w.ptr = nullptr;
-        w.bytes = 0;
-    }
-    size_t grow = bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes;
-    if (cudaMalloc(&w.ptr, grow) != cudaSuccess) {
-        w.ptr = nullptr;
-        return nullptr;
-    }
-    if (cudaMemsetAsync(w.ptr, 0, grow, stream) != cudaSuccess) return nullptr;
-    w.bytes = grow;
-    return w.ptr;
+    return grow_zeroed(g_workspaces[{dev, stream}], stream, bytes);
+}
+
+int *library_counters(cudaStream_t stream, size_t bytes) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    return static_cast<int *>(grow_zeroed(g_counters[{dev, stream}], stream, bytes));
 }
 
 }  // namespace tqk

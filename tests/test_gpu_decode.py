@@ -221,6 +221,94 @@ def test_zero_length_items_and_partial_output(tqk, port, cuda):
         assert ok, (n, max_abs, rel)
 
 
+@pytest.mark.parametrize("out_mode", [0, 1])
+def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
+    """The automatic split for 4 q heads per kv head (the packed kernel):
+    ragged device lengths with empty items, tile-edge lengths, a fused append,
+    both output modes, and a single short sequence."""
+    import torch
+    nq, nkv, hd, mt = 16, 4, 128, 4200
+    lens = np.array([0, 1, 31, 32, 33, 4097, 0, 2048, 100, 4200, 64, 7], dtype=np.int32)
+    B = len(lens)
+    rng = np.random.default_rng(11)
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    kp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    vp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    q = rng.standard_normal((B, nq * hd), dtype=np.float32)
+    k_new = rng.standard_normal((B, nkv * hd), dtype=np.float32)
+    v_new = rng.standard_normal((B, nkv * hd), dtype=np.float32)
+    kh0, vh0 = kp.cpu().numpy(), vp.cpu().numpy()
+    width = hd + 2 if out_mode == 1 else hd
+    out = torch.full((B, nq * width), 7.0, device=cuda)
+    nonzero = torch.from_numpy(np.maximum(lens, 1)).to(cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=B,
+                           item_stride_blocks=nkv * mt * (hd // 32), lens=nonzero, max_len=int(lens.max()),
+                           q_item_stride=nq * hd, out_item_stride=nq * width, k_new=torch.from_numpy(k_new).to(cuda),
+                           v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd, out_mode=out_mode)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    for b in range(B):
+        n = max(int(lens[b]), 1)
+        kref, vref = kh0[b].copy(), vh0[b].copy()
+        assert port.store_kv(kref, vref, nkv, hd, mt, n - 1, k_new[b], v_new[b]) == 0
+        assert np.array_equal(kref, kh[b]) and np.array_equal(vref, vh[b]), f"append item {b}"
+        ref = port.attend(kref, vref, nq, nkv, hd, mt, n - 1, q[b])
+        g = got[b].reshape(nq, width)
+        if out_mode == 1:  # acc, m (natural log), l per head
+            g = g[:, :hd] / g[:, hd + 1:hd + 2]
+        ok, max_abs, rel = tolerance_ok(g.reshape(-1), ref)
+        assert ok, f"item {b} (len {n}): max abs {max_abs:.3g} rel {rel:.3g}"
+
+    # zero-length items without an append, and the single-item case with fewer tiles than CTAs
+    lens_d = torch.from_numpy(lens).to(cuda)
+    out = torch.full((B, nq * hd), 7.0, device=cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=B,
+                           item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
+                           q_item_stride=nq * hd, out_item_stride=nq * hd)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    for b in range(B):
+        if lens[b] == 0:
+            assert (got[b] == 0).all()
+        else:
+            ok, max_abs, rel = tolerance_ok(got[b], port.attend(kh[b], vh[b], nq, nkv, hd, mt, int(lens[b]) - 1, q[b]))
+            assert ok, f"item {b}: max abs {max_abs:.3g} rel {rel:.3g}"
+    one = torch.empty(nq * hd, device=cuda)
+    tqk.attend(kp[9], vp[9], nq, nkv, hd, mt, 39, torch.from_numpy(q[9]).to(cuda), one)
+    ok, max_abs, rel = tolerance_ok(one.cpu().numpy(), port.attend(kh[9], vh[9], nq, nkv, hd, mt, 39, q[9]))
+    assert ok, (max_abs, rel)
+    assert tqk.device_status() == 0
+
+
+def test_config3_auto_schedule(tqk, port, cuda):
+    """Config 3 through the automatic split, checked against an explicit split
+    and, on a sample of sequences, the oracle."""
+    import torch
+    B, nq, nkv, hd, mt = 64, 32, 8, 128, 8192
+    rng = np.random.default_rng(13)
+    lens = rng.integers(512, 8193, B).astype(np.int32)
+    gen = torch.Generator(device="cuda").manual_seed(13)
+    kp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    vp = _gpu_planes(gen, (B, nkv, mt, hd), tqk, 0.01)
+    q = torch.from_numpy(rng.standard_normal((B, nq * hd), dtype=np.float32)).to(cuda)
+    lens_d = torch.from_numpy(lens).to(cuda)
+    outs = []
+    for split in (0, 1024):
+        out = torch.empty(B, nq * hd, device=cuda)
+        tqk.decode(tqk.decode_args(kp, vp, nq, nkv, hd, mt, q, out, n_items=B,
+                                   item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
+                                   q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=split))
+        outs.append(out.cpu().numpy())
+    # schedules differ only in where fp32 partials are merged
+    assert np.abs(outs[0] - outs[1]).max() <= 1e-5 * max(1.0, np.abs(outs[1]).max())
+    kh, vh, qh = kp.cpu().numpy(), vp.cpu().numpy(), q.cpu().numpy()
+    for b in (0, 17, 63):
+        ok, max_abs, rel = tolerance_ok(outs[0][b], port.attend(kh[b], vh[b], nq, nkv, hd, mt, int(lens[b]) - 1, qh[b]))
+        assert ok, f"seq {b}: max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
 def test_prefill_matches_golden_and_sequential(tqk, port, cuda):
     import torch
     from _cases import prefill_inputs
