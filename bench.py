@@ -13,9 +13,8 @@ is needed between steps.
 
 For N > 1 (torchrun, one process per GPU) every rank decodes its own sequence
 (batch sharding, no collective): weak scaling, value = all ranks' tokens / the
-slowest rank's time.  Other configs: --config 1 (1 layer, n = 1024),
-3 (ragged batch 64), 4 (context 131072, sequence split across ranks with an
-NCCL all-gather of log-sum-exp partials), 5 (chunked causal prefill).
+slowest rank's time.  The timed region is about 2 s by default so that the
+clock sampler sees it several times.
 
 Rank 0 prints one JSON line.  --impl reference times the reference's own CPU
 code for the same workload (oracle/_ref/libtqref_avx2.so: the reference's AVX2
@@ -397,7 +396,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=2, choices=[2])
