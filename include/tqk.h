@@ -159,6 +159,29 @@ TQK_API int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes);
 TQK_API int tqk_workspace_init(void *workspace, size_t bytes, tqk_stream_t stream);
 TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes, tqk_stream_t stream);
 
+/* tqk_decode_q8 without any device allocation (no counterpart in the
+ * reference): for callers that cannot allocate device memory at run time, for
+ * instance a runtime whose memory is fully reserved up front.  The split
+ * tickets and partials live in fixed static device arrays of this library
+ * (16384 tickets, 4 MiB of partials, present from module load); nothing else
+ * is allocated, not even the device error word.  Same arguments, results and
+ * automatic split as tqk_decode_q8.
+ *   - Calls whose split needs more than 16384 (item, head unit) pairs or more
+ *     than 4 MiB of partials fail with TQK_EWORKSPACE; use tqk_decode_q8 with
+ *     a workspace, or a larger split_tokens.
+ *   - Each call clears its tickets on the stream (one memset) before the
+ *     kernel, so nothing needs initialising by the caller.
+ *   - The first call on a device sets up that device (looks up the static
+ *     arrays' addresses and the kernels' attributes); make it before any
+ *     stream capture begins.
+ *   - The arrays are shared by every call in the process: calls that may
+ *     overlap (other streams, other host threads) race on them and give wrong
+ *     results; order such calls on one stream.
+ *   - Device-side checks (lengths from a device array outside [0, max_tokens],
+ *     pipeline waits over 1 s) still clamp or stop safely, but there is no
+ *     error word to report them: tqk_device_status does not see this entry. */
+TQK_API int tqk_decode_q8_static(const tqk_decode_args *a, tqk_stream_t stream);
+
 /* attend_q8 for one layer of one sequence: n = pos + 1 positions
  * (reference model/attention_layer.c:125-150); TQK_EPOS if pos is out of range. */
 TQK_API int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,

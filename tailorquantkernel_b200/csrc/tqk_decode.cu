@@ -860,6 +860,136 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode (tqk_decode_q8_static): the split tickets and
+// partials live in file-scope device arrays of fixed size, so a call makes no
+// device allocation of any kind (no workspace, no library buffers, no error
+// word).  Their device addresses are looked up once per device.
+// ---------------------------------------------------------------------------
+namespace tqk {
+namespace {
+
+constexpr int STATIC_TICKETS = 16384;               // (item, head unit) pairs per call
+constexpr size_t STATIC_PART_FLOATS = 1u << 20;     // 4 MiB of split partials
+
+static __device__ __align__(256) int g_static_tickets[STATIC_TICKETS];
+static __device__ __align__(256) float g_static_part[STATIC_PART_FLOATS];
+
+struct StaticScratch {
+    bool ready = false;
+    int *tickets = nullptr;
+    float *part = nullptr;
+};
+
+// Device addresses of the static arrays for the current device (set up on the
+// first call made with that device current).
+int static_scratch(int dev, StaticScratch *out) {
+    static std::mutex mu;
+    static StaticScratch by_dev[64];
+    if (dev < 0 || dev >= 64) return fail(TQK_ENODEV, "tqk_decode_q8_static: device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    StaticScratch &s = by_dev[dev];
+    if (!s.ready) {
+        void *t = nullptr, *q = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&t, g_static_tickets);
+        if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: cudaGetSymbolAddress(tickets)");
+        e = cudaGetSymbolAddress(&q, g_static_part);
+        if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: cudaGetSymbolAddress(partials)");
+        s.tickets = static_cast<int *>(t);
+        s.part = static_cast<float *>(q);
+        s.ready = true;
+    }
+    *out = s;
+    return TQK_OK;
+}
+
+}  // namespace
+}  // namespace tqk
+
+extern "C" int tqk_decode_q8_static(const tqk_decode_args *args, tqk_stream_t stream) {
+    if (!args) return fail(TQK_EINVAL, "tqk_decode_q8_static: NULL args");
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: cudaGetDevice");
+    // plan with a provisional split (no device queries), then pick the split
+    // the way tqk_decode_q8 does, from the SM count and the kernel's occupancy
+    tqk_decode_args a = *args;
+    if (a.split_tokens <= 0) a.split_tokens = a.max_tokens > 0 ? a.max_tokens : 1;
+    Plan pl;
+    int rc = make_plan(&a, &pl);
+    if (rc) return rc;
+    if (args->split_tokens <= 0) {
+        int sms = 0, occ = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: SM count");
+        DecodeParams dummy{};
+        rc = pl.pack  ? dispatch_pack(pl.nb, dummy, dim3(1), nullptr, &occ)
+             : pl.mma ? dispatch_mma(pl.nb, pl.gmax, dummy, dim3(1), nullptr, &occ)
+                      : dispatch(pl.nb, pl.gmax, dummy, dim3(1), nullptr, &occ);
+        if (rc) return rc;
+        const long long slots = (long long)sms * (occ > 0 ? occ : 1);
+        const long long units = (long long)a.n_items * pl.pairs;
+        const bool uniform = !a.lens && a.len_step == 0;
+        long long want = uniform ? slots / units : (2 * slots + units - 1) / units;
+        if (want < 1) want = 1;
+        a.split_tokens = (int)((pl.max_len + want - 1) / want);
+        if (a.split_tokens < 1) a.split_tokens = 1;
+        rc = make_plan(&a, &pl);
+        if (rc) return rc;
+    }
+    const long long units = (long long)a.n_items * pl.pairs;
+    if (pl.max_splits > 1) {
+        if (units > STATIC_TICKETS)
+            return fail(TQK_EWORKSPACE, "tqk_decode_q8_static: more than 16384 (item, head unit) pairs to split; "
+                                        "use tqk_decode_q8 with a workspace");
+        if (pl.part_bytes > STATIC_PART_FLOATS * sizeof(float))
+            return fail(TQK_EWORKSPACE, "tqk_decode_q8_static: split partials exceed the 4 MiB static scratch; "
+                                        "use tqk_decode_q8 with a workspace or a larger split_tokens");
+    }
+    StaticScratch sc;
+    rc = static_scratch(dev, &sc);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (pl.max_splits > 1) {
+        // the tickets must start at zero: clear this call's range on the stream
+        e = cudaMemsetAsync(sc.tickets, 0, (size_t)units * sizeof(int), st);
+        if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: clearing the tickets");
+    }
+    DecodeParams p{};
+    p.k = reinterpret_cast<const uint8_t *>(a.k);
+    p.v = reinterpret_cast<const uint8_t *>(a.v);
+    p.kw = reinterpret_cast<uint8_t *>(a.k);
+    p.vw = reinterpret_cast<uint8_t *>(a.v);
+    p.item_stride = a.item_stride * BLOCK_BYTES;
+    p.n_items = a.n_items;
+    p.n_kv = a.n_kv_heads;
+    p.group = a.n_q_heads / a.n_kv_heads;
+    p.max_tokens = a.max_tokens;
+    p.heads_per_cta = pl.heads_per_cta;
+    p.head_slices = pl.head_slices;
+    p.pairs = pl.pairs;
+    p.lens = a.lens;
+    p.len0 = a.len0;
+    p.len_step = a.len_step;
+    p.q = a.q;
+    p.q_item_stride = a.q_item_stride;
+    p.out = a.out;
+    p.out_item_stride = a.out_item_stride;
+    p.k_new = a.k_new;
+    p.v_new = a.v_new;
+    p.kv_new_item_stride = a.kv_new_item_stride;
+    p.out_mode = a.out_mode;
+    p.split_tokens = pl.split_tokens;
+    p.max_splits = pl.max_splits;
+    p.scale = 1.0f / sqrtf((float)a.head_dim);  // as attend_q8 computes it (attention_layer.c:131)
+    p.counters = pl.max_splits > 1 ? sc.tickets : nullptr;
+    p.part = pl.max_splits > 1 ? sc.part : nullptr;
+    p.err = nullptr;  // no device error word: device-side checks still clamp or stop safely
+    const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a.n_items);
+    if (pl.pack) return dispatch_pack(pl.nb, p, grid, st, nullptr);
+    return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
+}
+
 extern "C" int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads,
                              int n_kv_heads, int head_dim, int max_tokens, int pos, const float *q, float *out,
                              tqk_stream_t stream) {

@@ -83,6 +83,7 @@ tqk_softmax_rows = _sig("tqk_softmax_rows", [_vp, _i, _i, _sz, _vp])
 tqk_decode_workspace_size = _sig("tqk_decode_workspace_size", [ctypes.POINTER(DecodeArgs), ctypes.POINTER(_sz)])
 tqk_workspace_init = _sig("tqk_workspace_init", [_vp, _sz, _vp])
 tqk_decode_q8 = _sig("tqk_decode_q8", [ctypes.POINTER(DecodeArgs), _vp, _sz, _vp])
+tqk_decode_q8_static = _sig("tqk_decode_q8_static", [ctypes.POINTER(DecodeArgs), _vp])
 tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
@@ -94,6 +95,7 @@ EXPORTED = [
     "tqk_attn_scores_q8", "tqk_attn_accum_q8", "tqk_softmax_rows",
     "tqk_decode_workspace_size", "tqk_workspace_init", "tqk_decode_q8",
     "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
+    "tqk_decode_q8_static",
 ]
 
 
@@ -216,6 +218,11 @@ def decode(args: DecodeArgs, workspace=None, stream=None) -> None:
     ws = _ptr(workspace) if workspace is not None else None
     nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(tqk_decode_q8(ctypes.byref(args), ws, nbytes, _stream(stream)), "tqk_decode_q8")
+
+
+def decode_static(args: DecodeArgs, stream=None) -> None:
+    """tqk_decode_q8_static: the decode with the library's static scratch (no device allocation)."""
+    check(tqk_decode_q8_static(ctypes.byref(args), _stream(stream)), "tqk_decode_q8_static")
 
 
 def decode_workspace_size(args: DecodeArgs) -> int:
