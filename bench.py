@@ -160,6 +160,7 @@ def barrier(dist):
 class Config2:
     """Llama-3-8B-shaped decode: L layers of one sequence, fused append + attention."""
     name = "config2"
+    scaling = "weak"  # every rank decodes its own sequence
 
     def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096):
         import torch
@@ -216,10 +217,82 @@ class Config2:
                 "layers": self.L, "seq_len": self.pos + 1, "kv_bytes_per_token": self.kv_bytes,
                 "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
 
+    @staticmethod
+    def parallelism(world):
+        return "batch-sharded: one sequence per GPU, no collective" if world > 1 else "single GPU"
+
     # the reference's CPU path on the same workload (host planes)
     def host_planes(self):
         return self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), \
             self.k_new.cpu().numpy(), self.v_new.cpu().numpy()
+
+
+class Config4:
+    """Llama-3-70B-shaped long-context decode: one layer, 64 q / 8 kv heads,
+    head_dim 128, context 131072.  With N ranks the context is split into N
+    contiguous token ranges; each rank computes log-sum-exp partials of its
+    range, the partials are all-gathered (NCCL over NVLink) and merged
+    (tqk_merge_partials).  One step is one token for the whole job."""
+    name = "config4"
+    scaling = "strong"  # the context is fixed; each rank gets 1/N of it
+
+    def __init__(self, seed: int, rank: int = 0, world: int = 1, dist=None, n=131072, n_q=64, n_kv=8, hd=128):
+        import torch
+        from tailorquantkernel_b200 import shard, tqk
+        self.tqk, self.shard, self.dist, self.world = tqk, shard, dist, world
+        self.L, self.nq, self.nkv, self.hd, self.n = 1, n_q, n_kv, hd, n
+        self.mt, self.pos = n, n - 1
+        self.nb = hd // QK
+        self.start, self.n_local = shard.seq_range(n, rank, world)
+        g = torch.Generator(device="cuda").manual_seed(seed + rank)
+        shape = (n_kv, max(self.n_local, 1), hd)
+        self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+        self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+        gq = torch.Generator(device="cuda").manual_seed(seed)  # the same q on every rank
+        self.q = torch.randn(n_q * hd, device="cuda", generator=gq)
+        self.out = torch.empty(n_q * hd, device="cuda")
+        self.partial = torch.empty(n_q * (hd + 2), device="cuda")
+        self.gathered = torch.empty(world, n_q * (hd + 2), device="cuda")
+        self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, max(self.n_local, 1), self.q, self.out,
+                                    len0=self.n_local)
+        self.kv_bytes = 2 * n_kv * n * self.nb * BB            # the whole context, all ranks
+        self.bytes_per_step = 2 * n_kv * self.n_local * self.nb * BB  # this rank's decode kernel
+        self.tokens_per_step = 1
+        self.launches_per_step = 1 if world == 1 else 2  # decode (+ merge); the all-gather is NCCL's
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_q.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+
+    def step(self):
+        if self.world == 1:
+            self.tqk.decode(self.args)
+        else:
+            self.shard.seqsplit_attend(self.dist, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
+                                       self.n_local, self.q, self.out, self.partial, gathered=self.gathered)
+
+    def step_e2e(self):
+        import torch
+        s = torch.cuda.current_stream()
+        self.q.copy_(self.h_q, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+        s.synchronize()
+
+    def describe(self):
+        return {"workload": "config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, 64 q / 8 kv heads, "
+                            "head_dim 128, context 131072",
+                "layers": 1, "seq_len": self.n, "kv_bytes_per_token": self.kv_bytes,
+                "tokens_per_rank": self.n_local,
+                "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
+
+    @staticmethod
+    def parallelism(world):
+        return (f"sequence-split over {world} GPUs: log-sum-exp partials all-gathered with NCCL, merged on device"
+                if world > 1 else "single GPU")
+
+    def host_planes(self):
+        return self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), None, None
 
 
 def rope_np(x, hd, pos, theta):
@@ -237,6 +310,7 @@ def rope_np(x, hd, pos, theta):
 class HostConfig2:
     """Config 2 built on the host only, for the reference arm: K/V ~ N(0,1) per
     layer quantised by the reference's own quantize_row_q8."""
+    name = "config2"
 
     def __init__(self, orc, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096):
         self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
@@ -262,6 +336,32 @@ class HostConfig2:
         return Config2.describe(self)
 
 
+class HostConfig4:
+    """Config 4 built on the host only, for the reference arm (one layer, 64 q /
+    8 kv heads, context 131072, no append)."""
+    name = "config4"
+
+    def __init__(self, orc, seed: int, n=131072, n_q=64, n_kv=8, hd=128):
+        self.L, self.nq, self.nkv, self.hd, self.n = 1, n_q, n_kv, hd, n
+        self.mt, self.pos = n, n - 1
+        self.nb = hd // QK
+        rng = np.random.default_rng(seed)
+        row = self.nb * BB
+        self.kp = orc.quantize_rows_bulk(rng.standard_normal((n_kv, n, hd), dtype=np.float32)).reshape(1, n_kv, n, row)
+        self.vp = orc.quantize_rows_bulk(rng.standard_normal((n_kv, n, hd), dtype=np.float32)).reshape(1, n_kv, n, row)
+        self.q = rng.standard_normal((1, n_q * hd), dtype=np.float32)
+        self.kv_bytes = 2 * n_kv * n * row
+        self.bytes_per_step = self.kv_bytes
+
+    def host_planes(self):
+        return self.kp, self.vp, self.q, None, None
+
+    def describe(self):
+        return {"workload": "config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, 64 q / 8 kv heads, "
+                            "head_dim 128, context 131072",
+                "layers": 1, "seq_len": self.n, "kv_bytes_per_token": self.kv_bytes}
+
+
 # ---------------------------------------------------------------------------
 # reference CPU path (oracle/_ref: the reference's AVX2 build) -- baseline only
 # ---------------------------------------------------------------------------
@@ -283,7 +383,8 @@ def reference_token_seconds(orc, wl, budget_s: float, max_tokens: int | None = N
     while (time.perf_counter() < t_end or len(times) < min_tokens) and (max_tokens is None or len(times) < max_tokens):
         t0 = time.perf_counter()
         for layer in range(wl.L):
-            orc.store_kv(kp[layer], vp[layer], wl.nkv, wl.hd, wl.mt, wl.pos, kn[layer], vn[layer])
+            if kn is not None:
+                orc.store_kv(kp[layer], vp[layer], wl.nkv, wl.hd, wl.mt, wl.pos, kn[layer], vn[layer])
             orc.attend(kp[layer], vp[layer], wl.nq, wl.nkv, wl.hd, wl.mt, wl.pos, q[layer], threads=threads)
         times.append(time.perf_counter() - t0)
     return statistics.median(times), len(times), threads
@@ -294,16 +395,20 @@ def run_reference(args):
     if rank != 0:
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
-    wl = HostConfig2(orc, seed=1000)
+    wl = HostConfig2(orc, seed=1000) if args.config == 2 else HostConfig4(orc, seed=4000)
+    # bounded: at most --steps whole tokens, stopping after ~60 s of CPU work
     reference_token_seconds(orc, wl, 0.0, max_tokens=args.warmup, min_tokens=args.warmup)
-    sec, n, threads = reference_token_seconds(orc, wl, 0.0, max_tokens=args.steps, min_tokens=args.steps)
+    sec, n, threads = reference_token_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
+                                              min_tokens=min(args.steps, 3))
     value = 1.0 / sec
+    scaling = "weak" if args.config == 2 else "strong"
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "impl": "reference",
             "config": {**wl.describe(), "global_batch": 1, "parallelism": "reference CPU (OpenMP over kv heads)"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
-                             "sample": f"{n} whole tokens of config 2 (32 layers of store_kv + attend_q8), median"},
+                             "sample": f"{n} whole tokens of {wl.name} ({wl.L} layer(s)), median per token, "
+                                       f"~{args.ref_seconds:.0f} s budget"},
             "hbm_gbs_equivalent": wl.bytes_per_step / sec / 1e9,
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -321,7 +426,7 @@ def run_ours(args):
     from tailorquantkernel_b200 import tqk
     peak, peak_kind = _peaks()
 
-    wl = Config2(seed=1000 + rank)
+    wl = Config2(seed=1000 + rank) if args.config == 2 else Config4(seed=4000, rank=rank, world=world, dist=dist)
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -353,36 +458,39 @@ def run_ours(args):
         orc, kind = reference_oracle()
         sec, n, threads = reference_token_seconds(orc, wl, args.cpu_seconds)
         cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
-               "sample": f"{n} whole tokens of config 2 (32 layers of store_kv + attend_q8), "
+               "sample": f"{n} whole tokens of {wl.name} ({wl.L} layer(s) of "
+                         f"{'store_kv + ' if wl.name == 'config2' else ''}attend_q8), "
                          f"~{args.cpu_seconds:.0f} s budget, median per token"}
 
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        per_launch = t_local / (args.steps * wl.launches_per_step)
+        # the decode kernel's share of a step: one launch per step (config 4 at N > 1 adds the
+        # all-gather and the merge, so this per-step figure understates the kernel's rate there)
+        per_launch = t_local / args.steps
         achieved = wl.bytes_per_step / per_launch / 1e9
-        traffic = _traffic_from_profile("decode_q8_config2")
+        traffic = _traffic_from_profile("decode_q8_" + wl.name)
+        jobs = world if wl.scaling == "weak" else 1  # weak: every rank runs its own sequence
         line = {
             "metric": METRIC,
-            "value": world * args.steps * wl.tokens_per_step / t,
+            "value": jobs * args.steps * wl.tokens_per_step / t,
             "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "int8+fp32",
             "data": "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q",
-            "config": {**wl.describe(), "global_batch": world, "parallelism":
-                       "batch-sharded: one sequence per GPU, no collective" if world > 1 else "single GPU"},
+            "config": {**wl.describe(), "global_batch": jobs, "parallelism": wl.parallelism(world)},
             "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": wl.bytes_per_step,
                          "traffic": traffic},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * args.steps / t_e2e, "unit": "tokens/s",
+            "e2e": {"value": jobs * args.steps / t_e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-                    "api": "tqk_decode_q8 (C ABI) with pinned host q/k/v in and attention output out, "
-                           "stream-synchronised every step"},
+                    "api": "tqk_decode_q8 (C ABI) with pinned host inputs (q, and the appended k/v for "
+                           "config 2) in and the attention output out, stream-synchronised every step"},
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clk.summary(),
             "device_status": status,
@@ -399,8 +507,9 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

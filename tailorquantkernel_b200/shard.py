@@ -1,0 +1,101 @@
+"""Multi-GPU partitioning of the Q8 decode attention (one process per GPU).
+
+The reference runs on one CPU; its decode attention has no cross-device
+dimension.  On a box of B200s the work splits three ways, only one of which
+needs a collective:
+
+* by kv-head group (one sequence, the kv heads and their q-head groups divided
+  over the ranks): every rank writes a disjoint slice of the output heads;
+* by batch (many sequences, divided over the ranks, balanced by length):
+  every rank owns whole sequences;
+* by sequence (one very long context, contiguous token ranges per rank): each
+  rank computes log-sum-exp partials {acc, m, l} of its range
+  (TQK_OUT_PARTIAL), the partials are all-gathered over NVLink, and
+  tqk_merge_partials combines them -- the only exchange step.
+
+The functions here are pure host logic plus torch.distributed calls; the GPU
+work goes through libtqk's C ABI (tailorquantkernel_b200.tqk).
+"""
+from __future__ import annotations
+
+from typing import List, Sequence, Tuple
+
+TILE_TOKENS = 64  # the decode kernels' tile: ranges start on tile boundaries
+
+
+def seq_range(n_tokens: int, rank: int, world: int, align: int = TILE_TOKENS) -> Tuple[int, int]:
+    """Token range [start, start + length) of `rank` when a context of n_tokens is
+    split into `world` contiguous ranges.  Range starts fall on multiples of
+    `align` (whole decode tiles); the last rank takes the remainder.  Ranges
+    are disjoint and cover [0, n_tokens); a rank may get an empty range when
+    n_tokens is smaller than world * align."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if n_tokens < 0:
+        raise ValueError("n_tokens must be >= 0")
+    tiles = (n_tokens + align - 1) // align
+    start_tile = tiles * rank // world
+    end_tile = tiles * (rank + 1) // world
+    start = min(start_tile * align, n_tokens)
+    end = min(end_tile * align, n_tokens) if rank + 1 < world else n_tokens
+    return start, end - start
+
+
+def head_range(n_kv: int, rank: int, world: int) -> Tuple[int, int]:
+    """kv heads [start, start + count) of `rank` for the kv-head-group split; the
+    q heads of a kv head travel with it.  n_kv must divide evenly."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if n_kv % world:
+        raise ValueError(f"{n_kv} kv heads do not divide over {world} ranks")
+    per = n_kv // world
+    return rank * per, per
+
+
+def batch_shard(lens: Sequence[int], world: int) -> List[List[int]]:
+    """Sequences of a ragged batch per rank, balanced by total length: longest
+    first, each to the currently lightest rank (ties to the lower rank).  Every
+    sequence index appears exactly once; each rank's list is in ascending order."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    loads = [0] * world
+    owned: List[List[int]] = [[] for _ in range(world)]
+    for i in sorted(range(len(lens)), key=lambda j: (-int(lens[j]), j)):
+        r = min(range(world), key=lambda w: (loads[w], w))
+        owned[r].append(i)
+        loads[r] += int(lens[i])
+    return [sorted(o) for o in owned]
+
+
+def gather_partials(dist, local, group=None):
+    """All-gathers each rank's partial records (a contiguous tensor of the same
+    shape on every rank) into one [world, *local.shape] tensor, rank order."""
+    import torch
+    world = dist.get_world_size(group)
+    out = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    if dist.get_backend(group) == "gloo":  # host ranks (tests): list form
+        dist.all_gather(list(out.unbind(0)), local.contiguous(), group=group)
+    else:
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out
+
+
+def seqsplit_attend(dist, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: int, n_local: int, q, out,
+                    partial, gathered=None, stream=None):
+    """One decode step of a context split by sequence: attention of q over this
+    rank's n_local tokens as partials, all-gather, log-sum-exp merge into out.
+
+    k_local / v_local: this rank's Q8 planes [n_kv][n_local][head_dim/32];
+    partial: device float tensor [n_q * (head_dim + 2)] for this rank's record;
+    gathered: optional preallocated [world, n_q * (head_dim + 2)] tensor.
+    Every rank ends with the full output."""
+    args = tqk.decode_args(k_local, v_local, n_q, n_kv, head_dim, max(n_local, 1), q, partial, len0=n_local,
+                           out_mode=tqk.OUT_PARTIAL)
+    tqk.decode(args, stream=stream)
+    world = dist.get_world_size()
+    if gathered is None:
+        gathered = gather_partials(dist, partial)
+    else:
+        dist.all_gather_into_tensor(gathered, partial)
+    tqk.merge_partials(gathered, world, n_q * (head_dim + 2), n_q, head_dim, out, stream=stream)
+    return out

@@ -1,0 +1,62 @@
+"""The sequence-split decode (config 4's multi-GPU path) on 2 GPUs: NCCL ranks,
+each with a contiguous token range, partials all-gathered and merged on
+device; every rank's merged output must match a single-GPU decode of the whole
+context within the attention tolerance.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, n, result_dir):
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    from tailorquantkernel_b200 import shard, tqk
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        nq, nkv, hd = 64, 8, 128
+        g = torch.Generator(device="cuda").manual_seed(77)  # the same full context on every rank
+        kp = tqk.quantize_rows(torch.randn(nkv, n, hd, device="cuda", generator=g))
+        vp = tqk.quantize_rows(torch.randn(nkv, n, hd, device="cuda", generator=g))
+        q = torch.randn(nq * hd, device="cuda", generator=g)
+        s, ln = shard.seq_range(n, rank, world)
+        kl, vl = kp[:, s:s + ln].contiguous(), vp[:, s:s + ln].contiguous()
+        out = torch.empty(nq * hd, device="cuda")
+        partial = torch.empty(nq * (hd + 2), device="cuda")
+        for _ in range(2):  # twice: the buffers are reusable
+            shard.seqsplit_attend(dist, tqk, kl, vl, nq, nkv, hd, ln, q, out, partial)
+        full = torch.empty(nq * hd, device="cuda")
+        tqk.attend(kp, vp, nq, nkv, hd, n, n - 1, q, full)
+        torch.cuda.synchronize()
+        np.save(os.path.join(result_dir, f"rank{rank}.npy"), np.stack([out.cpu().numpy(), full.cpu().numpy()]))
+        assert tqk.device_status() == 0
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [20000, 100])
+def test_sequence_split_two_gpus(cuda, tmp_path, n):
+    import torch
+    import torch.multiprocessing as mp
+    from _cases import tolerance_ok
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_rank_main, args=(2, _free_port(), n, str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        got, ref = np.load(tmp_path / f"rank{r}.npy")
+        ok, max_abs, rel = tolerance_ok(got, ref)
+        assert ok, f"rank {r}: max abs {max_abs:.3g} rel {rel:.3g}"
