@@ -153,6 +153,16 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst_smem, const void *src_gm
         : "memory");
 }
 
+// Barrier over the first NT threads of the CTA (named barrier BAR; 0 = all).
+template <int BAR, int NT>
+__device__ __forceinline__ void cta_sync() {
+    if constexpr (BAR == 0) {
+        __syncthreads();
+    } else {
+        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+    }
+}
+
 // ----------------------------------------------------------------------------
 // int8 helpers
 // ----------------------------------------------------------------------------

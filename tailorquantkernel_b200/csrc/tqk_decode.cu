@@ -135,17 +135,6 @@ __device__ __forceinline__ float score_row(const uint8_t *row, const uint32_t (&
     return __fmul_rn(acc, scale);
 }
 
-// Barrier over the first NT threads of the CTA: bar 0 with the whole CTA, or a
-// named barrier when only the consumer warps take part.
-template <int BAR, int NT>
-__device__ __forceinline__ void cta_sync() {
-    if constexpr (BAR == 0) {
-        __syncthreads();
-    } else {
-        asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
-    }
-}
-
 // Finishes one split of one (item, kv-head slice).  acc(g, c) is the CTA's
 // unnormalised sum for its q head g and column c, relative to the running max
 // ms[g], with softmax denominator ls[g].  A single split writes the output (or
@@ -1036,6 +1025,10 @@ extern "C" int tqk_prefill_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int 
     if (pos0 < 0 || (long long)pos0 + n > max_tokens) return fail(TQK_EPOS, "tqk_prefill_q8: range out of cache");
     int rc = tqk_store_kv_q8_batch(k_plane, v_plane, n_kv_heads, head_dim, max_tokens, pos0, n, k, v, stream);
     if (rc) return rc;
+    // tensor-core path (head_dim 128, 1/2/4/8 q heads per kv head); other shapes use the decode kernel
+    rc = prefill_attend_tc(k_plane, v_plane, n_q_heads, n_kv_heads, head_dim, max_tokens, pos0, n, q, out,
+                           (cudaStream_t)stream);
+    if (rc != TQK_EUNSUPPORTED) return rc;
     tqk_decode_args a{};
     a.k = k_plane;
     a.v = v_plane;

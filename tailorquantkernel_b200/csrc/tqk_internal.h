@@ -36,4 +36,10 @@ void *library_workspace(cudaStream_t stream, size_t bytes);
 // leaves its tickets at zero, so the buffer stays zero between calls.
 int *library_counters(cudaStream_t stream, size_t bytes);
 
+// Tensor-core prefill attention over the chunk [pos0, pos0 + n) whose K/V rows
+// are already in the planes (tqk_prefill.cu).  TQK_EUNSUPPORTED for shapes it
+// does not cover (the caller then uses the decode kernel).
+int prefill_attend_tc(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
+                      int head_dim, int max_tokens, int pos0, int n, const float *q, float *out, cudaStream_t stream);
+
 }  // namespace tqk

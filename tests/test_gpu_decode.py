@@ -326,6 +326,42 @@ def test_prefill_matches_golden_and_sequential(tqk, port, cuda):
     assert ok, (max_abs, rel)
 
 
+@pytest.mark.parametrize("nq,nkv,pos0,n,mt", [
+    (8, 8, 0, 1, 64),        # one token, group 1
+    (16, 8, 5, 77, 100),     # group 2, ragged last CTA
+    (32, 8, 2000, 40, 2100), # group 4, partial key tiles
+    (32, 4, 100, 300, 500),  # group 8
+    (32, 32, 64, 130, 200),  # group 1, 128 tokens per CTA
+    (32, 2, 10, 20, 40),     # group 16: not a tensor-core shape, decode kernel
+])
+def test_prefill_tensor_core_shapes(tqk, port, cuda, nq, nkv, pos0, n, mt):
+    """tqk_prefill_q8 (the tcgen05 prefill kernel for head_dim 128) against the
+    oracle's attention_layer_batch restatement: appended rows bit-exact,
+    attention within tolerance, for several group sizes and ragged tiles."""
+    import torch
+    hd = 128
+    rng = np.random.default_rng(nq * 1000 + n)
+    kf = np.zeros((nkv, mt, hd), np.float32)
+    vf = np.zeros((nkv, mt, hd), np.float32)
+    kf[:, :pos0] = rng.standard_normal((nkv, pos0, hd))
+    vf[:, :pos0] = rng.standard_normal((nkv, pos0, hd))
+    qn = rng.standard_normal((n, nq * hd)).astype(np.float32)
+    kn = rng.standard_normal((n, nkv * hd)).astype(np.float32)
+    vn = rng.standard_normal((n, nkv * hd)).astype(np.float32)
+    kp = tqk.quantize_rows(torch.from_numpy(kf).to(cuda))
+    vp = tqk.quantize_rows(torch.from_numpy(vf).to(cuda))
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    out = torch.full((n, nq * hd), float("nan"), device=cuda)
+    tqk.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, torch.from_numpy(qn).to(cuda), torch.from_numpy(kn).to(cuda),
+                torch.from_numpy(vn).to(cuda), out)
+    ref = port.prefill(kh, vh, nq, nkv, hd, mt, pos0, n, qn, kn, vn).reshape(n, nq * hd)
+    assert np.array_equal(kp.cpu().numpy(), kh) and np.array_equal(vp.cpu().numpy(), vh)  # oracle appended in place
+    got = out.cpu().numpy()
+    ok, max_abs, rel = tolerance_ok(got, ref)
+    assert ok, f"max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
 def test_config5_prefill_full(tqk, port, cuda):
     """Config 5: 2048 new tokens at positions 2048..4095 over a 2048-token Q8
     cache, 32 q / 8 kv heads, causal -- checked on a spread of query tokens."""
