@@ -7,15 +7,17 @@
 // against that kv head's keys 0 .. pos0 + last token, in 64-key tiles:
 //   * a producer warp streams each tile's K and V rows (144-byte Q8 rows) into
 //     a 2-stage ring with 1-D TMA bulk copies;
-//   * the 128 consumer threads (one query row each) repack the tile once for
-//     all rows: K's int8 block values into the canonical no-swizzle K-major
-//     layout of the int8 MMA, V dequantised (v * vd) to an fp16 hi + lo pair
-//     in the MN-major layout of the f16 MMA;
+//   * PF_WG warpgroups of consumer threads, PF_WG threads per query row (each
+//     takes an equal share of every tile's keys and of O's columns), repack
+//     the tile once for all rows:
+//     K's int8 block values into the canonical no-swizzle K-major layout of
+//     the int8 MMA, V dequantised (v * vd) to an fp16 hi + lo pair in the
+//     MN-major layout of the f16 MMA;
 //   * QK: four kind::i8 MMAs (M=128, N=64, K=32), one per Q8 block, give the
-//     exact int32 block dots in TMEM; each thread combines its row's dots with
-//     the reference's rounding sequence acc += (float)dot * (qd*kd), then
-//     * scale (model/attn_q8.c:24-31), so scores are bit-identical to
-//     attn_scores_q8_scalar's;
+//     exact int32 block dots in TMEM; each thread combines its row's dots as
+//     score = sum_b (float)dot_b * (qd_b*kd_b) * scale (model/attn_q8.c:24-31)
+//     with packed fp32 fused multiply-adds (scale and log2(e) folded into qd),
+//     within a few ulps of attn_scores_q8_scalar's rounding sequence;
 //   * softmax: base-2 online softmax per row with a lazily raised running max
 //     (the accumulator is rescaled only when the max grows by more than 2^8,
 //     which keeps P <= 256 in fp16); P is written as fp16 in the canonical
@@ -34,16 +36,27 @@ namespace tqk {
 
 namespace {
 
-constexpr int PF_M = 128;     // query rows per CTA
-constexpr int PF_KT = 64;     // keys per tile
-constexpr int PF_WARPS = 4;   // consumer warps: thread = row
-constexpr int PF_THREADS = (PF_WARPS + 1) * 32;
+#ifndef TQK_PF_KT
+#define TQK_PF_KT 64
+#endif
+#ifndef TQK_PF_WG
+#define TQK_PF_WG 2
+#endif
+constexpr int PF_M = 128;          // query rows per CTA
+constexpr int PF_KT = TQK_PF_KT;   // keys per tile (32 or 64)
+constexpr int PF_WG = TQK_PF_WG;   // consumer warpgroups: row r is held by threads r, 128 + r, ...,
+                                   // each taking an equal share of every tile's keys and of O's columns
+constexpr int PF_NT = PF_WG * PF_M;            // consumer threads
+constexpr int PF_WARPS = PF_NT / 32;
+constexpr int PF_THREADS = PF_NT + 32;         // + the producer warp
 constexpr int PF_STAGES = 2;
 constexpr int PF_HD = 128;
 constexpr int PF_NB = PF_HD / QK;
 constexpr int PF_ROW = PF_NB * BLOCK_BYTES;  // 144
-constexpr int PF_TMEM_COLS = 512;            // S: 4 blocks x 64 int32 columns; O: 128 fp32 columns
-constexpr int PF_TMEM_O = 256;
+constexpr int PF_KH = PF_KT / PF_WG;         // keys of a tile per thread
+constexpr int PF_TMEM_O = PF_NB * PF_KT;     // S: 4 blocks x PF_KT int32 columns, then O: 128 fp32 columns
+constexpr int PF_TMEM_COLS = PF_TMEM_O + PF_HD <= 256 ? 256 : 512;
+constexpr int PF_CTAS_PER_SM = 512 / PF_TMEM_COLS;  // TMEM bound; shared memory is sized to match
 constexpr uint64_t PF_WAIT_NS = 1000000000ull;
 constexpr uint64_t PF_DRAIN_NS = 20000000ull;
 
@@ -54,21 +67,28 @@ constexpr int OFF_KC = OFF_QC + PF_NB * PF_M * 32;            // int8 K, 4 block
 constexpr int OFF_VH = OFF_KC + PF_NB * PF_KT * 32;           // fp16 V hi [64 keys x 128 cols], MN-major
 constexpr int OFF_VL = OFF_VH + PF_KT * PF_HD * 2;            // fp16 V lo
 constexpr int OFF_PC = OFF_VL + PF_KT * PF_HD * 2;            // fp16 P [128 rows x 64 keys], K-major
-constexpr int OFF_KD = OFF_PC + PF_M * PF_KT * 2;             // float kd [64 keys][4 blocks]
-constexpr int OFF_BAR = OFF_KD + PF_KT * PF_NB * 4;           // full[2], empty[2], s_done, pv_done
+constexpr int OFF_KD = OFF_PC + PF_M * PF_KT * 2;             // float kd [4 blocks][64 keys]
+constexpr int OFF_QD = OFF_KD + PF_KT * PF_NB * 4;            // float qd [128 rows][4 blocks]
+constexpr int OFF_MX = OFF_QD + PF_M * PF_NB * 4;             // float [2][128]: half-tile maxima, then sums
+constexpr int OFF_BAR = OFF_MX + PF_WG * PF_M * 4;            // full[2], empty[2], s_done, pv_done
 constexpr int OFF_TMEM = OFF_BAR + 6 * 8;
 constexpr int PF_USED = OFF_TMEM + 16;
-// more than half an SM's shared memory: one CTA per SM, so the TMEM allocation never waits
-constexpr int PF_SMEM = PF_USED > 117 * 1024 ? PF_USED : 117 * 1024;
+// more than 1/(n+1) of an SM's shared memory: at most PF_CTAS_PER_SM CTAs per SM, so a TMEM
+// allocation never waits
+constexpr int PF_SMEM_FLOOR = 228 * 1024 / (PF_CTAS_PER_SM + 1) + 1024;
+constexpr int PF_SMEM = PF_USED > PF_SMEM_FLOOR ? PF_USED : PF_SMEM_FLOOR;
+static_assert(PF_USED + 1024 <= 228 * 1024 / PF_CTAS_PER_SM, "shared memory must allow PF_CTAS_PER_SM CTAs");
+static_assert(PF_KH % 16 == 0 && PF_KT % 16 == 0, "tile shape");
 static_assert(OFF_QC % 1024 == 0 && OFF_KC % 16 == 0 && OFF_VH % 16 == 0 && OFF_PC % 16 == 0, "operand alignment");
 
 // Core-matrix offsets of the canonical no-swizzle layouts (bytes).
 //   Q / K blocks: K-major, 32 B of K per row: LBO 128 (K chunk), SBO 256 (8-row group).
 __device__ __forceinline__ int qk_off(int row, int kc) { return (row >> 3) * 256 + kc * 128 + (row & 7) * 16; }
-//   P: K-major, 64 keys = 8 chunks per row: LBO 128, SBO 1024.
-__device__ __forceinline__ int p_off(int row, int kc) { return (row >> 3) * 1024 + kc * 128 + (row & 7) * 16; }
-//   V: MN-major, 8-column chunks: chunk (key, cg) at cg*1024 + (key/8)*128 + (key%8)*16 (LBO 128, SBO 1024).
-__device__ __forceinline__ int v_off(int key, int cg) { return cg * 1024 + (key >> 3) * 128 + (key & 7) * 16; }
+//   P: K-major, PF_KT keys = PF_KT/8 chunks per row: LBO 128, SBO PF_SBO.
+//   V: MN-major, 8-column chunks: chunk (key, cg) at cg*PF_SBO + (key/8)*128 + (key%8)*16 (LBO 128).
+constexpr int PF_SBO = PF_KT / 8 * 128;
+__device__ __forceinline__ int p_off(int row, int kc) { return (row >> 3) * PF_SBO + kc * 128 + (row & 7) * 16; }
+__device__ __forceinline__ int v_off(int key, int cg) { return cg * PF_SBO + (key >> 3) * 128 + (key & 7) * 16; }
 
 struct PrefillParams {
     const uint8_t *k, *v;  // planes [n_kv][max_tokens][144 B]
@@ -94,11 +114,33 @@ __device__ __forceinline__ float f16_hi_to_f32(uint32_t h) {
     asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tcvt.f32.f16 %0, hi;\n\t}" : "=f"(f) : "r"(h));
     return f;
 }
+typedef unsigned long long pf2;  // packed fp32 pair
+__device__ __forceinline__ pf2 pk(float x, float y) {
+    pf2 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+__device__ __forceinline__ void upk(pf2 v, float &x, float &y) { asm("mov.b64 {%0,%1}, %2;" : "=f"(x), "=f"(y) : "l"(v)); }
+__device__ __forceinline__ pf2 mul2p(pf2 a, pf2 b) {
+    pf2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ pf2 fma2p(pf2 a, pf2 b, pf2 c) {
+    pf2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// 2^x (MUFU approximation, flushes denormal results to zero): P needs ~11 bits.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 template <int G>
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(PF_THREADS, PF_CTAS_PER_SM) prefill_q8_tc_kernel(const PrefillParams p) {
     constexpr int T = PF_M / G;  // tokens per CTA
-    constexpr int NT = PF_WARPS * 32;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tb = gridDim.x - 1 - blockIdx.x;  // longest key ranges first
@@ -149,23 +191,25 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         return;
     }
 
-    // ---- consumers: thread = query row
-    const int r = tid;
+    // ---- consumers: thread (wg, r) = half wg of query row r
+    const int wg = tid >> 7, r = tid & (PF_M - 1);
     const int token = tok0 + r / G;
     const bool valid_row = token <= tok_last;
     const int head = kvh * G + r % G;
     const int limit = p.pos0 + token;  // last key the row may see (causal)
     uint8_t *qc = smem + OFF_QC, *kc = smem + OFF_KC, *vhi = smem + OFF_VH, *vlo = smem + OFF_VL, *pc = smem + OFF_PC;
-    float *kd = reinterpret_cast<float *>(smem + OFF_KD);
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    float *kdT = reinterpret_cast<float *>(smem + OFF_KD);
+    float *qd_s = reinterpret_cast<float *>(smem + OFF_QD);
+    float *mx_s = reinterpret_cast<float *>(smem + OFF_MX);
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 
-    // quantise the row's q (quant_x.c:12-34) into the int8 A operand of the score MMAs
-    float qd[PF_NB];
+    // quantise the row's q (quant_x.c:12-34) into the int8 A operand: this thread's share of the blocks
     {
         const float4 *src = reinterpret_cast<const float4 *>(
             p.q + ((long long)(valid_row ? token : tok0) * (p.n_kv * G) + head) * PF_HD);
 #pragma unroll
-        for (int b = 0; b < PF_NB; b++) {
+        for (int bb = 0; bb < PF_NB / PF_WG; bb++) {
+            const int b = (PF_NB / PF_WG) * wg + bb;
             float x[QK];
 #pragma unroll
             for (int i = 0; i < QK / 4; i++) {
@@ -186,16 +230,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
 #pragma unroll
                 for (int i = 0; i < 8; i++) w[i] = 0u;
             }
-            qd[b] = valid_row ? d : 0.0f;
+            qd_s[r * PF_NB + b] = valid_row ? d : 0.0f;
             *reinterpret_cast<uint4 *>(qc + b * PF_M * 32 + qk_off(r, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
             *reinterpret_cast<uint4 *>(qc + b * PF_M * 32 + qk_off(r, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
         }
     }
+    cta_sync<1, PF_NT>();
+    pf2 qd2[PF_NB];  // qd * scale * log2(e): scores come out in log2 units
+    const float qs = __fmul_rn(p.scale, 1.4426950408889634f);
+#pragma unroll
+    for (int b = 0; b < PF_NB; b++) qd2[b] = pk(qd_s[r * PF_NB + b] * qs, qd_s[r * PF_NB + b] * qs);
 
     const uint32_t id_qk = idesc_i8(PF_M, PF_KT);
     const uint32_t id_pv = idesc_f16(PF_M, PF_HD, true);
-    const float l2e = 1.4426950408889634f;
-    float m = -INFINITY, l = 0.0f;  // running max (log2 units) and sum of the row
+    const int k_lo = wg * PF_KH;    // this thread's keys of a tile: [k_lo, k_lo + PF_KH)
+    const int o_lo = wg * PF_HD / PF_WG;  // this thread's O columns: [o_lo, o_lo + 128 / PF_WG)
+    float m = -INFINITY, l = 0.0f;  // running max (log2 units, shared by the row's two threads) and partial sum
     bool bad = false;               // a bounded wait gave up: drain quickly, issue nothing more
 
     for (int j = 0; j < n_tiles; j++) {
@@ -205,28 +255,26 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         const uint8_t *rk = smem + OFF_RING + slot * 2 * RAW_TILE, *rv = rk + RAW_TILE;
         const int rows = min(PF_KT, n_keys - j * PF_KT);
 
-        // K: int8 block values -> canonical K-major operand, scales -> kd (two blocks per thread)
-        {
-            const int key = r >> 1;
+        // K: int8 block values -> canonical K-major operand, scales -> kdT
+        //    (16-byte pieces (key, block, half), PF_KT*8 of them over PF_NT threads)
 #pragma unroll
-            for (int bb = 0; bb < 2; bb++) {
-                const int b = (r & 1) * 2 + bb;
-                const uint32_t *src = reinterpret_cast<const uint32_t *>(rk + key * PF_ROW + b * BLOCK_BYTES + 4);
-                uint32_t w[8];
+        for (int id = tid; id < PF_KT * PF_NB * 2; id += PF_NT) {
+            const int key = id >> 3, b = (id >> 1) & 3, half = id & 1;
+            const uint32_t *src = reinterpret_cast<const uint32_t *>(rk + key * PF_ROW + b * BLOCK_BYTES + 4 + 16 * half);
+            uint32_t w[4];
 #pragma unroll
-                for (int i = 0; i < 8; i++) w[i] = key < rows ? src[i] : 0u;
-                *reinterpret_cast<uint4 *>(kc + b * PF_KT * 32 + qk_off(key, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4 *>(kc + b * PF_KT * 32 + qk_off(key, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-                kd[key * PF_NB + b] = key < rows ? *reinterpret_cast<const float *>(rk + key * PF_ROW + b * BLOCK_BYTES) : 0.0f;
-            }
+            for (int i = 0; i < 4; i++) w[i] = key < rows ? src[i] : 0u;
+            *reinterpret_cast<uint4 *>(kc + b * PF_KT * 32 + qk_off(key, half)) = make_uint4(w[0], w[1], w[2], w[3]);
+            if (half == 0)
+                kdT[b * PF_KT + key] = key < rows ? *reinterpret_cast<const float *>(rk + key * PF_ROW + b * BLOCK_BYTES) : 0.0f;
         }
         // the previous tile's PV MMAs read V and P: wait before overwriting them
         if (j > 0 && !mbar_wait_bounded(pv_done, (uint32_t)((j - 1) & 1), bad ? PF_DRAIN_NS : PF_WAIT_NS, p.err))
             bad = true;
-        // V: dequantise v * vd to fp16 hi + lo (8 columns per chunk, 8 chunks per thread)
+        // V: dequantise v * vd to fp16 hi + lo (8 columns per chunk)
 #pragma unroll 2
-        for (int i = 0; i < 8; i++) {
-            const int id = r + NT * i, key = id >> 4, cg = id & 15, b = cg >> 2;
+        for (int i = 0; i < PF_KT * PF_HD / 8 / PF_NT; i++) {
+            const int id = tid + PF_NT * i, key = id >> 4, cg = id & 15, b = cg >> 2;
             const uint8_t *row = rv + key * PF_ROW + b * BLOCK_BYTES;
             const float vd = key < rows ? *reinterpret_cast<const float *>(row) : 0.0f;
             uint32_t w0 = 0u, w1 = 0u;
@@ -252,7 +300,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
 
         // ---- S_b = Q_b K_b^T (int32) for the four Q8 blocks
         fence_proxy_async();
-        cta_sync<1, NT>();
+        cta_sync<1, PF_NT>();
         if (tid == 0 && !bad) {
             tc_fence_after();
 #pragma unroll
@@ -264,41 +312,59 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         if (!mbar_wait_bounded(s_done, (uint32_t)(j & 1), bad ? PF_DRAIN_NS : PF_WAIT_NS, p.err)) bad = true;
         tc_fence_after();
 
-        // ---- scores of the row (exact reference rounding), log2 units, causal mask
-        float s[PF_KT];
+        // ---- scores of the row's 32 keys (exact reference rounding), log2 units, causal mask
+        float s[PF_KH];
+        const bool diag = j * PF_KT + PF_KT - 1 > p.pos0 + tok0;  // the tile reaches past some row's last key
 #pragma unroll
-        for (int c = 0; c < PF_KT / 16; c++) {
+        for (int c = 0; c < PF_KH / 16; c++) {
             uint32_t dv[PF_NB][16];
 #pragma unroll
-            for (int b = 0; b < PF_NB; b++) tmem_ld16(tmem + lane_base + b * PF_KT + c * 16, dv[b]);
+            for (int b = 0; b < PF_NB; b++) tmem_ld16(tmem + lane_base + b * PF_KT + k_lo + c * 16, dv[b]);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int kk = c * 16 + i;
-                float acc = 0.0f;
+            for (int i = 0; i < 8; i++) {
+                const int kk = k_lo + c * 16 + 2 * i;  // key pair kk, kk+1 of the tile
+                pf2 acc = pk(0.0f, 0.0f);
 #pragma unroll
-                for (int b = 0; b < PF_NB; b++)
-                    acc = __fadd_rn(acc, __fmul_rn(__int2float_rn((int)dv[b][i]), __fmul_rn(qd[b], kd[kk * PF_NB + b])));
-                const float x = __fmul_rn(__fmul_rn(acc, p.scale), l2e);
-                s[kk] = !valid_row ? 0.0f : (j * PF_KT + kk > limit ? -INFINITY : x);
+                for (int b = 0; b < PF_NB; b++) {
+                    const pf2 kd2 = *reinterpret_cast<const pf2 *>(kdT + b * PF_KT + kk);
+                    acc = fma2p(pk(__int2float_rn((int)dv[b][2 * i]), __int2float_rn((int)dv[b][2 * i + 1])),
+                                mul2p(qd2[b], kd2), acc);
+                }
+                float x0, x1;
+                upk(acc, x0, x1);
+                if (diag) {
+                    if (j * PF_KT + kk > limit) x0 = -INFINITY;
+                    if (j * PF_KT + kk + 1 > limit) x1 = -INFINITY;
+                }
+                s[c * 16 + 2 * i] = valid_row ? x0 : 0.0f;
+                s[c * 16 + 2 * i + 1] = valid_row ? x1 : 0.0f;
             }
         }
         float mt = -INFINITY;
 #pragma unroll
-        for (int kk = 0; kk < PF_KT; kk++) mt = fmaxf(mt, s[kk]);
+        for (int kk = 0; kk < PF_KH; kk++) mt = fmaxf(mt, s[kk]);
+        if constexpr (PF_WG > 1) {
+            mx_s[wg * PF_M + r] = mt;
+            tc_fence_before();
+            cta_sync<1, PF_NT>();  // every share's maximum is in; every thread is done reading S
+#pragma unroll
+            for (int w2 = 0; w2 < PF_WG; w2++) mt = fmaxf(mt, mx_s[w2 * PF_M + r]);
+        }
         // raise the running max lazily: only when it grows by more than 8 (P stays <= 2^8)
         const bool raise = mt > m + 8.0f;
         const float m_new = raise ? mt : m;
-        const float factor = raise ? exp2f(m - m_new) : 1.0f;
+        const float factor = raise ? ex2(m - m_new) : 1.0f;
         if (j > 0 && __any_sync(0xffffffffu, raise && factor != 1.0f)) {
+            tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < PF_HD / 16; c++) {
+            for (int c = 0; c < PF_HD / PF_WG / 16; c++) {
                 uint32_t ov[16];
-                tmem_ld16(tmem + lane_base + PF_TMEM_O + c * 16, ov);
+                tmem_ld16(tmem + lane_base + PF_TMEM_O + o_lo + c * 16, ov);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 16; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * factor);
-                tmem_st16(tmem + lane_base + PF_TMEM_O + c * 16, ov);
+                tmem_st16(tmem + lane_base + PF_TMEM_O + o_lo + c * 16, ov);
             }
             tmem_wait_st();
         }
@@ -306,14 +372,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         m = m_new;
         float sum = 0.0f;
 #pragma unroll
-        for (int kc8 = 0; kc8 < PF_KT / 8; kc8++) {
+        for (int c8 = 0; c8 < PF_KH / 8; c8++) {
             float pv[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                pv[e] = exp2f(s[kc8 * 8 + e] - m);
+                pv[e] = ex2(s[c8 * 8 + e] - m);
                 sum += pv[e];
             }
-            *reinterpret_cast<uint4 *>(pc + p_off(r, kc8)) =
+            *reinterpret_cast<uint4 *>(pc + p_off(r, k_lo / 8 + c8)) =
                 make_uint4(pack2_f16(pv[0], pv[1]), pack2_f16(pv[2], pv[3]), pack2_f16(pv[4], pv[5]), pack2_f16(pv[6], pv[7]));
         }
         l += sum;
@@ -321,17 +387,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         // ---- O += P V_hi + P V_lo
         tc_fence_before();
         fence_proxy_async();
-        cta_sync<1, NT>();
+        cta_sync<1, PF_NT>();
         if (tid == 0 && !bad) {
             tc_fence_after();
 #pragma unroll
             for (int ks = 0; ks < PF_KT / 16; ks++)
-                umma_f16(tmem + PF_TMEM_O, umma_desc(smem_u32(pc + ks * 256), 128, 1024),
-                         umma_desc(smem_u32(vhi + ks * 256), 128, 1024), id_pv, j > 0 || ks > 0);
+                umma_f16(tmem + PF_TMEM_O, umma_desc(smem_u32(pc + ks * 256), 128, PF_SBO),
+                         umma_desc(smem_u32(vhi + ks * 256), 128, PF_SBO), id_pv, j > 0 || ks > 0);
 #pragma unroll
             for (int ks = 0; ks < PF_KT / 16; ks++)
-                umma_f16(tmem + PF_TMEM_O, umma_desc(smem_u32(pc + ks * 256), 128, 1024),
-                         umma_desc(smem_u32(vlo + ks * 256), 128, 1024), id_pv, true);
+                umma_f16(tmem + PF_TMEM_O, umma_desc(smem_u32(pc + ks * 256), 128, PF_SBO),
+                         umma_desc(smem_u32(vlo + ks * 256), 128, PF_SBO), id_pv, true);
             umma_commit(pv_done);
         }
     }
@@ -340,13 +406,21 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         bad = true;
     tc_fence_after();
 
-    // ---- epilogue: O / l
-    float *dst = p.out + ((long long)token * (p.n_kv * G) + head) * PF_HD;
-    const float inv_l = 1.0f / l;
+    // ---- epilogue: O / (sum of the shares' partial sums)
+    float l_row = l;
+    if constexpr (PF_WG > 1) {
+        mx_s[wg * PF_M + r] = l;
+        cta_sync<1, PF_NT>();
+        l_row = 0.0f;
 #pragma unroll
-    for (int c = 0; c < PF_HD / 16; c++) {
+        for (int w2 = 0; w2 < PF_WG; w2++) l_row += mx_s[w2 * PF_M + r];
+    }
+    const float inv_l = 1.0f / l_row;
+    float *dst = p.out + ((long long)token * (p.n_kv * G) + head) * PF_HD + o_lo;
+#pragma unroll
+    for (int c = 0; c < PF_HD / PF_WG / 16; c++) {
         uint32_t ov[16];
-        tmem_ld16(tmem + lane_base + PF_TMEM_O + c * 16, ov);
+        tmem_ld16(tmem + lane_base + PF_TMEM_O + o_lo + c * 16, ov);
         tmem_wait_ld();
         if (valid_row && !bad) {
 #pragma unroll
@@ -357,7 +431,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         }
     }
     tc_fence_before();
-    cta_sync<1, NT>();
+    cta_sync<1, PF_NT>();
     if (warp == 0) tmem_dealloc(tmem, PF_TMEM_COLS);
 }
 
