@@ -49,6 +49,14 @@ def _peaks():
         return 6650.0, "fallback"
 
 
+def _tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (bf16 dense, burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def _traffic_from_profile(name: str):
     """dram bytes per launch recorded from an ncu capture (profiles/<name>.txt)."""
     path = os.path.join(ROOT, "profiles", name + ".txt")
@@ -307,6 +315,75 @@ def rope_np(x, hd, pos, theta):
     return h.astype(np.float32).reshape(x.shape)
 
 
+class Config5:
+    """Chunked causal prefill: 2048 new tokens at positions
+    2048..4095 appended to a Q8 cache holding 2048 prior positions, each
+    attending causally to everything before it; 32 q / 8 kv heads, head_dim
+    128.  One step = one tqk_prefill_q8 call (bit-exact Q8 append of the 2048
+    K/V rows + the tcgen05 attention kernel), i.e. 2048 tokens."""
+    name = "config5"
+    scaling = "weak"  # replicas: every rank prefills its own sequence
+    bound = "tensor"
+    FLOPS = 103095992320  # 32 heads x (2048*2048 + 2048*2049/2) key pairs x 2*2*128
+    e2e_steps = 50        # each end-to-end step moves 82 MB over PCIe
+
+    def __init__(self, seed: int, n_q=32, n_kv=8, hd=128, pos0=2048, n=2048):
+        import torch
+        from tailorquantkernel_b200 import tqk
+        self.tqk = tqk
+        self.L, self.nq, self.nkv, self.hd, self.pos0, self.n = 1, n_q, n_kv, hd, pos0, n
+        self.mt = pos0 + n
+        self.nb = hd // QK
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        kf = torch.zeros(n_kv, self.mt, hd, device="cuda")
+        vf = torch.zeros(n_kv, self.mt, hd, device="cuda")
+        kf[:, :pos0] = torch.randn(n_kv, pos0, hd, device="cuda", generator=g)
+        vf[:, :pos0] = torch.randn(n_kv, pos0, hd, device="cuda", generator=g)
+        self.kp, self.vp = tqk.quantize_rows(kf), tqk.quantize_rows(vf)
+        del kf, vf
+        self.q = torch.randn(n, n_q * hd, device="cuda", generator=g)
+        self.k_new = torch.randn(n, n_kv * hd, device="cuda", generator=g)
+        self.v_new = torch.randn(n, n_kv * hd, device="cuda", generator=g)
+        self.out = torch.empty(n, n_q * hd, device="cuda")
+        self.tokens_per_step = n
+        self.launches_per_step = 2  # the append and the attention
+        self.bytes_per_step = 2 * n_kv * self.mt * self.nb * BB
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_k = self.k_new.cpu().pin_memory()
+        self.h_v = self.v_new.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = (self.h_q.numel() + self.h_k.numel() + self.h_v.numel()) * 4
+        self.d2h = self.h_out.numel() * 4
+
+    def step(self):
+        self.tqk.prefill(self.kp, self.vp, self.nq, self.nkv, self.hd, self.mt, self.pos0, self.n, self.q,
+                         self.k_new, self.v_new, self.out)
+
+    def step_e2e(self):
+        import torch
+        s = torch.cuda.current_stream()
+        self.q.copy_(self.h_q, non_blocking=True)
+        self.k_new.copy_(self.h_k, non_blocking=True)
+        self.v_new.copy_(self.h_v, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+        s.synchronize()
+
+    def describe(self):
+        return {"workload": "config5: chunked causal prefill, 2048 new tokens at positions 2048..4095 over a "
+                            "2048-position Q8 cache, 32 q / 8 kv heads, head_dim 128",
+                "tokens_per_step": self.n, "flops_per_step": self.FLOPS,
+                "l2": "the 2.4 MB of Q8 K/V per kv head is L2-resident by design; timed back to back"}
+
+    @staticmethod
+    def parallelism(world):
+        return "replicas: one sequence per GPU, no collective" if world > 1 else "single GPU"
+
+    def host_planes(self):
+        return (self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), self.k_new.cpu().numpy(),
+                self.v_new.cpu().numpy())
+
+
 class HostConfig2:
     """Config 2 built on the host only, for the reference arm: K/V ~ N(0,1) per
     layer quantised by the reference's own quantize_row_q8."""
@@ -362,6 +439,34 @@ class HostConfig4:
                 "layers": 1, "seq_len": self.n, "kv_bytes_per_token": self.kv_bytes}
 
 
+class HostConfig5:
+    """Config 5 built on the host only, for the reference arm."""
+    name = "config5"
+    FLOPS = Config5.FLOPS
+
+    def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, pos0=2048, n=2048):
+        self.L, self.nq, self.nkv, self.hd, self.pos0, self.n = 1, n_q, n_kv, hd, pos0, n
+        self.mt = pos0 + n
+        rng = np.random.default_rng(seed)
+        row = hd // QK * BB
+        kf = np.zeros((n_kv, self.mt, hd), np.float32)
+        vf = np.zeros((n_kv, self.mt, hd), np.float32)
+        kf[:, :pos0] = rng.standard_normal((n_kv, pos0, hd), dtype=np.float32)
+        vf[:, :pos0] = rng.standard_normal((n_kv, pos0, hd), dtype=np.float32)
+        self.kp = orc.quantize_rows_bulk(kf).reshape(n_kv, self.mt, row)
+        self.vp = orc.quantize_rows_bulk(vf).reshape(n_kv, self.mt, row)
+        self.q = rng.standard_normal((n, n_q * hd), dtype=np.float32)
+        self.k_new = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+        self.v_new = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+        self.bytes_per_step = 2 * n_kv * self.mt * row
+
+    def host_planes(self):
+        return self.kp, self.vp, self.q, self.k_new, self.v_new
+
+    def describe(self):
+        return Config5.describe(self)
+
+
 # ---------------------------------------------------------------------------
 # reference CPU path (oracle/_ref: the reference's AVX2 build) -- baseline only
 # ---------------------------------------------------------------------------
@@ -390,18 +495,39 @@ def reference_token_seconds(orc, wl, budget_s: float, max_tokens: int | None = N
     return statistics.median(times), len(times), threads
 
 
+def reference_prefill_token_seconds(orc, wl, budget_s: float, sample: int = 32, min_reps: int = 2):
+    """Times the reference's CPU attention_layer_batch path (append + causal
+    attention, all host threads) on the first `sample` tokens of the chunk,
+    repeated until `budget_s` passes.  Returns (median seconds per token,
+    tokens timed, threads)."""
+    threads = os.cpu_count() or 1
+    kp, vp, q, kn, vn = wl.host_planes()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < min_reps:
+        t0 = time.perf_counter()
+        orc.prefill(kp, vp, wl.nq, wl.nkv, wl.hd, wl.mt, wl.pos0, sample, q[:sample], kn[:sample], vn[:sample],
+                    threads=threads)
+        times.append((time.perf_counter() - t0) / sample)
+    return statistics.median(times), len(times) * sample, threads
+
+
 def run_reference(args):
     rank, local, world = dist_init(args.gpus)
     if rank != 0:
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
-    wl = HostConfig2(orc, seed=1000) if args.config == 2 else HostConfig4(orc, seed=4000)
-    # bounded: at most --steps whole tokens, stopping after ~60 s of CPU work
-    reference_token_seconds(orc, wl, 0.0, max_tokens=args.warmup, min_tokens=args.warmup)
-    sec, n, threads = reference_token_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
-                                              min_tokens=min(args.steps, 3))
+    if args.config == 5:
+        wl = HostConfig5(orc, seed=5000)
+        sec, n, threads = reference_prefill_token_seconds(orc, wl, args.ref_seconds)
+    else:
+        wl = HostConfig2(orc, seed=1000) if args.config == 2 else HostConfig4(orc, seed=4000)
+        # bounded: at most --steps whole tokens, stopping after ~60 s of CPU work
+        reference_token_seconds(orc, wl, 0.0, max_tokens=args.warmup, min_tokens=args.warmup)
+        sec, n, threads = reference_token_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
+                                                  min_tokens=min(args.steps, 3))
     value = 1.0 / sec
-    scaling = "weak" if args.config == 2 else "strong"
+    scaling = "strong" if args.config == 4 else "weak"
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
             "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "impl": "reference",
@@ -409,7 +535,7 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                              "sample": f"{n} whole tokens of {wl.name} ({wl.L} layer(s)), median per token, "
                                        f"~{args.ref_seconds:.0f} s budget"},
-            "hbm_gbs_equivalent": wl.bytes_per_step / sec / 1e9,
+            "hbm_gbs_equivalent": wl.bytes_per_step / sec / 1e9 * (wl.n if args.config == 5 else 1),
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -426,7 +552,12 @@ def run_ours(args):
     from tailorquantkernel_b200 import tqk
     peak, peak_kind = _peaks()
 
-    wl = Config2(seed=1000 + rank) if args.config == 2 else Config4(seed=4000, rank=rank, world=world, dist=dist)
+    if args.config == 2:
+        wl = Config2(seed=1000 + rank)
+    elif args.config == 4:
+        wl = Config4(seed=4000, rank=rank, world=world, dist=dist)
+    else:
+        wl = Config5(seed=5000 + rank)
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -445,16 +576,23 @@ def run_ours(args):
     status = tqk.device_status()
 
     # end to end through the C ABI with host buffers (pinned H2D of q/k/v, D2H of out)
+    e2e_steps = min(args.steps, getattr(wl, "e2e_steps", args.steps))
     for _ in range(2):
         wl.step_e2e()
     barrier(dist)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         wl.step_e2e()
     t_e2e = max_over_ranks(dist, time.perf_counter() - t0)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config5":
+        orc, kind = reference_oracle()
+        sec, n, threads = reference_prefill_token_seconds(orc, wl, args.cpu_seconds)
+        cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{n} tokens: the first 32 tokens of the chunk through the reference's append + causal "
+                         f"attention, repeated for ~{args.cpu_seconds:.0f} s, median per token"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         orc, kind = reference_oracle()
         sec, n, threads = reference_token_seconds(orc, wl, args.cpu_seconds)
         cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
@@ -468,8 +606,20 @@ def run_ours(args):
         # the decode kernel's share of a step: one launch per step (config 4 at N > 1 adds the
         # all-gather and the merge, so this per-step figure understates the kernel's rate there)
         per_launch = t_local / args.steps
-        achieved = wl.bytes_per_step / per_launch / 1e9
-        traffic = _traffic_from_profile("decode_q8_" + wl.name)
+        if getattr(wl, "bound", "hbm") == "tensor":
+            tpeak, tpeak_kind = _tensor_peak()
+            achieved = wl.FLOPS / per_launch / 1e12
+            roofline = {"bound": "tensor", "achieved": achieved, "peak": tpeak, "unit": "TFLOP/s",
+                        "frac": achieved / tpeak, "peak_kind": tpeak_kind,
+                        "algorithmic_flops_per_step": wl.FLOPS,
+                        "note": "step time includes the 2048-row Q8 append (a separate small kernel)",
+                        "traffic": _traffic_from_profile("prefill_q8_" + wl.name)}
+        else:
+            achieved = wl.bytes_per_step / per_launch / 1e9
+            roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_kind": peak_kind,
+                        "algorithmic_bytes_per_launch": wl.bytes_per_step,
+                        "traffic": _traffic_from_profile("decode_q8_" + wl.name)}
         jobs = world if wl.scaling == "weak" else 1  # weak: every rank runs its own sequence
         line = {
             "metric": METRIC,
@@ -481,17 +631,14 @@ def run_ours(args):
             "dtype": "int8+fp32",
             "data": "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q",
             "config": {**wl.describe(), "global_batch": jobs, "parallelism": wl.parallelism(world)},
-            "hbm_gbs": achieved,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": wl.bytes_per_step,
-                         "traffic": traffic},
+            "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": jobs * args.steps / t_e2e, "unit": "tokens/s",
+            "e2e": {"value": jobs * e2e_steps * wl.tokens_per_step / t_e2e, "unit": "tokens/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
                     "api": "tqk_decode_q8 (C ABI) with pinned host inputs (q, and the appended k/v for "
                            "config 2) in and the attention output out, stream-synchronised every step"},
             "gpu_launches": args.steps * wl.launches_per_step,
+            **({"hbm_gbs": achieved} if roofline["bound"] == "hbm" else {}),
             "clocks": clk.summary(),
             "device_status": status,
         }
@@ -507,7 +654,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4, 5])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")

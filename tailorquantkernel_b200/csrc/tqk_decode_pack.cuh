@@ -41,15 +41,19 @@ struct PackLayout {
     static constexpr int HD = NB * QK;
     static constexpr int ROW = NB * BLOCK_BYTES;
     static constexpr int TILE = PK_T * ROW;       // one plane of one kv head
+    // planes K_A, K_B, V_A, V_B of a stage, 16 bytes apart beyond the tile: TILE is a
+    // multiple of 128 bytes, so without the pad head A and head B rows would share banks
+    static constexpr int PLANE = TILE + 16;
     static constexpr int STAGES = TQK_PK_STAGES;
-    static constexpr int STAGE_BYTES = 4 * TILE;  // K_A, K_B, V_A, V_B
+    static constexpr int STAGE_BYTES = 4 * PLANE;
     static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
     static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [8][HD]
     static constexpr int OFF_QD = OFF_QQ + 8 * HD;                              // float [8][NB]
     static constexpr int OFF_NEW = OFF_QD + ((8 * NB * 4 + 15) / 16) * 16;     // appended rows [head][K,V][ROW]
     static constexpr int OFF_FLAG = OFF_NEW + ((4 * ROW + 15) / 16) * 16;
     static constexpr int BYTES = OFF_FLAG + 16;
-    static constexpr int RED_FLOATS = PK_WARPS * 8 * HD;
+    static constexpr int RED_STRIDE = HD + 1;  // reduction rows padded: the 32 lanes' stores hit 32 banks
+    static constexpr int RED_FLOATS = PK_WARPS * 8 * RED_STRIDE;
     static constexpr int SCRATCH_FLOATS = RED_FLOATS + 3 * PK_WARPS * 8 + 2 * 8 + 2 * MAX_SPLITS * 8;
     static_assert(SCRATCH_FLOATS * 4 <= OFF_BAR, "stage ring too small for the epilogue scratch");
 };
@@ -238,16 +242,18 @@ __device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a,
 template <int NB>
 __device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int qh0, int warp, int lane, int8_t *qq,
                                             float *qd) {
-    constexpr int HD = NB * QK, QR = 8 / PK_WARPS;
+    constexpr int HD = NB * QK, QR = (8 + PK_WARPS - 1) / PK_WARPS;
     const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
     float x[QR][NB];  // loads first
 #pragma unroll
     for (int r = 0; r < QR; r++)
 #pragma unroll
-        for (int b = 0; b < NB; b++) x[r][b] = __ldg(qsrc + (warp + PK_WARPS * r) * HD + b * QK + lane);
+        for (int b = 0; b < NB; b++)
+            x[r][b] = warp + PK_WARPS * r < 8 ? __ldg(qsrc + (warp + PK_WARPS * r) * HD + b * QK + lane) : 0.0f;
 #pragma unroll
     for (int r = 0; r < QR; r++) {
         const int g = warp + PK_WARPS * r;
+        if (g >= 8) break;
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float d;
@@ -371,9 +377,9 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         const long long o = (long long)t0 * ROW;
         mbar_arrive_expect_tx(&full[slot], 4 * bytes);
         bulk_copy_g2s(st, ka + o, bytes, &full[slot]);
-        bulk_copy_g2s(st + L::TILE, ka + head_bytes + o, bytes, &full[slot]);
-        bulk_copy_g2s(st + 2 * L::TILE, va + o, bytes, &full[slot]);
-        bulk_copy_g2s(st + 3 * L::TILE, va + head_bytes + o, bytes, &full[slot]);
+        bulk_copy_g2s(st + L::PLANE, ka + head_bytes + o, bytes, &full[slot]);
+        bulk_copy_g2s(st + 2 * L::PLANE, va + o, bytes, &full[slot]);
+        bulk_copy_g2s(st + 3 * L::PLANE, va + head_bytes + o, bytes, &full[slot]);
     };
 
     const int producer = PK_WARPS * 32;
@@ -431,8 +437,8 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         const int nvalid = rows - r0;
         if (nvalid > 0) {
             uint8_t *stg = smem + slot * L::STAGE_BYTES;
-            uint8_t *k_a = stg + r0 * ROW, *k_b = stg + L::TILE + r0 * ROW;
-            uint8_t *v_a = stg + 2 * L::TILE + r0 * ROW, *v_b = stg + 3 * L::TILE + r0 * ROW;
+            uint8_t *k_a = stg + r0 * ROW, *k_b = stg + L::PLANE + r0 * ROW;
+            uint8_t *v_a = stg + 2 * L::PLANE + r0 * ROW, *v_b = stg + 3 * L::PLANE + r0 * ROW;
             if (do_append) pack_patch<NB>(pos, t0, r0, lane, k_a, k_b, v_a, v_b, newrow);
             if (nvalid >= PK_ROWS)
                 pack_step<NB, true>(st, k_a, k_b, v_a, v_b, nvalid, p.scale, g, t, hb, mask_a, mask_b);
@@ -448,7 +454,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     cta_sync<1, PK_WARPS * 32>();
     if (*timeout) return;
 
-    float *red = reinterpret_cast<float *>(smem);  // [W][8][HD]
+    float *red = reinterpret_cast<float *>(smem);  // [W][8][RED_STRIDE]
     float *wm = red + L::RED_FLOATS;               // [W][8]
     float *wl = wm + PK_WARPS * 8;
     float *wsc = wl + PK_WARPS * 8;
@@ -465,8 +471,8 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
 #pragma unroll
         for (int jj = 0; jj < 4; jj++) {
             const int c = b * QK + 8 * t + jj;  // permuted n-tile column n = 2t, 2t+1 -> 4n + jj
-            red[(warp * 8 + g) * HD + c] = st.acc[b][jj][0] * unscale;
-            red[(warp * 8 + g) * HD + c + 4] = st.acc[b][jj][1] * unscale;
+            red[(warp * 8 + g) * L::RED_STRIDE + c] = st.acc[b][jj][0] * unscale;
+            red[(warp * 8 + g) * L::RED_STRIDE + c + 4] = st.acc[b][jj][1] * unscale;
         }
     cta_sync<1, PK_WARPS * 32>();
     if (tid < 8) {
@@ -488,7 +494,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     auto acc_of = [&](int gg, int c) {
         float a = 0.0f;
 #pragma unroll
-        for (int w = 0; w < PK_WARPS; w++) a = fmaf(red[(w * 8 + gg) * HD + c], wsc[w * 8 + gg], a);
+        for (int w = 0; w < PK_WARPS; w++) a = fmaf(red[(w * 8 + gg) * L::RED_STRIDE + c], wsc[w * 8 + gg], a);
         return a;
     };
     finish_split<HD, 8, PK_WARPS * 32, 1>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, fm, fl, wts, flag);

@@ -256,10 +256,13 @@ __global__ void __launch_bounds__(PF_THREADS, PF_CTAS_PER_SM) prefill_q8_tc_kern
         const int rows = min(PF_KT, n_keys - j * PF_KT);
 
         // K: int8 block values -> canonical K-major operand, scales -> kdT
-        //    (16-byte pieces (key, block, half), PF_KT*8 of them over PF_NT threads)
+        //    (16-byte pieces (key, block, half), PF_KT*8 of them over PF_NT threads).  A warp takes
+        //    8 consecutive keys x 4 blocks: each 8-lane store phase fills one 128-byte row of core
+        //    matrices, and the 32 loads of a warp fall in 32 different banks.
 #pragma unroll
         for (int id = tid; id < PF_KT * PF_NB * 2; id += PF_NT) {
-            const int key = id >> 3, b = (id >> 1) & 3, half = id & 1;
+            const int ln = id & 31, grp = id >> 5;
+            const int key = (ln & 7) + 8 * (grp % (PF_KT / 8)), b = ln >> 3, half = grp / (PF_KT / 8);
             const uint32_t *src = reinterpret_cast<const uint32_t *>(rk + key * PF_ROW + b * BLOCK_BYTES + 4 + 16 * half);
             uint32_t w[4];
 #pragma unroll
@@ -274,7 +277,10 @@ __global__ void __launch_bounds__(PF_THREADS, PF_CTAS_PER_SM) prefill_q8_tc_kern
         // V: dequantise v * vd to fp16 hi + lo (8 columns per chunk)
 #pragma unroll 2
         for (int i = 0; i < PF_KT * PF_HD / 8 / PF_NT; i++) {
-            const int id = tid + PF_NT * i, key = id >> 4, cg = id & 15, b = cg >> 2;
+            // a warp takes 8 consecutive keys x 4 blocks at one 8-column offset: conflict-free
+            // 16-byte stores (one 128-byte core-matrix row per phase) and 32 banks for the loads
+            const int id = tid + PF_NT * i, ln = id & 31, grp = id >> 5;
+            const int key = (ln & 7) + 8 * (grp % (PF_KT / 8)), b = ln >> 3, cg = 4 * b + grp / (PF_KT / 8);
             const uint8_t *row = rv + key * PF_ROW + b * BLOCK_BYTES;
             const float vd = key < rows ? *reinterpret_cast<const float *>(row) : 0.0f;
             uint32_t w0 = 0u, w1 = 0u;
