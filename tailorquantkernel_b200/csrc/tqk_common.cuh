@@ -163,6 +163,15 @@ __device__ __forceinline__ void cta_sync() {
     }
 }
 
+// 2^x as the MUFU computes it (ex2.approx, denormal results flushed to zero):
+// exact at x = 0 and 0 at x = -inf.  Softmax weights need ~11 bits; the
+// running-max correction is written as 1 exactly when the max is unchanged.
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ----------------------------------------------------------------------------
 // int8 helpers
 // ----------------------------------------------------------------------------

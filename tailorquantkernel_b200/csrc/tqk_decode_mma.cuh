@@ -239,11 +239,11 @@ __device__ __forceinline__ void mma_slice(SliceState<NB, HI> &st, const uint8_t 
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float mn = fmaxf(st.m_lo, mx);
-        corr_lo = exp2f(st.m_lo - mn);
-        pr[0][0] = exp2f(sc[0][0] - mn);
-        pr[0][1] = exp2f(sc[0][1] - mn);
-        pr[1][0] = exp2f(sc[1][0] - mn);
-        pr[1][1] = exp2f(sc[1][1] - mn);
+        corr_lo = mn == st.m_lo ? 1.0f : ex2f(st.m_lo - mn);
+        pr[0][0] = ex2f(sc[0][0] - mn);
+        pr[0][1] = ex2f(sc[0][1] - mn);
+        pr[1][0] = ex2f(sc[1][0] - mn);
+        pr[1][1] = ex2f(sc[1][1] - mn);
         float sum = (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
@@ -255,11 +255,11 @@ __device__ __forceinline__ void mma_slice(SliceState<NB, HI> &st, const uint8_t 
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float mn = fmaxf(st.m_hi, mx);
-        corr_hi = exp2f(st.m_hi - mn);
-        pr[0][2] = exp2f(sc[0][2] - mn);
-        pr[0][3] = exp2f(sc[0][3] - mn);
-        pr[1][2] = exp2f(sc[1][2] - mn);
-        pr[1][3] = exp2f(sc[1][3] - mn);
+        corr_hi = mn == st.m_hi ? 1.0f : ex2f(st.m_hi - mn);
+        pr[0][2] = ex2f(sc[0][2] - mn);
+        pr[0][3] = ex2f(sc[0][3] - mn);
+        pr[1][2] = ex2f(sc[1][2] - mn);
+        pr[1][3] = ex2f(sc[1][3] - mn);
         float sum = (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);

@@ -158,8 +158,8 @@ __device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a,
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float mn = fmaxf(st.m, mx);
-    const float corr = exp2f(st.m - mn);
-    const float p0 = exp2f(s0 - mn), p1 = exp2f(s1 - mn), p2 = exp2f(s2 - mn), p3 = exp2f(s3 - mn);
+    const float corr = mn == st.m ? 1.0f : ex2f(st.m - mn);
+    const float p0 = ex2f(s0 - mn), p1 = ex2f(s1 - mn), p2 = ex2f(s2 - mn), p3 = ex2f(s3 - mn);
     float sum = (p0 + p1) + (p2 + p3);
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
