@@ -315,6 +315,77 @@ def rope_np(x, hd, pos, theta):
     return h.astype(np.float32).reshape(x.shape)
 
 
+class Config3:
+    """Ragged batched decode: 64 sequences, lengths uniform
+    in [512, 8192], 32 q / 8 kv heads, head_dim 128, K/V ~ N(0,1) with 1% of
+    the entries x8 (outlier blocks).  One launch attends every sequence of
+    the rank's share (ragged device lengths).  With N ranks the 64 sequences
+    are divided by total length (shard.batch_shard); one step = one token
+    for each of the 64 sequences."""
+    name = "config3"
+    scaling = "strong"  # the batch of 64 is fixed; each rank takes a share
+    B = 64
+
+    def __init__(self, seed: int, rank: int = 0, world: int = 1, n_q=32, n_kv=8, hd=128, mt=8192):
+        import torch
+        from tailorquantkernel_b200 import shard, tqk
+        self.tqk = tqk
+        self.L, self.nq, self.nkv, self.hd, self.mt = 1, n_q, n_kv, hd, mt
+        self.nb = hd // QK
+        rng = np.random.default_rng(seed)
+        self.all_lens = rng.integers(512, mt + 1, self.B).astype(np.int32)
+        self.mine = shard.batch_shard(self.all_lens, world)[rank]
+        lens = self.all_lens[self.mine]
+        nloc = len(self.mine)
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.kp = torch.empty(nloc, n_kv, mt, self.nb * BB, dtype=torch.uint8, device="cuda")
+        self.vp = torch.empty_like(self.kp)
+        for i in range(nloc):  # one sequence at a time: bounded fp32 scratch
+            for plane in (self.kp, self.vp):
+                x = torch.randn(n_kv, mt, hd, device="cuda", generator=g)
+                x = torch.where(torch.rand(n_kv, mt, hd, device="cuda", generator=g) < 0.01, x * 8, x)
+                plane[i] = tqk.quantize_rows(x).view(n_kv, mt, self.nb * BB)
+        self.lens = torch.from_numpy(lens).cuda()
+        self.q = torch.randn(nloc, n_q * hd, device="cuda", generator=g)
+        self.out = torch.empty(nloc, n_q * hd, device="cuda")
+        self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, mt, self.q, self.out, n_items=nloc,
+                                    item_stride_blocks=n_kv * mt * self.nb, lens=self.lens,
+                                    max_len=int(lens.max()), q_item_stride=n_q * hd, out_item_stride=n_q * hd)
+        self.kv_bytes = 2 * n_kv * int(self.all_lens.sum()) * self.nb * BB  # the whole batch
+        self.bytes_per_step = 2 * n_kv * int(lens.sum()) * self.nb * BB   # this rank's decode kernel
+        self.tokens_per_step = self.B  # for the whole job: each step is one token of every sequence
+        self.launches_per_step = 1
+        self.h_q = self.q.cpu().pin_memory()
+        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
+        self.h2d = self.h_q.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+
+    def step(self):
+        self.tqk.decode(self.args)
+
+    def step_e2e(self):
+        import torch
+        s = torch.cuda.current_stream()
+        self.q.copy_(self.h_q, non_blocking=True)
+        self.tqk.decode(self.args)
+        self.h_out.copy_(self.out, non_blocking=True)
+        s.synchronize()
+
+    def describe(self):
+        return {"workload": "config3: ragged batched Q8 GQA decode, 64 sequences, lengths U[512, 8192] "
+                            f"(sum {int(self.all_lens.sum())}), 32 q / 8 kv heads, head_dim 128, 1% x8 outliers",
+                "layers": 1, "batch": self.B, "sequences_per_rank": len(self.mine),
+                "kv_bytes_per_step": self.kv_bytes,
+                "l2": "no flush: inputs larger than L2 (628 MB of K/V per step vs 126 MB L2)"}
+
+    @staticmethod
+    def parallelism(world):
+        return (f"batch-sharded over {world} GPUs by total length, no collective" if world > 1 else "single GPU")
+
+    def host_planes(self):
+        raise NotImplementedError("the CPU baseline of config 3 uses HostConfig3")
+
+
 class Config5:
     """Chunked causal prefill: 2048 new tokens at positions
     2048..4095 appended to a Q8 cache holding 2048 prior positions, each
@@ -413,6 +484,36 @@ class HostConfig2:
         return Config2.describe(self)
 
 
+class HostConfig3:
+    """Config 3 on the host for the reference CPU path: the batch's lengths, with
+    planes built (reference quantiser) for the first 4 sequences only -- the
+    bounded sample the CPU baseline times."""
+    name = "config3"
+
+    def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, mt=8192, sample=4):
+        self.L, self.nq, self.nkv, self.hd, self.mt = 1, n_q, n_kv, hd, mt
+        rng = np.random.default_rng(seed)
+        self.all_lens = rng.integers(512, mt + 1, Config3.B).astype(np.int32)
+        self.sample = list(range(sample))
+        self.sample_lens = self.all_lens[:sample]
+        row = hd // QK * BB
+        self.kp, self.vp = [], []
+        for i in self.sample:
+            n = int(self.sample_lens[i])
+            for planes in (self.kp, self.vp):
+                x = rng.standard_normal((n_kv, mt, hd), dtype=np.float32)
+                x[:, n:] = 0.0
+                x = np.where(rng.random((n_kv, mt, hd), dtype=np.float32) < 0.01, x * 8, x)
+                planes.append(orc.quantize_rows_bulk(x).reshape(n_kv, mt, row))
+        self.q = rng.standard_normal((sample, n_q * hd), dtype=np.float32)
+        self.bytes_per_step = 2 * n_kv * int(self.all_lens.sum()) * row
+        self.n = 1
+
+    def describe(self):
+        return {"workload": "config3: ragged batched Q8 GQA decode, 64 sequences, lengths U[512, 8192], "
+                            "32 q / 8 kv heads, head_dim 128, 1% x8 outliers"}
+
+
 class HostConfig4:
     """Config 4 built on the host only, for the reference arm (one layer, 64 q /
     8 kv heads, context 131072, no append)."""
@@ -495,6 +596,23 @@ def reference_token_seconds(orc, wl, budget_s: float, max_tokens: int | None = N
     return statistics.median(times), len(times), threads
 
 
+def reference_ragged_seconds(orc, wl, budget_s: float, min_reps: int = 2):
+    """Times the reference's CPU attend_q8 (all host threads) on the sampled
+    sequences of config 3; returns (median seconds per batch token at the
+    batch's mean length, sequence-tokens timed, threads)."""
+    threads = os.cpu_count() or 1
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < min_reps:
+        t0 = time.perf_counter()
+        for i in range(len(wl.sample)):
+            n = int(wl.sample_lens[i])
+            orc.attend(wl.kp[i], wl.vp[i], wl.nq, wl.nkv, wl.hd, wl.mt, n - 1, wl.q[i], threads=threads)
+        per_key = (time.perf_counter() - t0) / float(wl.sample_lens.sum())  # seconds per cached position
+        times.append(per_key * float(wl.all_lens.mean()))
+    return statistics.median(times), len(times) * len(wl.sample), threads
+
+
 def reference_prefill_token_seconds(orc, wl, budget_s: float, sample: int = 32, min_reps: int = 2):
     """Times the reference's CPU attention_layer_batch path (append + causal
     attention, all host threads) on the first `sample` tokens of the chunk,
@@ -520,6 +638,9 @@ def run_reference(args):
     if args.config == 5:
         wl = HostConfig5(orc, seed=5000)
         sec, n, threads = reference_prefill_token_seconds(orc, wl, args.ref_seconds)
+    elif args.config == 3:
+        wl = HostConfig3(orc, seed=3000)
+        sec, n, threads = reference_ragged_seconds(orc, wl, args.ref_seconds)
     else:
         wl = HostConfig2(orc, seed=1000) if args.config == 2 else HostConfig4(orc, seed=4000)
         # bounded: at most --steps whole tokens, stopping after ~60 s of CPU work
@@ -527,7 +648,7 @@ def run_reference(args):
         sec, n, threads = reference_token_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
                                                   min_tokens=min(args.steps, 3))
     value = 1.0 / sec
-    scaling = "strong" if args.config == 4 else "weak"
+    scaling = "strong" if args.config in (3, 4) else "weak"
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
             "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "impl": "reference",
@@ -535,7 +656,8 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                              "sample": f"{n} whole tokens of {wl.name} ({wl.L} layer(s)), median per token, "
                                        f"~{args.ref_seconds:.0f} s budget"},
-            "hbm_gbs_equivalent": wl.bytes_per_step / sec / 1e9 * (wl.n if args.config == 5 else 1),
+            "hbm_gbs_equivalent": (wl.bytes_per_step / Config3.B if args.config == 3 else wl.bytes_per_step)
+                                  / sec / 1e9 * (wl.n if args.config == 5 else 1),
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -554,6 +676,8 @@ def run_ours(args):
 
     if args.config == 2:
         wl = Config2(seed=1000 + rank)
+    elif args.config == 3:
+        wl = Config3(seed=3000, rank=rank, world=world)
     elif args.config == 4:
         wl = Config4(seed=4000, rank=rank, world=world, dist=dist)
     else:
@@ -586,7 +710,14 @@ def run_ours(args):
     t_e2e = max_over_ranks(dist, time.perf_counter() - t0)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config5":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config3":
+        orc, kind = reference_oracle()
+        sec, n, threads = reference_ragged_seconds(orc, HostConfig3(orc, seed=3000), args.cpu_seconds)
+        cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{n} sequence-tokens of config 3 (the first 4 sequences through the reference's "
+                         f"attend_q8), ~{args.cpu_seconds:.0f} s budget, median per token, scaled to the batch's "
+                         f"mean length"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config5":
         orc, kind = reference_oracle()
         sec, n, threads = reference_prefill_token_seconds(orc, wl, args.cpu_seconds)
         cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
@@ -654,7 +785,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")

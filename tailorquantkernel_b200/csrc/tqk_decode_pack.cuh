@@ -106,6 +106,52 @@ struct PackState {
     }
 };
 
+// Scores of lane (g, t)'s row for tokens 2t, 2t+1 (n-tile 0) and 8+2t, 9+2t
+// (n-tile 1) of its head, in log2 units; masked tokens are -inf.  Rounded as
+// the reference: acc += (float)dot * (qd*kd) per block, then * scale.
+template <int NB, bool FULL>
+__device__ __forceinline__ void pack_scores(const uint32_t (&qa)[NB][2], const uint32_t (&qb)[NB][2],
+                                            const f32x2 (&qd2)[NB], const uint8_t *k_a, const uint8_t *k_b,
+                                            const uint8_t *kmine, int nvalid, float scale, int g, int t, float &s0,
+                                            float &s1, float &s2, float &s3) {
+    constexpr int ROW = NB * BLOCK_BYTES;
+    // ---- scores of row g for tokens 2t, 2t+1 (n-tile 0) and 8+2t, 9+2t (n-tile 1),
+    //      rounded exactly as the reference: acc += (float)dot * (qd*kd) per block
+    f32x2 sc0 = pk2(0.0f, 0.0f), sc1 = pk2(0.0f, 0.0f);
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+        const int kb = b * BLOCK_BYTES + 4 + 4 * t;
+        int c00 = 0, c01 = 0, c10 = 0, c11 = 0;
+        mma_s8_k32_lo(c00, c01, qa[b][0], qa[b][1], *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb + 16));
+        mma_s8_k32_lo(c10, c11, qa[b][0], qa[b][1],
+                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb + 16));
+        mma_s8_k32_lo(c00, c01, qb[b][0], qb[b][1], *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb + 16));
+        mma_s8_k32_lo(c10, c11, qb[b][0], qb[b][1],
+                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb),
+                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb + 16));
+        const uint8_t *kd = kmine + (2 * t) * ROW + b * BLOCK_BYTES;
+        const f32x2 kd0 = pk2(*reinterpret_cast<const float *>(kd), *reinterpret_cast<const float *>(kd + ROW));
+        const f32x2 kd1 =
+            pk2(*reinterpret_cast<const float *>(kd + 8 * ROW), *reinterpret_cast<const float *>(kd + 9 * ROW));
+        sc0 = add2(sc0, mul2(pk2(__int2float_rn(c00), __int2float_rn(c01)), mul2(qd2[b], kd0)));
+        sc1 = add2(sc1, mul2(pk2(__int2float_rn(c10), __int2float_rn(c11)), mul2(qd2[b], kd1)));
+    }
+    const f32x2 sl2 = pk2(scale, scale), l2e = pk2(1.4426950408889634f, 1.4426950408889634f);
+    // the reference's scores (acc * scale), then in log2 units
+    upk2(mul2(mul2(sc0, sl2), l2e), s0, s1);
+    upk2(mul2(mul2(sc1, sl2), l2e), s2, s3);
+    if constexpr (!FULL) {
+        if (2 * t >= nvalid) s0 = -INFINITY;
+        if (2 * t + 1 >= nvalid) s1 = -INFINITY;
+        if (8 + 2 * t >= nvalid) s2 = -INFINITY;
+        if (9 + 2 * t >= nvalid) s3 = -INFINITY;
+    }
+
+}
+
 // One warp step: tokens 0-15 of kv head A (k_a, v_a) and of kv head B (k_b,
 // v_b), 144*NB/4-byte rows; FULL steps skip the masking of tokens >= nvalid.
 // g = lane/4, t = lane%4, hb = g >= 4; mask_a / mask_b = f16x2 1.0 for the
@@ -118,40 +164,8 @@ __device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a,
     const uint8_t *kmine = hb ? k_b : k_a;  // the lane's own head for scales
     const uint8_t *vmine = hb ? v_b : v_a;
 
-    // ---- scores of row g for tokens 2t, 2t+1 (n-tile 0) and 8+2t, 9+2t (n-tile 1),
-    //      rounded exactly as the reference: acc += (float)dot * (qd*kd) per block
-    f32x2 sc0 = pk2(0.0f, 0.0f), sc1 = pk2(0.0f, 0.0f);
-#pragma unroll
-    for (int b = 0; b < NB; b++) {
-        const int kb = b * BLOCK_BYTES + 4 + 4 * t;
-        int c00 = 0, c01 = 0, c10 = 0, c11 = 0;
-        mma_s8_k32_lo(c00, c01, st.qa[b][0], st.qa[b][1], *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb),
-                      *reinterpret_cast<const uint32_t *>(k_a + g * ROW + kb + 16));
-        mma_s8_k32_lo(c10, c11, st.qa[b][0], st.qa[b][1],
-                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb),
-                      *reinterpret_cast<const uint32_t *>(k_a + (8 + g) * ROW + kb + 16));
-        mma_s8_k32_lo(c00, c01, st.qb[b][0], st.qb[b][1], *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb),
-                      *reinterpret_cast<const uint32_t *>(k_b + g * ROW + kb + 16));
-        mma_s8_k32_lo(c10, c11, st.qb[b][0], st.qb[b][1],
-                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb),
-                      *reinterpret_cast<const uint32_t *>(k_b + (8 + g) * ROW + kb + 16));
-        const uint8_t *kd = kmine + (2 * t) * ROW + b * BLOCK_BYTES;
-        const f32x2 kd0 = pk2(*reinterpret_cast<const float *>(kd), *reinterpret_cast<const float *>(kd + ROW));
-        const f32x2 kd1 =
-            pk2(*reinterpret_cast<const float *>(kd + 8 * ROW), *reinterpret_cast<const float *>(kd + 9 * ROW));
-        sc0 = add2(sc0, mul2(pk2(__int2float_rn(c00), __int2float_rn(c01)), mul2(st.qd2[b], kd0)));
-        sc1 = add2(sc1, mul2(pk2(__int2float_rn(c10), __int2float_rn(c11)), mul2(st.qd2[b], kd1)));
-    }
-    const f32x2 sl2 = pk2(scale, scale), l2e = pk2(1.4426950408889634f, 1.4426950408889634f);
-    float s0, s1, s2, s3;  // the reference's scores (acc * scale), then in log2 units
-    upk2(mul2(mul2(sc0, sl2), l2e), s0, s1);
-    upk2(mul2(mul2(sc1, sl2), l2e), s2, s3);
-    if constexpr (!FULL) {
-        if (2 * t >= nvalid) s0 = -INFINITY;
-        if (2 * t + 1 >= nvalid) s1 = -INFINITY;
-        if (8 + 2 * t >= nvalid) s2 = -INFINITY;
-        if (9 + 2 * t >= nvalid) s3 = -INFINITY;
-    }
+    float s0, s1, s2, s3;
+    pack_scores<NB, FULL>(st.qa, st.qb, st.qd2, k_a, k_b, kmine, nvalid, scale, g, t, s0, s1, s2, s3);
 
     // ---- online softmax of the row over its 16 tokens (the quad)
     float mx = fmaxf(fmaxf(s0, s1), fmaxf(s2, s3));
@@ -461,11 +475,11 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     float *fm = wsc + PK_WARPS * 8;                // [8]
     float *fl = fm + 8;
     float *wts = fl + 8;                           // [2][MAX_SPLITS][8]
-    const float unscale = exp2_int(st.kscale);
     if (t == 0) {
         wm[warp * 8 + g] = st.m;
         wl[warp * 8 + g] = st.l;
     }
+    const float unscale = exp2_int(st.kscale);
 #pragma unroll
     for (int b = 0; b < NB; b++)
 #pragma unroll
