@@ -86,6 +86,19 @@ __device__ __forceinline__ void mma_f16_k16_lo(float &d0, float &d1, uint32_t a0
         : "r"(a0), "r"(0u), "r"(a2), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
+// P*V with P's hi half in rows 0-7 and its lo half in rows 8-15 of one
+// m16n8k16 (A = {hi k0-7, lo k0-7, hi k8-15, lo k8-15}): the two products come
+// out of one MMA, and the lo rows are added into the hi rows' accumulators.
+__device__ __forceinline__ void mma_f16_k16_hl(float &d0, float &d1, uint32_t h0, uint32_t l0, uint32_t h2,
+                                               uint32_t l2, uint32_t b0, uint32_t b1) {
+    float x2, x3;
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%10,%10};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(h0), "r"(l0), "r"(h2), "r"(l2), "r"(b0), "r"(b1), "f"(0.0f));
+    d0 += x2;
+    d1 += x3;
+}
+
 // Packed fp32 pairs (Blackwell f32x2 ALU ops, each lane of the pair rounded
 // like the scalar instruction).
 typedef unsigned long long f32x2;
@@ -336,8 +349,7 @@ __device__ __forceinline__ void mma_slice(SliceState<NB, HI> &st, const uint8_t 
         mma_f16_k16(a[0], a[1], a[2], a[3], ah0, ah1, ah2, ah3, bb0, bb1);                         \
         mma_f16_k16(a[0], a[1], a[2], a[3], al0, al1, al2, al3, bb0, bb1);                         \
     } else {                                                                                       \
-        mma_f16_k16_lo(a[0], a[1], ah0, ah2, bb0, bb1);                                            \
-        mma_f16_k16_lo(a[0], a[1], al0, al2, bb0, bb1);                                            \
+        mma_f16_k16_hl(a[0], a[1], ah0, al0, ah2, al2, bb0, bb1);                                  \
     }                                                                                              \
 }
         TQK_PV_NTILE(0)
