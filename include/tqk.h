@@ -86,6 +86,24 @@ TQK_API int tqk_store_kv_q8_batch(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, 
                           tqk_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * The step before the attention: per-head RMSNorm of q and k and rotary
+ * embedding, in place.  Replaces norm_heads + rope_heads as attention_layer
+ * calls them (reference model/attention_layer.c:48-60, :183-189;
+ * model/rmsnorm.c:4-19, model/rope.c:14-22), bit-exact with the reference's
+ * fp32 arithmetic so the K rows appended afterwards give identical Q8 bytes.
+ * For each of n_items items: q + i*q_item_stride holds n_q_heads rows and
+ * k + i*k_item_stride n_kv_heads rows of head_dim floats (strides in floats;
+ * 0 = packed).  q_norm / k_norm: [head_dim] weights (+ i*norm_item_stride;
+ * both NULL = no norm).  rope_cos / rope_sin: the [head_dim/2] table of
+ * rope_table (reference model/rope.c:4-12) computed on the host (+
+ * i*rope_item_stride; both NULL = no rope).  head_dim must be even.
+ */
+TQK_API int tqk_qk_norm_rope(float *q, float *k, int n_items, int64_t q_item_stride, int64_t k_item_stride,
+                             int n_q_heads, int n_kv_heads, int head_dim, const float *q_norm, const float *k_norm,
+                             int64_t norm_item_stride, float eps, const float *rope_cos, const float *rope_sin,
+                             int64_t rope_item_stride, tqk_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Reference-shaped single kernels (model/attn_q8.c:56-76 dispatchers and
  * model/softmax.c:4).  These keep the reference's per-op contract (strided score
  * rows, strided outputs, nothing written past n or head_dim) so the reference's
@@ -143,13 +161,26 @@ typedef struct {
     int64_t kv_new_item_stride;
     int out_mode;                 /* TQK_OUT_NORMALIZED or TQK_OUT_PARTIAL */
     int split_tokens;             /* tokens per split (multiple of 64); 0 = choose automatically */
+    /* Optional fused prologue (attention_layer.c:183-189, norm_heads + rope_heads): each q head
+     * of item i, and each appended k_new head, is first RMS-normalised with q_norm / k_norm +
+     * i*norm_item_stride ([head_dim] floats, shared by the heads; both NULL = no norm) and then
+     * rotated with rope_cos / rope_sin + i*rope_item_stride ([head_dim/2] floats, the table of
+     * the appended token's position; both NULL = no rope).  Bit-exact with tqk_qk_norm_rope
+     * followed by the plain call.  q and k_new are read only: the normed rows are not written
+     * back.  Zero-initialise the struct so that callers which set none of these get none. */
+    const float *q_norm, *k_norm;
+    int64_t norm_item_stride;
+    float norm_eps;
+    const float *rope_cos, *rope_sin;
+    int64_t rope_item_stride;
 } tqk_decode_args;
 
 /* Bytes of device workspace tqk_decode_q8 needs for these arguments. */
 TQK_API int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes);
-/* A caller workspace starts with the split-merge tickets (one int per item and
- * head unit, at least 64 KiB) followed by the partials.  It must be zeroed once
- * before first use (tqk_workspace_init); every completed call leaves the
+/* A caller workspace starts with the split-merge tickets (17 ints per item and
+ * head unit, at least 16384 units' worth: 1088 KiB) followed by the partials.
+ * It must be zeroed once before first use (tqk_workspace_init); every
+ * completed call leaves the
  * tickets at zero again, so calls of up to 16384 units (n_items x kv-head
  * units) can reuse it without re-initialising.  Zero it again before a call
  * with more units than any earlier one, and after a call that reported
@@ -163,7 +194,7 @@ TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t work
  * reference): for callers that cannot allocate device memory at run time, for
  * instance a runtime whose memory is fully reserved up front.  The split
  * tickets and partials live in fixed static device arrays of this library
- * (16384 tickets, 4 MiB of partials, present from module load); nothing else
+ * (tickets for 16384 units, 4 MiB of partials, present from module load); nothing else
  * is allocated, not even the device error word.  Same arguments, results and
  * automatic split as tqk_decode_q8.
  *   - Calls whose split needs more than 16384 (item, head unit) pairs or more

@@ -42,6 +42,9 @@ _NAMES = {
     "store_kv": ("tqo_store_kv_q8", "refdrv_store_kv_q8"),
     "attend": ("tqo_attend_q8", "refdrv_attend_q8"),
     "prefill": ("tqo_prefill_q8", "refdrv_prefill_q8"),
+    "rmsnorm": ("tqo_rmsnorm", "rmsnorm"),
+    "rope_table": ("tqo_rope_table", "rope_table"),
+    "rope_apply": ("tqo_rope_apply", "rope_apply"),
 }
 
 
@@ -89,6 +92,11 @@ class Oracle:
         self._fn["store_kv"].argtypes = [vp, vp, i, i, i, i, vp, vp]
         self._fn["attend"].argtypes = [vp, vp, i, i, i, i, i, vp, vp, vp, i]
         self._fn["prefill"].argtypes = [vp, vp, i, i, i, i, i, i, vp, vp, vp, vp, vp, i]
+        self._fn["rmsnorm"].argtypes = [vp, vp, vp, i, f]
+        self._fn["rope_table"].argtypes = [vp, vp, i, i, f]
+        self._fn["rope_apply"].argtypes = [vp, i, vp, vp]
+        for k in ("rmsnorm", "rope_table", "rope_apply"):
+            self._fn[k].restype = None
         if kind != "port":
             self.lib.refdrv_max_threads.restype = i
             self.lib.refdrv_quantize_rows.argtypes = [vp, vp, i, i]
@@ -174,6 +182,29 @@ class Oracle:
         if rc != 0:
             raise ValueError(f"prefill returned {rc}")
         return out
+
+    def rope_table(self, head_dim: int, pos: int, theta: float):
+        """(cos, sin) tables of rope_table (model/rope.c:4-12)."""
+        c = np.zeros(head_dim // 2, np.float32)
+        s = np.zeros(head_dim // 2, np.float32)
+        self._fn["rope_table"](_vp(c), _vp(s), head_dim, pos, theta)
+        return c, s
+
+    def qk_norm_rope(self, x, n_heads, head_dim, weight, eps, cos_t, sin_t):
+        """norm_heads + rope_heads as attention_layer applies them (attention_layer.c:183-189):
+        rmsnorm in place per head row, then rope_apply with the table.  weight / cos_t may
+        be None to skip that part.  Returns a new array."""
+        y = np.ascontiguousarray(x, dtype=np.float32).copy()
+        rows = y.reshape(-1, head_dim)
+        for r in range(rows.shape[0]):
+            row = rows[r]
+            if weight is not None:
+                w = np.ascontiguousarray(weight, dtype=np.float32)
+                self._fn["rmsnorm"](_vp(row), _vp(w), _vp(row), head_dim, eps)
+            if cos_t is not None:
+                self._fn["rope_apply"](_vp(row), head_dim, _vp(np.ascontiguousarray(cos_t, dtype=np.float32)),
+                                       _vp(np.ascontiguousarray(sin_t, dtype=np.float32)))
+        return y
 
     def max_threads(self) -> int:
         return self.lib.refdrv_max_threads() if self.kind != "port" else os.cpu_count() or 1

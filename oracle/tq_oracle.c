@@ -195,3 +195,33 @@ void tqo_attention_f64(const float *q, const float *k, const float *v, int n, in
     }
     for (int j = 0; j < head_dim; j++) out[j] /= l;
 }
+
+/* model/rmsnorm.c:4-19: sum of squares in index order, sqrtf(eps + sum/n),
+ * out = x * (1/rms) * w. */
+void tqo_rmsnorm(const float *x, const float *weight, float *out, int n, float eps) {
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum += x[i] * x[i];
+    const float inv_rms = 1.0f / sqrtf(eps + sum / (float)n);
+    for (int i = 0; i < n; i++) out[i] = x[i] * inv_rms * weight[i];
+}
+
+/* model/rope.c:4-12: freq = theta^(-2i/head_dim), angle = pos * freq. */
+void tqo_rope_table(float *cos_t, float *sin_t, int head_dim, int pos, float theta) {
+    const float inv_head_dim = 1.0f / (float)head_dim;
+    for (int i = 0; i < head_dim / 2; i++) {
+        const float freq = powf(theta, -2.0f * i * inv_head_dim);
+        const float a = pos * freq;
+        cos_t[i] = cosf(a);
+        sin_t[i] = sinf(a);
+    }
+}
+
+/* model/rope.c:14-22: rotate (x[i], x[i+half]) by the table. */
+void tqo_rope_apply(float *x, int head_dim, const float *cos_t, const float *sin_t) {
+    const int half = head_dim / 2;
+    for (int i = 0; i < half; i++) {
+        const float x0 = x[i], x1 = x[i + half];
+        x[i] = x0 * cos_t[i] - x1 * sin_t[i];
+        x[i + half] = x0 * sin_t[i] + x1 * cos_t[i];
+    }
+}

@@ -67,6 +67,13 @@ int tqo_prefill_q8(tqo_block_q8 *k_plane, tqo_block_q8 *v_plane, int n_q, int n_
 
 /* Float64 attention of one q head over dequantised data (the reference test's
  * attention_reference, tools/test_model.c:424-454), for tolerance checks. */
+/* model/rmsnorm.c:4-19 */
+void tqo_rmsnorm(const float *x, const float *weight, float *out, int n, float eps);
+/* model/rope.c:4-12 */
+void tqo_rope_table(float *cos_t, float *sin_t, int head_dim, int pos, float theta);
+/* model/rope.c:14-22 */
+void tqo_rope_apply(float *x, int head_dim, const float *cos_t, const float *sin_t);
+
 void tqo_attention_f64(const float *q, const float *k, const float *v, int n, int head_dim,
                        double *out);
 

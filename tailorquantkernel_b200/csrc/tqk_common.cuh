@@ -69,6 +69,74 @@ __device__ __forceinline__ int8_t warp_quantize_block(float x, float *d) {
     return q8_round(x, q8_inverse(s));
 }
 
+// The attention prologue on R head rows of head_dim = NB*32 floats held by a
+// full warp, element b*32 + lane of row r in x[r][b]: RMSNorm with weight w
+// (model/rmsnorm.c:4-19; w == NULL skips it) and then the half-split RoPE
+// rotation with the tables cs/sn of head_dim/2 floats (model/rope.c:14-22;
+// cs == NULL skips it).  Rounds exactly as the reference's scalar C: each
+// row's squares are added in index order as one chain, sqrt and both
+// divisions are IEEE, products and sums are never contracted.  For the chain
+// the squares are staged in `scratch` (R rows of pro_stride<NB>() floats,
+// 16-byte aligned, private to the warp) and lane r walks row r with 16-byte loads, so
+// the R chains run side by side and only the adds are serial.
+constexpr int PRO_PAD = 4;  // floats of padding per staged row: the R lanes' loads hit distinct banks
+template <int NB>
+__host__ __device__ constexpr int pro_stride() { return NB * 32 + PRO_PAD; }
+
+template <int NB, int R>
+__device__ __forceinline__ void warp_norm_rope(float (&x)[R][NB], const float *w, const float *cs, const float *sn,
+                                               float eps, float *scratch, int lane) {
+    static_assert(R <= 32, "one lane per row");
+    constexpr int HD = NB * 32, STRIDE = pro_stride<NB>();
+    if (w) {
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int b = 0; b < NB; b++) scratch[r * STRIDE + b * 32 + lane] = __fmul_rn(x[r][b], x[r][b]);
+        __syncwarp();
+        float sum = 0.0f;
+        if (lane < R) {
+            const float4 *row = reinterpret_cast<const float4 *>(scratch + lane * STRIDE);
+#pragma unroll
+            for (int i = 0; i < HD / 4; i++) {
+                const float4 v = row[i];
+                sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
+            }
+        }
+        __syncwarp();  // the scratch is free again
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const float sr = __shfl_sync(0xffffffffu, sum, r);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(eps, __fdiv_rn(sr, (float)HD))));
+#pragma unroll
+            for (int b = 0; b < NB; b++) x[r][b] = __fmul_rn(__fmul_rn(x[r][b], inv), __ldg(w + b * 32 + lane));
+        }
+    }
+    if (cs) {
+        if constexpr (NB == 1) {
+            // head_dim 32: the pair (i, i + 16) sits in lanes i and i + 16
+            const float c = __ldg(cs + (lane & 15)), s = __ldg(sn + (lane & 15));
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float other = __shfl_xor_sync(0xffffffffu, x[r][0], 16);
+                x[r][0] = lane < 16 ? __fsub_rn(__fmul_rn(x[r][0], c), __fmul_rn(other, s))
+                                    : __fadd_rn(__fmul_rn(other, s), __fmul_rn(x[r][0], c));
+            }
+        } else {
+#pragma unroll
+            for (int b = 0; b < NB / 2; b++) {
+                const float c = __ldg(cs + b * 32 + lane), s = __ldg(sn + b * 32 + lane);
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    const float x0 = x[r][b], x1 = x[r][b + NB / 2];
+                    x[r][b] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                    x[r][b + NB / 2] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+                }
+            }
+        }
+    }
+}
+
 // ----------------------------------------------------------------------------
 // PTX wrappers: mbarrier + 1-D bulk async copy global -> shared.
 // ----------------------------------------------------------------------------

@@ -30,6 +30,8 @@ constexpr int DEC_THREADS = 128;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_T = 64;          // tokens per tile
 constexpr int MAX_SPLITS = 128;    // bound on splits per (item, kv head)
+constexpr int MERGE_GROUP = 8;     // splits merged per first-level group
+constexpr int TICKETS_PER_UNIT = 1 + MAX_SPLITS / MERGE_GROUP;  // final ticket + one per group
 constexpr uint64_t WAIT_NS = 1000000000ull;   // 1 s bound on any mbarrier wait
 constexpr uint64_t DRAIN_NS = 20000000ull;    // 20 ms bound when draining after a timeout
 
@@ -47,6 +49,11 @@ struct DecodeParams {
     long long out_item_stride;   // floats
     const float *k_new, *v_new;
     long long kv_new_item_stride;  // floats
+    const float *q_norm, *k_norm;  // optional prologue: RMSNorm weights [head_dim] per item
+    long long norm_item_stride;    // floats
+    float norm_eps;
+    const float *rope_cos, *rope_sin;  // optional prologue: RoPE tables [head_dim/2] per item
+    long long rope_item_stride;        // floats
     int out_mode;
     int split_tokens;            // multiple of DEC_T
     int max_splits;
@@ -74,7 +81,8 @@ struct DecLayout {
     static constexpr int OFF_PV = OFF_SC + GMAX * DEC_T * 4;
     static constexpr int OFF_STATE = OFF_PV + DEC_T * NB * GMAX * 4;  // m, l, corr
     static constexpr int OFF_NEW = OFF_STATE + ((3 * GMAX * 4 + 15) / 16) * 16;
-    static constexpr int OFF_FLAG = OFF_NEW + ((2 * ROW + 15) / 16) * 16;
+    static constexpr int OFF_PRO = OFF_NEW + ((2 * ROW + 15) / 16) * 16;  // prologue row per warp
+    static constexpr int OFF_FLAG = OFF_PRO + DEC_WARPS * pro_stride<NB>() * 4;
     static constexpr int BYTES = OFF_FLAG + 16;
     // after the pipeline drains, the stage ring is reused for the cross-warp
     // reduction and the merge weights
@@ -135,19 +143,129 @@ __device__ __forceinline__ float score_row(const uint8_t *row, const uint32_t (&
     return __fmul_rn(acc, scale);
 }
 
+// The call's fused prologue (norm_heads + rope_heads, attention_layer.c:183-189)
+// on R q rows (is_k false) or the appended K row of `item`, held by a warp as
+// x[r][b] = row_r[b*32 + lane]; `scratch` is the warp's R * pro_stride<NB>()
+// floats.  A no-op when the call asks for none.
+template <int NB, int R>
+__device__ __forceinline__ void row_prologue(const DecodeParams &p, int item, bool is_k, float (&x)[R][NB],
+                                             float *scratch, int lane) {
+    const float *w = is_k ? p.k_norm : p.q_norm;
+    if (!w && !p.rope_cos) return;
+    const long long ni = (long long)item * p.norm_item_stride, ri = (long long)item * p.rope_item_stride;
+    warp_norm_rope<NB, R>(x, w ? w + ni : nullptr, p.rope_cos ? p.rope_cos + ri : nullptr,
+                          p.rope_cos ? p.rope_sin + ri : nullptr, p.norm_eps, scratch, lane);
+}
+template <int NB>
+__device__ __forceinline__ void row_prologue(const DecodeParams &p, int item, bool is_k, float (&x)[NB],
+                                             float *scratch, int lane) {
+    row_prologue<NB, 1>(p, item, is_k, reinterpret_cast<float(&)[1][NB]>(x), scratch, lane);
+}
+
+// Tickets and the arrival test of the split merge.  A CTA that wrote its
+// partial takes a ticket; the one that draws the last number of its group
+// merges (never a wait).
+template <int BAR, int NT>
+__device__ __forceinline__ bool last_arrival(int *ticket, int n, int tid, int *flag) {
+    __threadfence();
+    cta_sync<BAR, NT>();
+    if (tid == 0) *flag = (atomicAdd(ticket, 1) == n - 1);
+    cta_sync<BAR, NT>();
+    const bool last = *flag;  // read by every thread before the next arrival's sync
+    if (last) __threadfence();
+    return last;
+}
+
+// Log-sum-exp merge, in slot order, of the n partials {acc[HD], m, l} in slots
+// first, first + stride, ... of one (item, head unit)'s partial area pb
+// ([slot][GROWS][HD + 2] floats).  to_part: the merged partial goes back into
+// slot `first`; otherwise into the call's output (normalised, or as a partial
+// in TQK_OUT_PARTIAL mode).  Each thread owns the same EPT elements across the
+// slots, so one slot's EPT loads are in flight together.
+template <int HD, int GROWS, int NT, int BAR>
+__device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, int first, int stride, int n, int G,
+                                            int tid, float *wts, float *ms, float *ls, bool to_part, float *out_item,
+                                            int qh0) {
+    constexpr int RS = HD + 2;
+    constexpr int EPT = (GROWS * HD + NT - 1) / NT;
+    const int lane = tid & 31, warp = tid >> 5;
+    float *lall = wts + MAX_SPLITS * GROWS;
+    for (int i = tid; i < n * G; i += NT) {  // every slot's (m, l) in one round trip
+        const int k = i / G, g = i - k * G;
+        const float2 ml =
+            __ldcg(reinterpret_cast<const float2 *>(pb + ((long long)(first + k * stride) * GROWS + g) * RS + HD));
+        wts[k * GROWS + g] = ml.x;
+        lall[k * GROWS + g] = ml.y;
+    }
+    cta_sync<BAR, NT>();
+    for (int g = warp; g < G; g += NT / 32) {
+        float M = -INFINITY;
+        for (int k = lane; k < n; k += 32) M = fmaxf(M, wts[k * GROWS + g]);
+        M = warp_max(M);
+        float Lsum = 0.0f;
+        for (int k = lane; k < n; k += 32) {
+            const float w = expf(wts[k * GROWS + g] - M);
+            wts[k * GROWS + g] = w;
+            Lsum += lall[k * GROWS + g] * w;
+        }
+        Lsum = warp_sum(Lsum);
+        if (lane == 0) { ms[g] = M; ls[g] = Lsum; }
+    }
+    cta_sync<BAR, NT>();
+    float a[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; e++) a[e] = 0.0f;
+#pragma unroll (EPT <= 16 ? 2 : 1)
+    for (int k = 0; k < n; k++) {
+        const float *src = pb + (long long)(first + k * stride) * GROWS * RS;
+        float x[EPT];
+#pragma unroll
+        for (int e = 0; e < EPT; e++) {
+            const int i = tid + e * NT, g = i / HD, c = i - g * HD;
+            x[e] = i < G * HD ? __ldcg(src + g * RS + c) : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < EPT; e++) {
+            const int i = tid + e * NT, g = i / HD;
+            if (i < G * HD) a[e] = fmaf(wts[k * GROWS + g], x[e], a[e]);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < EPT; e++) {
+        const int i = tid + e * NT, g = i / HD, c = i - g * HD;
+        if (i >= G * HD) continue;
+        if (to_part) {
+            float *d = pb + ((long long)first * GROWS + g) * RS;
+            d[c] = a[e];
+            if (c == 0) { d[HD] = ms[g]; d[HD + 1] = ls[g]; }
+        } else if (p.out_mode == TQK_OUT_NORMALIZED) {
+            out_item[(long long)(qh0 + g) * HD + c] = a[e] / ls[g];
+        } else {
+            float *o = out_item + (long long)(qh0 + g) * RS;
+            o[c] = a[e];
+            if (c == 0) { o[HD] = ms[g]; o[HD + 1] = ls[g]; }
+        }
+    }
+}
+
 // Finishes one split of one (item, kv-head slice).  acc(g, c) is the CTA's
 // unnormalised sum for its q head g and column c, relative to the running max
 // ms[g], with softmax denominator ls[g].  A single split writes the output (or
 // the partial, in TQK_OUT_PARTIAL mode); otherwise the split's partial goes to
-// the workspace and the last-arriving split (atomic ticket, never a wait)
-// merges all splits by log-sum-exp, in split order, so results are
-// deterministic.  ms/ls are overwritten by the merge.
+// the workspace and the splits are merged by log-sum-exp without any wait:
+//   n_splits <= MERGE_GROUP: the last-arriving split merges them all;
+//   more: the last arrival of each group of MERGE_GROUP splits merges its group
+//   into the group's first slot, and the last group to finish merges the
+//   groups -- two short merges instead of one long serial one.
+// Merges run in slot order, so results are deterministic.  ms/ls are
+// overwritten by the merge; the tickets used are left at zero.
 template <int HD, int GROWS, int NT, int BAR, typename AccFn>
 __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int item, int pair, int s, int n_splits,
                                              int qh0, int G, float *out_item, AccFn acc, float *ms, float *ls,
                                              float *wts, int *flag) {
     const bool single = n_splits == 1;
-    const long long pair_base = ((long long)item * p.pairs + pair) * p.max_splits;
+    const long long unit = (long long)item * p.pairs + pair;
+    float *pb = p.part + unit * p.max_splits * GROWS * (HD + 2);
     for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, c = i - g * HD;
         const float a = acc(g, c);
@@ -160,72 +278,28 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
                 if (c == 0) { o[HD] = ms[g]; o[HD + 1] = ls[g]; }
             }
         } else {
-            float *pp = p.part + ((pair_base + s) * GROWS + g) * (HD + 2);
+            float *pp = pb + ((long long)s * GROWS + g) * (HD + 2);
             pp[c] = a;
             if (c == 0) { pp[HD] = ms[g]; pp[HD + 1] = ls[g]; }
         }
     }
     if (single) return;
 
-    __threadfence();
-    cta_sync<BAR, NT>();
-    if (tid == 0) {
-        const int prev = atomicAdd(&p.counters[(long long)item * p.pairs + pair], 1);
-        *flag = (prev == n_splits - 1);
+    int *tickets = p.counters + unit * TICKETS_PER_UNIT;  // [0] final, [1 + i] group i
+    if (n_splits > MERGE_GROUP) {
+        const int gi = s / MERGE_GROUP, first = gi * MERGE_GROUP;
+        const int gsz = min(MERGE_GROUP, n_splits - first);
+        if (!last_arrival<BAR, NT>(tickets + 1 + gi, gsz, tid, flag)) return;
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, first, 1, gsz, G, tid, wts, ms, ls, true, out_item, qh0);
+        if (tid == 0) tickets[1 + gi] = 0;
+        const int n_groups = (n_splits + MERGE_GROUP - 1) / MERGE_GROUP;
+        if (!last_arrival<BAR, NT>(tickets, n_groups, tid, flag)) return;
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, MERGE_GROUP, n_groups, G, tid, wts, ms, ls, false, out_item, qh0);
+    } else {
+        if (!last_arrival<BAR, NT>(tickets, n_splits, tid, flag)) return;
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, 1, n_splits, G, tid, wts, ms, ls, false, out_item, qh0);
     }
-    cta_sync<BAR, NT>();
-    if (!*flag) return;
-    __threadfence();
-
-    const int lane = tid & 31, warp = tid >> 5;
-    const float *pb = p.part + pair_base * GROWS * (HD + 2);
-    // every split's (m, l) in one round trip (wts holds m, ls_all holds l)
-    float *lall = wts + MAX_SPLITS * GROWS;
-    for (int i = tid; i < n_splits * G; i += NT) {
-        const int sp = i / G, g = i - sp * G;
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pb + (sp * GROWS + g) * (HD + 2) + HD));
-        wts[sp * GROWS + g] = ml.x;
-        lall[sp * GROWS + g] = ml.y;
-    }
-    cta_sync<BAR, NT>();
-    for (int g = warp; g < G; g += NT / 32) {
-        float M = -INFINITY;
-        for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, wts[sp * GROWS + g]);
-        M = warp_max(M);
-        float Lsum = 0.0f;
-        for (int sp = lane; sp < n_splits; sp += 32) {
-            const float w = expf(wts[sp * GROWS + g] - M);
-            wts[sp * GROWS + g] = w;
-            Lsum += lall[sp * GROWS + g] * w;
-        }
-        Lsum = warp_sum(Lsum);
-        if (lane == 0) { ms[g] = M; ls[g] = Lsum; }
-    }
-    cta_sync<BAR, NT>();
-    for (int i = tid; i < G * HD; i += NT) {
-        const int g = i / HD, c = i - g * HD;
-        float a = 0.0f;
-        int sp = 0;
-        for (; sp + 4 <= n_splits; sp += 4) {  // four independent loads in flight
-            const float x0 = __ldcg(pb + ((sp + 0) * GROWS + g) * (HD + 2) + c);
-            const float x1 = __ldcg(pb + ((sp + 1) * GROWS + g) * (HD + 2) + c);
-            const float x2 = __ldcg(pb + ((sp + 2) * GROWS + g) * (HD + 2) + c);
-            const float x3 = __ldcg(pb + ((sp + 3) * GROWS + g) * (HD + 2) + c);
-            a = fmaf(wts[(sp + 0) * GROWS + g], x0, a);
-            a = fmaf(wts[(sp + 1) * GROWS + g], x1, a);
-            a = fmaf(wts[(sp + 2) * GROWS + g], x2, a);
-            a = fmaf(wts[(sp + 3) * GROWS + g], x3, a);
-        }
-        for (; sp < n_splits; sp++) a = fmaf(wts[sp * GROWS + g], __ldcg(pb + (sp * GROWS + g) * (HD + 2) + c), a);
-        if (p.out_mode == TQK_OUT_NORMALIZED) {
-            out_item[(long long)(qh0 + g) * HD + c] = a / ls[g];
-        } else {
-            float *o = out_item + (long long)(qh0 + g) * (HD + 2);
-            o[c] = a;
-            if (c == 0) { o[HD] = ms[g]; o[HD + 1] = ls[g]; }
-        }
-    }
-    if (tid == 0) p.counters[(long long)item * p.pairs + pair] = 0;  // ready for the next launch
+    if (tid == 0) tickets[0] = 0;  // ready for the next launch
 }
 
 template <int NB, int GMAX>
@@ -292,6 +366,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
     float *l_s = m_s + GMAX;
     float *corr_s = l_s + GMAX;
     uint8_t *newrow = smem + L::OFF_NEW;
+    float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * pro_stride<NB>();
     int *flag = reinterpret_cast<int *>(smem + L::OFF_FLAG);
 
     auto issue = [&](int j) {
@@ -320,13 +395,30 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
 
     // quantise this CTA's q heads: one warp per 32-float block (quant_x.c:12-34)
     const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
-    for (int blk = warp; blk < GMAX * NB; blk += DEC_WARPS) {
-        const int g = blk / NB, b = blk - g * NB;
-        const float x = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
-        float d;
-        const int8_t v8 = warp_quantize_block(x, &d);
-        qq[g * HD + b * QK + lane] = v8;
-        if (lane == 0) qd[g * NB + b] = d;
+    if (p.q_norm || p.rope_cos) {
+        // with the fused prologue, which needs whole rows: one warp per q row
+        for (int g = warp; g < GMAX; g += DEC_WARPS) {
+            float x[NB];
+#pragma unroll
+            for (int b = 0; b < NB; b++) x[b] = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
+            if (g < G) row_prologue<NB>(p, item, false, x, pro, lane);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float d;
+                const int8_t v8 = warp_quantize_block(x[b], &d);
+                qq[g * HD + b * QK + lane] = v8;
+                if (lane == 0) qd[g * NB + b] = d;
+            }
+        }
+    } else {
+        for (int blk = warp; blk < GMAX * NB; blk += DEC_WARPS) {
+            const int g = blk / NB, b = blk - g * NB;
+            const float x = g < G ? __ldg(qsrc + g * HD + b * QK + lane) : 0.0f;
+            float d;
+            const int8_t v8 = warp_quantize_block(x, &d);
+            qq[g * HD + b * QK + lane] = v8;
+            if (lane == 0) qd[g * NB + b] = d;
+        }
     }
 
     // fused append (store_kv, attention_layer.c:66-90): the split holding
@@ -339,10 +431,14 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
                            (long long)kvh * HD;
         uint8_t *nrow = newrow + warp * ROW;
         uint8_t *grow = (warp == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + head_off + (long long)pos * ROW;
+        float x[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) x[b] = __ldg(src + b * QK + lane);
+        if (warp == 0) row_prologue<NB>(p, item, true, x, pro, lane);
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float d;
-            const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+            const int8_t v8 = warp_quantize_block(x[b], &d);
             nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
             if (lane == 0) *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
             if (slice == 0) {
@@ -674,13 +770,12 @@ int dispatch_gmax(int gmax, const DecodeParams &p, dim3 grid, cudaStream_t strea
     }
 }
 
+// CUDA-core kernel: head_dim 32 and 64 (128 and 256 go to the tensor-core kernels).
 int dispatch(int nb, int gmax, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
     switch (nb) {
         case 1: return dispatch_gmax<1>(gmax, p, grid, stream, occ);
         case 2: return dispatch_gmax<2>(gmax, p, grid, stream, occ);
-        case 4: return dispatch_gmax<4>(gmax, p, grid, stream, occ);
-        case 8: return dispatch_gmax<8>(gmax, p, grid, stream, occ);
-        default: return fail(TQK_EUNSUPPORTED, "decode: head_dim must be 32, 64, 128 or 256");
+        default: return fail(TQK_EUNSUPPORTED, "decode: the CUDA-core kernel takes head_dim 32 or 64");
     }
 }
 
@@ -691,14 +786,17 @@ struct Plan {
     size_t counters_bytes, part_bytes;
 };
 
-// Tickets of the split merge: one int per (item, head unit), at the start of a
-// caller workspace, followed by the partials.  Every completed call leaves its
-// tickets at zero but writes partials right after them, so the region has a
-// fixed floor of 64 KiB: calls of up to 16384 units all use the same ticket
-// bytes and can share a workspace without re-initialisation.
+// Tickets of the split merge: TICKETS_PER_UNIT ints per (item, head unit), at
+// the start of a caller workspace, followed by the partials.  Every completed
+// call leaves its tickets at zero but writes partials right after them, so the
+// region has a fixed floor (16384 units' worth): calls of up to 16384 units
+// all use the same ticket bytes and can share a workspace without
+// re-initialisation.
+constexpr int TICKET_FLOOR_UNITS = 16384;
 size_t counters_region(int n_items, int units) {
-    const size_t b = (((size_t)n_items * units * sizeof(int)) + 255) / 256 * 256;
-    return b < 65536 ? 65536 : b;
+    const size_t n = (size_t)n_items * units;
+    const size_t b = ((n < TICKET_FLOOR_UNITS ? TICKET_FLOOR_UNITS : n) * TICKETS_PER_UNIT * sizeof(int) + 255) / 256 * 256;
+    return b;
 }
 
 int make_plan(const tqk_decode_args *a, Plan *pl) {
@@ -712,6 +810,9 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     if (!a->k || !a->v || !a->q || !a->out) return fail(TQK_EINVAL, "decode: NULL pointer");
     if ((a->k_new == nullptr) != (a->v_new == nullptr)) return fail(TQK_EINVAL, "decode: k_new and v_new go together");
     if (a->out_mode != TQK_OUT_NORMALIZED && a->out_mode != TQK_OUT_PARTIAL) return fail(TQK_EINVAL, "decode: out_mode");
+    if ((a->q_norm == nullptr) != (a->k_norm == nullptr)) return fail(TQK_EINVAL, "decode: q_norm and k_norm go together");
+    if ((a->rope_cos == nullptr) != (a->rope_sin == nullptr))
+        return fail(TQK_EINVAL, "decode: rope_cos and rope_sin go together");
     if (a->n_items > 65535) return fail(TQK_EINVAL, "decode: n_items > 65535");
     int max_len;
     if (a->lens) {
@@ -777,6 +878,46 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     return TQK_OK;
 }
 
+// Kernel parameters of a validated call (everything but the scratch pointers).
+DecodeParams fill_params(const tqk_decode_args *a, const Plan &pl) {
+    DecodeParams p{};
+    p.k = reinterpret_cast<const uint8_t *>(a->k);
+    p.v = reinterpret_cast<const uint8_t *>(a->v);
+    p.kw = reinterpret_cast<uint8_t *>(a->k);
+    p.vw = reinterpret_cast<uint8_t *>(a->v);
+    p.item_stride = a->item_stride * BLOCK_BYTES;
+    p.n_items = a->n_items;
+    p.n_kv = a->n_kv_heads;
+    p.group = a->n_q_heads / a->n_kv_heads;
+    p.max_tokens = a->max_tokens;
+    p.heads_per_cta = pl.heads_per_cta;
+    p.head_slices = pl.head_slices;
+    p.pairs = pl.pairs;
+    p.lens = a->lens;
+    p.len0 = a->len0;
+    p.len_step = a->len_step;
+    p.q = a->q;
+    p.q_item_stride = a->q_item_stride;
+    p.out = a->out;
+    p.out_item_stride = a->out_item_stride;
+    p.k_new = a->k_new;
+    p.v_new = a->v_new;
+    p.kv_new_item_stride = a->kv_new_item_stride;
+    p.q_norm = a->q_norm;
+    p.k_norm = a->k_norm;
+    p.norm_item_stride = a->norm_item_stride;
+    p.norm_eps = a->norm_eps;
+    p.rope_cos = a->rope_cos;
+    p.rope_sin = a->rope_sin;
+    p.rope_item_stride = a->rope_item_stride;
+    p.out_mode = a->out_mode;
+    p.split_tokens = pl.split_tokens;
+    p.max_splits = pl.max_splits;
+    p.scale = 1.0f / sqrtf((float)a->head_dim);  // as attend_q8 computes it (attention_layer.c:131)
+    return p;
+}
+
+
 }  // namespace
 }  // namespace tqk
 
@@ -814,33 +955,7 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
             part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + pl.counters_bytes);
         }
     }
-    DecodeParams p{};
-    p.k = reinterpret_cast<const uint8_t *>(a->k);
-    p.v = reinterpret_cast<const uint8_t *>(a->v);
-    p.kw = reinterpret_cast<uint8_t *>(a->k);
-    p.vw = reinterpret_cast<uint8_t *>(a->v);
-    p.item_stride = a->item_stride * BLOCK_BYTES;
-    p.n_items = a->n_items;
-    p.n_kv = a->n_kv_heads;
-    p.group = a->n_q_heads / a->n_kv_heads;
-    p.max_tokens = a->max_tokens;
-    p.heads_per_cta = pl.heads_per_cta;
-    p.head_slices = pl.head_slices;
-    p.pairs = pl.pairs;
-    p.lens = a->lens;
-    p.len0 = a->len0;
-    p.len_step = a->len_step;
-    p.q = a->q;
-    p.q_item_stride = a->q_item_stride;
-    p.out = a->out;
-    p.out_item_stride = a->out_item_stride;
-    p.k_new = a->k_new;
-    p.v_new = a->v_new;
-    p.kv_new_item_stride = a->kv_new_item_stride;
-    p.out_mode = a->out_mode;
-    p.split_tokens = pl.split_tokens;
-    p.max_splits = pl.max_splits;
-    p.scale = 1.0f / sqrtf((float)a->head_dim);  // as attend_q8 computes it (attention_layer.c:131)
+    DecodeParams p = fill_params(a, pl);
     p.counters = counters;
     p.part = part;
     p.err = device_info()->err_word;
@@ -861,7 +976,7 @@ namespace {
 constexpr int STATIC_TICKETS = 16384;               // (item, head unit) pairs per call
 constexpr size_t STATIC_PART_FLOATS = 1u << 20;     // 4 MiB of split partials
 
-static __device__ __align__(256) int g_static_tickets[STATIC_TICKETS];
+static __device__ __align__(256) int g_static_tickets[STATIC_TICKETS * TICKETS_PER_UNIT];
 static __device__ __align__(256) float g_static_part[STATIC_PART_FLOATS];
 
 struct StaticScratch {
@@ -941,36 +1056,10 @@ extern "C" int tqk_decode_q8_static(const tqk_decode_args *args, tqk_stream_t st
     cudaStream_t st = (cudaStream_t)stream;
     if (pl.max_splits > 1) {
         // the tickets must start at zero: clear this call's range on the stream
-        e = cudaMemsetAsync(sc.tickets, 0, (size_t)units * sizeof(int), st);
+        e = cudaMemsetAsync(sc.tickets, 0, (size_t)units * TICKETS_PER_UNIT * sizeof(int), st);
         if (e != cudaSuccess) return fail_cuda(e, "tqk_decode_q8_static: clearing the tickets");
     }
-    DecodeParams p{};
-    p.k = reinterpret_cast<const uint8_t *>(a.k);
-    p.v = reinterpret_cast<const uint8_t *>(a.v);
-    p.kw = reinterpret_cast<uint8_t *>(a.k);
-    p.vw = reinterpret_cast<uint8_t *>(a.v);
-    p.item_stride = a.item_stride * BLOCK_BYTES;
-    p.n_items = a.n_items;
-    p.n_kv = a.n_kv_heads;
-    p.group = a.n_q_heads / a.n_kv_heads;
-    p.max_tokens = a.max_tokens;
-    p.heads_per_cta = pl.heads_per_cta;
-    p.head_slices = pl.head_slices;
-    p.pairs = pl.pairs;
-    p.lens = a.lens;
-    p.len0 = a.len0;
-    p.len_step = a.len_step;
-    p.q = a.q;
-    p.q_item_stride = a.q_item_stride;
-    p.out = a.out;
-    p.out_item_stride = a.out_item_stride;
-    p.k_new = a.k_new;
-    p.v_new = a.v_new;
-    p.kv_new_item_stride = a.kv_new_item_stride;
-    p.out_mode = a.out_mode;
-    p.split_tokens = pl.split_tokens;
-    p.max_splits = pl.max_splits;
-    p.scale = 1.0f / sqrtf((float)a.head_dim);  // as attend_q8 computes it (attention_layer.c:131)
+    DecodeParams p = fill_params(&a, pl);
     p.counters = pl.max_splits > 1 ? sc.tickets : nullptr;
     p.part = pl.max_splits > 1 ? sc.part : nullptr;
     p.err = nullptr;  // no device error word: device-side checks still clamp or stop safely

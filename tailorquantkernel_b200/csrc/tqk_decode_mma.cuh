@@ -52,7 +52,8 @@ struct MmaLayout {
     static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [16][HD]
     static constexpr int OFF_QD = OFF_QQ + 16 * HD;                // float [16][NB]
     static constexpr int OFF_NEW = OFF_QD + ((16 * NB * 4 + 15) / 16) * 16;   // appended K, V rows
-    static constexpr int OFF_FLAG = OFF_NEW + ((2 * ROW + 15) / 16) * 16;     // int flag, int timeout
+    static constexpr int OFF_PRO = OFF_NEW + ((2 * ROW + 15) / 16) * 16;      // prologue row per warp
+    static constexpr int OFF_FLAG = OFF_PRO + MMA_WARPS * pro_stride<NB>() * 4;  // int flag, int timeout
     static constexpr int BYTES = OFF_FLAG + 16;
     // epilogue scratch, in the idle stage ring
     static constexpr int RED_FLOATS = MMA_WARPS * GPAD * HD;
@@ -449,11 +450,13 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         // quantise this CTA's G q heads (quant_x.c:12-34), one row per warp with
         // the row's loads issued together; the padding rows G..15 are zero
         const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
+        float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * pro_stride<NB>();
         for (int g = warp; g < 16; g += MMA_WARPS) {
             if (g < G) {
                 float x[NB];
 #pragma unroll
                 for (int b = 0; b < NB; b++) x[b] = __ldg(qsrc + g * HD + b * QK + lane);
+                row_prologue<NB>(p, item, false, x, pro, lane);  // fused prologue, if asked for
 #pragma unroll
                 for (int b = 0; b < NB; b++) {
                     float d;
@@ -474,10 +477,14 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
             uint8_t *nrow = newrow + warp * ROW;
             uint8_t *grow = (warp == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + head_off +
                             (long long)pos * ROW;
+            float x[NB];
+#pragma unroll
+            for (int b = 0; b < NB; b++) x[b] = __ldg(src + b * QK + lane);
+            if (warp == 0) row_prologue<NB>(p, item, true, x, pro, lane);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
                 float d;
-                const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+                const int8_t v8 = warp_quantize_block(x[b], &d);
                 nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
                 if (lane == 0) *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
                 if (slice == 0) {

@@ -41,6 +41,7 @@ constexpr int PK_WARPS = TQK_PK_WARPS;         // consumer warps
 constexpr int PK_THREADS = (PK_WARPS + (PK_INLINE_TMA ? 0 : 1)) * 32;
 constexpr int PK_ROWS = 16;                    // tokens of each kv head per warp step
 constexpr int PK_T = PK_ROWS * PK_WARPS;       // tokens per tile, per kv head
+constexpr int PK_QR = (8 + PK_WARPS - 1) / PK_WARPS;  // q rows per consumer warp (8 q heads per CTA)
 
 template <int NB>
 struct PackLayout {
@@ -56,7 +57,8 @@ struct PackLayout {
     static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [8][HD]
     static constexpr int OFF_QD = OFF_QQ + 8 * HD;                              // float [8][NB]
     static constexpr int OFF_NEW = OFF_QD + ((8 * NB * 4 + 15) / 16) * 16;     // appended rows [head][K,V][ROW]
-    static constexpr int OFF_FLAG = OFF_NEW + ((4 * ROW + 15) / 16) * 16;
+    static constexpr int OFF_PRO = OFF_NEW + ((4 * ROW + 15) / 16) * 16;       // prologue rows [warp][PK_QR]
+    static constexpr int OFF_FLAG = OFF_PRO + PK_WARPS * PK_QR * pro_stride<NB>() * 4;
     static constexpr int BYTES = OFF_FLAG + 16;
     static constexpr int RED_STRIDE = HD + 1;  // reduction rows padded: the 32 lanes' stores hit 32 banks
     static constexpr int RED_FLOATS = PK_WARPS * 8 * RED_STRIDE;
@@ -259,8 +261,8 @@ __device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a,
 // [8][HD] / qd [8][NB]; consumer warp `warp` does rows warp, warp+PK_WARPS, ...
 template <int NB>
 __device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int qh0, int warp, int lane, int8_t *qq,
-                                            float *qd) {
-    constexpr int HD = NB * QK, QR = (8 + PK_WARPS - 1) / PK_WARPS;
+                                            float *qd, float *scratch) {
+    constexpr int HD = NB * QK, QR = PK_QR;
     const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
     float x[QR][NB];  // loads first
 #pragma unroll
@@ -268,6 +270,7 @@ __device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int
 #pragma unroll
         for (int b = 0; b < NB; b++)
             x[r][b] = warp + PK_WARPS * r < 8 ? __ldg(qsrc + (warp + PK_WARPS * r) * HD + b * QK + lane) : 0.0f;
+    row_prologue<NB, QR>(p, item, false, x, scratch, lane);  // fused prologue, if the call asks for one
 #pragma unroll
     for (int r = 0; r < QR; r++) {
         const int g = warp + PK_WARPS * r;
@@ -288,7 +291,7 @@ __device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int
 // Jobs 0/1 = K/V of head A, 2/3 = K/V of head B, one per consumer warp.
 template <int NB>
 __device__ __forceinline__ void pack_append(const DecodeParams &p, int item, int kvh_a, int pos, int warp, int lane,
-                                            uint8_t *newrow) {
+                                            uint8_t *newrow, float *scratch) {
     constexpr int HD = NB * QK, ROW = NB * BLOCK_BYTES;
     const long long head_bytes = (long long)p.max_tokens * ROW;
     for (int job = warp; job < 4; job += PK_WARPS) {
@@ -299,10 +302,14 @@ __device__ __forceinline__ void pack_append(const DecodeParams &p, int item, int
         uint8_t *nrow = newrow + (hsel * 2 + plane) * ROW;
         uint8_t *grow = (plane == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + (long long)kvh * head_bytes +
                         (long long)pos * ROW;
+        float x[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) x[b] = __ldg(src + b * QK + lane);
+        if (plane == 0) row_prologue<NB>(p, item, true, x, scratch, lane);
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float d;
-            const int8_t v8 = warp_quantize_block(__ldg(src + b * QK + lane), &d);
+            const int8_t v8 = warp_quantize_block(x[b], &d);
             nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
             grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
             if (lane == 0) {
@@ -415,8 +422,9 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     const bool do_append = p.k_new != nullptr && s == n_splits - 1;
     const int pos = len - 1;
     if (warp < PK_WARPS) {
-        pack_load_q<NB>(p, item, qh0, warp, lane, qq, qd);
-        if (do_append) pack_append<NB>(p, item, kvh_a, pos, warp, lane, newrow);
+        float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * PK_QR * pro_stride<NB>();
+        pack_load_q<NB>(p, item, qh0, warp, lane, qq, qd, pro);
+        if (do_append) pack_append<NB>(p, item, kvh_a, pos, warp, lane, newrow, pro);
     }
     __syncthreads();
 

@@ -60,6 +60,11 @@ class DecodeArgs(ctypes.Structure):
         ("kv_new_item_stride", _i64),
         ("out_mode", _i),
         ("split_tokens", _i),
+        ("q_norm", _vp), ("k_norm", _vp),
+        ("norm_item_stride", _i64),
+        ("norm_eps", _f),
+        ("rope_cos", _vp), ("rope_sin", _vp),
+        ("rope_item_stride", _i64),
     ]
 
 
@@ -84,6 +89,8 @@ tqk_decode_workspace_size = _sig("tqk_decode_workspace_size", [ctypes.POINTER(De
 tqk_workspace_init = _sig("tqk_workspace_init", [_vp, _sz, _vp])
 tqk_decode_q8 = _sig("tqk_decode_q8", [ctypes.POINTER(DecodeArgs), _vp, _sz, _vp])
 tqk_decode_q8_static = _sig("tqk_decode_q8_static", [ctypes.POINTER(DecodeArgs), _vp])
+tqk_qk_norm_rope = _sig("tqk_qk_norm_rope", [_vp, _vp, _i, _i64, _i64, _i, _i, _i, _vp, _vp, _i64, _f, _vp, _vp,
+                                              _i64, _vp])
 tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
@@ -95,7 +102,7 @@ EXPORTED = [
     "tqk_attn_scores_q8", "tqk_attn_accum_q8", "tqk_softmax_rows",
     "tqk_decode_workspace_size", "tqk_workspace_init", "tqk_decode_q8",
     "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
-    "tqk_decode_q8_static",
+    "tqk_decode_q8_static", "tqk_qk_norm_rope",
 ]
 
 
@@ -197,7 +204,8 @@ def softmax_rows(x, rows, n, stride, stream=None):
 
 def decode_args(k, v, n_q, n_kv, head_dim, max_tokens, q, out, *, n_items=1, item_stride_blocks=0, lens=None,
                 len0=0, len_step=0, max_len=0, q_item_stride=0, out_item_stride=0, k_new=None, v_new=None,
-                kv_new_item_stride=0, out_mode=OUT_NORMALIZED, split_tokens=0) -> DecodeArgs:
+                kv_new_item_stride=0, out_mode=OUT_NORMALIZED, split_tokens=0, q_norm=None, k_norm=None,
+                norm_item_stride=0, norm_eps=1e-6, rope_cos=None, rope_sin=None, rope_item_stride=0) -> DecodeArgs:
     a = DecodeArgs()
     a.k, a.v = _ptr(k), _ptr(v)
     a.item_stride = item_stride_blocks
@@ -211,6 +219,10 @@ def decode_args(k, v, n_q, n_kv, head_dim, max_tokens, q, out, *, n_items=1, ite
     a.kv_new_item_stride = kv_new_item_stride
     a.out_mode = out_mode
     a.split_tokens = split_tokens
+    a.q_norm, a.k_norm = _ptr(q_norm), _ptr(k_norm)
+    a.norm_item_stride, a.norm_eps = norm_item_stride, norm_eps
+    a.rope_cos, a.rope_sin = _ptr(rope_cos), _ptr(rope_sin)
+    a.rope_item_stride = rope_item_stride
     return a
 
 
@@ -218,6 +230,15 @@ def decode(args: DecodeArgs, workspace=None, stream=None) -> None:
     ws = _ptr(workspace) if workspace is not None else None
     nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(tqk_decode_q8(ctypes.byref(args), ws, nbytes, _stream(stream)), "tqk_decode_q8")
+
+
+def qk_norm_rope(q, k, n_items, n_q, n_kv, head_dim, q_norm=None, k_norm=None, eps=1e-6, rope_cos=None,
+                 rope_sin=None, q_item_stride=0, k_item_stride=0, norm_item_stride=0, rope_item_stride=0,
+                 stream=None) -> None:
+    """tqk_qk_norm_rope: in-place per-head RMSNorm and RoPE of q and k (the reference's norm_heads + rope_heads)."""
+    check(tqk_qk_norm_rope(_ptr(q), _ptr(k), n_items, q_item_stride, k_item_stride, n_q, n_kv, head_dim,
+                           _ptr(q_norm), _ptr(k_norm), norm_item_stride, eps, _ptr(rope_cos), _ptr(rope_sin),
+                           rope_item_stride, _stream(stream)), "tqk_qk_norm_rope")
 
 
 def decode_static(args: DecodeArgs, stream=None) -> None:

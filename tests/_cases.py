@@ -125,3 +125,15 @@ def prefill_inputs(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, pos
     kn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
     vn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
     return kf, vf, qn, kn, vn
+
+
+def norm_rope_inputs(seed: int, n_items: int, n_q: int, n_kv: int, hd: int, per_item_weights: bool):
+    """q [items, n_q*hd], k [items, n_kv*hd] and the q/k norm weights (per item when asked) of one
+    attention_layer.c:183-189 prologue case; q is scaled x4 so the norm does real work."""
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((n_items, n_q * hd), dtype=np.float32) * np.float32(4.0)
+    k = rng.standard_normal((n_items, n_kv * hd), dtype=np.float32)
+    nw = n_items if per_item_weights else 1
+    qw = (np.float32(1.0) + np.float32(0.1) * rng.standard_normal((nw, hd), dtype=np.float32))
+    kw = (np.float32(1.0) + np.float32(0.1) * rng.standard_normal((nw, hd), dtype=np.float32))
+    return q, k, qw, kw

@@ -64,6 +64,19 @@ def test_decode_args_layout_matches_c(tmp_path):
     assert vals[1:] == [getattr(tqk.DecodeArgs, f).offset for f in fields]
 
 
+def test_decode_prologue_arguments_checked_before_the_device():
+    """q_norm/k_norm and rope_cos/rope_sin come in pairs; the check precedes any device work."""
+    from tailorquantkernel_b200 import tqk
+    fake = ctypes.c_void_p(4096)
+    for kw in (dict(q_norm=fake), dict(k_norm=fake), dict(rope_cos=fake), dict(rope_sin=fake)):
+        a = tqk.DecodeArgs()
+        a.k = a.v = a.q = a.out = fake
+        a.n_items, a.n_q_heads, a.n_kv_heads, a.head_dim, a.max_tokens, a.len0 = 1, 32, 8, 128, 64, 10
+        for f, v in kw.items():
+            setattr(a, f, v)
+        assert tqk.tqk_decode_q8(ctypes.byref(a), None, 0, None) == tqk.EINVAL
+
+
 def test_error_codes_without_device():
     from tailorquantkernel_b200 import tqk
     # position checks come first and never touch a device (reference: -1 on bad pos)

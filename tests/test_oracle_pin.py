@@ -11,8 +11,8 @@ import numpy as np
 import pytest
 
 import oracle
-from _cases import (decode_case, digest, head_inputs, prefill_inputs, quant_edge_rows, sweep_inputs,
-                    tolerance_ok)
+from _cases import (decode_case, digest, head_inputs, norm_rope_inputs, prefill_inputs, quant_edge_rows,
+                    sweep_inputs, tolerance_ok)
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -153,3 +153,47 @@ def test_store_kv_rejects_bad_pos(port):
     for pos in (-1, 4, 9):
         assert port.store_kv(kp, vp, 2, 32, 4, pos, k, k) == -1
     assert (kp == 7).all() and (vp == 7).all()
+
+
+# name: (seed, n_items, n_q, n_kv, hd, first_pos, theta, eps, per_item_weights, norm); mirrors
+# NORM_ROPE_CASES of tests/golden/make_golden.py.
+NORM_ROPE = {
+    "qwen3_like": (41, 1, 32, 8, 128, 4096, 1000000.0, 1e-6, False, True),
+    "llama3_rope_only": (42, 1, 32, 8, 128, 4096, 500000.0, 1e-5, False, False),
+    "batch3_hd64": (43, 3, 6, 2, 64, 17, 10000.0, 1e-6, True, True),
+}
+
+
+@pytest.mark.parametrize("name", sorted(NORM_ROPE))
+def test_norm_rope_golden(port, name):
+    """rmsnorm + rope (model/rmsnorm.c:4-19, model/rope.c:4-22) bit-exact with the reference's outputs."""
+    g = _load("norm_rope.npz")
+    seed, items, nq, nkv, hd, p0, theta, eps, per_item, norm = NORM_ROPE[name]
+    q, k, qw, kw = norm_rope_inputs(seed, items, nq, nkv, hd, per_item)
+    assert digest(q, k, qw, kw) == str(g[name + "__in_sha"])
+    for it in range(items):
+        c, s = port.rope_table(hd, p0 + it, theta)
+        assert np.array_equal(c, g[name + "__cos"][it]) and np.array_equal(s, g[name + "__sin"][it])
+        wi = it if per_item else 0
+        qo = port.qk_norm_rope(q[it], nq, hd, qw[wi] if norm else None, eps, c, s)
+        ko = port.qk_norm_rope(k[it], nkv, hd, kw[wi] if norm else None, eps, c, s)
+        assert np.array_equal(qo.view(np.uint32), g[name + "__q"][it].view(np.uint32))
+        assert np.array_equal(ko.view(np.uint32), g[name + "__k"][it].view(np.uint32))
+
+
+def test_norm_rope_against_reference_build(port):
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    ref = oracle.Oracle("ref_scalar")
+    rng = np.random.default_rng(5)
+    for hd, pos, theta in ((32, 0, 10000.0), (128, 131071, 500000.0), (256, 777, 1000000.0)):
+        c, s = port.rope_table(hd, pos, theta)
+        cr, sr = ref.rope_table(hd, pos, theta)
+        assert np.array_equal(c, cr) and np.array_equal(s, sr)
+        x = rng.standard_normal((5, hd), dtype=np.float32) * np.float32(50.0)
+        x[0] = 0.0                       # rms = sqrt(eps)
+        x[1, ::3] = np.float32(3e18)     # sum of squares overflows to inf: output 0 * w
+        w = rng.standard_normal(hd, dtype=np.float32)
+        a = port.qk_norm_rope(x, 5, hd, w, 1e-6, c, s)
+        b = ref.qk_norm_rope(x, 5, hd, w, 1e-6, cr, sr)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
