@@ -69,71 +69,110 @@ __device__ __forceinline__ int8_t warp_quantize_block(float x, float *d) {
     return q8_round(x, q8_inverse(s));
 }
 
-// The attention prologue on R head rows of head_dim = NB*32 floats held by a
-// full warp, element b*32 + lane of row r in x[r][b]: RMSNorm with weight w
-// (model/rmsnorm.c:4-19; w == NULL skips it) and then the half-split RoPE
-// rotation with the tables cs/sn of head_dim/2 floats (model/rope.c:14-22;
-// cs == NULL skips it).  Rounds exactly as the reference's scalar C: each
-// row's squares are added in index order as one chain, sqrt and both
-// divisions are IEEE, products and sums are never contracted.  For the chain
-// the squares are staged in `scratch` (R rows of pro_stride<NB>() floats,
-// 16-byte aligned, private to the warp) and lane r walks row r with 16-byte loads, so
-// the R chains run side by side and only the adds are serial.
+// The attention prologue on head rows of head_dim = NB*32 floats held by a
+// full warp, element b*32 + lane of a row in x[b]: RMSNorm with a weight
+// (model/rmsnorm.c:4-19) and then the half-split RoPE rotation with a cos/sin
+// table of head_dim/2 floats (model/rope.c:14-22).  Rounds exactly as the
+// reference's scalar C: each row's squares are added in index order as one
+// chain, sqrt and both divisions are IEEE, products and sums are never
+// contracted.
 constexpr int PRO_PAD = 4;  // floats of padding per staged row: the R lanes' loads hit distinct banks
 template <int NB>
 __host__ __device__ constexpr int pro_stride() { return NB * 32 + PRO_PAD; }
 
+// This lane's elements of a norm weight ([head_dim] floats, element b*32 + lane).
+template <int NB>
+__device__ __forceinline__ void load_row(float (&w)[NB], const float *src, int lane) {
+#pragma unroll
+    for (int b = 0; b < NB; b++) w[b] = __ldg(src + b * 32 + lane);
+}
+
+// This lane's entries of a RoPE table pair ([head_dim/2] floats each): the
+// pair (i, i + head_dim/2) sits in one lane for NB >= 2 (element b*32 + lane
+// with b + NB/2), and in lanes i and i + 16 for head_dim 32.
+template <int NB>
+struct RopeTab {
+    static constexpr int N = NB >= 2 ? NB / 2 : 1;
+    float c[N], s[N];
+    __device__ __forceinline__ void load(const float *cs, const float *sn, int lane) {
+#pragma unroll
+        for (int b = 0; b < N; b++) {
+            const int i = NB >= 2 ? b * 32 + lane : (lane & 15);
+            c[b] = __ldg(cs + i);
+            s[b] = __ldg(sn + i);
+        }
+    }
+};
+
+// Sum of squares of each of R rows, added in index order as one chain per row:
+// the squares are staged in `scratch` (R rows of pro_stride<NB>() floats,
+// 16-byte aligned, private to the warp) and lane r walks row r with 16-byte
+// loads, so the R chains run side by side and only the adds are serial.
+template <int NB, int R>
+__device__ __forceinline__ void warp_row_sumsq(const float (&x)[R][NB], float *scratch, int lane, float (&sums)[R]) {
+    static_assert(R <= 32, "one lane per row");
+    constexpr int HD = NB * 32, STRIDE = pro_stride<NB>();
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) scratch[r * STRIDE + b * 32 + lane] = __fmul_rn(x[r][b], x[r][b]);
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane < R) {
+        const float4 *row = reinterpret_cast<const float4 *>(scratch + lane * STRIDE);
+#pragma unroll
+        for (int i = 0; i < HD / 4; i++) {
+            const float4 v = row[i];
+            sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
+        }
+    }
+    __syncwarp();  // the scratch is free again
+#pragma unroll
+    for (int r = 0; r < R; r++) sums[r] = __shfl_sync(0xffffffffu, sum, r);
+}
+
+// x * (1 / sqrtf(eps + sum/n)) * w, left to right, as model/rmsnorm.c:4-19.
+template <int NB>
+__device__ __forceinline__ void apply_norm(float (&x)[NB], float sum, const float (&w)[NB], float eps) {
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(eps, __fdiv_rn(sum, (float)(NB * 32)))));
+#pragma unroll
+    for (int b = 0; b < NB; b++) x[b] = __fmul_rn(__fmul_rn(x[b], inv), w[b]);
+}
+
+// (x0, x1) -> (x0*c - x1*s, x0*s + x1*c) per pair, as model/rope.c:14-22.
+template <int NB>
+__device__ __forceinline__ void apply_rope(float (&x)[NB], const RopeTab<NB> &t, int lane) {
+    if constexpr (NB == 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, x[0], 16);
+        x[0] = lane < 16 ? __fsub_rn(__fmul_rn(x[0], t.c[0]), __fmul_rn(other, t.s[0]))
+                         : __fadd_rn(__fmul_rn(other, t.s[0]), __fmul_rn(x[0], t.c[0]));
+    } else {
+#pragma unroll
+        for (int b = 0; b < NB / 2; b++) {
+            const float x0 = x[b], x1 = x[b + NB / 2];
+            x[b] = __fsub_rn(__fmul_rn(x0, t.c[b]), __fmul_rn(x1, t.s[b]));
+            x[b + NB / 2] = __fadd_rn(__fmul_rn(x0, t.s[b]), __fmul_rn(x1, t.c[b]));
+        }
+    }
+}
+
+// The whole prologue on R rows sharing one weight and one table (either
+// pointer NULL skips that part).
 template <int NB, int R>
 __device__ __forceinline__ void warp_norm_rope(float (&x)[R][NB], const float *w, const float *cs, const float *sn,
                                                float eps, float *scratch, int lane) {
-    static_assert(R <= 32, "one lane per row");
-    constexpr int HD = NB * 32, STRIDE = pro_stride<NB>();
     if (w) {
+        float wv[NB], sums[R];
+        load_row<NB>(wv, w, lane);
+        warp_row_sumsq<NB, R>(x, scratch, lane, sums);
 #pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int b = 0; b < NB; b++) scratch[r * STRIDE + b * 32 + lane] = __fmul_rn(x[r][b], x[r][b]);
-        __syncwarp();
-        float sum = 0.0f;
-        if (lane < R) {
-            const float4 *row = reinterpret_cast<const float4 *>(scratch + lane * STRIDE);
-#pragma unroll
-            for (int i = 0; i < HD / 4; i++) {
-                const float4 v = row[i];
-                sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
-            }
-        }
-        __syncwarp();  // the scratch is free again
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const float sr = __shfl_sync(0xffffffffu, sum, r);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(eps, __fdiv_rn(sr, (float)HD))));
-#pragma unroll
-            for (int b = 0; b < NB; b++) x[r][b] = __fmul_rn(__fmul_rn(x[r][b], inv), __ldg(w + b * 32 + lane));
-        }
+        for (int r = 0; r < R; r++) apply_norm<NB>(x[r], sums[r], wv, eps);
     }
     if (cs) {
-        if constexpr (NB == 1) {
-            // head_dim 32: the pair (i, i + 16) sits in lanes i and i + 16
-            const float c = __ldg(cs + (lane & 15)), s = __ldg(sn + (lane & 15));
+        RopeTab<NB> t;
+        t.load(cs, sn, lane);
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                const float other = __shfl_xor_sync(0xffffffffu, x[r][0], 16);
-                x[r][0] = lane < 16 ? __fsub_rn(__fmul_rn(x[r][0], c), __fmul_rn(other, s))
-                                    : __fadd_rn(__fmul_rn(other, s), __fmul_rn(x[r][0], c));
-            }
-        } else {
-#pragma unroll
-            for (int b = 0; b < NB / 2; b++) {
-                const float c = __ldg(cs + b * 32 + lane), s = __ldg(sn + b * 32 + lane);
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    const float x0 = x[r][b], x1 = x[r][b + NB / 2];
-                    x[r][b] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-                    x[r][b + NB / 2] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-                }
-            }
-        }
+        for (int r = 0; r < R; r++) apply_rope<NB>(x[r], t, lane);
     }
 }
 

@@ -42,6 +42,7 @@ constexpr int PK_THREADS = (PK_WARPS + (PK_INLINE_TMA ? 0 : 1)) * 32;
 constexpr int PK_ROWS = 16;                    // tokens of each kv head per warp step
 constexpr int PK_T = PK_ROWS * PK_WARPS;       // tokens per tile, per kv head
 constexpr int PK_QR = (8 + PK_WARPS - 1) / PK_WARPS;  // q rows per consumer warp (8 q heads per CTA)
+constexpr int PK_NJ = (4 + PK_WARPS - 1) / PK_WARPS;  // appended rows per consumer warp (K, V of 2 heads)
 
 template <int NB>
 struct PackLayout {
@@ -57,8 +58,8 @@ struct PackLayout {
     static constexpr int OFF_QQ = OFF_BAR + ((2 * STAGES * 8 + 15) / 16) * 16;  // int8 [8][HD]
     static constexpr int OFF_QD = OFF_QQ + 8 * HD;                              // float [8][NB]
     static constexpr int OFF_NEW = OFF_QD + ((8 * NB * 4 + 15) / 16) * 16;     // appended rows [head][K,V][ROW]
-    static constexpr int OFF_PRO = OFF_NEW + ((4 * ROW + 15) / 16) * 16;       // prologue rows [warp][PK_QR]
-    static constexpr int OFF_FLAG = OFF_PRO + PK_WARPS * PK_QR * pro_stride<NB>() * 4;
+    static constexpr int OFF_PRO = OFF_NEW + ((4 * ROW + 15) / 16) * 16;       // prologue rows [warp][PK_QR + PK_NJ]
+    static constexpr int OFF_FLAG = OFF_PRO + PK_WARPS * (PK_QR + PK_NJ) * pro_stride<NB>() * 4;
     static constexpr int BYTES = OFF_FLAG + 16;
     static constexpr int RED_STRIDE = HD + 1;  // reduction rows padded: the 32 lanes' stores hit 32 banks
     static constexpr int RED_FLOATS = PK_WARPS * 8 * RED_STRIDE;
@@ -257,20 +258,64 @@ __device__ __forceinline__ void pack_step(PackState<NB> &st, const uint8_t *k_a,
     }
 }
 
-// Quantises the 8 q heads qh0..qh0+7 of `item` (quant_x.c:12-34) into qq
-// [8][HD] / qd [8][NB]; consumer warp `warp` does rows warp, warp+PK_WARPS, ...
+// The CTA's preamble, per consumer warp `warp`:
+//  * quantises q heads qh0 + warp, qh0 + warp + PK_WARPS, ... of `item`
+//    (quant_x.c:12-34) into qq [8][HD] / qd [8][NB];
+//  * with do_append, the fused append (store_kv, attention_layer.c:66-90):
+//    quantises new-row jobs warp, warp + PK_WARPS, ... (job 0/1 = K/V of head
+//    A, 2/3 = K/V of head B), writes them to the cache at position pos and to
+//    newrow [head][K,V][ROW] for patching the staged tile;
+//  * with a fused prologue (norm_heads + rope_heads), normalises and rotates
+//    the q rows and the K rows first.  Every global load (q, new rows, norm
+//    weights, RoPE table) is issued up front, and the rows' sum-of-squares
+//    chains run side by side, so the prologue adds one short serial chain.
 template <int NB>
-__device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int qh0, int warp, int lane, int8_t *qq,
-                                            float *qd, float *scratch) {
-    constexpr int HD = NB * QK, QR = PK_QR;
+__device__ __forceinline__ void pack_preamble(const DecodeParams &p, int item, int qh0, int kvh_a, int pos,
+                                              bool do_append, int warp, int lane, int8_t *qq, float *qd,
+                                              uint8_t *newrow, float *scratch) {
+    constexpr int HD = NB * QK, ROW = NB * BLOCK_BYTES, QR = PK_QR, NJ = PK_NJ, R = QR + NJ;
     const float *qsrc = p.q + (long long)item * p.q_item_stride + (long long)qh0 * HD;
-    float x[QR][NB];  // loads first
+    float x[R][NB];  // q rows, then this warp's new rows
 #pragma unroll
     for (int r = 0; r < QR; r++)
 #pragma unroll
         for (int b = 0; b < NB; b++)
             x[r][b] = warp + PK_WARPS * r < 8 ? __ldg(qsrc + (warp + PK_WARPS * r) * HD + b * QK + lane) : 0.0f;
-    row_prologue<NB, QR>(p, item, false, x, scratch, lane);  // fused prologue, if the call asks for one
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+        const int job = warp + PK_WARPS * j, kvh = kvh_a + (job >> 1);
+        const float *src = ((job & 1) == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride +
+                           (long long)kvh * HD;
+#pragma unroll
+        for (int b = 0; b < NB; b++) x[QR + j][b] = do_append && job < 4 ? __ldg(src + b * QK + lane) : 0.0f;
+    }
+    const bool norm = p.q_norm != nullptr, rope = p.rope_cos != nullptr;
+    if (norm || rope) {
+        float wq[NB], wk[NB];
+        RopeTab<NB> tab;
+        if (norm) {
+            load_row<NB>(wq, p.q_norm + (long long)item * p.norm_item_stride, lane);
+            load_row<NB>(wk, p.k_norm + (long long)item * p.norm_item_stride, lane);
+        }
+        if (rope) tab.load(p.rope_cos + (long long)item * p.rope_item_stride,
+                           p.rope_sin + (long long)item * p.rope_item_stride, lane);
+        if (norm) {
+            float sums[R];
+            warp_row_sumsq<NB, R>(x, scratch, lane, sums);
+#pragma unroll
+            for (int r = 0; r < QR; r++) apply_norm<NB>(x[r], sums[r], wq, p.norm_eps);
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if ((warp + PK_WARPS * j) % 2 == 0) apply_norm<NB>(x[QR + j], sums[QR + j], wk, p.norm_eps);
+        }
+        if (rope) {
+#pragma unroll
+            for (int r = 0; r < QR; r++) apply_rope<NB>(x[r], tab, lane);
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if ((warp + PK_WARPS * j) % 2 == 0) apply_rope<NB>(x[QR + j], tab, lane);
+        }
+    }
 #pragma unroll
     for (int r = 0; r < QR; r++) {
         const int g = warp + PK_WARPS * r;
@@ -283,33 +328,20 @@ __device__ __forceinline__ void pack_load_q(const DecodeParams &p, int item, int
             if (lane == 0) qd[g * NB + b] = d;
         }
     }
-}
-
-// Fused append (store_kv, attention_layer.c:66-90): quantises the new K and V
-// rows of kv heads kvh_a, kvh_a+1 of `item`, writes them to the cache at
-// position pos and to newrow [head][K,V][ROW] for patching the staged tile.
-// Jobs 0/1 = K/V of head A, 2/3 = K/V of head B, one per consumer warp.
-template <int NB>
-__device__ __forceinline__ void pack_append(const DecodeParams &p, int item, int kvh_a, int pos, int warp, int lane,
-                                            uint8_t *newrow, float *scratch) {
-    constexpr int HD = NB * QK, ROW = NB * BLOCK_BYTES;
+    if (!do_append) return;
     const long long head_bytes = (long long)p.max_tokens * ROW;
-    for (int job = warp; job < 4; job += PK_WARPS) {
-        const int hsel = job >> 1, plane = job & 1;
-        const int kvh = kvh_a + hsel;
-        const float *src =
-            (plane == 0 ? p.k_new : p.v_new) + (long long)item * p.kv_new_item_stride + (long long)kvh * HD;
-        uint8_t *nrow = newrow + (hsel * 2 + plane) * ROW;
-        uint8_t *grow = (plane == 0 ? p.kw : p.vw) + (long long)item * p.item_stride + (long long)kvh * head_bytes +
-                        (long long)pos * ROW;
-        float x[NB];
 #pragma unroll
-        for (int b = 0; b < NB; b++) x[b] = __ldg(src + b * QK + lane);
-        if (plane == 0) row_prologue<NB>(p, item, true, x, scratch, lane);
+    for (int j = 0; j < NJ; j++) {
+        const int job = warp + PK_WARPS * j;
+        if (job >= 4) break;
+        const int hsel = job >> 1, plane = job & 1;
+        uint8_t *nrow = newrow + (hsel * 2 + plane) * ROW;
+        uint8_t *grow = (plane == 0 ? p.kw : p.vw) + (long long)item * p.item_stride +
+                        (long long)(kvh_a + hsel) * head_bytes + (long long)pos * ROW;
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float d;
-            const int8_t v8 = warp_quantize_block(x[b], &d);
+            const int8_t v8 = warp_quantize_block(x[QR + j][b], &d);
             nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
             grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
             if (lane == 0) {
@@ -422,9 +454,8 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     const bool do_append = p.k_new != nullptr && s == n_splits - 1;
     const int pos = len - 1;
     if (warp < PK_WARPS) {
-        float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * PK_QR * pro_stride<NB>();
-        pack_load_q<NB>(p, item, qh0, warp, lane, qq, qd, pro);
-        if (do_append) pack_append<NB>(p, item, kvh_a, pos, warp, lane, newrow, pro);
+        float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * (PK_QR + PK_NJ) * pro_stride<NB>();
+        pack_preamble<NB>(p, item, qh0, kvh_a, pos, do_append, warp, lane, qq, qd, newrow, pro);
     }
     __syncthreads();
 
