@@ -170,11 +170,12 @@ class Config2:
     name = "config2"
     scaling = "weak"  # every rank decodes its own sequence
 
-    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096):
+    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096, prologue=False):
         import torch
         from tailorquantkernel_b200 import tqk
         self.tqk = tqk
         self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
+        self.prologue = prologue
         self.mt = pos + 1
         self.nb = hd // QK
         g = torch.Generator(device="cuda").manual_seed(seed)
@@ -183,7 +184,21 @@ class Config2:
         self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         rng = np.random.default_rng(seed)
-        q = rope_np(rng.standard_normal((layers, n_q * hd), dtype=np.float32), hd, pos, 500000.0)
+        q = rng.standard_normal((layers, n_q * hd), dtype=np.float32)
+        pro = {}
+        if prologue:
+            # Qwen3-style layer: per-layer q/k RMSNorm weights and the RoPE table of position pos,
+            # applied inside the decode launch (q and the appended k arrive un-normalised)
+            inv = np.float32(500000.0) ** (-2.0 * np.arange(hd // 2, dtype=np.float32) / np.float32(hd))
+            ang = np.float32(pos) * inv.astype(np.float32)
+            self.rope_cos = torch.from_numpy(np.tile(np.cos(ang).astype(np.float32), (layers, 1))).cuda()
+            self.rope_sin = torch.from_numpy(np.tile(np.sin(ang).astype(np.float32), (layers, 1))).cuda()
+            self.q_norm = torch.from_numpy(1 + 0.1 * rng.standard_normal((layers, hd), dtype=np.float32)).cuda()
+            self.k_norm = torch.from_numpy(1 + 0.1 * rng.standard_normal((layers, hd), dtype=np.float32)).cuda()
+            pro = dict(q_norm=self.q_norm, k_norm=self.k_norm, norm_item_stride=hd, norm_eps=1e-6,
+                       rope_cos=self.rope_cos, rope_sin=self.rope_sin, rope_item_stride=hd // 2)
+        else:
+            q = rope_np(q, hd, pos, 500000.0)
         self.q = torch.from_numpy(q).cuda()
         self.k_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
         self.v_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
@@ -191,7 +206,7 @@ class Config2:
         self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
                                     item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
                                     q_item_stride=n_q * hd, out_item_stride=n_q * hd, k_new=self.k_new,
-                                    v_new=self.v_new, kv_new_item_stride=n_kv * hd)
+                                    v_new=self.v_new, kv_new_item_stride=n_kv * hd, **pro)
         # algorithmic bytes of one step: K/V rows read + the appended Q8 rows written
         self.kv_bytes = 2 * layers * n_kv * (pos + 1) * self.nb * BB
         self.append_bytes = 2 * layers * n_kv * self.nb * BB
@@ -220,8 +235,10 @@ class Config2:
         s.synchronize()
 
     def describe(self):
+        pro = (", q/k RMSNorm + RoPE(500000) fused into the launch (Qwen3-style prologue)" if self.prologue
+               else ", RoPE(500000) q")
         return {"workload": "config2: Llama-3-8B-shaped Q8 GQA decode, all 32 layers, 32 q / 8 kv heads, "
-                            "head_dim 128, context 4096 + 1 appended token (n=4097), RoPE(500000) q",
+                            "head_dim 128, context 4096 + 1 appended token (n=4097)" + pro,
                 "layers": self.L, "seq_len": self.pos + 1, "kv_bytes_per_token": self.kv_bytes,
                 "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
 
@@ -675,7 +692,7 @@ def run_ours(args):
     peak, peak_kind = _peaks()
 
     if args.config == 2:
-        wl = Config2(seed=1000 + rank)
+        wl = Config2(seed=1000 + rank, prologue=args.prologue)
     elif args.config == 3:
         wl = Config3(seed=3000, rank=rank, world=world)
     elif args.config == 4:
@@ -789,6 +806,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prologue", action="store_true",
+                    help="config 2 with the q/k RMSNorm + RoPE prologue fused into the decode launch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
