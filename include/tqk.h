@@ -213,6 +213,47 @@ TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t work
  *     error word to report them: tqk_device_status does not see this entry. */
 TQK_API int tqk_decode_q8_static(const tqk_decode_args *a, tqk_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * The projections around the attention: Q8 / Q4 weight rows (the reference's
+ * packed format, packer/packer.h:9-10) times Q8 activations.  Bit-exact with
+ * the reference's scalar kernels: each output adds, in block order,
+ * (float)(int dot) * w.d * x.d rounded left to right.
+ */
+typedef struct { float d; uint8_t q[16]; } tqk_block_q4;  /* low nibble: element j, high: j + 16; value - 8 */
+#define TQK_FMT_Q8 0
+#define TQK_FMT_Q4 1
+
+/* matmul_q8_scalar / matmul_q4_scalar (kernel/q8_scalar.c:15-22,
+ * kernel/q4_scalar.c:17-24; MatmulFn of kernel/kernel.h:17): y[r] = W[r] . xq
+ * for rows x cols (cols % 32 == 0), all pointers on the device. */
+TQK_API int tqk_matmul_q8(const tqk_block_q8 *W, const tqk_block_q8 *xq, float *y, int rows, int cols,
+                          tqk_stream_t stream);
+TQK_API int tqk_matmul_q4(const tqk_block_q4 *W, const tqk_block_q8 *xq, float *y, int rows, int cols,
+                          tqk_stream_t stream);
+/* matmul_*_scalar_batch (q8_scalar.c:25-29, q4_scalar.c:27-31; MatmulBatchFn,
+ * kernel/kernel.h:21): n_tok activation rows xq [n_tok][cols/32], outputs
+ * y[t*rows + r].  Up to 8 tokens share one read of W; more are looped. */
+TQK_API int tqk_matmul_q8_batch(const tqk_block_q8 *W, const tqk_block_q8 *xq, float *y, int rows, int cols,
+                                int n_tok, tqk_stream_t stream);
+TQK_API int tqk_matmul_q4_batch(const tqk_block_q4 *W, const tqk_block_q8 *xq, float *y, int rows, int cols,
+                                int n_tok, tqk_stream_t stream);
+
+/* One matrix of a projection call: `rows` weight rows w (Q8 or Q4 blocks,
+ * device), outputs y[t*rows + r] (device). */
+typedef struct {
+    const void *w;
+    float *y;
+    int rows;
+} tqk_proj_job;
+/* quantize_row_q8 of n_tok fp32 rows x [n_tok][cols] (bit-exact with
+ * kernel/quant_x.c:12-34) and every job's matmul, in one launch: project_qkv
+ * (model/attention_layer.c:38-46: jobs wq, wk, wv), project_output (:161-167:
+ * job wo) and their batched forms (:207-214, :239-242).  1 to 4 jobs, all of
+ * `format` (TQK_FMT_Q8 / TQK_FMT_Q4) and `cols` columns; weights 4-byte aligned
+ * (16-byte aligned rows of whole 16-byte units take the TMA path). */
+TQK_API int tqk_project(const tqk_proj_job *jobs, int n_jobs, int format, const float *x, int cols, int n_tok,
+                        tqk_stream_t stream);
+
 /* attend_q8 for one layer of one sequence: n = pos + 1 positions
  * (reference model/attention_layer.c:125-150); TQK_EPOS if pos is out of range. */
 TQK_API int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,

@@ -45,6 +45,9 @@ _NAMES = {
     "rmsnorm": ("tqo_rmsnorm", "rmsnorm"),
     "rope_table": ("tqo_rope_table", "rope_table"),
     "rope_apply": ("tqo_rope_apply", "rope_apply"),
+    "pack": ("tqo_pack_matrix", "pack_matrix"),
+    "matmul_q8": ("tqo_matmul_q8", "matmul_q8_scalar"),
+    "matmul_q4": ("tqo_matmul_q4", "matmul_q4_scalar"),
 }
 
 
@@ -96,6 +99,11 @@ class Oracle:
         self._fn["rope_table"].argtypes = [vp, vp, i, i, f]
         self._fn["rope_apply"].argtypes = [vp, i, vp, vp]
         for k in ("rmsnorm", "rope_table", "rope_apply"):
+            self._fn[k].restype = None
+        self._fn["pack"].argtypes = [vp, i, i, vp, ctypes.c_char]
+        self._fn["pack"].restype = i
+        for k in ("matmul_q8", "matmul_q4"):
+            self._fn[k].argtypes = [vp, vp, vp, i, i]
             self._fn[k].restype = None
         if kind != "port":
             self.lib.refdrv_max_threads.restype = i
@@ -204,6 +212,25 @@ class Oracle:
             if cos_t is not None:
                 self._fn["rope_apply"](_vp(row), head_dim, _vp(np.ascontiguousarray(cos_t, dtype=np.float32)),
                                        _vp(np.ascontiguousarray(sin_t, dtype=np.float32)))
+        return y
+
+    def pack_matrix(self, w: np.ndarray, fmt: str) -> np.ndarray:
+        """pack_matrix (packer/packer.c:77-88) of fp32 W [rows, cols]: '8' -> Q8, '4' -> Q4 rows (uint8)."""
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        rows, cols = w.shape
+        nb = cols // QK
+        out = np.zeros((rows, nb * (BLOCK_BYTES if fmt == "8" else 20)), dtype=np.uint8)
+        rc = self._fn["pack"](_vp(w), rows, cols, _vp(out), fmt.encode())
+        if rc != 0:
+            raise ValueError(f"pack_matrix returned {rc}")
+        return out
+
+    def matmul(self, w_packed: np.ndarray, fmt: str, xq: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        """matmul_q8_scalar / matmul_q4_scalar (kernel/q8_scalar.c:15-22, q4_scalar.c:17-24) of one Q8
+        activation row xq (uint8 [cols/32*36]); matmul_*_scalar_batch is this per token."""
+        y = np.zeros(rows, dtype=np.float32)
+        self._fn["matmul_q8" if fmt == "8" else "matmul_q4"](_vp(np.ascontiguousarray(w_packed)),
+                                                             _vp(np.ascontiguousarray(xq)), _vp(y), rows, cols)
         return y
 
     def max_threads(self) -> int:

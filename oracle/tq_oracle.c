@@ -225,3 +225,90 @@ void tqo_rope_apply(float *x, int head_dim, const float *cos_t, const float *sin
         x[i + half] = x0 * sin_t[i] + x1 * cos_t[i];
     }
 }
+
+/* ---------------------------------------------------------------------------
+ * Weight packing and the projections' matrix-vector products.
+ * ------------------------------------------------------------------------- */
+
+/* packer/packer.c:4-9: round half away from zero, clamp to +-qmax. */
+static int tqo_pack_round(float x, float inv, int qmax) {
+    int q = (int)lroundf(x * inv);
+    return q > qmax ? qmax : q < -qmax ? -qmax : q;
+}
+
+/* packer/packer.c:11-19: max |w| / qmax over the block, 1.0 for an all-zero block. */
+static float tqo_pack_scale(const float *w, float qmax) {
+    float amax = 0.0f;
+    for (int j = 0; j < TQO_QK; j++) {
+        const float a = fabsf(w[j]);
+        if (a > amax) amax = a;
+    }
+    const float d = amax / qmax;
+    return d == 0.0f ? 1.0f : d;
+}
+
+/* packer/packer.c:22-33 (Q8), 40-53 (Q4: element j in the low nibble and j+16 in the
+ * high nibble of byte j, both offset by 8), 63-88 (row bytes, whole matrix). */
+int tqo_pack_matrix(const float *W, int rows, int cols, void *out, char bit_type) {
+    if (cols <= 0 || cols % TQO_QK != 0 || rows <= 0 || (bit_type != '8' && bit_type != '4')) return -1;
+    const int nb = cols / TQO_QK;
+    uint8_t *dst = (uint8_t *)out;
+    for (int r = 0; r < rows; r++) {
+        for (int b = 0; b < nb; b++) {
+            const float *w = W + (size_t)r * cols + (size_t)b * TQO_QK;
+            if (bit_type == '8') {
+                tqo_block_q8 *o = (tqo_block_q8 *)dst + (size_t)r * nb + b;
+                const float d = tqo_pack_scale(w, 127.0f), inv = 1.0f / d;
+                o->d = d;
+                for (int j = 0; j < TQO_QK; j++) o->q[j] = (int8_t)tqo_pack_round(w[j], inv, 127);
+            } else {
+                tqo_block_q4 *o = (tqo_block_q4 *)dst + (size_t)r * nb + b;
+                const float d = tqo_pack_scale(w, 7.0f), inv = 1.0f / d;
+                o->d = d;
+                for (int j = 0; j < TQO_QK / 2; j++) {
+                    const int lo = tqo_pack_round(w[j], inv, 7) + 8;
+                    const int hi = tqo_pack_round(w[j + TQO_QK / 2], inv, 7) + 8;
+                    o->q[j] = (uint8_t)((hi << 4) | lo);
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* kernel/q8_scalar.c:3-22: y[r] = sum over blocks, in block order, of
+ * (float)(int dot of the int8 values) * w.d * x.d, rounded left to right. */
+void tqo_matmul_q8(const void *W, const tqo_block_q8 *xq, float *y, int rows, int cols) {
+    const int nb = cols / TQO_QK;
+    const tqo_block_q8 *w = (const tqo_block_q8 *)W;
+    for (int r = 0; r < rows; r++) {
+        const tqo_block_q8 *wr = w + (size_t)r * nb;
+        float sum = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            int32_t s = 0;
+            for (int j = 0; j < TQO_QK; j++) s += (int32_t)wr[b].q[j] * xq[b].q[j];
+            sum += (float)s * wr[b].d * xq[b].d;
+        }
+        y[r] = sum;
+    }
+}
+
+/* kernel/q4_scalar.c:3-24: as tqo_matmul_q8 with the Q4 nibbles (value - 8) paired
+ * with x[j] (low) and x[j + 16] (high). */
+void tqo_matmul_q4(const void *W, const tqo_block_q8 *xq, float *y, int rows, int cols) {
+    const int nb = cols / TQO_QK;
+    const tqo_block_q4 *w = (const tqo_block_q4 *)W;
+    for (int r = 0; r < rows; r++) {
+        const tqo_block_q4 *wr = w + (size_t)r * nb;
+        float sum = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            int32_t s = 0;
+            for (int j = 0; j < TQO_QK / 2; j++) {
+                const int lo = (wr[b].q[j] & 0x0F) - 8, hi = (wr[b].q[j] >> 4) - 8;
+                s += lo * xq[b].q[j] + hi * xq[b].q[j + TQO_QK / 2];
+            }
+            sum += (float)s * wr[b].d * xq[b].d;
+        }
+        y[r] = sum;
+    }
+}

@@ -26,6 +26,8 @@ extern "C" {
 
 /* Same 36-byte layout as the reference block_q8 (packer/packer.h:7-11). */
 typedef struct { float d; int8_t q[TQO_QK]; } tqo_block_q8;
+/* packer/packer.h:10 */
+typedef struct { float d; uint8_t q[TQO_QK / 2]; } tqo_block_q4;
 
 /* kernel/quant_x.c:5-34 */
 void tqo_quantize_row_q8(const float *x, tqo_block_q8 *out, int n);
@@ -73,6 +75,13 @@ void tqo_rmsnorm(const float *x, const float *weight, float *out, int n, float e
 void tqo_rope_table(float *cos_t, float *sin_t, int head_dim, int pos, float theta);
 /* model/rope.c:14-22 */
 void tqo_rope_apply(float *x, int head_dim, const float *cos_t, const float *sin_t);
+
+/* packer/packer.c:4-88 (bit_type '8' or '4'); 0 or -1 like pack_matrix */
+int tqo_pack_matrix(const float *W, int rows, int cols, void *out, char bit_type);
+/* kernel/q8_scalar.c:3-22 */
+void tqo_matmul_q8(const void *W, const tqo_block_q8 *xq, float *y, int rows, int cols);
+/* kernel/q4_scalar.c:3-24 */
+void tqo_matmul_q4(const void *W, const tqo_block_q8 *xq, float *y, int rows, int cols);
 
 void tqo_attention_f64(const float *q, const float *k, const float *v, int n, int head_dim,
                        double *out);

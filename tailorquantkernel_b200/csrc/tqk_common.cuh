@@ -187,6 +187,23 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch (sm_90+).  grid_dependents_launch lets the
+// next kernel on the stream, when it was launched with programmatic stream
+// serialization, begin before this grid ends; grid_dependency_wait blocks
+// until every prerequisite grid has completed and its memory is visible (a
+// no-op when there is none).  Code before the wait may only read data that no
+// earlier kernel of the stream writes.
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Orders this thread's earlier shared-memory accesses (generic proxy) before
+// later async-proxy (TMA) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Makes barrier initialisation visible to the async (TMA) proxy.
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

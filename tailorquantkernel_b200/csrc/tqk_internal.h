@@ -35,6 +35,29 @@ void *library_workspace(cudaStream_t stream, size_t bytes);
 // holds nothing but tickets, zeroed when (re)allocated; every completed decode
 // leaves its tickets at zero, so the buffer stays zero between calls.
 int *library_counters(cudaStream_t stream, size_t bytes);
+// Library-owned staging buffer per (device, stream) for intermediate rows that
+// one call produces and consumes (e.g. quantised activations); grows on demand.
+void *library_scratch(cudaStream_t stream, size_t bytes);
+
+// Launches `kernel` with programmatic stream serialization, so that it may
+// start while the previous kernel of the stream finishes (the kernel must call
+// grid_dependency_wait before it reads anything that kernel wrote).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+    if (e != cudaSuccess) return fail_cuda(e, "kernel launch");
+    return check_launch("kernel launch");
+}
 
 // Tensor-core prefill attention over the chunk [pos0, pos0 + n) whose K/V rows
 // are already in the planes (tqk_prefill.cu).  TQK_EUNSUPPORTED for shapes it

@@ -22,6 +22,7 @@ struct Workspace {
 };
 std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
 std::map<std::pair<int, cudaStream_t>, Workspace> g_counters;
+std::map<std::pair<int, cudaStream_t>, Workspace> g_scratch;
 
 // Grows `w` to at least `bytes` (minimum 1 MiB), zeroing the new buffer on `stream`.
 void *grow_zeroed(Workspace &w, cudaStream_t stream, size_t bytes) {
@@ -100,6 +101,13 @@ int *library_counters(cudaStream_t stream, size_t bytes) {
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lock(g_mutex);
     return static_cast<int *>(grow_zeroed(g_counters[{dev, stream}], stream, bytes));
+}
+
+void *library_scratch(cudaStream_t stream, size_t bytes) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    return grow_zeroed(g_scratch[{dev, stream}], stream, bytes);
 }
 
 }  // namespace tqk

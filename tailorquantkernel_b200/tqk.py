@@ -91,6 +91,18 @@ tqk_decode_q8 = _sig("tqk_decode_q8", [ctypes.POINTER(DecodeArgs), _vp, _sz, _vp
 tqk_decode_q8_static = _sig("tqk_decode_q8_static", [ctypes.POINTER(DecodeArgs), _vp])
 tqk_qk_norm_rope = _sig("tqk_qk_norm_rope", [_vp, _vp, _i, _i64, _i64, _i, _i, _i, _vp, _vp, _i64, _f, _vp, _vp,
                                               _i64, _vp])
+tqk_matmul_q8 = _sig("tqk_matmul_q8", [_vp, _vp, _vp, _i, _i, _vp])
+tqk_matmul_q4 = _sig("tqk_matmul_q4", [_vp, _vp, _vp, _i, _i, _vp])
+tqk_matmul_q8_batch = _sig("tqk_matmul_q8_batch", [_vp, _vp, _vp, _i, _i, _i, _vp])
+tqk_matmul_q4_batch = _sig("tqk_matmul_q4_batch", [_vp, _vp, _vp, _i, _i, _i, _vp])
+
+
+class ProjJob(ctypes.Structure):
+    """Mirror of tqk_proj_job (include/tqk.h)."""
+    _fields_ = [("w", _vp), ("y", _vp), ("rows", _i)]
+
+
+tqk_project = _sig("tqk_project", [ctypes.POINTER(ProjJob), _i, _i, _vp, _i, _i, _vp])
 tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
@@ -103,6 +115,7 @@ EXPORTED = [
     "tqk_decode_workspace_size", "tqk_workspace_init", "tqk_decode_q8",
     "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
     "tqk_decode_q8_static", "tqk_qk_norm_rope",
+    "tqk_matmul_q8", "tqk_matmul_q4", "tqk_matmul_q8_batch", "tqk_matmul_q4_batch", "tqk_project",
 ]
 
 
@@ -239,6 +252,22 @@ def qk_norm_rope(q, k, n_items, n_q, n_kv, head_dim, q_norm=None, k_norm=None, e
     check(tqk_qk_norm_rope(_ptr(q), _ptr(k), n_items, q_item_stride, k_item_stride, n_q, n_kv, head_dim,
                            _ptr(q_norm), _ptr(k_norm), norm_item_stride, eps, _ptr(rope_cos), _ptr(rope_sin),
                            rope_item_stride, _stream(stream)), "tqk_qk_norm_rope")
+
+
+FMT_Q8, FMT_Q4 = 0, 1
+Q4_BLOCK_BYTES = 20
+
+
+def matmul(w, fmt, xq, y, rows, cols, n_tok=1, stream=None) -> None:
+    """tqk_matmul_{q8,q4}[_batch]: y[t*rows + r] = W[r] . xq[t] (fmt FMT_Q8 / FMT_Q4; device tensors)."""
+    fn = tqk_matmul_q8_batch if fmt == FMT_Q8 else tqk_matmul_q4_batch
+    check(fn(_ptr(w), _ptr(xq), _ptr(y), rows, cols, n_tok, _stream(stream)), "tqk_matmul")
+
+
+def project(jobs, fmt, x, cols, n_tok=1, stream=None) -> None:
+    """tqk_project: quantise the n_tok fp32 rows of x and run every (w, y, rows) job in one launch."""
+    arr = (ProjJob * len(jobs))(*[ProjJob(_ptr(w), _ptr(y), rows) for (w, y, rows) in jobs])
+    check(tqk_project(arr, len(jobs), fmt, _ptr(x), cols, n_tok, _stream(stream)), "tqk_project")
 
 
 def decode_static(args: DecodeArgs, stream=None) -> None:

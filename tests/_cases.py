@@ -137,3 +137,17 @@ def norm_rope_inputs(seed: int, n_items: int, n_q: int, n_kv: int, hd: int, per_
     qw = (np.float32(1.0) + np.float32(0.1) * rng.standard_normal((nw, hd), dtype=np.float32))
     kw = (np.float32(1.0) + np.float32(0.1) * rng.standard_normal((nw, hd), dtype=np.float32))
     return q, k, qw, kw
+
+
+def matmul_inputs(seed: int, rows: int, cols: int, x_kind: str = "random"):
+    """W [rows, cols] and x [cols] of one matmul case (tools/test_kernel.c:52-75 style: uniform in
+    [-1, 1); x constant 1 or all zero for the edge cases)."""
+    rng = np.random.default_rng(seed)
+    w = rng.uniform(-1.0, 1.0, (rows, cols)).astype(np.float32)
+    if x_kind == "random":
+        x = rng.uniform(-1.0, 1.0, cols).astype(np.float32)
+    elif x_kind == "constant":
+        x = np.ones(cols, np.float32)
+    else:
+        x = np.zeros(cols, np.float32)
+    return w, x

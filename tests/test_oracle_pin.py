@@ -11,8 +11,8 @@ import numpy as np
 import pytest
 
 import oracle
-from _cases import (decode_case, digest, head_inputs, norm_rope_inputs, prefill_inputs, quant_edge_rows,
-                    sweep_inputs, tolerance_ok)
+from _cases import (decode_case, digest, head_inputs, matmul_inputs, norm_rope_inputs, prefill_inputs,
+                    quant_edge_rows, sweep_inputs, tolerance_ok)
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -197,3 +197,44 @@ def test_norm_rope_against_reference_build(port):
         a = port.qk_norm_rope(x, 5, hd, w, 1e-6, c, s)
         b = ref.qk_norm_rope(x, 5, hd, w, 1e-6, cr, sr)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+# (rows, cols, x kind) of tests/golden/make_golden.py MATMUL_CASES, seeds 500 + index
+MATMUL_CASES = [(rows, cols, "random") for rows, cols in
+                ((256, 512), (7, 64), (10, 32), (1027, 96), (1024, 1024), (3072, 1024), (1024, 3072))] + \
+               [(256, 512, "constant"), (256, 512, "zero")]
+
+
+@pytest.mark.parametrize("i", range(len(MATMUL_CASES)))
+@pytest.mark.parametrize("fmt", ["8", "4"])
+def test_matmul_golden(port, i, fmt):
+    """pack_matrix + matmul_q{8,4}_scalar (packer/packer.c, kernel/q8_scalar.c, q4_scalar.c)
+    bit-exact with the reference's outputs on the reference test's shapes."""
+    rows, cols, kind = MATMUL_CASES[i]
+    g = _load("matmul.npz")
+    key = f"{rows}x{cols}_{kind}"
+    w, x = matmul_inputs(500 + i, rows, cols, kind)
+    assert digest(w, x) == str(g[key + "__in_sha"])
+    wp = port.pack_matrix(w, fmt)
+    assert digest(wp) == str(g[f"{key}__q{fmt}_packed_sha"])
+    y = port.matmul(wp, fmt, port.quantize_rows(x[None])[0], rows, cols)
+    assert np.array_equal(y.view(np.uint32), g[f"{key}__q{fmt}_y"].view(np.uint32))
+    if kind == "zero":
+        assert not np.any(y)
+
+
+def test_matmul_against_reference_build(port):
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    ref = oracle.Oracle("ref_scalar")
+    rng = np.random.default_rng(77)
+    for rows, cols in ((33, 128), (5, 4096)):
+        w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(3.0)
+        w[0, :32] = 0.0  # an all-zero block: scale 1.0
+        x = rng.standard_normal(cols, dtype=np.float32)
+        xq = port.quantize_rows(x[None])[0]
+        for fmt in "84":
+            wp = port.pack_matrix(w, fmt)
+            assert np.array_equal(wp, ref.pack_matrix(w, fmt))
+            assert np.array_equal(port.matmul(wp, fmt, xq, rows, cols).view(np.uint32),
+                                  ref.matmul(wp, fmt, xq, rows, cols).view(np.uint32))
