@@ -254,6 +254,38 @@ typedef struct {
 TQK_API int tqk_project(const tqk_proj_job *jobs, int n_jobs, int format, const float *x, int cols, int n_tok,
                         tqk_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * One attention layer for one token, on the device: attention_layer
+ * (model/attention_layer.c:169-194) -- project_qkv, norm_heads + rope_heads,
+ * store_kv + attend_q8, project_output -- as three launches (q/k/v
+ * projection with the activation quantisation, decode with the fused norm,
+ * RoPE and append, output projection) chained by programmatic dependent
+ * launch, so each launch's weight prefetch overlaps the previous kernel.
+ * The appended cache rows are bit-exact with the reference's; the output
+ * follows the decode's tolerance through the output projection.
+ */
+typedef struct {
+    const void *wq, *wk, *wv, *wo;     /* packed weight rows (device), all of `format` */
+    int format;                        /* TQK_FMT_Q8 or TQK_FMT_Q4 */
+    const float *q_norm, *k_norm;      /* [head_dim] each (device) */
+    int n_q_heads, n_kv_heads, head_dim, hidden_size;
+    float rms_eps;
+    tqk_block_q8 *k, *v;               /* the layer's cache planes [n_kv][max_tokens][head_dim/32] (device) */
+    int max_tokens;
+    int pos;                           /* the token's position: appended at pos, attention over [0, pos] */
+    const int32_t *len;                /* optional device int holding pos + 1, read when the kernels run
+                                          (CUDA-graph replay across tokens); pos then only bounds it */
+    const float *rope_cos, *rope_sin;  /* rope_table of the position, [head_dim/2] each (device) */
+    const float *xn;                   /* [hidden_size] input (device) */
+    float *out;                        /* [hidden_size] output (device) */
+    float *scratch;                    /* device floats: 2*n_q*head_dim + 2*n_kv*head_dim (q, k, v, attention) */
+} tqk_attn_layer_args;
+/* workspace: as tqk_decode_q8's (NULL = library-owned); a call made under
+ * stream capture needs a caller workspace, or one earlier call on the same
+ * stream outside capture. */
+TQK_API int tqk_attention_layer(const tqk_attn_layer_args *a, void *workspace, size_t workspace_bytes,
+                                tqk_stream_t stream);
+
 /* attend_q8 for one layer of one sequence: n = pos + 1 positions
  * (reference model/attention_layer.c:125-150); TQK_EPOS if pos is out of range. */
 TQK_API int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,

@@ -70,6 +70,29 @@ def _f32p(a):
 def _vp(a):
     return ctypes.c_void_p(a.ctypes.data)
 
+class _TqMatrix(ctypes.Structure):
+    """tq_matrix (model/model_ops.h): packed rows, tq_format (0 = Q8, 1 = Q4), rows, cols."""
+    _fields_ = [("data", ctypes.c_void_p), ("format", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int)]
+
+
+class _TqAttnWeights(ctypes.Structure):
+    """tq_attn_weights (model/model_ops.h)."""
+    _fields_ = [("wq", _TqMatrix), ("wk", _TqMatrix), ("wv", _TqMatrix), ("wo", _TqMatrix),
+                ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+
+
+class _TqAttnConfig(ctypes.Structure):
+    """tq_attn_config (model/model_ops.h)."""
+    _fields_ = [("n_q_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("hidden_size", ctypes.c_int), ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+
+class _TqKvCache(ctypes.Structure):
+    """tq_kv_cache (model/model_ops.h): type (0 = F32, 1 = Q8), four plane pointers, max_tokens."""
+    _fields_ = [("type", ctypes.c_int), ("k_f32", ctypes.c_void_p), ("v_f32", ctypes.c_void_p),
+                ("k_q8", ctypes.c_void_p), ("v_q8", ctypes.c_void_p), ("max_tokens", ctypes.c_int)]
+
+
 
 class Oracle:
     def __init__(self, kind: str = "port"):
@@ -232,6 +255,48 @@ class Oracle:
         self._fn["matmul_q8" if fmt == "8" else "matmul_q4"](_vp(np.ascontiguousarray(w_packed)),
                                                              _vp(np.ascontiguousarray(xq)), _vp(y), rows, cols)
         return y
+
+    def attention_layer(self, w: dict, fmt: str, q_norm, k_norm, n_q: int, n_kv: int, head_dim: int,
+                        hidden: int, theta: float, eps: float, kp, vp, max_tokens: int, pos: int, xn):
+        """One attention_layer step (model/attention_layer.c:169-194) for one token at pos: w holds the
+        packed 'wq', 'wk', 'wv', 'wo' rows; kp/vp (the layer's Q8 cache planes) get the appended rows
+        in place.  The reference kinds call the reference's own attention_layer; the port composes the
+        restated steps (quantize_row_q8, matmul, norm_heads + rope_heads, store_kv, attend_q8,
+        quantize_row_q8, matmul).  Returns the output [hidden]."""
+        q_dim, kv_dim = n_q * head_dim, n_kv * head_dim
+        xn = np.ascontiguousarray(xn, dtype=np.float32)
+        if self.kind == "port":
+            xq = self.quantize_rows(xn[None])[0]
+            q = self.matmul(w["wq"], fmt, xq, q_dim, hidden)
+            k = self.matmul(w["wk"], fmt, xq, kv_dim, hidden)
+            v = self.matmul(w["wv"], fmt, xq, kv_dim, hidden)
+            c, s = self.rope_table(head_dim, pos, theta)
+            q = self.qk_norm_rope(q, n_q, head_dim, q_norm, eps, c, s)
+            k = self.qk_norm_rope(k, n_kv, head_dim, k_norm, eps, c, s)
+            if self.store_kv(kp, vp, n_kv, head_dim, max_tokens, pos, k, v) != 0:
+                raise ValueError("store_kv refused the position")
+            attn = self.attend(kp, vp, n_q, n_kv, head_dim, max_tokens, pos, q)
+            aq = self.quantize_rows(attn[None])[0]
+            return self.matmul(w["wo"], fmt, aq, hidden, q_dim)
+        f = 0 if fmt == "8" else 1
+        keep = [np.ascontiguousarray(w[n]) for n in ("wq", "wk", "wv", "wo")]
+        qn = np.ascontiguousarray(q_norm, dtype=np.float32)
+        kn = np.ascontiguousarray(k_norm, dtype=np.float32)
+        mats = [_TqMatrix(_vp(keep[0]), f, q_dim, hidden), _TqMatrix(_vp(keep[1]), f, kv_dim, hidden),
+                _TqMatrix(_vp(keep[2]), f, kv_dim, hidden), _TqMatrix(_vp(keep[3]), f, hidden, q_dim)]
+        aw = _TqAttnWeights(*mats, _vp(qn), _vp(kn))
+        cfg = _TqAttnConfig(n_q, n_kv, head_dim, hidden, theta, eps)
+        cache = _TqKvCache(1, None, None, _vp(kp), _vp(vp), max_tokens)
+        scores = np.zeros(n_q * max_tokens, dtype=np.float32)  # one slice per q head (model/context.c:34)
+        out = np.zeros(hidden, dtype=np.float32)
+        fn = self.lib.attention_layer
+        fn.argtypes = [ctypes.POINTER(_TqAttnWeights), ctypes.POINTER(_TqAttnConfig), ctypes.POINTER(_TqKvCache),
+                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        fn.restype = ctypes.c_int
+        rc = fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos, _vp(xn), _vp(scores), _vp(out))
+        if rc != 0:
+            raise ValueError(f"attention_layer returned {rc}")
+        return out
 
     def max_threads(self) -> int:
         return self.lib.refdrv_max_threads() if self.kind != "port" else os.cpu_count() or 1

@@ -313,6 +313,11 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // programmatic dependent launch: everything this kernel reads (q, new rows,
+    // lengths, cache rows) may come from earlier kernels of the stream, so wait
+    // for them first; then the next kernel may start its own prefetch
+    grid_dependency_wait();
+    grid_dependents_launch();
 
     const int item = blockIdx.z;
     const int pair = blockIdx.y;
@@ -685,8 +690,7 @@ int launch_mma(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_
         *ctas_per_sm = occ;
         return TQK_OK;
     }
-    decode_q8_mma_kernel<NB, GPAD><<<grid, MMA_THREADS, L::BYTES, stream>>>(p);
-    return check_launch("decode_q8_mma_kernel");
+    return launch_pdl(decode_q8_mma_kernel<NB, GPAD>, grid, dim3(MMA_THREADS), L::BYTES, stream, p);
 }
 
 // Two-kv-heads-per-CTA kernel for 4 q heads per kv head.
@@ -715,8 +719,7 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
         *ctas_per_sm = occ;
         return TQK_OK;
     }
-    decode_q8_pack_kernel<NB><<<grid, PK_THREADS, L::BYTES, stream>>>(p);
-    return check_launch("decode_q8_pack_kernel");
+    return launch_pdl(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, p);
 }
 
 int dispatch_pack(int nb, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
@@ -756,8 +759,7 @@ int launch_decode(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ct
         *ctas_per_sm = occ;
         return TQK_OK;
     }
-    decode_q8_kernel<NB, GMAX><<<grid, DEC_THREADS, L::BYTES, stream>>>(p);
-    return check_launch("decode_q8_kernel");
+    return launch_pdl(decode_q8_kernel<NB, GMAX>, grid, dim3(DEC_THREADS), L::BYTES, stream, p);
 }
 
 template <int NB>

@@ -369,6 +369,11 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // programmatic dependent launch: everything this kernel reads (q, new rows,
+    // lengths, cache rows) may come from earlier kernels of the stream, so wait
+    // for them first; then the next kernel may start its own prefetch
+    grid_dependency_wait();
+    grid_dependents_launch();
 
     const int item = blockIdx.z;
     const int pair = blockIdx.y;

@@ -375,6 +375,11 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // programmatic dependent launch: everything this kernel reads (q, new rows,
+    // lengths, cache rows) may come from earlier kernels of the stream, so wait
+    // for them first; then the next kernel may start its own prefetch
+    grid_dependency_wait();
+    grid_dependents_launch();
 
     const int item = blockIdx.z;
     const int pair = blockIdx.y;  // kv heads 2*pair and 2*pair+1

@@ -18,6 +18,11 @@
 // (row, token, block) term into the warp's scratch.  After MB groups (or the
 // last one) lanes 0 .. MB*R*n_tok - 1 each walk one (row, token) chain over the
 // scratch with 16-byte loads and write y.
+// The kernel is launched with programmatic stream serialization: before
+// griddepcontrol.wait it only issues weight copies (weights are never written
+// by kernels), so in a chain of launches its weight prefetch overlaps the
+// previous kernel.  Weights must not be modified by kernels on the stream
+// while a call that reads them may be in flight.
 // The activations sit in shared memory for the whole CTA, per token in
 // chunks of four blocks (128 bytes of int8 + 16 bytes of padding, so that the
 // lanes' chunk loads hit distinct banks), with the scales and (Q4) int8 sums
@@ -174,11 +179,12 @@ __global__ void __launch_bounds__(MV_MAX_WARPS * 32, 1) matvec_kernel(const MvPa
         }
     };
     if (active && p.tma) fetch(gw, 0);
-    // programmatic dependent launch: the next kernel on the stream may start
-    // its own weight prefetch now; the activations below may come from the
-    // previous kernel, so they are read only after it completed
-    grid_dependents_launch();
+    // programmatic dependent launch: the weights (which no kernel writes) are
+    // already in flight; the activations below may come from earlier kernels,
+    // so they are read only after those completed.  Then the next kernel may
+    // start its own weight prefetch.
     grid_dependency_wait();
+    grid_dependents_launch();
 
     // the activations, quantised here when fp32 x is given: one thread per
     // 32-float block (quant_x.c:12-34), all blocks at once

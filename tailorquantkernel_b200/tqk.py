@@ -103,6 +103,28 @@ class ProjJob(ctypes.Structure):
 
 
 tqk_project = _sig("tqk_project", [ctypes.POINTER(ProjJob), _i, _i, _vp, _i, _i, _vp])
+
+
+class AttnLayerArgs(ctypes.Structure):
+    """Mirror of tqk_attn_layer_args (include/tqk.h)."""
+    _fields_ = [
+        ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp),
+        ("format", _i),
+        ("q_norm", _vp), ("k_norm", _vp),
+        ("n_q_heads", _i), ("n_kv_heads", _i), ("head_dim", _i), ("hidden_size", _i),
+        ("rms_eps", _f),
+        ("k", _vp), ("v", _vp),
+        ("max_tokens", _i),
+        ("pos", _i),
+        ("len", _vp),
+        ("rope_cos", _vp), ("rope_sin", _vp),
+        ("xn", _vp),
+        ("out", _vp),
+        ("scratch", _vp),
+    ]
+
+
+tqk_attention_layer = _sig("tqk_attention_layer", [ctypes.POINTER(AttnLayerArgs), _vp, _sz, _vp])
 tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
@@ -116,6 +138,7 @@ EXPORTED = [
     "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
     "tqk_decode_q8_static", "tqk_qk_norm_rope",
     "tqk_matmul_q8", "tqk_matmul_q4", "tqk_matmul_q8_batch", "tqk_matmul_q4_batch", "tqk_project",
+    "tqk_attention_layer",
 ]
 
 
@@ -268,6 +291,35 @@ def project(jobs, fmt, x, cols, n_tok=1, stream=None) -> None:
     """tqk_project: quantise the n_tok fp32 rows of x and run every (w, y, rows) job in one launch."""
     arr = (ProjJob * len(jobs))(*[ProjJob(_ptr(w), _ptr(y), rows) for (w, y, rows) in jobs])
     check(tqk_project(arr, len(jobs), fmt, _ptr(x), cols, n_tok, _stream(stream)), "tqk_project")
+
+
+def layer_scratch_floats(n_q, n_kv, head_dim) -> int:
+    """Floats of scratch tqk_attention_layer needs (q, k, v, attention)."""
+    return 2 * n_q * head_dim + 2 * n_kv * head_dim
+
+
+def attention_layer_args(w, fmt, q_norm, k_norm, n_q, n_kv, head_dim, hidden, eps, k, v, max_tokens, pos,
+                         rope_cos, rope_sin, xn, out, scratch, len_dev=None) -> AttnLayerArgs:
+    """tqk_attn_layer_args from device tensors; w maps 'wq', 'wk', 'wv', 'wo' to packed rows."""
+    a = AttnLayerArgs()
+    a.wq, a.wk, a.wv, a.wo = (_ptr(w[n]) for n in ("wq", "wk", "wv", "wo"))
+    a.format = fmt
+    a.q_norm, a.k_norm = _ptr(q_norm), _ptr(k_norm)
+    a.n_q_heads, a.n_kv_heads, a.head_dim, a.hidden_size = n_q, n_kv, head_dim, hidden
+    a.rms_eps = eps
+    a.k, a.v = _ptr(k), _ptr(v)
+    a.max_tokens, a.pos = max_tokens, pos
+    a.len = _ptr(len_dev)
+    a.rope_cos, a.rope_sin = _ptr(rope_cos), _ptr(rope_sin)
+    a.xn, a.out, a.scratch = _ptr(xn), _ptr(out), _ptr(scratch)
+    return a
+
+
+def attention_layer(args: AttnLayerArgs, workspace=None, stream=None) -> None:
+    """tqk_attention_layer: one token through one attention layer on the device."""
+    ws = _ptr(workspace) if workspace is not None else None
+    nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(tqk_attention_layer(ctypes.byref(args), ws, nbytes, _stream(stream)), "tqk_attention_layer")
 
 
 def decode_static(args: DecodeArgs, stream=None) -> None:

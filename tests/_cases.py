@@ -151,3 +151,21 @@ def matmul_inputs(seed: int, rows: int, cols: int, x_kind: str = "random"):
     else:
         x = np.zeros(cols, np.float32)
     return w, x
+
+
+def layer_inputs(seed: int, n_q: int, n_kv: int, hd: int, hidden: int, max_tokens: int, pos: int, fmt: str, port):
+    """One attention_layer case (model/attention_layer.c:169-194): packed wq/wk/wv/wo (uniform in
+    [-1, 1), packed by the pinned oracle packer), q/k norm weights, Q8 cache planes holding
+    positions [0, pos) and the input xn."""
+    rng = np.random.default_rng(seed)
+    shapes = {"wq": (n_q * hd, hidden), "wk": (n_kv * hd, hidden), "wv": (n_kv * hd, hidden),
+              "wo": (hidden, n_q * hd)}
+    w = {n: port.pack_matrix(rng.uniform(-1.0, 1.0, sh).astype(np.float32), fmt) for n, sh in shapes.items()}
+    qn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
+    vf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
+    kf[:, pos:] = 0.0
+    vf[:, pos:] = 0.0
+    xn = rng.standard_normal(hidden, dtype=np.float32)
+    return w, qn, kn, port.quantize_rows(kf), port.quantize_rows(vf), xn

@@ -64,6 +64,22 @@ def test_decode_args_layout_matches_c(tmp_path):
     assert vals[1:] == [getattr(tqk.DecodeArgs, f).offset for f in fields]
 
 
+def test_attn_layer_args_layout_matches_c(tmp_path):
+    """The ctypes mirror of tqk_attn_layer_args has the C layout (size and offsets)."""
+    from tailorquantkernel_b200 import tqk
+    fields = [f for f, _ in tqk.AttnLayerArgs._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "tqk.h"\nint main(void){\n'
+                   'printf("%zu\\n", sizeof(tqk_attn_layer_args));\n' +
+                   "".join(f'printf("%zu\\n", offsetof(tqk_attn_layer_args, {f}));\n' for f in fields) +
+                   "return 0;}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["/usr/bin/gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(tqk.AttnLayerArgs)
+    assert vals[1:] == [getattr(tqk.AttnLayerArgs, f).offset for f in fields]
+
+
 def test_decode_prologue_arguments_checked_before_the_device():
     """q_norm/k_norm and rope_cos/rope_sin come in pairs; the check precedes any device work."""
     from tailorquantkernel_b200 import tqk

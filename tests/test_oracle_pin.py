@@ -11,8 +11,8 @@ import numpy as np
 import pytest
 
 import oracle
-from _cases import (decode_case, digest, head_inputs, matmul_inputs, norm_rope_inputs, prefill_inputs,
-                    quant_edge_rows, sweep_inputs, tolerance_ok)
+from _cases import (decode_case, digest, head_inputs, layer_inputs, matmul_inputs, norm_rope_inputs,
+                    prefill_inputs, quant_edge_rows, sweep_inputs, tolerance_ok)
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
@@ -238,3 +238,25 @@ def test_matmul_against_reference_build(port):
             assert np.array_equal(wp, ref.pack_matrix(w, fmt))
             assert np.array_equal(port.matmul(wp, fmt, xq, rows, cols).view(np.uint32),
                                   ref.matmul(wp, fmt, xq, rows, cols).view(np.uint32))
+
+
+# tests/golden/make_golden.py LAYER_CASES
+LAYER_CASES = {
+    "small_g4": (61, 8, 2, 64, 256, 40, 25, 1000000.0, 1e-6),
+    "llama_heads": (62, 32, 8, 128, 512, 70, 64, 500000.0, 1e-5),
+}
+
+
+@pytest.mark.parametrize("name", sorted(LAYER_CASES))
+@pytest.mark.parametrize("fmt", ["8", "4"])
+def test_attention_layer_golden(port, name, fmt):
+    """The port's composition of attention_layer's steps equals the reference's attention_layer
+    bit for bit: output and appended cache rows."""
+    seed, nq, nkv, hd, hidden, mt, pos, theta, eps = LAYER_CASES[name]
+    g = _load("layer.npz")
+    key = f"{name}_q{fmt}"
+    w, qn, kn, kp, vp, xn = layer_inputs(seed, nq, nkv, hd, hidden, mt, pos, fmt, port)
+    assert digest(*[w[n] for n in ("wq", "wk", "wv", "wo")], qn, kn, kp, vp, xn) == str(g[key + "__in_sha"])
+    y = port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp, vp, mt, pos, xn)
+    assert np.array_equal(y.view(np.uint32), g[key + "__out"].view(np.uint32))
+    assert np.array_equal(kp[:, pos], g[key + "__k_row"]) and np.array_equal(vp[:, pos], g[key + "__v_row"])
