@@ -472,6 +472,157 @@ class Config5:
                 self.v_new.cpu().numpy())
 
 
+def q8_weight_rows_np(rng, rows: int, cols: int) -> np.ndarray:
+    """Random packed Q8 weight rows (packer/packer.h layout: per 32 columns a float scale and 32
+    int8): int8 uniform in [-127, 127], scales uniform in [0.002, 0.02)."""
+    nb = cols // QK
+    w = np.empty((rows, nb, BB), np.uint8)
+    w[:, :, 4:] = rng.integers(-127, 128, (rows, nb, QK), dtype=np.int8).view(np.uint8)
+    w[:, :, :4] = rng.uniform(0.002, 0.02, (rows, nb)).astype(np.float32).view(np.uint8).reshape(rows, nb, 4)
+    return w.reshape(rows, nb * BB)
+
+
+class Config6:
+    """A Llama-3-8B-shaped attention stack on the device: one token through 32 attention layers
+    (tqk_attention_layer: q/k/v projection with the activation quantisation, decode with the fused
+    q/k RMSNorm + RoPE + append at position 4096, output projection), each layer's output feeding
+    the next layer's input, the 96 launches captured once in a CUDA graph and replayed per step.
+    Q8 weights (1.51 GB for the 32 layers) and the Q8 cache (302 MB) stay in HBM."""
+    name = "config6"
+    scaling = "weak"
+    e2e_steps = 2000
+    data = ("synthetic: seeded random packed Q8 weights (int8 uniform, scales uniform in [0.002, 0.02)), "
+            "N(0,1) K/V quantised to Q8 on the device, N(0,1) input")
+
+    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, pos=4096):
+        import torch
+        from tailorquantkernel_b200 import tqk
+        self.tqk = tqk
+        self.L, self.nq, self.nkv, self.hd, self.hidden, self.pos = layers, n_q, n_kv, hd, hidden, pos
+        self.mt = pos + 1
+        self.nb = hd // QK
+        rng = np.random.default_rng(seed)
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        q_dim, kv_dim = n_q * hd, n_kv * hd
+        shapes = {"wq": (q_dim, hidden), "wk": (kv_dim, hidden), "wv": (kv_dim, hidden), "wo": (hidden, q_dim)}
+        self.w = [{n: torch.from_numpy(q8_weight_rows_np(rng, *sh)).cuda() for n, sh in shapes.items()}
+                  for _ in range(layers)]
+        self.qn = [torch.from_numpy((1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)).cuda()
+                   for _ in range(layers)]
+        self.kn = [torch.from_numpy((1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)).cuda()
+                   for _ in range(layers)]
+        shape = (n_kv, self.mt, hd)
+        self.kp = [tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g)) for _ in range(layers)]
+        self.vp = [tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g)) for _ in range(layers)]
+        inv = np.float32(500000.0) ** (-2.0 * np.arange(hd // 2, dtype=np.float32) / np.float32(hd))
+        ang = np.float32(pos) * inv.astype(np.float32)
+        self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
+        self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).cuda()
+        self.acts = [torch.from_numpy(rng.standard_normal(hidden, dtype=np.float32)).cuda()]
+        self.acts += [torch.empty(hidden, device="cuda") for _ in range(layers)]
+        self.scratch = torch.empty(tqk.layer_scratch_floats(n_q, n_kv, hd), device="cuda")
+        self.ws = torch.zeros(1 << 22, dtype=torch.uint8, device="cuda")
+        self.args = [tqk.attention_layer_args(self.w[l], tqk.FMT_Q8, self.qn[l], self.kn[l], n_q, n_kv, hd, hidden,
+                                              1e-6, self.kp[l], self.vp[l], self.mt, pos, self.cos, self.sin,
+                                              self.acts[l], self.acts[l + 1], self.scratch)
+                     for l in range(layers)]
+        # captured on a side stream (CUDA requires it), replayed on the current one
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            tqk.workspace_init(self.ws, cap)
+            for l in range(layers):  # eager once: sets the kernels up outside capture
+                tqk.attention_layer(self.args[l], self.ws, cap)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=cap):
+                for l in range(layers):
+                    tqk.attention_layer(self.args[l], self.ws, cap)
+        cap.synchronize()
+        self.stream = torch.cuda.current_stream()
+        wbytes = sum(t.numel() for t in self.w[0].values()) * layers
+        self.weight_bytes = wbytes
+        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * self.nb * BB
+        self.bytes_per_step = wbytes + self.kv_bytes + 2 * layers * n_kv * self.nb * BB
+        self.tokens_per_step = 1
+        self.launches_per_step = 3 * layers
+        self.h_x = self.acts[0].cpu().pin_memory()
+        self.h_out = torch.empty(hidden).pin_memory()
+        self.h2d = self.h_x.numel() * 4
+        self.d2h = self.h_out.numel() * 4
+        self.e2e_api = ("tqk_attention_layer x 32 (C ABI) replayed as one CUDA graph, with the token's input "
+                        "copied in from pinned host memory and the last layer's output copied out, "
+                        "stream-synchronised every step")
+
+    def step(self):
+        self.graph.replay()
+
+    def step_e2e(self):
+        self.acts[0].copy_(self.h_x, non_blocking=True)
+        self.graph.replay()
+        self.h_out.copy_(self.acts[-1], non_blocking=True)
+        self.stream.synchronize()
+
+    def describe(self):
+        return {"workload": "config6: Llama-3-8B-shaped attention stack, one token through 32 attention layers "
+                            "(Q8 wq/wk/wv/wo, q/k RMSNorm + RoPE(500000), Q8 cache append at 4096 and attention "
+                            "over 4097 positions, output projection), each layer's output feeding the next",
+                "layers": self.L, "seq_len": self.pos + 1, "hidden": self.hidden,
+                "weight_bytes_per_token": self.weight_bytes, "kv_bytes_per_token": self.kv_bytes,
+                "l2": "no flush: inputs larger than L2 (1.81 GB per step vs 126 MB L2)"}
+
+    @staticmethod
+    def parallelism(world):
+        return "replicas: every GPU runs its own token" if world > 1 else "single GPU"
+
+
+class HostConfig6:
+    """Config 6 on the host only, for the reference's attention_layer (CPU): the same shapes, random
+    packed Q8 weights and a cache quantised by the reference's own quantiser."""
+    name = "config6"
+
+    def __init__(self, orc, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, pos=4096):
+        self.L, self.nq, self.nkv, self.hd, self.hidden, self.pos = layers, n_q, n_kv, hd, hidden, pos
+        self.mt = pos + 1
+        self.nb = hd // QK
+        rng = np.random.default_rng(seed)
+        q_dim, kv_dim = n_q * hd, n_kv * hd
+        shapes = {"wq": (q_dim, hidden), "wk": (kv_dim, hidden), "wv": (kv_dim, hidden), "wo": (hidden, q_dim)}
+        self.w = [{n: q8_weight_rows_np(rng, *sh) for n, sh in shapes.items()} for _ in range(layers)]
+        self.qn = [(1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) for _ in range(layers)]
+        self.kn = [(1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) for _ in range(layers)]
+        row = self.nb * BB
+        self.kp = [orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
+                   for _ in range(layers)]
+        self.vp = [orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
+                   for _ in range(layers)]
+        self.x = rng.standard_normal(hidden, dtype=np.float32)
+        wbytes = sum(a.size for a in self.w[0].values()) * layers
+        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * row
+        self.bytes_per_step = wbytes + self.kv_bytes + 2 * layers * n_kv * row
+
+    def describe(self):
+        return {"workload": "config6: Llama-3-8B-shaped attention stack, one token through 32 attention layers "
+                            "(the reference's attention_layer, Q8 weights, Q8 cache at 4096)",
+                "layers": self.L, "seq_len": self.pos + 1, "hidden": self.hidden}
+
+
+def reference_layers_seconds(orc, wl, budget_s: float, max_tokens: int | None = None, min_tokens: int = 2):
+    """Times the reference's attention_layer (model/attention_layer.c:169-194) through all layers for
+    whole tokens on the host's cores, until budget_s passes.  Returns (median seconds per token,
+    tokens, threads)."""
+    threads = os.cpu_count() or 1
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end or len(times) < min_tokens) and (max_tokens is None or len(times) < max_tokens):
+        t0 = time.perf_counter()
+        x = wl.x
+        for layer in range(wl.L):
+            x = orc.attention_layer(wl.w[layer], "8", wl.qn[layer], wl.kn[layer], wl.nq, wl.nkv, wl.hd, wl.hidden,
+                                    500000.0, 1e-6, wl.kp[layer], wl.vp[layer], wl.mt, wl.pos, x)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times), threads
+
+
 class HostConfig2:
     """Config 2 built on the host only, for the reference arm: K/V ~ N(0,1) per
     layer quantised by the reference's own quantize_row_q8."""
@@ -652,7 +803,12 @@ def run_reference(args):
     if rank != 0:
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
-    if args.config == 5:
+    if args.config == 6:
+        wl = HostConfig6(orc, seed=6000)
+        reference_layers_seconds(orc, wl, 0.0, max_tokens=1, min_tokens=1)
+        sec, n, threads = reference_layers_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
+                                                   min_tokens=min(args.steps, 3))
+    elif args.config == 5:
         wl = HostConfig5(orc, seed=5000)
         sec, n, threads = reference_prefill_token_seconds(orc, wl, args.ref_seconds)
     elif args.config == 3:
@@ -697,6 +853,8 @@ def run_ours(args):
         wl = Config3(seed=3000, rank=rank, world=world)
     elif args.config == 4:
         wl = Config4(seed=4000, rank=rank, world=world, dist=dist)
+    elif args.config == 6:
+        wl = Config6(seed=6000 + rank)
     else:
         wl = Config5(seed=5000 + rank)
     stream = torch.cuda.current_stream()
@@ -740,6 +898,12 @@ def run_ours(args):
         cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
                "sample": f"{n} tokens: the first 32 tokens of the chunk through the reference's append + causal "
                          f"attention, repeated for ~{args.cpu_seconds:.0f} s, median per token"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config6":
+        orc, kind = reference_oracle()
+        sec, n, threads = reference_layers_seconds(orc, HostConfig6(orc, seed=6000), args.cpu_seconds)
+        cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
+               "sample": f"{n} whole tokens through the reference's attention_layer x 32 (its AVX2 matmuls, "
+                         f"Q8 cache at 4096), ~{args.cpu_seconds:.0f} s budget, median per token"}
     elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         orc, kind = reference_oracle()
         sec, n, threads = reference_token_seconds(orc, wl, args.cpu_seconds)
@@ -767,7 +931,8 @@ def run_ours(args):
             roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                         "frac": achieved / peak, "peak_kind": peak_kind,
                         "algorithmic_bytes_per_launch": wl.bytes_per_step,
-                        "traffic": _traffic_from_profile("decode_q8_" + wl.name)}
+                        "traffic": _traffic_from_profile(("layers_" if wl.name == "config6" else "decode_q8_")
+                                                         + wl.name)}
         jobs = world if wl.scaling == "weak" else 1  # weak: every rank runs its own sequence
         line = {
             "metric": METRIC,
@@ -777,14 +942,15 @@ def run_ours(args):
             "ms_per_step": t / args.steps * 1e3,
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "int8+fp32",
-            "data": "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q",
+            "data": getattr(wl, "data", "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q"),
             "config": {**wl.describe(), "global_batch": jobs, "parallelism": wl.parallelism(world)},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": jobs * e2e_steps * wl.tokens_per_step / t_e2e, "unit": "tokens/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-                    "api": "tqk_decode_q8 (C ABI) with pinned host inputs (q, and the appended k/v for "
-                           "config 2) in and the attention output out, stream-synchronised every step"},
+                    "api": getattr(wl, "e2e_api", "tqk_decode_q8 (C ABI) with pinned host inputs (q, and the "
+                                                  "appended k/v for config 2) in and the attention output out, "
+                                                  "stream-synchronised every step")},
             "gpu_launches": args.steps * wl.launches_per_step,
             **({"hbm_gbs": achieved} if roofline["bound"] == "hbm" else {}),
             "clocks": clk.summary(),
@@ -802,7 +968,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")

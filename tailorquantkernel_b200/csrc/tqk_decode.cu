@@ -165,15 +165,22 @@ __device__ __forceinline__ void row_prologue(const DecodeParams &p, int item, bo
 // Tickets and the arrival test of the split merge.  A CTA that wrote its
 // partial takes a ticket; the one that draws the last number of its group
 // merges (never a wait).
+// The CTA's barrier orders every thread's partial writes before thread 0's
+// gpu-scope acquire-release ticket increment (fence cumulativity), so one
+// thread publishes for the whole CTA; the CTA that draws the last ticket
+// acquires every earlier CTA's writes through the same atomic.
+__device__ __forceinline__ int ticket_add_acq_rel(int *ticket) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ticket) : "memory");
+    return old;
+}
+
 template <int BAR, int NT>
 __device__ __forceinline__ bool last_arrival(int *ticket, int n, int tid, int *flag) {
-    __threadfence();
     cta_sync<BAR, NT>();
-    if (tid == 0) *flag = (atomicAdd(ticket, 1) == n - 1);
+    if (tid == 0) *flag = (ticket_add_acq_rel(ticket) == n - 1);
     cta_sync<BAR, NT>();
-    const bool last = *flag;  // read by every thread before the next arrival's sync
-    if (last) __threadfence();
-    return last;
+    return *flag;  // read by every thread before the next arrival's sync
 }
 
 // Log-sum-exp merge, in slot order, of the n partials {acc[HD], m, l} in slots
@@ -181,16 +188,33 @@ __device__ __forceinline__ bool last_arrival(int *ticket, int n, int tid, int *f
 // ([slot][GROWS][HD + 2] floats).  to_part: the merged partial goes back into
 // slot `first`; otherwise into the call's output (normalised, or as a partial
 // in TQK_OUT_PARTIAL mode).  Each thread owns the same EPT elements across the
-// slots, so one slot's EPT loads are in flight together.
+// slots.  The loads are the latency: the accumulators of up to KB slots are
+// loaded in one batch, the first batch together with every slot's (m, l), so
+// a merge of up to KB slots costs one L2 round trip.
 template <int HD, int GROWS, int NT, int BAR>
 __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, int first, int stride, int n, int G,
                                             int tid, float *wts, float *ms, float *ls, bool to_part, float *out_item,
                                             int qh0) {
     constexpr int RS = HD + 2;
     constexpr int EPT = (GROWS * HD + NT - 1) / NT;
+    constexpr int KB = EPT >= 64 ? 1 : 64 / EPT;  // slots per batch of loads in flight
     const int lane = tid & 31, warp = tid >> 5;
     float *lall = wts + MAX_SPLITS * GROWS;
-    for (int i = tid; i < n * G; i += NT) {  // every slot's (m, l) in one round trip
+    float xb[KB][EPT];
+    auto load_batch = [&](int k0) {
+#pragma unroll
+        for (int kk = 0; kk < KB; kk++) {
+            const int k = k0 + kk;
+            const float *src = pb + (long long)(first + k * stride) * GROWS * RS;
+#pragma unroll
+            for (int e = 0; e < EPT; e++) {
+                const int i = tid + e * NT, g = i / HD, c = i - g * HD;
+                xb[kk][e] = (k < n && i < G * HD) ? __ldcg(src + g * RS + c) : 0.0f;
+            }
+        }
+    };
+    load_batch(0);
+    for (int i = tid; i < n * G; i += NT) {  // every slot's (m, l), in the same round trip
         const int k = i / G, g = i - k * G;
         const float2 ml =
             __ldcg(reinterpret_cast<const float2 *>(pb + ((long long)(first + k * stride) * GROWS + g) * RS + HD));
@@ -215,19 +239,17 @@ __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, in
     float a[EPT];
 #pragma unroll
     for (int e = 0; e < EPT; e++) a[e] = 0.0f;
-#pragma unroll (EPT <= 16 ? 2 : 1)
-    for (int k = 0; k < n; k++) {
-        const float *src = pb + (long long)(first + k * stride) * GROWS * RS;
-        float x[EPT];
+    for (int k0 = 0; k0 < n; k0 += KB) {
+        if (k0 > 0) load_batch(k0);
 #pragma unroll
-        for (int e = 0; e < EPT; e++) {
-            const int i = tid + e * NT, g = i / HD, c = i - g * HD;
-            x[e] = i < G * HD ? __ldcg(src + g * RS + c) : 0.0f;
-        }
+        for (int kk = 0; kk < KB; kk++) {
+            const int k = k0 + kk;
+            if (k >= n) break;
 #pragma unroll
-        for (int e = 0; e < EPT; e++) {
-            const int i = tid + e * NT, g = i / HD;
-            if (i < G * HD) a[e] = fmaf(wts[k * GROWS + g], x[e], a[e]);
+            for (int e = 0; e < EPT; e++) {
+                const int i = tid + e * NT, g = i / HD;
+                if (i < G * HD) a[e] = fmaf(wts[k * GROWS + g], xb[kk][e], a[e]);
+            }
         }
     }
 #pragma unroll
