@@ -31,14 +31,8 @@ namespace tqk {
 #ifndef TQK_PK_MINB
 #define TQK_PK_MINB 2  // CTAs per SM the register budget is sized for
 #endif
-#ifndef TQK_PK_INLINE_TMA
-#define TQK_PK_INLINE_TMA 0
-#endif
-// Inline TMA: consumer warp 0's lane 0 issues the copies (no producer warp), so a
-// CTA is 4 warps and 3 CTAs fit an SM's register file.
-constexpr bool PK_INLINE_TMA = TQK_PK_INLINE_TMA != 0;
 constexpr int PK_WARPS = TQK_PK_WARPS;         // consumer warps
-constexpr int PK_THREADS = (PK_WARPS + (PK_INLINE_TMA ? 0 : 1)) * 32;
+constexpr int PK_THREADS = (PK_WARPS + 1) * 32; // + the producer warp
 constexpr int PK_ROWS = 16;                    // tokens of each kv head per warp step
 constexpr int PK_T = PK_ROWS * PK_WARPS;       // tokens per tile, per kv head
 constexpr int PK_QR = (8 + PK_WARPS - 1) / PK_WARPS;  // q rows per consumer warp (8 q heads per CTA)
@@ -444,7 +438,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         bulk_copy_g2s(st + 3 * L::PLANE, va + head_bytes + o, bytes, &full[slot]);
     };
 
-    const int producer = PK_INLINE_TMA ? 0 : PK_WARPS * 32;
+    const int producer = PK_WARPS * 32;
     if (tid == producer) {
 #pragma unroll
         for (int st = 0; st < STAGES; st++) {
@@ -464,7 +458,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     }
     __syncthreads();
 
-    if (!PK_INLINE_TMA && warp == PK_WARPS) {
+    if (warp == PK_WARPS) {
         if (lane == 0) {
             for (int j = STAGES; j < n_tiles; j++) {
                 const int slot = j % STAGES;
@@ -487,7 +481,6 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
 
     const int r0 = warp * PK_ROWS;  // this warp's tokens of each head in a tile
     bool timed_out = false;
-    bool issuing = true;  // inline TMA: false once a wait for a free slot gave up
     for (int j = 0; j < n_tiles; j++) {
         const int slot = j % STAGES;
         const int t0 = t_begin + j * PK_T;
@@ -510,16 +503,6 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         }
         __syncwarp();
         if (lane == 0) mbar_arrive_release(&empty[slot]);
-        if (PK_INLINE_TMA && warp == 0) {
-            // refill this slot with tile j + STAGES once every warp has released tile j
-            if (lane == 0 && issuing && j + STAGES < n_tiles) {
-                if (mbar_wait_bounded(&empty[slot], (uint32_t)((j / STAGES) & 1), WAIT_NS, p.err))
-                    issue(j + STAGES);
-                else
-                    issuing = false;
-            }
-            __syncwarp();
-        }
     }
 
     // ------------------------------------------------------------------ epilogue
