@@ -223,6 +223,14 @@ typedef struct { float d; uint8_t q[16]; } tqk_block_q4;  /* low nibble: element
 #define TQK_FMT_Q8 0
 #define TQK_FMT_Q4 1
 
+/* pack_matrix / packed_matrix_bytes (packer/packer.c:63-88) on the device:
+ * fp32 rows W [rows][cols] (cols % 32 == 0) to Q8 ('8') or Q4 ('4') blocks in
+ * out, bit-exact (scale max|w|/qmax, 1.0 for an all-zero block, values
+ * lroundf(w / scale) clamped to +-127 / +-7).  tqk_packed_matrix_bytes returns
+ * 0 for invalid arguments, as the reference's returns 0. */
+TQK_API size_t tqk_packed_matrix_bytes(int rows, int cols, char bit_type);
+TQK_API int tqk_pack_matrix(const float *W, int rows, int cols, void *out, char bit_type, tqk_stream_t stream);
+
 /* matmul_q8_scalar / matmul_q4_scalar (kernel/q8_scalar.c:15-22,
  * kernel/q4_scalar.c:17-24; MatmulFn of kernel/kernel.h:17): y[r] = W[r] . xq
  * for rows x cols (cols % 32 == 0), all pointers on the device. */

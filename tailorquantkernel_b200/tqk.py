@@ -91,6 +91,8 @@ tqk_decode_q8 = _sig("tqk_decode_q8", [ctypes.POINTER(DecodeArgs), _vp, _sz, _vp
 tqk_decode_q8_static = _sig("tqk_decode_q8_static", [ctypes.POINTER(DecodeArgs), _vp])
 tqk_qk_norm_rope = _sig("tqk_qk_norm_rope", [_vp, _vp, _i, _i64, _i64, _i, _i, _i, _vp, _vp, _i64, _f, _vp, _vp,
                                               _i64, _vp])
+tqk_packed_matrix_bytes = _sig("tqk_packed_matrix_bytes", [_i, _i, ctypes.c_char], _sz)
+tqk_pack_matrix = _sig("tqk_pack_matrix", [_vp, _i, _i, _vp, ctypes.c_char, _vp])
 tqk_matmul_q8 = _sig("tqk_matmul_q8", [_vp, _vp, _vp, _i, _i, _vp])
 tqk_matmul_q4 = _sig("tqk_matmul_q4", [_vp, _vp, _vp, _i, _i, _vp])
 tqk_matmul_q8_batch = _sig("tqk_matmul_q8_batch", [_vp, _vp, _vp, _i, _i, _i, _vp])
@@ -138,7 +140,7 @@ EXPORTED = [
     "tqk_attend_q8", "tqk_append_attend_q8", "tqk_prefill_q8", "tqk_merge_partials",
     "tqk_decode_q8_static", "tqk_qk_norm_rope",
     "tqk_matmul_q8", "tqk_matmul_q4", "tqk_matmul_q8_batch", "tqk_matmul_q4_batch", "tqk_project",
-    "tqk_attention_layer",
+    "tqk_attention_layer", "tqk_pack_matrix", "tqk_packed_matrix_bytes",
 ]
 
 
@@ -279,6 +281,17 @@ def qk_norm_rope(q, k, n_items, n_q, n_kv, head_dim, q_norm=None, k_norm=None, e
 
 FMT_Q8, FMT_Q4 = 0, 1
 Q4_BLOCK_BYTES = 20
+
+
+def pack_matrix(w, fmt: str, out=None, stream=None):
+    """tqk_pack_matrix: fp32 CUDA tensor W [rows, cols] -> packed Q8 ('8') / Q4 ('4') rows (uint8)."""
+    import torch
+    rows, cols = w.shape
+    nbytes = tqk_packed_matrix_bytes(rows, cols, fmt.encode())
+    if out is None:
+        out = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+    check(tqk_pack_matrix(_ptr(w), rows, cols, _ptr(out), fmt.encode(), _stream(stream)), "tqk_pack_matrix")
+    return out.view(rows, -1)
 
 
 def matmul(w, fmt, xq, y, rows, cols, n_tok=1, stream=None) -> None:

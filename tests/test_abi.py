@@ -93,6 +93,16 @@ def test_decode_prologue_arguments_checked_before_the_device():
         assert tqk.tqk_decode_q8(ctypes.byref(a), None, 0, None) == tqk.EINVAL
 
 
+def test_packed_matrix_bytes_without_device():
+    """packed_matrix_bytes (packer/packer.c:63-75): 36 / 20 bytes per 32 columns, 0 when invalid."""
+    from tailorquantkernel_b200 import tqk
+    assert tqk.tqk_packed_matrix_bytes(3, 64, b"8") == 3 * 2 * 36
+    assert tqk.tqk_packed_matrix_bytes(3, 64, b"4") == 3 * 2 * 20
+    assert tqk.tqk_packed_matrix_bytes(3, 48, b"8") == 0
+    assert tqk.tqk_packed_matrix_bytes(0, 64, b"8") == 0
+    assert tqk.tqk_packed_matrix_bytes(3, 64, b"x") == 0
+
+
 def test_error_codes_without_device():
     from tailorquantkernel_b200 import tqk
     # position checks come first and never touch a device (reference: -1 on bad pos)

@@ -260,3 +260,18 @@ def test_attention_layer_golden(port, name, fmt):
     y = port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp, vp, mt, pos, xn)
     assert np.array_equal(y.view(np.uint32), g[key + "__out"].view(np.uint32))
     assert np.array_equal(kp[:, pos], g[key + "__k_row"]) and np.array_equal(vp[:, pos], g[key + "__v_row"])
+
+
+def test_pack_edges_against_reference_build(port):
+    """pack_matrix on edge values (zero blocks, exact .5 products, NaN / Inf, tiny and huge
+    values): the restatement equals the reference build byte for byte."""
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("gpu_pack", os.path.join(os.path.dirname(__file__), "test_gpu_pack.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    w = mod._edge_rows()
+    ref = oracle.Oracle("ref_scalar")
+    for fmt in "84":
+        assert np.array_equal(port.pack_matrix(w, fmt), ref.pack_matrix(w, fmt))
