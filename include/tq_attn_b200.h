@@ -135,6 +135,23 @@ TQ_B200_API void attn_accum_q8(const float *w, size_t w_stride, int g, const blo
 
 /* ---- exported: drop-in control (no reference counterpart) ---- */
 
+/* Device-resident attention layers.  Copies one layer's packed wq/wk/wv/wo rows
+ * and q/k norm weights to the device and registers them under the caller's
+ * tq_attn_weights (and the data pointers it holds now).  From then on
+ * attention_layer and attention_layer_batch with these weights and a Q8 cache
+ * run the whole layer on the B200 -- projections with the activation
+ * quantisation, norm + RoPE, the Q8 append and attention, the output
+ * projection (tqk_attention_layer / tqk_project) -- and move only xn, the RoPE
+ * tables, the output and the appended cache rows across PCIe.  The host
+ * weights must stay unchanged while registered (register again after changing
+ * them).  All four matrices must share one format.  Returns 0, the
+ * tq_attn_validate code of invalid weights, -10 for mixed formats, or a
+ * negative status for a GPU failure.  A runtime calls it once per layer after
+ * loading its weights. */
+TQ_B200_API int tq_b200_register_attn_weights(const tq_attn_weights *w, const tq_attn_config *cfg);
+/* Releases the device copy made for w (no-op when none). */
+TQ_B200_API void tq_b200_unregister_attn_weights(const tq_attn_weights *w);
+
 /* Status of the last drop-in call on this thread (0 = ok); the void entry points
  * report GPU failures here and fill their outputs with NaN. */
 TQ_B200_API int tq_b200_last_status(void);

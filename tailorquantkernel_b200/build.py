@@ -104,7 +104,8 @@ def build_oracle(verbose: bool = False) -> None:
     if os.path.isdir(ref):
         _run(["make", "-s", "-C", oracle, f"REF={ref}", "ref"], verbose)
         if os.path.exists(os.path.join(PKG, "libtq_attn_b200.so")):
-            _run(["make", "-s", "-C", oracle, f"REF={ref}", "_ref/test_model_dropin"], verbose)
+            _run(["make", "-s", "-C", oracle, f"REF={ref}", "_ref/test_model_dropin", "_ref/libtqref_dropin.so"],
+                 verbose)
 
 
 def build_all(verbose: bool = False, force: bool = False) -> None:

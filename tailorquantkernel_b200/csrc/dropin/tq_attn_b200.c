@@ -44,6 +44,19 @@ typedef struct mirror {
     struct mirror *next;
 } mirror;
 
+/* One layer's attention weights copied to the device by
+ * tq_b200_register_attn_weights, keyed by the caller's tq_attn_weights and the
+ * host data pointers it held at registration. */
+typedef struct wreg {
+    const tq_attn_weights *key;
+    const void *src[4];          /* wq, wk, wv, wo data at registration */
+    const float *src_norm[2];    /* q_norm, k_norm at registration */
+    int device, format, hd;
+    void *dw[4];                 /* device packed rows */
+    float *dnorm[2];             /* device q_norm, k_norm */
+    struct wreg *next;
+} wreg;
+
 static struct {
     int ready;
     int device;
@@ -53,6 +66,7 @@ static struct {
     void *hstage;
     size_t hstage_bytes;
     mirror *mirrors;
+    wreg *wregs;
 } G;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
@@ -328,6 +342,206 @@ int tq_kv_cache_init(tq_kv_cache *cache, tq_kv_type type, const tq_attn_config *
 }
 
 /* ---------------------------------------------------------------------------
+ * device-resident attention layers (weights registered by the runtime)
+ * ------------------------------------------------------------------------- */
+static const tq_matrix *wmat(const tq_attn_weights *w, int i) {
+    return i == 0 ? &w->wq : i == 1 ? &w->wk : i == 2 ? &w->wv : &w->wo;
+}
+
+static wreg *wreg_find(const tq_attn_weights *w) {
+    for (wreg *r = G.wregs; r; r = r->next) {
+        if (r->key != w || r->device != G.device) continue;
+        int same = r->src_norm[0] == w->q_norm && r->src_norm[1] == w->k_norm;
+        for (int i = 0; i < 4; i++) same = same && r->src[i] == wmat(w, i)->data;
+        if (same) return r;
+    }
+    return NULL;
+}
+
+static void wreg_release(wreg *r) {
+    for (int i = 0; i < 4; i++) cudaFree(r->dw[i]);
+    cudaFree(r->dnorm[0]);
+    cudaFree(r->dnorm[1]);
+    free(r);
+}
+
+static void wreg_drop(const tq_attn_weights *w) {
+    wreg **pp = &G.wregs;
+    while (*pp) {
+        if ((*pp)->key == w) {
+            wreg *dead = *pp;
+            *pp = dead->next;
+            if (G.ready) cudaStreamSynchronize(G.stream);
+            wreg_release(dead);
+            continue;
+        }
+        pp = &(*pp)->next;
+    }
+}
+
+int tq_b200_register_attn_weights(const tq_attn_weights *w, const tq_attn_config *cfg) {
+    if (!w || !cfg) return set_status(-1);
+    const int v = tq_attn_validate(w, cfg);
+    if (v) return set_status(v);
+    const tq_format f = w->wq.format;
+    if (w->wk.format != f || w->wv.format != f || w->wo.format != f || (f != TQ_FORMAT_Q8 && f != TQ_FORMAT_Q4))
+        return set_status(-10);
+    for (int i = 0; i < 4; i++)
+        if (!wmat(w, i)->data) return set_status(-10);
+    pthread_mutex_lock(&g_mu);
+    int rc = use_device();
+    if (rc) {
+        pthread_mutex_unlock(&g_mu);
+        return rc;
+    }
+    wreg_drop(w);
+    wreg *r = (wreg *)calloc(1, sizeof *r);
+    if (!r) {
+        pthread_mutex_unlock(&g_mu);
+        return set_status(-1);
+    }
+    r->key = w;
+    r->device = G.device;
+    r->format = f == TQ_FORMAT_Q8 ? TQK_FMT_Q8 : TQK_FMT_Q4;
+    r->hd = cfg->head_dim;
+    const size_t block = f == TQ_FORMAT_Q8 ? 36 : 20;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 4 && e == cudaSuccess; i++) {
+        const tq_matrix *m = wmat(w, i);
+        const size_t bytes = (size_t)m->rows * (size_t)(m->cols / QK) * block;
+        r->src[i] = m->data;
+        e = cudaMalloc(&r->dw[i], bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(r->dw[i], m->data, bytes, cudaMemcpyHostToDevice);
+    }
+    const float *norms[2] = {w->q_norm, w->k_norm};
+    for (int i = 0; i < 2 && e == cudaSuccess; i++) {
+        r->src_norm[i] = norms[i];
+        e = cudaMalloc((void **)&r->dnorm[i], (size_t)cfg->head_dim * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemcpy(r->dnorm[i], norms[i], (size_t)cfg->head_dim * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        wreg_release(r);
+        pthread_mutex_unlock(&g_mu);
+        return cuda_fail(e, "register attention weights");
+    }
+    r->next = G.wregs;
+    G.wregs = r;
+    pthread_mutex_unlock(&g_mu);
+    return set_status(0);
+}
+
+void tq_b200_unregister_attn_weights(const tq_attn_weights *w) {
+    pthread_mutex_lock(&g_mu);
+    wreg_drop(w);
+    pthread_mutex_unlock(&g_mu);
+}
+
+/* attention_layer (n == 1) or attention_layer_batch (n > 1) with registered
+ * weights and a Q8 cache, all on the device: xn (and the RoPE tables, computed
+ * here by the reference's rope_table) go up, out and the appended cache rows
+ * come back.  Caller holds g_mu. */
+static int device_layers(const wreg *r, tq_kv_cache *cache, const tq_attn_config *cfg, int pos0, int n,
+                         const float *xn, float *out) {
+    int rc = use_device();
+    if (rc) return rc;
+    mirror *m = NULL;
+    rc = mirror_get(cache, cfg, &m);
+    if (rc) return rc;
+    rc = mirror_sync_prefix(m, cache, pos0);
+    if (rc) {
+        m->synced = -1;
+        return rc;
+    }
+    const int hd = cfg->head_dim, hidden = cfg->hidden_size;
+    const size_t q_dim = (size_t)cfg->n_q_heads * hd, kv_dim = (size_t)cfg->n_kv_heads * hd;
+    const size_t row = (size_t)(hd / QK) * sizeof(block_q8);
+    const size_t pitch = (size_t)cache->max_tokens * row;
+    const size_t x_bytes = (size_t)n * hidden * sizeof(float);
+    const size_t tab_bytes = (size_t)n * hd * sizeof(float);  /* cos [n][hd/2], then sin [n][hd/2] */
+    const size_t rows_bytes = (size_t)cfg->n_kv_heads * n * row;
+    /* host staging: [xn][tables] up, [out][K rows][V rows] down */
+    const size_t h_tab = align256(x_bytes), h_out = h_tab + align256(tab_bytes),
+                 h_rk = h_out + align256(x_bytes), h_rv = h_rk + align256(rows_bytes), h_total = h_rv + align256(rows_bytes);
+    /* device scratch: [xn][tables][out][q][k][v][attention] */
+    const size_t d_out = align256(x_bytes) + align256(tab_bytes), d_q = d_out + align256(x_bytes),
+                 d_k = d_q + align256((size_t)n * q_dim * sizeof(float)),
+                 d_v = d_k + align256((size_t)n * kv_dim * sizeof(float)),
+                 d_a = d_v + align256((size_t)n * kv_dim * sizeof(float)),
+                 d_total = d_a + align256((size_t)n * q_dim * sizeof(float));
+    unsigned char *h = (unsigned char *)host_stage(h_total);
+    unsigned char *d = (unsigned char *)dev_scratch(d_total);
+    if (!h || !d) return cuda_fail(cudaErrorMemoryAllocation, "staging buffers");
+    memcpy(h, xn, x_bytes);
+    float *hcos = (float *)(h + h_tab), *hsin = hcos + (size_t)n * (hd / 2);
+    for (int i = 0; i < n; i++) rope_table(hcos + (size_t)i * (hd / 2), hsin + (size_t)i * (hd / 2), hd, pos0 + i,
+                                           cfg->rope_theta);
+    float *dx = (float *)d, *dcos = (float *)(d + align256(x_bytes)), *dsin = dcos + (size_t)n * (hd / 2);
+    float *dout = (float *)(d + d_out), *dq = (float *)(d + d_q), *dk = (float *)(d + d_k), *dvv = (float *)(d + d_v),
+          *da = (float *)(d + d_a);
+
+    m->synced = -1;  /* until this call has fully completed */
+    CU(cudaMemcpyAsync(d, h, align256(x_bytes) + tab_bytes, cudaMemcpyHostToDevice, G.stream), "upload xn");
+    if (n == 1) {
+        tqk_attn_layer_args a;
+        memset(&a, 0, sizeof a);
+        a.wq = r->dw[0];
+        a.wk = r->dw[1];
+        a.wv = r->dw[2];
+        a.wo = r->dw[3];
+        a.format = r->format;
+        a.q_norm = r->dnorm[0];
+        a.k_norm = r->dnorm[1];
+        a.n_q_heads = cfg->n_q_heads;
+        a.n_kv_heads = cfg->n_kv_heads;
+        a.head_dim = hd;
+        a.hidden_size = hidden;
+        a.rms_eps = cfg->rms_eps;
+        a.k = m->dk;
+        a.v = m->dv;
+        a.max_tokens = cache->max_tokens;
+        a.pos = pos0;
+        a.rope_cos = dcos;
+        a.rope_sin = dsin;
+        a.xn = dx;
+        a.out = dout;
+        a.scratch = dq;  /* q, k, v, attention follow one another */
+        rc = tqk_attention_layer(&a, NULL, 0, G.stream);
+        if (rc) return tqk_fail(rc, "tqk_attention_layer");
+    } else {
+        const tqk_proj_job qkv[3] = {{r->dw[0], dq, (int)q_dim}, {r->dw[1], dk, (int)kv_dim}, {r->dw[2], dvv, (int)kv_dim}};
+        rc = tqk_project(qkv, 3, r->format, dx, hidden, n, G.stream);
+        if (!rc)
+            rc = tqk_qk_norm_rope(dq, dk, n, (int64_t)q_dim, (int64_t)kv_dim, cfg->n_q_heads, cfg->n_kv_heads, hd,
+                                  r->dnorm[0], r->dnorm[1], 0, cfg->rms_eps, dcos, dsin, hd / 2, G.stream);
+        if (!rc)
+            rc = tqk_prefill_q8(m->dk, m->dv, cfg->n_q_heads, cfg->n_kv_heads, hd, cache->max_tokens, pos0, n, dq, dk,
+                                dvv, da, G.stream);
+        if (!rc) {
+            const tqk_proj_job o = {r->dw[3], dout, hidden};
+            rc = tqk_project(&o, 1, r->format, da, (int)q_dim, n, G.stream);
+        }
+        if (rc) return tqk_fail(rc, "device attention_layer_batch");
+    }
+    CU(cudaMemcpyAsync(h + h_out, dout, x_bytes, cudaMemcpyDeviceToHost, G.stream), "download output");
+    CU(cudaMemcpy2DAsync(h + h_rk, (size_t)n * row, (const unsigned char *)m->dk + (size_t)pos0 * row, pitch,
+                         (size_t)n * row, (size_t)cfg->n_kv_heads, cudaMemcpyDeviceToHost, G.stream),
+       "download K rows");
+    CU(cudaMemcpy2DAsync(h + h_rv, (size_t)n * row, (const unsigned char *)m->dv + (size_t)pos0 * row, pitch,
+                         (size_t)n * row, (size_t)cfg->n_kv_heads, cudaMemcpyDeviceToHost, G.stream),
+       "download V rows");
+    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    memcpy(out, h + h_out, x_bytes);
+    for (int kvh = 0; kvh < cfg->n_kv_heads; kvh++) {
+        const size_t dst = ((size_t)kvh * cache->max_tokens + pos0) * row;
+        memcpy((unsigned char *)cache->k_q8 + dst, h + h_rk + (size_t)kvh * n * row, (size_t)n * row);
+        memcpy((unsigned char *)cache->v_q8 + dst, h + h_rv + (size_t)kvh * n * row, (size_t)n * row);
+    }
+    m->synced = pos0 + n;
+    return set_status(0);
+}
+
+/* ---------------------------------------------------------------------------
  * model/attention_layer.c
  * ------------------------------------------------------------------------- */
 int tq_attn_validate(const tq_attn_weights *w, const tq_attn_config *cfg) {
@@ -390,6 +604,13 @@ static void f32_store_attend(tq_kv_cache *cache, const tq_attn_config *cfg, int 
 int attention_layer(const tq_attn_weights *w, const tq_attn_config *cfg, tq_kv_cache *cache, int pos,
                     const float *xn, float *scores, float *out) {
     if (pos < 0 || pos >= cache->max_tokens) return -1;
+    if (cache->type == TQ_KV_Q8) {  /* registered weights: the whole layer on the device */
+        pthread_mutex_lock(&g_mu);
+        const wreg *r = G.ready ? wreg_find(w) : NULL;
+        const int rc = r ? device_layers(r, cache, cfg, pos, 1, xn, out) : 1;
+        pthread_mutex_unlock(&g_mu);
+        if (rc <= 0) return rc == 0 ? 0 : (rc < -1 ? rc : TQB_ECUDA);
+    }
 
     const int hd = cfg->head_dim;
     const int q_dim = cfg->n_q_heads * hd;
@@ -426,6 +647,13 @@ int attention_layer_batch(const tq_attn_weights *w, const tq_attn_config *cfg, t
                           const float *xn, float *scores, float *out, tq_batch_ws *ws) {
     if (n <= 0 || n > ws->cap) return -1;
     if (pos0 < 0 || pos0 + n > cache->max_tokens) return -1;
+    if (cache->type == TQ_KV_Q8) {  /* registered weights: the whole chunk on the device */
+        pthread_mutex_lock(&g_mu);
+        const wreg *r = G.ready ? wreg_find(w) : NULL;
+        const int rc = r ? device_layers(r, cache, cfg, pos0, n, xn, out) : 1;
+        pthread_mutex_unlock(&g_mu);
+        if (rc <= 0) return rc == 0 ? 0 : (rc < -1 ? rc : TQB_ECUDA);
+    }
 
     const int hd = cfg->head_dim;
     const int q_dim = cfg->n_q_heads * hd;

@@ -69,6 +69,32 @@ __device__ __forceinline__ int8_t warp_quantize_block(float x, float *d) {
     return q8_round(x, q8_inverse(s));
 }
 
+// warp_quantize_block for N blocks at once (block k's element on this lane in
+// x[k]), phase by phase across the blocks -- the N max reductions, then the N
+// scales, the N inverses and the N roundings -- so the N independent
+// shuffle / division chains overlap instead of running one after another.
+// Same arithmetic, same results.
+template <int N>
+__device__ __forceinline__ void warp_quantize_blocks(const float (&x)[N], int8_t (&q)[N], float (&d)[N]) {
+    float m[N];
+#pragma unroll
+    for (int k = 0; k < N; k++) m[k] = q8_absmax(0.0f, x[k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < N; k++) {
+            const float other = __shfl_xor_sync(0xffffffffu, m[k], o);
+            m[k] = other > m[k] ? other : m[k];
+        }
+    float inv[N];
+#pragma unroll
+    for (int k = 0; k < N; k++) d[k] = q8_scale(m[k]);
+#pragma unroll
+    for (int k = 0; k < N; k++) inv[k] = q8_inverse(d[k]);
+#pragma unroll
+    for (int k = 0; k < N; k++) q[k] = q8_round(x[k], inv[k]);
+}
+
 // The attention prologue on head rows of head_dim = NB*32 floats held by a
 // full warp, element b*32 + lane of a row in x[b]: RMSNorm with a weight
 // (model/rmsnorm.c:4-19) and then the half-split RoPE rotation with a cos/sin

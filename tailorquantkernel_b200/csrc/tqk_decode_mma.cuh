@@ -462,12 +462,13 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
 #pragma unroll
                 for (int b = 0; b < NB; b++) x[b] = __ldg(qsrc + g * HD + b * QK + lane);
                 row_prologue<NB>(p, item, false, x, pro, lane);  // fused prologue, if asked for
+                int8_t q8[NB];
+                float dq[NB];
+                warp_quantize_blocks<NB>(x, q8, dq);
 #pragma unroll
                 for (int b = 0; b < NB; b++) {
-                    float d;
-                    const int8_t v8 = warp_quantize_block(x[b], &d);
-                    qq[g * HD + b * QK + lane] = v8;
-                    if (lane == 0) qd[g * NB + b] = d;
+                    qq[g * HD + b * QK + lane] = q8[b];
+                    if (lane == 0) qd[g * NB + b] = dq[b];
                 }
             } else {
 #pragma unroll
@@ -486,10 +487,13 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
 #pragma unroll
             for (int b = 0; b < NB; b++) x[b] = __ldg(src + b * QK + lane);
             if (warp == 0) row_prologue<NB>(p, item, true, x, pro, lane);
+            int8_t q8[NB];
+            float dq[NB];
+            warp_quantize_blocks<NB>(x, q8, dq);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
-                float d;
-                const int8_t v8 = warp_quantize_block(x[b], &d);
+                const float d = dq[b];
+                const int8_t v8 = q8[b];
                 nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
                 if (lane == 0) *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
                 if (slice == 0) {

@@ -310,16 +310,23 @@ __device__ __forceinline__ void pack_preamble(const DecodeParams &p, int item, i
                 if ((warp + PK_WARPS * j) % 2 == 0) apply_rope<NB>(x[QR + j], tab, lane);
         }
     }
+    // every block of the q rows and the new rows quantised together (their
+    // shuffle and division chains overlap)
+    float xf[R * NB], dq[R * NB];
+    int8_t q8[R * NB];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int b = 0; b < NB; b++) xf[r * NB + b] = x[r][b];
+    warp_quantize_blocks<R * NB>(xf, q8, dq);
 #pragma unroll
     for (int r = 0; r < QR; r++) {
         const int g = warp + PK_WARPS * r;
         if (g >= 8) break;
 #pragma unroll
         for (int b = 0; b < NB; b++) {
-            float d;
-            const int8_t v8 = warp_quantize_block(x[r][b], &d);
-            qq[g * HD + b * QK + lane] = v8;
-            if (lane == 0) qd[g * NB + b] = d;
+            qq[g * HD + b * QK + lane] = q8[r * NB + b];
+            if (lane == 0) qd[g * NB + b] = dq[r * NB + b];
         }
     }
     if (!do_append) return;
@@ -334,10 +341,10 @@ __device__ __forceinline__ void pack_preamble(const DecodeParams &p, int item, i
                         (long long)(kvh_a + hsel) * head_bytes + (long long)pos * ROW;
 #pragma unroll
         for (int b = 0; b < NB; b++) {
-            float d;
-            const int8_t v8 = warp_quantize_block(x[QR + j][b], &d);
-            nrow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
-            grow[b * BLOCK_BYTES + 4 + lane] = (uint8_t)v8;
+            const uint8_t v8 = (uint8_t)q8[(QR + j) * NB + b];
+            const float d = dq[(QR + j) * NB + b];
+            nrow[b * BLOCK_BYTES + 4 + lane] = v8;
+            grow[b * BLOCK_BYTES + 4 + lane] = v8;
             if (lane == 0) {
                 *reinterpret_cast<float *>(nrow + b * BLOCK_BYTES) = d;
                 *reinterpret_cast<float *>(grow + b * BLOCK_BYTES) = d;
