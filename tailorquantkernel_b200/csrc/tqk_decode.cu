@@ -58,9 +58,10 @@ struct DecodeParams {
     int split_tokens;            // multiple of DEC_T
     int max_splits;
     float scale;
-    float *part;                 // [n_items][pairs][max_splits][GMAX][HD+2]
-    int *counters;               // [n_items][pairs]
+    float *part;                 // [n_items][pairs][max_splits][GMAX][HD+2]; balanced: [ctas + units][8][HD+2]
+    int *counters;               // tickets: [n_items][pairs][TICKETS_PER_UNIT]; balanced: [..][tickets_per_unit]
     int *err;
+    int tickets_per_unit;        // balanced schedule only
 };
 
 template <int NB>
@@ -281,13 +282,13 @@ __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, in
 //   groups -- two short merges instead of one long serial one.
 // Merges run in slot order, so results are deterministic.  ms/ls are
 // overwritten by the merge; the tickets used are left at zero.
+// pb: the unit's partial slots ([slot][GROWS][HD + 2] floats); tickets: its
+// ticket block ([0] final, [1 + i] group i).
 template <int HD, int GROWS, int NT, int BAR, typename AccFn>
-__device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int item, int pair, int s, int n_splits,
-                                             int qh0, int G, float *out_item, AccFn acc, float *ms, float *ls,
-                                             float *wts, int *flag) {
+__device__ __forceinline__ void finish_split_at(const DecodeParams &p, int tid, float *pb, int *tickets, int s,
+                                                int n_splits, int qh0, int G, float *out_item, AccFn acc, float *ms,
+                                                float *ls, float *wts, int *flag) {
     const bool single = n_splits == 1;
-    const long long unit = (long long)item * p.pairs + pair;
-    float *pb = p.part + unit * p.max_splits * GROWS * (HD + 2);
     for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, c = i - g * HD;
         const float a = acc(g, c);
@@ -307,7 +308,6 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
     }
     if (single) return;
 
-    int *tickets = p.counters + unit * TICKETS_PER_UNIT;  // [0] final, [1 + i] group i
     if (n_splits > MERGE_GROUP) {
         const int gi = s / MERGE_GROUP, first = gi * MERGE_GROUP;
         const int gsz = min(MERGE_GROUP, n_splits - first);
@@ -322,6 +322,18 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
         merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, 1, n_splits, G, tid, wts, ms, ls, false, out_item, qh0);
     }
     if (tid == 0) tickets[0] = 0;  // ready for the next launch
+}
+
+// The fixed-split layout: unit (item, pair) owns max_splits slots and
+// TICKETS_PER_UNIT tickets.
+template <int HD, int GROWS, int NT, int BAR, typename AccFn>
+__device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int item, int pair, int s, int n_splits,
+                                             int qh0, int G, float *out_item, AccFn acc, float *ms, float *ls,
+                                             float *wts, int *flag) {
+    const long long unit = (long long)item * p.pairs + pair;
+    finish_split_at<HD, GROWS, NT, BAR>(p, tid, p.part + unit * p.max_splits * GROWS * (HD + 2),
+                                        p.counters + unit * TICKETS_PER_UNIT, s, n_splits, qh0, G, out_item, acc, ms,
+                                        ls, wts, flag);
 }
 
 template <int NB, int GMAX>
@@ -744,8 +756,39 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
     return launch_pdl(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, p);
 }
 
-int dispatch_pack(int nb, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ) {
-    if (nb == 4) return launch_pack<4>(p, grid, stream, occ);
+// The balanced (stream-K) schedule of the same kernel: a 1-D grid of equal tile runs.
+template <int NB>
+int launch_pack_bal(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
+    using L = PackBalLayout<NB>;
+    static std::mutex mu;
+    static int occ_by_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail_cuda(e, "decode: cudaGetDevice");
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (occ_by_dev[dev] == 0) {
+            e = cudaFuncSetAttribute(decode_q8_pack_bal_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     L::BYTES);
+            int o = 0;
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, decode_q8_pack_bal_kernel<NB>, PK_THREADS,
+                                                                  L::BYTES);
+            if (e != cudaSuccess) return fail_cuda(e, "decode_q8_pack_bal_kernel attributes");
+            occ_by_dev[dev] = o > 0 ? o : -1;
+        }
+        occ = occ_by_dev[dev] > 0 ? occ_by_dev[dev] : 0;
+    }
+    if (ctas_per_sm) {
+        *ctas_per_sm = occ;
+        return TQK_OK;
+    }
+    return launch_pdl(decode_q8_pack_bal_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, p);
+}
+
+int dispatch_pack(int nb, const DecodeParams &p, dim3 grid, cudaStream_t stream, int *occ, bool balanced = false) {
+    if (nb == 4) return balanced ? launch_pack_bal<4>(p, grid, stream, occ) : launch_pack<4>(p, grid, stream, occ);
     return fail(TQK_EUNSUPPORTED, "decode: packed kernel needs head_dim 128");
 }
 
@@ -807,6 +850,8 @@ struct Plan {
     int nb, gmax, heads_per_cta, head_slices, pairs, split_tokens, max_splits, max_len;
     bool mma;   // tensor-core kernel (head_dim 128/256) or the CUDA-core one (32/64)
     bool pack;  // tensor-core kernel with two kv heads per CTA (4 q heads per kv head)
+    bool balanced;          // packed kernel on the balanced schedule: bal_ctas equal tile runs
+    int bal_ctas, tickets_per_unit;
     size_t counters_bytes, part_bytes;
 };
 
@@ -867,18 +912,45 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     pl->max_len = max_len;
 
     int split = a->split_tokens;
+    pl->balanced = false;
+    pl->bal_ctas = 0;
+    pl->tickets_per_unit = TICKETS_PER_UNIT;
     if (split <= 0) {
         const int rc = ensure_device();
         if (rc) return rc;
         const DeviceInfo *d = device_info();
+        // the balanced schedule pays a segment switch mid-run; it wins where the
+        // fixed split cannot even out the work: unequal lengths across items
+        const bool ragged = a->n_items > 1 && (a->lens != nullptr || a->len_step != 0);
+        const bool balanced = pl->pack && ragged && a->n_items <= BAL_MAX_ITEMS;
         int occ = 0;
         DecodeParams dummy{};
-        const int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ)
+        const int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ, balanced)
                         : pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
                                   : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
         if (orc) return orc;
         const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
         const long long pairs_total = (long long)a->n_items * pl->pairs;
+        if (balanced) {
+            // one CTA per resident slot (never more than there are tiles), each
+            // streaming an equal run of the units' tiles
+            const long long tiles = pairs_total * ((max_len + PK_T - 1) / PK_T);
+            long long ctas = slots < tiles ? slots : tiles;
+            if (ctas > BAL_MAX_CTAS) ctas = BAL_MAX_CTAS;
+            if (ctas < 1) ctas = 1;
+            pl->balanced = true;
+            pl->bal_ctas = (int)ctas;
+            pl->tickets_per_unit = 1 + (int)((ctas + MERGE_GROUP - 1) / MERGE_GROUP);
+            pl->split_tokens = 0;
+            pl->max_splits = (int)ctas;
+            // tickets inside the fixed-floor region (so workspaces stay shareable
+            // across calls), then one partial slot per (CTA, unit) segment
+            pl->counters_bytes = counters_region(a->n_items, pl->pairs);
+            if ((size_t)pairs_total * pl->tickets_per_unit * sizeof(int) > pl->counters_bytes)
+                return fail(TQK_EINVAL, "decode: balanced schedule tickets exceed the ticket region");
+            pl->part_bytes = (size_t)(ctas + pairs_total) * 8 * (a->head_dim + 2) * sizeof(float);
+            return TQK_OK;
+        }
         // equal lengths: as many splits as keep every CTA in one wave (a second,
         // partly filled wave costs more than the shorter splits save); unequal
         // lengths: about two CTAs per slot, so short and long items even out
@@ -937,6 +1009,7 @@ DecodeParams fill_params(const tqk_decode_args *a, const Plan &pl) {
     p.out_mode = a->out_mode;
     p.split_tokens = pl.split_tokens;
     p.max_splits = pl.max_splits;
+    p.tickets_per_unit = pl.tickets_per_unit;
     p.scale = 1.0f / sqrtf((float)a->head_dim);  // as attend_q8 computes it (attention_layer.c:131)
     return p;
 }
@@ -983,6 +1056,7 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     p.counters = counters;
     p.part = part;
     p.err = device_info()->err_word;
+    if (pl.balanced) return dispatch_pack(pl.nb, p, dim3((unsigned)pl.bal_ctas), st, nullptr, true);
     const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
     if (pl.pack) return dispatch_pack(pl.nb, p, grid, st, nullptr);
     return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);

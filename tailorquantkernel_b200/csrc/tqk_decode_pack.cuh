@@ -369,6 +369,64 @@ __device__ __forceinline__ void pack_patch(int pos, int t0, int r0, int lane, ui
     __syncwarp();
 }
 
+// Cross-warp reduction of a CTA's span: every consumer warp's unnormalised
+// P*V rows (red, [W][8][RED_STRIDE]) and its (m, l) go to shared memory; the
+// per-row maximum fm (natural log units), sum fl and per-warp weights wsc
+// follow.  acc(g, c) is then the CTA's sum for q row g, column c, relative to
+// fm[g].
+struct PackRed {
+    float *red, *small;  // small: wm [W][8], wl [W][8], wsc [W][8], fm [8], fl [8]
+    __device__ __forceinline__ float *wm() const { return small; }
+    __device__ __forceinline__ float *wl() const { return small + PK_WARPS * 8; }
+    __device__ __forceinline__ float *wsc() const { return small + 2 * PK_WARPS * 8; }
+    __device__ __forceinline__ float *fm() const { return small + 3 * PK_WARPS * 8; }
+    __device__ __forceinline__ float *fl() const { return small + 3 * PK_WARPS * 8 + 8; }
+    template <int RS>
+    __device__ __forceinline__ float acc(int g, int c) const {
+        float a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < PK_WARPS; w++) a = fmaf(red[(w * 8 + g) * RS + c], wsc()[w * 8 + g], a);
+        return a;
+    }
+};
+constexpr int PK_RED_SMALL = 3 * PK_WARPS * 8 + 16;  // floats of PackRed::small
+
+template <int NB, int RS>
+__device__ __forceinline__ void pack_reduce(const PackState<NB> &st, const PackRed &r, int warp, int g, int t,
+                                            int tid) {
+    float *wm = r.wm(), *wl = r.wl(), *wsc = r.wsc(), *fm = r.fm(), *fl = r.fl();
+    if (t == 0) {
+        wm[warp * 8 + g] = st.m;
+        wl[warp * 8 + g] = st.l;
+    }
+    const float unscale = exp2_int(st.kscale);
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            const int c = b * QK + 8 * t + jj;  // permuted n-tile column n = 2t, 2t+1 -> 4n + jj
+            r.red[(warp * 8 + g) * RS + c] = st.acc[b][jj][0] * unscale;
+            r.red[(warp * 8 + g) * RS + c + 4] = st.acc[b][jj][1] * unscale;
+        }
+    cta_sync<1, PK_WARPS * 32>();
+    if (tid < 8) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < PK_WARPS; w++) M = fmaxf(M, wm[w * 8 + tid]);
+        float Lsum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < PK_WARPS; w++) {
+            const float mw = wm[w * 8 + tid];
+            const float e = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+            wsc[w * 8 + tid] = e;
+            Lsum += wl[w * 8 + tid] * e;
+        }
+        fm[tid] = M * 0.6931471805599453f;
+        fl[tid] = Lsum;
+    }
+    cta_sync<1, PK_WARPS * 32>();
+}
+
 template <int NB>
 __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel(const DecodeParams p) {
     using L = PackLayout<NB>;
@@ -518,49 +576,277 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     if (*timeout) return;
 
     float *red = reinterpret_cast<float *>(smem);  // [W][8][RED_STRIDE]
-    float *wm = red + L::RED_FLOATS;               // [W][8]
-    float *wl = wm + PK_WARPS * 8;
-    float *wsc = wl + PK_WARPS * 8;
-    float *fm = wsc + PK_WARPS * 8;                // [8]
-    float *fl = fm + 8;
-    float *wts = fl + 8;                           // [2][MAX_SPLITS][8]
-    if (t == 0) {
-        wm[warp * 8 + g] = st.m;
-        wl[warp * 8 + g] = st.l;
+    PackRed r{red, red + L::RED_FLOATS};
+    pack_reduce<NB, L::RED_STRIDE>(st, r, warp, g, t, tid);
+    float *wts = r.fl() + 8;                       // [2][MAX_SPLITS][8]
+    auto acc_of = [&](int gg, int c) { return r.acc<L::RED_STRIDE>(gg, c); };
+    finish_split<HD, 8, PK_WARPS * 32, 1>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, r.fm(), r.fl(),
+                                          wts, flag);
+}
+
+
+// ---------------------------------------------------------------------------
+// Balanced schedule (split_tokens = 0): the tiles of every (item, kv-head
+// pair) unit, laid end to end in unit order, are cut into gridDim.x equal
+// runs, one per CTA (stream-K).  A CTA's run crosses unit boundaries, so it
+// walks one or more segments (unit, tiles [lt0, lt1)), each finished like a
+// split: its partial goes to slot c + unit of the workspace and the CTAs that
+// share a unit merge through that unit's tickets.  Every SM then streams the
+// same number of tiles whatever the number of units or their lengths; a
+// fixed split leaves the SMs that hold fewer CTAs idle for the tail.
+// ---------------------------------------------------------------------------
+constexpr int BAL_MAX_ITEMS = 256;  // items whose lengths and tile prefix fit in shared memory
+constexpr int BAL_MAX_CTAS = 1024;
+
+template <int NB>
+struct PackBalLayout {
+    using P = PackLayout<NB>;
+    static constexpr int HD = P::HD, ROW = P::ROW, PLANE = P::PLANE, STAGES = P::STAGES;
+    static constexpr int STAGE_BYTES = P::STAGE_BYTES;
+    static constexpr int OFF_BAR = P::OFF_BAR;
+    static constexpr int OFF_QQ = P::OFF_QQ, OFF_QD = P::OFF_QD, OFF_NEW = P::OFF_NEW, OFF_PRO = P::OFF_PRO;
+    static constexpr int RED_STRIDE = P::RED_STRIDE;
+    static constexpr int RED_FLOATS = P::RED_FLOATS;
+    // the reduction lives beside the ring, which keeps streaming the next segment;
+    // the merge weights [2][MAX_SPLITS][8] reuse the reduction rows once read
+    static constexpr int OFF_RED = P::OFF_FLAG;
+    static constexpr int OFF_SMALL = OFF_RED + RED_FLOATS * 4;
+    static constexpr int OFF_LENS = OFF_SMALL + ((PK_RED_SMALL * 4 + 15) / 16) * 16;  // int [BAL_MAX_ITEMS]
+    static constexpr int OFF_PRE = OFF_LENS + BAL_MAX_ITEMS * 4;                      // int [BAL_MAX_ITEMS + 1]
+    static constexpr int OFF_FLAG = OFF_PRE + ((BAL_MAX_ITEMS + 1) * 4 + 15) / 16 * 16;
+    static constexpr int BYTES = OFF_FLAG + 16;
+    static_assert(2 * MAX_SPLITS * 8 <= RED_FLOATS, "merge weights must fit in the reduction rows");
+};
+
+// One segment of a CTA's run: tiles [lt0, lt1) of unit (item, pair), whose
+// first tile is global tile ubase.
+struct BalSeg {
+    int item, pair, lt0, lt1, tiles, len, ubase;
+};
+
+// The segment holding global tile g, cut at g1 (the run's end).  pre[i] is the
+// global index of item i's first tile (pre[n_items] = total); items without
+// tiles have pre[i] == pre[i + 1] and are never chosen.
+__device__ __forceinline__ BalSeg bal_segment(const int *pre, const int *lens, int n_items, int pairs, int g, int g1) {
+    int lo = 0, hi = n_items - 1;  // the last item with pre[item] <= g
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= g) lo = mid;
+        else hi = mid - 1;
     }
-    const float unscale = exp2_int(st.kscale);
+    BalSeg s;
+    s.item = lo;
+    s.len = lens[lo];
+    s.tiles = (s.len + PK_T - 1) / PK_T;
+    const int off = g - pre[lo];
+    s.pair = off / s.tiles;
+    s.lt0 = off - s.pair * s.tiles;
+    s.ubase = pre[lo] + s.pair * s.tiles;
+    s.lt1 = min(s.tiles, s.lt0 + (g1 - g));
+    return s;
+}
+
+template <int NB>
+__global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_bal_kernel(const DecodeParams p) {
+    using L = PackBalLayout<NB>;
+    constexpr int HD = L::HD, ROW = L::ROW, STAGES = L::STAGES;
+    constexpr int G = 8;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    grid_dependency_wait();  // lengths, q, new rows and cache rows may come from earlier kernels
+    grid_dependents_launch();
+
+    const int n_items = p.n_items, pairs = p.pairs;
+    int *lens = reinterpret_cast<int *>(smem + L::OFF_LENS);
+    int *pre = reinterpret_cast<int *>(smem + L::OFF_PRE);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint64_t *empty = full + STAGES;
+    int *flag = reinterpret_cast<int *>(smem + L::OFF_FLAG);
+    int *timeout = flag + 1;
+    const int producer = PK_WARPS * 32;
+
+    if (warp == 0) {
+        // lengths (clamped like the fixed-split kernel) and the exclusive prefix of tiles
+        constexpr int PER = BAL_MAX_ITEMS / 32;
+        int tl[PER];
+        int sum = 0;
 #pragma unroll
-    for (int b = 0; b < NB; b++)
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-            const int c = b * QK + 8 * t + jj;  // permuted n-tile column n = 2t, 2t+1 -> 4n + jj
-            red[(warp * 8 + g) * L::RED_STRIDE + c] = st.acc[b][jj][0] * unscale;
-            red[(warp * 8 + g) * L::RED_STRIDE + c + 4] = st.acc[b][jj][1] * unscale;
+        for (int k = 0; k < PER; k++) {
+            const int i = lane * PER + k;
+            int len = 0;
+            if (i < n_items) {
+                len = p.lens ? p.lens[i] : p.len0 + i * p.len_step;
+                if (len < 0 || len > p.max_tokens) {
+                    record_error(p.err, DEVERR_BADLEN);
+                    len = len < 0 ? 0 : p.max_tokens;
+                }
+                lens[i] = len;
+            }
+            tl[k] = (len + PK_T - 1) / PK_T * pairs;
+            sum += tl[k];
         }
-    cta_sync<1, PK_WARPS * 32>();
-    if (tid < 8) {
-        float M = -INFINITY;
+        int incl = sum;
 #pragma unroll
-        for (int w = 0; w < PK_WARPS; w++) M = fmaxf(M, wm[w * 8 + tid]);
-        float Lsum = 0.0f;
-#pragma unroll
-        for (int w = 0; w < PK_WARPS; w++) {
-            const float mw = wm[w * 8 + tid];
-            const float e = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-            wsc[w * 8 + tid] = e;
-            Lsum += wl[w * 8 + tid] * e;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
         }
-        fm[tid] = M * 0.6931471805599453f;
-        fl[tid] = Lsum;
+        int run = incl - sum;
+#pragma unroll
+        for (int k = 0; k < PER; k++) {
+            const int i = lane * PER + k;
+            if (i < n_items) pre[i] = run;
+            run += tl[k];
+        }
+        if (lane == 31) pre[n_items] = incl;
+    } else if (tid == producer) {
+#pragma unroll
+        for (int st = 0; st < STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], PK_WARPS);
+        }
+        fence_barrier_init();
+        *timeout = 0;
     }
-    cta_sync<1, PK_WARPS * 32>();
-    auto acc_of = [&](int gg, int c) {
-        float a = 0.0f;
-#pragma unroll
-        for (int w = 0; w < PK_WARPS; w++) a = fmaf(red[(w * 8 + gg) * L::RED_STRIDE + c], wsc[w * 8 + gg], a);
-        return a;
+    __syncthreads();
+
+    // items of length 0 attend nothing: zero outputs, written by a share of the CTAs
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x) {
+        if (lens[i] != 0) continue;
+        float *out_item = p.out + (long long)i * p.out_item_stride;
+        const int heads = pairs * G;
+        for (int e = tid; e < heads * HD; e += PK_THREADS) {
+            const int h = e / HD, c = e - h * HD;
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                out_item[(long long)h * HD + c] = 0.0f;
+            } else {
+                float *o = out_item + (long long)h * (HD + 2);
+                o[c] = 0.0f;
+                if (c == 0) { o[HD] = -INFINITY; o[HD + 1] = 0.0f; }
+            }
+        }
+    }
+
+    const int T = pre[n_items];
+    const int C = min((int)gridDim.x, T);  // every CTA below C gets at least one tile
+    const int c = blockIdx.x;
+    if (c >= C) return;
+    const int g0 = (int)((long long)c * T / C), g1 = (int)((long long)(c + 1) * T / C);
+    const long long head_bytes = (long long)p.max_tokens * ROW;
+
+    if (warp == PK_WARPS) {
+        if (lane != 0) return;
+        int j = 0;
+        for (int g = g0; g < g1;) {
+            const BalSeg sg = bal_segment(pre, lens, n_items, pairs, g, g1);
+            const long long off_a = (long long)sg.item * p.item_stride + (long long)(2 * sg.pair) * head_bytes;
+            const uint8_t *ka = p.k + off_a, *va = p.v + off_a;
+            for (int lt = sg.lt0; lt < sg.lt1; lt++, j++) {
+                const int slot = j % STAGES;
+                if (j >= STAGES &&
+                    !mbar_wait_bounded(&empty[slot], (uint32_t)(((j / STAGES) - 1) & 1), WAIT_NS, p.err)) {
+                    *timeout = 1;
+                    return;
+                }
+                const int t0 = lt * PK_T;
+                const uint32_t bytes = (uint32_t)(min(PK_T, sg.len - t0) * ROW);
+                uint8_t *stg = smem + slot * L::STAGE_BYTES;
+                const long long o = (long long)t0 * ROW;
+                mbar_arrive_expect_tx(&full[slot], 4 * bytes);
+                bulk_copy_g2s(stg, ka + o, bytes, &full[slot]);
+                bulk_copy_g2s(stg + L::PLANE, ka + head_bytes + o, bytes, &full[slot]);
+                bulk_copy_g2s(stg + 2 * L::PLANE, va + o, bytes, &full[slot]);
+                bulk_copy_g2s(stg + 3 * L::PLANE, va + head_bytes + o, bytes, &full[slot]);
+            }
+            g = sg.ubase + sg.lt1;
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------------ consumers
+    int8_t *qq = reinterpret_cast<int8_t *>(smem + L::OFF_QQ);
+    float *qd = reinterpret_cast<float *>(smem + L::OFF_QD);
+    uint8_t *newrow = smem + L::OFF_NEW;
+    float *pro = reinterpret_cast<float *>(smem + L::OFF_PRO) + warp * (PK_QR + PK_NJ) * pro_stride<NB>();
+    const PackRed red{reinterpret_cast<float *>(smem + L::OFF_RED), reinterpret_cast<float *>(smem + L::OFF_SMALL)};
+    const int g = lane >> 2, t = lane & 3;
+    const bool hb = g >= 4;
+    const uint32_t mask_a = hb ? 0u : 0x3C003C00u, mask_b = hb ? 0x3C003C00u : 0u;
+    const int r0 = warp * PK_ROWS;
+
+    // The segment is looked up again from shared memory where it is needed
+    // rather than kept in registers across the tile loop (which holds the
+    // P*V accumulators and the q operands).
+    // the run's end, recomputed from shared memory
+    auto run_end = [&]() {
+        const int Tn = pre[n_items], Cn = min((int)gridDim.x, Tn);
+        return (int)((long long)(blockIdx.x + 1) * Tn / Cn);
     };
-    finish_split<HD, 8, PK_WARPS * 32, 1>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, fm, fl, wts, flag);
+    int j = 0;  // ring position of the next tile
+    for (int gt = g0;;) {
+        {
+            const BalSeg sg = bal_segment(pre, lens, n_items, pairs, gt, run_end());
+            const bool do_append = p.k_new != nullptr && sg.lt1 == sg.tiles;  // the segment holding the last tile
+            pack_preamble<NB>(p, sg.item, 2 * sg.pair * p.group, 2 * sg.pair, sg.len - 1, do_append, warp, lane, qq,
+                              qd, newrow, pro);
+        }
+        cta_sync<1, PK_WARPS * 32>();  // q operands visible; the previous segment's scratch is free
+        PackState<NB> st;
+        st.begin(qq, qd, g, t, hb);
+
+        bool timed_out = false;
+        {
+            const BalSeg sg = bal_segment(pre, lens, n_items, pairs, gt, run_end());
+            const bool do_append = p.k_new != nullptr && sg.lt1 == sg.tiles;
+            const int pos = sg.len - 1;
+            for (int lt = sg.lt0; lt < sg.lt1; lt++, j++) {
+                const int slot = j % STAGES;
+                const int t0 = lt * PK_T;
+                const int rows = min(PK_T, sg.len - t0);
+                const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((j / STAGES) & 1), WAIT_NS, p.err);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    timed_out = true;
+                    break;
+                }
+                const int nvalid = rows - r0;
+                if (nvalid > 0) {
+                    uint8_t *stg = smem + slot * L::STAGE_BYTES;
+                    uint8_t *k_a = stg + r0 * ROW, *k_b = stg + L::PLANE + r0 * ROW;
+                    uint8_t *v_a = stg + 2 * L::PLANE + r0 * ROW, *v_b = stg + 3 * L::PLANE + r0 * ROW;
+                    if (do_append) pack_patch<NB>(pos, t0, r0, lane, k_a, k_b, v_a, v_b, newrow);
+                    if (nvalid >= PK_ROWS)
+                        pack_step<NB, true>(st, k_a, k_b, v_a, v_b, nvalid, p.scale, g, t, hb, mask_a, mask_b);
+                    else
+                        pack_step<NB, false>(st, k_a, k_b, v_a, v_b, nvalid, p.scale, g, t, hb, mask_a, mask_b);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive_release(&empty[slot]);
+            }
+        }
+        if (timed_out) *timeout = 1;
+        cta_sync<1, PK_WARPS * 32>();
+        if (*timeout) return;
+
+        pack_reduce<NB, L::RED_STRIDE>(st, red, warp, g, t, tid);
+        const int Tn = pre[n_items];
+        const int Cn = min((int)gridDim.x, Tn);
+        const int cn = blockIdx.x;
+        const int g1n = (int)((long long)(cn + 1) * Tn / Cn);
+        const BalSeg sg = bal_segment(pre, lens, n_items, pairs, gt, g1n);
+        // the CTAs covering this unit: c0 .. c1 (the owners of its first and last tiles)
+        const int c0 = (int)((((long long)sg.ubase + 1) * Cn - 1) / Tn);
+        const int c1 = (int)((((long long)sg.ubase + sg.tiles) * Cn - 1) / Tn);
+        const long long unit = (long long)sg.item * pairs + sg.pair;
+        float *pb = p.part + ((long long)c0 + unit) * G * (HD + 2);
+        int *tickets = p.counters + unit * p.tickets_per_unit;
+        float *out_item = p.out + (long long)sg.item * p.out_item_stride;
+        auto acc_of = [&](int gg, int cc) { return red.acc<L::RED_STRIDE>(gg, cc); };
+        finish_split_at<HD, G, PK_WARPS * 32, 1>(p, tid, pb, tickets, cn - c0, c1 - c0 + 1, 2 * sg.pair * p.group, G,
+                                                 out_item, acc_of, red.fm(), red.fl(), red.red, flag);
+        gt = sg.ubase + sg.lt1;
+        if (gt >= g1n) break;
+    }
 }
 
 }  // namespace tqk

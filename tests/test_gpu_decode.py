@@ -281,6 +281,85 @@ def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
     assert tqk.device_status() == 0
 
 
+@pytest.mark.parametrize("n_items", [256, 300])
+def test_balanced_schedule_items_and_workspace_reuse(tqk, port, cuda, n_items):
+    """The packed kernel's automatic schedule: up to 256 items the units' tiles are cut into
+    equal per-CTA runs that cross unit boundaries (256 here, with empty and one-token items);
+    above that it falls back to the fixed split (300).  Checked against the oracle on a sample
+    of items; repeated calls through one caller workspace give identical bytes (the tickets
+    are left at zero), and so does a fixed-split call in between."""
+    import torch
+    nq, nkv, hd, mt = 8, 2, 128, 300
+    rng = np.random.default_rng(21 + n_items)
+    lens = rng.integers(1, mt + 1, n_items).astype(np.int32)
+    lens[::37] = 0
+    lens[5] = 1
+    lens[6] = mt
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    kp = _gpu_planes(gen, (n_items, nkv, mt, hd), tqk)
+    vp = _gpu_planes(gen, (n_items, nkv, mt, hd), tqk)
+    q = torch.from_numpy(rng.standard_normal((n_items, nq * hd), dtype=np.float32)).to(cuda)
+    lens_d = torch.from_numpy(lens).to(cuda)
+
+    def call(split, ws=None):
+        out = torch.full((n_items, nq * hd), 3.0, device=cuda)
+        a = tqk.decode_args(kp, vp, nq, nkv, hd, mt, q, out, n_items=n_items,
+                            item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
+                            q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=split)
+        tqk.decode(a, workspace=ws)
+        return out.cpu().numpy(), a
+
+    first, a = call(0)
+    ws = torch.empty(max(tqk.decode_workspace_size(a), 1 << 24), dtype=torch.uint8, device=cuda)
+    tqk.workspace_init(ws)
+    assert np.array_equal(call(0, ws)[0], first)
+    fixed = call(64, ws)[0]
+    assert np.array_equal(call(0, ws)[0], first)
+    assert np.abs(fixed - first).max() <= 2e-6 * max(1.0, np.abs(first).max())
+    kh, vh, qh = kp.cpu().numpy(), vp.cpu().numpy(), q.cpu().numpy()
+    for b in (0, 5, 6, 37, 100, n_items - 1):
+        if lens[b] == 0:
+            assert (first[b] == 0).all(), b
+            continue
+        ok, max_abs, rel = tolerance_ok(first[b], port.attend(kh[b], vh[b], nq, nkv, hd, mt, int(lens[b]) - 1, qh[b]))
+        assert ok, f"item {b} (len {lens[b]}): max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
+def test_balanced_schedule_long_ragged_two_level_merge(tqk, port, cuda):
+    """Two items of very different lengths on the balanced schedule: the long one's units are
+    each covered by dozens of CTAs, so their partials go through the two-level (group, then
+    final) merge; the short one's units sit inside one CTA's run.  With a fused append."""
+    import torch
+    nq, nkv, hd, mt = 32, 8, 128, 20000
+    lens = np.array([20000, 100], dtype=np.int32)
+    rng = np.random.default_rng(23)
+    gen = torch.Generator(device="cuda").manual_seed(23)
+    kp = _gpu_planes(gen, (2, nkv, mt, hd), tqk)
+    vp = _gpu_planes(gen, (2, nkv, mt, hd), tqk)
+    q = rng.standard_normal((2, nq * hd), dtype=np.float32)
+    k_new = rng.standard_normal((2, nkv * hd), dtype=np.float32)
+    v_new = rng.standard_normal((2, nkv * hd), dtype=np.float32)
+    kh0, vh0 = kp.cpu().numpy(), vp.cpu().numpy()
+    out = torch.empty(2, nq * hd, device=cuda)
+    args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=2,
+                           item_stride_blocks=nkv * mt * (hd // 32), lens=torch.from_numpy(lens).to(cuda),
+                           max_len=int(lens.max()), q_item_stride=nq * hd, out_item_stride=nq * hd,
+                           k_new=torch.from_numpy(k_new).to(cuda), v_new=torch.from_numpy(v_new).to(cuda),
+                           kv_new_item_stride=nkv * hd)
+    tqk.decode(args)
+    got = out.cpu().numpy()
+    kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+    for b in range(2):
+        n = int(lens[b])
+        kref, vref = kh0[b].copy(), vh0[b].copy()
+        assert port.store_kv(kref, vref, nkv, hd, mt, n - 1, k_new[b], v_new[b]) == 0
+        assert np.array_equal(kref, kh[b]) and np.array_equal(vref, vh[b]), f"append item {b}"
+        ok, max_abs, rel = tolerance_ok(got[b], port.attend(kref, vref, nq, nkv, hd, mt, n - 1, q[b]))
+        assert ok, f"item {b} (len {n}): max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
 def test_config3_auto_schedule(tqk, port, cuda):
     """Config 3 through the automatic split, checked against an explicit split
     and, on a sample of sequences, the oracle."""
