@@ -434,8 +434,10 @@ class Config5:
         self.v_new = torch.randn(n, n_kv * hd, device="cuda", generator=g)
         self.out = torch.empty(n, n_q * hd, device="cuda")
         self.tokens_per_step = n
-        self.launches_per_step = 2  # the append and the attention
+        self.launches_per_step = 3  # the append, the K/V tile staging and the attention
         self.bytes_per_step = 2 * n_kv * self.mt * self.nb * BB
+        self.e2e_api = ("tqk_prefill_q8 (C ABI) with the chunk's pinned host q, k and v in and the attention "
+                        "output out, stream-synchronised every step")
         self.h_q = self.q.cpu().pin_memory()
         self.h_k = self.k_new.cpu().pin_memory()
         self.h_v = self.v_new.cpu().pin_memory()

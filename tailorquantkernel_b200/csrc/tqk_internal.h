@@ -38,6 +38,9 @@ int *library_counters(cudaStream_t stream, size_t bytes);
 // Library-owned staging buffer per (device, stream) for intermediate rows that
 // one call produces and consumes (e.g. quantised activations); grows on demand.
 void *library_scratch(cudaStream_t stream, size_t bytes);
+// Library-owned buffer per (device, stream) for the prefill's staged K/V tiles
+// (MMA-ready images of the cache rows, written and read within one call).
+void *library_prefill_stage(cudaStream_t stream, size_t bytes);
 
 // Launches `kernel` with programmatic stream serialization, so that it may
 // start while the previous kernel of the stream finishes (the kernel must call

@@ -23,6 +23,7 @@ struct Workspace {
 std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
 std::map<std::pair<int, cudaStream_t>, Workspace> g_counters;
 std::map<std::pair<int, cudaStream_t>, Workspace> g_scratch;
+std::map<std::pair<int, cudaStream_t>, Workspace> g_prefill_stage;
 
 // Grows `w` to at least `bytes` (minimum 1 MiB), zeroing the new buffer on `stream`.
 void *grow_zeroed(Workspace &w, cudaStream_t stream, size_t bytes) {
@@ -108,6 +109,13 @@ void *library_scratch(cudaStream_t stream, size_t bytes) {
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lock(g_mutex);
     return grow_zeroed(g_scratch[{dev, stream}], stream, bytes);
+}
+
+void *library_prefill_stage(cudaStream_t stream, size_t bytes) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    return grow_zeroed(g_prefill_stage[{dev, stream}], stream, bytes);
 }
 
 }  // namespace tqk
