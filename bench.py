@@ -256,12 +256,15 @@ class Config4:
     """Llama-3-70B-shaped long-context decode: one layer, 64 q / 8 kv heads,
     head_dim 128, context 131072.  With N ranks the context is split into N
     contiguous token ranges; each rank computes log-sum-exp partials of its
-    range, the partials are all-gathered (NCCL over NVLink) and merged
-    (tqk_merge_partials).  One step is one token for the whole job."""
+    range, and the ranks exchange and merge them: by default in one
+    tqk_exchange_merge launch over peer memory (P2P stores into the peers'
+    mailboxes over NVLink), with exchange="nccl" by an NCCL all-gather and
+    tqk_merge_partials.  One step is one token for the whole job."""
     name = "config4"
     scaling = "strong"  # the context is fixed; each rank gets 1/N of it
 
-    def __init__(self, seed: int, rank: int = 0, world: int = 1, dist=None, n=131072, n_q=64, n_kv=8, hd=128):
+    def __init__(self, seed: int, rank: int = 0, world: int = 1, dist=None, n=131072, n_q=64, n_kv=8, hd=128,
+                 exchange: str = "p2p"):
         import torch
         from tailorquantkernel_b200 import shard, tqk
         self.tqk, self.shard, self.dist, self.world = tqk, shard, dist, world
@@ -283,7 +286,9 @@ class Config4:
         self.kv_bytes = 2 * n_kv * n * self.nb * BB            # the whole context, all ranks
         self.bytes_per_step = 2 * n_kv * self.n_local * self.nb * BB  # this rank's decode kernel
         self.tokens_per_step = 1
-        self.launches_per_step = 1 if world == 1 else 2  # decode (+ merge); the all-gather is NCCL's
+        self.launches_per_step = 1 if world == 1 else 2  # decode (+ exchange-merge, or merge after NCCL)
+        self.exchange = exchange
+        self.peer = shard.PeerExchange(dist, tqk, n_q, hd) if world > 1 and exchange == "p2p" else None
         self.h_q = self.q.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
         self.h2d = self.h_q.numel() * 4
@@ -292,6 +297,9 @@ class Config4:
     def step(self):
         if self.world == 1:
             self.tqk.decode(self.args)
+        elif self.peer is not None:
+            self.shard.seqsplit_attend_p2p(self.peer, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
+                                           self.n_local, self.q, self.out, self.partial)
         else:
             self.shard.seqsplit_attend(self.dist, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
                                        self.n_local, self.q, self.out, self.partial, gathered=self.gathered)
@@ -311,10 +319,18 @@ class Config4:
                 "tokens_per_rank": self.n_local,
                 "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
 
-    @staticmethod
-    def parallelism(world):
-        return (f"sequence-split over {world} GPUs: log-sum-exp partials all-gathered with NCCL, merged on device"
-                if world > 1 else "single GPU")
+    def parallelism(self, world):
+        if world == 1:
+            return "single GPU"
+        if self.peer is not None:
+            return (f"sequence-split over {world} GPUs: log-sum-exp partials exchanged over peer memory and "
+                    "merged in one kernel (tqk_exchange_merge)")
+        return f"sequence-split over {world} GPUs: log-sum-exp partials all-gathered with NCCL, merged on device"
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def host_planes(self):
         return self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), None, None
@@ -854,7 +870,7 @@ def run_ours(args):
     elif args.config == 3:
         wl = Config3(seed=3000, rank=rank, world=world)
     elif args.config == 4:
-        wl = Config4(seed=4000, rank=rank, world=world, dist=dist)
+        wl = Config4(seed=4000, rank=rank, world=world, dist=dist, exchange=args.exchange)
     elif args.config == 6:
         wl = Config6(seed=6000 + rank)
     else:
@@ -959,6 +975,8 @@ def run_ours(args):
             "device_status": status,
         }
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0
@@ -974,6 +992,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="config 4 on several GPUs: the partials' exchange over peer memory or by NCCL")
     ap.add_argument("--prologue", action="store_true",
                     help="config 2 with the q/k RMSNorm + RoPE prologue fused into the decode launch")
     args = ap.parse_args()

@@ -10,8 +10,11 @@ needs a collective:
   every rank owns whole sequences;
 * by sequence (one very long context, contiguous token ranges per rank): each
   rank computes log-sum-exp partials {acc, m, l} of its range
-  (TQK_OUT_PARTIAL), the partials are all-gathered over NVLink, and
-  tqk_merge_partials combines them -- the only exchange step.
+  (TQK_OUT_PARTIAL) and the ranks exchange and merge them -- the only
+  exchange step.  PeerExchange does it in one kernel over peer memory
+  (tqk_exchange_merge: P2P stores into the peers' mailboxes, a flag per
+  epoch, local merge); seqsplit_attend does it with an NCCL all-gather and
+  tqk_merge_partials.
 
 The functions here are pure host logic plus torch.distributed calls; the GPU
 work goes through libtqk's C ABI (tailorquantkernel_b200.tqk).
@@ -99,3 +102,61 @@ def seqsplit_attend(dist, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: 
         dist.all_gather_into_tensor(gathered, partial)
     tqk.merge_partials(gathered, world, n_q * (head_dim + 2), n_q, head_dim, out, stream=stream)
     return out
+
+
+class PeerExchange:
+    """The sequence split's exchange step over peer memory for ranks on the GPUs of
+    one box: one mailbox per rank (tqk_peer_buffer_alloc), mapped in every other
+    rank through CUDA IPC handles swapped once with torch.distributed, and one
+    tqk_exchange_merge launch per step.  Every rank must call step() the same
+    number of times, in the same order; close() unmaps and frees."""
+
+    def __init__(self, dist, tqk, n_heads: int, head_dim: int, group=None):
+        import torch
+        self.tqk, self.n_heads, self.head_dim = tqk, n_heads, head_dim
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        nbytes = tqk.tqk_exchange_mailbox_bytes(self.world, n_heads, head_dim)
+        if nbytes == 0:
+            raise ValueError(f"no mailbox layout for world {self.world}, {n_heads} heads of {head_dim}")
+        self.local = tqk.peer_buffer_alloc(nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, tqk.ipc_get_handle(self.local), group=group)
+        self.opened = []
+        self.mailboxes = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.mailboxes.append(self.local)
+            else:
+                ptr = tqk.ipc_open_handle(h)
+                self.opened.append(ptr)
+                self.mailboxes.append(ptr)
+        self.epoch = 0
+        torch.cuda.synchronize()
+        dist.barrier(group=group)  # every mailbox is zeroed and mapped before the first step
+
+    def step(self, partial, out, stream=None):
+        """Merges every rank's partial records of this step into out (all ranks get the same)."""
+        self.epoch += 1
+        self.tqk.exchange_merge(partial, self.n_heads, self.head_dim, self.world, self.rank, self.mailboxes,
+                                self.epoch, out, stream=stream)
+        return out
+
+    def close(self):
+        import torch
+        torch.cuda.synchronize()
+        for ptr in self.opened:
+            self.tqk.ipc_close_handle(ptr)
+        self.opened = []
+        if self.local:
+            self.tqk.peer_buffer_free(self.local)
+            self.local = None
+
+
+def seqsplit_attend_p2p(exchange: PeerExchange, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: int,
+                        n_local: int, q, out, partial, stream=None):
+    """seqsplit_attend with the exchange over peer memory: decode of this rank's
+    range into partial records, then one tqk_exchange_merge launch."""
+    args = tqk.decode_args(k_local, v_local, n_q, n_kv, head_dim, max(n_local, 1), q, partial, len0=n_local,
+                           out_mode=tqk.OUT_PARTIAL)
+    tqk.decode(args, stream=stream)
+    return exchange.step(partial, out, stream=stream)

@@ -131,6 +131,14 @@ tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_merge_partials = _sig("tqk_merge_partials", [_vp, _i, _i64, _i, _i, _vp, _vp])
+tqk_exchange_mailbox_bytes = _sig("tqk_exchange_mailbox_bytes", [_i, _i, _i], _sz)
+tqk_peer_buffer_alloc = _sig("tqk_peer_buffer_alloc", [_sz, ctypes.POINTER(_vp)])
+tqk_peer_buffer_free = _sig("tqk_peer_buffer_free", [_vp])
+tqk_ipc_get_handle = _sig("tqk_ipc_get_handle", [_vp, ctypes.c_char_p])
+tqk_ipc_open_handle = _sig("tqk_ipc_open_handle", [ctypes.c_char_p, ctypes.POINTER(_vp)])
+tqk_ipc_close_handle = _sig("tqk_ipc_close_handle", [_vp])
+tqk_exchange_merge = _sig("tqk_exchange_merge", [_vp, _i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+IPC_HANDLE_BYTES = 64
 
 EXPORTED = [
     "tqk_status_string", "tqk_last_error", "tqk_version", "tqk_device_status",
@@ -141,6 +149,8 @@ EXPORTED = [
     "tqk_decode_q8_static", "tqk_qk_norm_rope",
     "tqk_matmul_q8", "tqk_matmul_q4", "tqk_matmul_q8_batch", "tqk_matmul_q4_batch", "tqk_project",
     "tqk_attention_layer", "tqk_pack_matrix", "tqk_packed_matrix_bytes",
+    "tqk_exchange_mailbox_bytes", "tqk_peer_buffer_alloc", "tqk_peer_buffer_free", "tqk_ipc_get_handle",
+    "tqk_ipc_open_handle", "tqk_ipc_close_handle", "tqk_exchange_merge",
 ]
 
 
@@ -354,6 +364,42 @@ def workspace_init(workspace, stream=None) -> None:
 def merge_partials(parts, n_parts, part_stride, n_heads, head_dim, out, stream=None):
     check(tqk_merge_partials(_ptr(parts), n_parts, part_stride, n_heads, head_dim, _ptr(out), _stream(stream)),
           "tqk_merge_partials")
+
+
+def peer_buffer_alloc(nbytes: int) -> int:
+    """A zeroed device buffer that is one whole allocation (so that its IPC handle maps exactly it)."""
+    p = _vp()
+    check(tqk_peer_buffer_alloc(nbytes, ctypes.byref(p)), "tqk_peer_buffer_alloc")
+    return p.value
+
+
+def peer_buffer_free(ptr: int) -> None:
+    check(tqk_peer_buffer_free(ptr), "tqk_peer_buffer_free")
+
+
+def ipc_get_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    check(tqk_ipc_get_handle(ptr, buf), "tqk_ipc_get_handle")
+    return buf.raw
+
+
+def ipc_open_handle(handle: bytes) -> int:
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("an IPC handle is 64 bytes")
+    p = _vp()
+    check(tqk_ipc_open_handle(handle, ctypes.byref(p)), "tqk_ipc_open_handle")
+    return p.value
+
+
+def ipc_close_handle(ptr: int) -> None:
+    check(tqk_ipc_close_handle(ptr), "tqk_ipc_close_handle")
+
+
+def exchange_merge(partial, n_heads, head_dim, world, rank, mailboxes, epoch, out, stream=None):
+    """tqk_exchange_merge: mailboxes is the list of every rank's mailbox address in this process."""
+    arr = (_vp * len(mailboxes))(*mailboxes)
+    check(tqk_exchange_merge(_ptr(partial), n_heads, head_dim, world, rank, arr, epoch, _ptr(out), _stream(stream)),
+          "tqk_exchange_merge")
 
 
 def device_status(clear: bool = False) -> int:

@@ -103,6 +103,23 @@ def test_packed_matrix_bytes_without_device():
     assert tqk.tqk_packed_matrix_bytes(3, 64, b"x") == 0
 
 
+def test_exchange_mailbox_without_device():
+    """tqk_exchange_mailbox_bytes: two parity slots of every rank's records plus flags and
+    tickets, 0 outside 1..8 ranks; tqk_exchange_merge rejects bad arguments before any
+    device work."""
+    from tailorquantkernel_b200 import tqk
+    for world in (1, 2, 8):
+        b = tqk.tqk_exchange_mailbox_bytes(world, 64, 128)
+        assert b >= 2 * world * 64 * 130 * 4 + 2 * world * 4 and b % 256 == 0
+    assert tqk.tqk_exchange_mailbox_bytes(2, 64, 128) < tqk.tqk_exchange_mailbox_bytes(4, 64, 128)
+    assert tqk.tqk_exchange_mailbox_bytes(0, 64, 128) == 0
+    assert tqk.tqk_exchange_mailbox_bytes(9, 64, 128) == 0
+    boxes = (ctypes.c_void_p * 2)(None, None)
+    assert tqk.tqk_exchange_merge(None, 64, 128, 2, 0, boxes, 1, None, None) == tqk.EINVAL
+    assert tqk.tqk_exchange_merge(1, 64, 128, 2, 2, boxes, 1, 1, None) == tqk.EINVAL  # rank outside the world
+    assert tqk.tqk_exchange_merge(1, 64, 128, 2, 0, boxes, 0, 1, None) == tqk.EINVAL  # epochs start at 1
+
+
 def test_error_codes_without_device():
     from tailorquantkernel_b200 import tqk
     # position checks come first and never touch a device (reference: -1 on bad pos)
