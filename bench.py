@@ -257,8 +257,9 @@ class Config4:
     head_dim 128, context 131072.  With N ranks the context is split into N
     contiguous token ranges; each rank computes log-sum-exp partials of its
     range, and the ranks exchange and merge them: by default in one
-    tqk_exchange_merge launch over peer memory (P2P stores into the peers'
-    mailboxes over NVLink), with exchange="nccl" by an NCCL all-gather and
+    tqk_exchange_merge launch over peer memory (the decode writes into the
+    rank's mailbox, the peers' records are read over NVLink), with
+    exchange="nccl" by an NCCL all-gather and
     tqk_merge_partials.  One step is one token for the whole job."""
     name = "config4"
     scaling = "strong"  # the context is fixed; each rank gets 1/N of it
@@ -299,7 +300,7 @@ class Config4:
             self.tqk.decode(self.args)
         elif self.peer is not None:
             self.shard.seqsplit_attend_p2p(self.peer, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
-                                           self.n_local, self.q, self.out, self.partial)
+                                           self.n_local, self.q, self.out)
         else:
             self.shard.seqsplit_attend(self.dist, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
                                        self.n_local, self.q, self.out, self.partial, gathered=self.gathered)

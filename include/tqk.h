@@ -329,25 +329,28 @@ TQK_API int tqk_merge_partials(const float *parts, int n_parts, int64_t part_str
  * tqk_exchange_mailbox_bytes with tqk_peer_buffer_alloc, publishes its IPC
  * handle (tqk_ipc_get_handle), maps every peer's (tqk_ipc_open_handle) and
  * then, once per step with epoch = 1, 2, 3, ...:
- *   tqk_exchange_merge(partial, ..., mailboxes, epoch, out, stream)
- * where partial holds this rank's TQK_OUT_PARTIAL records [n_heads][head_dim+2]
- * and mailboxes[r] is rank r's mailbox as mapped in this process
- * (mailboxes[rank] = the local one).  The kernel stores this rank's records
- * into every peer's mailbox, raises its flag there, waits for every peer's
- * flag of this epoch (1 s limit: TQK_ETIMEOUT in tqk_device_status, output
- * left unwritten) and writes the merged output (tqk_merge_partials'
- * arithmetic).  All ranks must call it with the same epoch sequence, one
- * call per epoch, each on one stream; world <= 8.
+ *   1. writes this rank's TQK_OUT_PARTIAL records [n_heads][head_dim+2] into
+ *      its own mailbox at byte offset tqk_exchange_slot_offset(epoch) (for
+ *      instance as the decode's out);
+ *   2. tqk_exchange_merge(..., mailboxes, epoch, out, stream), where
+ *      mailboxes[r] is rank r's mailbox as mapped in this process
+ *      (mailboxes[rank] = the local one).
+ * The kernel raises this rank's flag in every peer's mailbox, waits for every
+ * peer's flag of this epoch (1 s limit: TQK_ETIMEOUT in tqk_device_status,
+ * output left unwritten), reads the peers' records over NVLink and writes the
+ * merged output (tqk_merge_partials' arithmetic).  All ranks must make the
+ * same calls with the same epoch sequence, each rank on one stream; world <= 8.
  */
 #define TQK_IPC_HANDLE_BYTES 64
 TQK_API size_t tqk_exchange_mailbox_bytes(int world, int n_heads, int head_dim);
+TQK_API size_t tqk_exchange_slot_offset(int n_heads, int head_dim, int epoch);
 TQK_API int tqk_peer_buffer_alloc(size_t bytes, void **ptr);
 TQK_API int tqk_peer_buffer_free(void *ptr);
 TQK_API int tqk_ipc_get_handle(void *ptr, unsigned char *handle);
 TQK_API int tqk_ipc_open_handle(const unsigned char *handle, void **ptr);
 TQK_API int tqk_ipc_close_handle(void *ptr);
-TQK_API int tqk_exchange_merge(const float *partial, int n_heads, int head_dim, int world, int rank,
-                       void *const *mailboxes, int epoch, float *out, tqk_stream_t stream);
+TQK_API int tqk_exchange_merge(int n_heads, int head_dim, int world, int rank, void *const *mailboxes, int epoch,
+                       float *out, tqk_stream_t stream);
 
 #ifdef __cplusplus
 }

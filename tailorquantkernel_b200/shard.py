@@ -12,9 +12,9 @@ needs a collective:
   rank computes log-sum-exp partials {acc, m, l} of its range
   (TQK_OUT_PARTIAL) and the ranks exchange and merge them -- the only
   exchange step.  PeerExchange does it in one kernel over peer memory
-  (tqk_exchange_merge: P2P stores into the peers' mailboxes, a flag per
-  epoch, local merge); seqsplit_attend does it with an NCCL all-gather and
-  tqk_merge_partials.
+  (tqk_exchange_merge: the decode writes into the rank's own mailbox, a flag
+  per epoch in every peer, the peers' records read over NVLink and merged);
+  seqsplit_attend does it with an NCCL all-gather and tqk_merge_partials.
 
 The functions here are pure host logic plus torch.distributed calls; the GPU
 work goes through libtqk's C ABI (tailorquantkernel_b200.tqk).
@@ -107,9 +107,10 @@ def seqsplit_attend(dist, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: 
 class PeerExchange:
     """The sequence split's exchange step over peer memory for ranks on the GPUs of
     one box: one mailbox per rank (tqk_peer_buffer_alloc), mapped in every other
-    rank through CUDA IPC handles swapped once with torch.distributed, and one
-    tqk_exchange_merge launch per step.  Every rank must call step() the same
-    number of times, in the same order; close() unmaps and frees."""
+    rank through CUDA IPC handles swapped once with torch.distributed.  Per step:
+    begin() gives the slot this rank's partial records go to, end() launches
+    tqk_exchange_merge.  Every rank must run the same steps in the same order;
+    close() unmaps and frees."""
 
     def __init__(self, dist, tqk, n_heads: int, head_dim: int, group=None):
         import torch
@@ -134,11 +135,15 @@ class PeerExchange:
         torch.cuda.synchronize()
         dist.barrier(group=group)  # every mailbox is zeroed and mapped before the first step
 
-    def step(self, partial, out, stream=None):
-        """Merges every rank's partial records of this step into out (all ranks get the same)."""
+    def begin(self) -> int:
+        """Starts the next step: the device address its partial records must be written to."""
         self.epoch += 1
-        self.tqk.exchange_merge(partial, self.n_heads, self.head_dim, self.world, self.rank, self.mailboxes,
-                                self.epoch, out, stream=stream)
+        return self.tqk.exchange_slot(self.local, self.n_heads, self.head_dim, self.epoch)
+
+    def end(self, out, stream=None):
+        """Merges every rank's records of the step into out (all ranks get the same)."""
+        self.tqk.exchange_merge(self.n_heads, self.head_dim, self.world, self.rank, self.mailboxes, self.epoch, out,
+                                stream=stream)
         return out
 
     def close(self):
@@ -153,10 +158,11 @@ class PeerExchange:
 
 
 def seqsplit_attend_p2p(exchange: PeerExchange, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: int,
-                        n_local: int, q, out, partial, stream=None):
+                        n_local: int, q, out, stream=None):
     """seqsplit_attend with the exchange over peer memory: decode of this rank's
-    range into partial records, then one tqk_exchange_merge launch."""
-    args = tqk.decode_args(k_local, v_local, n_q, n_kv, head_dim, max(n_local, 1), q, partial, len0=n_local,
+    range straight into its mailbox slot, then one tqk_exchange_merge launch."""
+    slot = exchange.begin()
+    args = tqk.decode_args(k_local, v_local, n_q, n_kv, head_dim, max(n_local, 1), q, slot, len0=n_local,
                            out_mode=tqk.OUT_PARTIAL)
     tqk.decode(args, stream=stream)
-    return exchange.step(partial, out, stream=stream)
+    return exchange.end(out, stream=stream)

@@ -137,7 +137,8 @@ tqk_peer_buffer_free = _sig("tqk_peer_buffer_free", [_vp])
 tqk_ipc_get_handle = _sig("tqk_ipc_get_handle", [_vp, ctypes.c_char_p])
 tqk_ipc_open_handle = _sig("tqk_ipc_open_handle", [ctypes.c_char_p, ctypes.POINTER(_vp)])
 tqk_ipc_close_handle = _sig("tqk_ipc_close_handle", [_vp])
-tqk_exchange_merge = _sig("tqk_exchange_merge", [_vp, _i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+tqk_exchange_slot_offset = _sig("tqk_exchange_slot_offset", [_i, _i, _i], _sz)
+tqk_exchange_merge = _sig("tqk_exchange_merge", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
 IPC_HANDLE_BYTES = 64
 
 EXPORTED = [
@@ -149,7 +150,8 @@ EXPORTED = [
     "tqk_decode_q8_static", "tqk_qk_norm_rope",
     "tqk_matmul_q8", "tqk_matmul_q4", "tqk_matmul_q8_batch", "tqk_matmul_q4_batch", "tqk_project",
     "tqk_attention_layer", "tqk_pack_matrix", "tqk_packed_matrix_bytes",
-    "tqk_exchange_mailbox_bytes", "tqk_peer_buffer_alloc", "tqk_peer_buffer_free", "tqk_ipc_get_handle",
+    "tqk_exchange_mailbox_bytes", "tqk_exchange_slot_offset", "tqk_peer_buffer_alloc", "tqk_peer_buffer_free",
+    "tqk_ipc_get_handle",
     "tqk_ipc_open_handle", "tqk_ipc_close_handle", "tqk_exchange_merge",
 ]
 
@@ -395,11 +397,17 @@ def ipc_close_handle(ptr: int) -> None:
     check(tqk_ipc_close_handle(ptr), "tqk_ipc_close_handle")
 
 
-def exchange_merge(partial, n_heads, head_dim, world, rank, mailboxes, epoch, out, stream=None):
-    """tqk_exchange_merge: mailboxes is the list of every rank's mailbox address in this process."""
+def exchange_merge(n_heads, head_dim, world, rank, mailboxes, epoch, out, stream=None):
+    """tqk_exchange_merge: mailboxes is the list of every rank's mailbox address in this process;
+    this rank's records of the epoch must already be in its slot (exchange_slot)."""
     arr = (_vp * len(mailboxes))(*mailboxes)
-    check(tqk_exchange_merge(_ptr(partial), n_heads, head_dim, world, rank, arr, epoch, _ptr(out), _stream(stream)),
+    check(tqk_exchange_merge(n_heads, head_dim, world, rank, arr, epoch, _ptr(out), _stream(stream)),
           "tqk_exchange_merge")
+
+
+def exchange_slot(mailbox: int, n_heads: int, head_dim: int, epoch: int) -> int:
+    """Address of the epoch's partial-record slot in a mailbox."""
+    return mailbox + tqk_exchange_slot_offset(n_heads, head_dim, epoch)
 
 
 def device_status(clear: bool = False) -> int:

@@ -110,14 +110,16 @@ def test_exchange_mailbox_without_device():
     from tailorquantkernel_b200 import tqk
     for world in (1, 2, 8):
         b = tqk.tqk_exchange_mailbox_bytes(world, 64, 128)
-        assert b >= 2 * world * 64 * 130 * 4 + 2 * world * 4 and b % 256 == 0
-    assert tqk.tqk_exchange_mailbox_bytes(2, 64, 128) < tqk.tqk_exchange_mailbox_bytes(4, 64, 128)
+        assert b >= 2 * 64 * 130 * 4 + 2 * world * 4 and b % 256 == 0
+    assert tqk.tqk_exchange_slot_offset(64, 128, 1) == 64 * 130 * 4  # odd epochs in the second slot
+    assert tqk.tqk_exchange_slot_offset(64, 128, 2) == 0
+    assert tqk.tqk_exchange_slot_offset(64, 128, 0) == 0
     assert tqk.tqk_exchange_mailbox_bytes(0, 64, 128) == 0
     assert tqk.tqk_exchange_mailbox_bytes(9, 64, 128) == 0
     boxes = (ctypes.c_void_p * 2)(None, None)
-    assert tqk.tqk_exchange_merge(None, 64, 128, 2, 0, boxes, 1, None, None) == tqk.EINVAL
-    assert tqk.tqk_exchange_merge(1, 64, 128, 2, 2, boxes, 1, 1, None) == tqk.EINVAL  # rank outside the world
-    assert tqk.tqk_exchange_merge(1, 64, 128, 2, 0, boxes, 0, 1, None) == tqk.EINVAL  # epochs start at 1
+    assert tqk.tqk_exchange_merge(64, 128, 2, 0, boxes, 1, None, None) == tqk.EINVAL
+    assert tqk.tqk_exchange_merge(64, 128, 2, 2, boxes, 1, 1, None) == tqk.EINVAL  # rank outside the world
+    assert tqk.tqk_exchange_merge(64, 128, 2, 0, boxes, 0, 1, None) == tqk.EINVAL  # epochs start at 1
 
 
 def test_error_codes_without_device():

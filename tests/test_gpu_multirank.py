@@ -85,10 +85,9 @@ def _rank_main_p2p(rank, world, port, n, steps, result_dir):
         s, ln = shard.seq_range(n, rank, world)
         kl, vl = kp[:, s:s + ln].contiguous(), vp[:, s:s + ln].contiguous()
         ex = shard.PeerExchange(dist, tqk, nq, hd)
-        partial = torch.empty(nq * (hd + 2), device="cuda")
         outs = torch.empty(steps, nq * hd, device="cuda")
         for i in range(steps):
-            shard.seqsplit_attend_p2p(ex, tqk, kl, vl, nq, nkv, hd, ln, qs[i], outs[i], partial)
+            shard.seqsplit_attend_p2p(ex, tqk, kl, vl, nq, nkv, hd, ln, qs[i], outs[i])
         refs = torch.empty(steps, nq * hd, device="cuda")
         for i in range(steps):
             tqk.attend(kp, vp, nq, nkv, hd, n, n - 1, qs[i], refs[i])
@@ -132,16 +131,16 @@ def test_exchange_merge_single_rank(cuda):
     try:
         for epoch in (1, 2, 3):
             q = torch.randn(nq * hd, device="cuda", generator=g)
-            partial = torch.empty(nq * (hd + 2), device="cuda")
-            tqk.decode(tqk.decode_args(kp, vp, nq, nkv, hd, n, q, partial, len0=n, out_mode=tqk.OUT_PARTIAL))
+            slot = tqk.exchange_slot(box, nq, hd, epoch)
+            tqk.decode(tqk.decode_args(kp, vp, nq, nkv, hd, n, q, slot, len0=n, out_mode=tqk.OUT_PARTIAL))
             got = torch.full((nq * hd,), float("nan"), device="cuda")
-            tqk.exchange_merge(partial, nq, hd, 1, 0, [box], epoch, got)
+            tqk.exchange_merge(nq, hd, 1, 0, [box], epoch, got)
             ref = torch.empty(nq * hd, device="cuda")
-            tqk.merge_partials(partial, 1, nq * (hd + 2), nq, hd, ref)
+            tqk.merge_partials(slot, 1, nq * (hd + 2), nq, hd, ref)
             torch.cuda.synchronize()
             assert torch.equal(got, ref), epoch
         with pytest.raises(tqk.TQKError):
-            tqk.exchange_merge(partial, nq, hd, 1, 0, [box + 4], 4, got)
+            tqk.exchange_merge(nq, hd, 1, 0, [box + 4], 4, got)
         assert tqk.device_status() == 0
     finally:
         tqk.peer_buffer_free(box)
