@@ -76,7 +76,6 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParam
     const int h = blockIdx.x, tid = threadIdx.x;
     const int rec = p.head_dim + 2, par = p.epoch & 1;
     __shared__ int s_ok;
-    __shared__ float s_m, s_l;
 
     // launched with programmatic stream serialization: the records come from the decode grid before
     grid_dependency_wait();
@@ -107,33 +106,35 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParam
     if (!s_ok) return;
 
     // ---- merge head h: out = sum_r acc_r e^(m_r - M) / sum_r l_r e^(m_r - M), M = max_r m_r
-    //      (tqk_merge_partials' arithmetic); peers' records are read over NVLink
+    //      (tqk_merge_partials' arithmetic).  Every thread issues all its loads of the ranks'
+    //      records (m, l and its column of acc) together, so the peers' records cost one
+    //      NVLink round trip, and derives M and L itself.
     auto rec_of = [&](int r) -> const float * { return p.mbox[r] + (long long)par * p.slot + (long long)h * rec; };
-    if (tid < 32) {
-        float M = -INFINITY, l = 0.0f;
-        if (tid < p.world) {
-            M = ld_relaxed_sys(rec_of(tid) + p.head_dim);
-            l = ld_relaxed_sys(rec_of(tid) + p.head_dim + 1);
-        }
-        const float m_own = M;
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = (tid < p.world && l > 0.0f) ? l * expf(m_own - M) : 0.0f;
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        if (tid == 0) {
-            s_m = M;
-            s_l = L;
-        }
-    }
-    __syncthreads();
-    const float M = s_m, L = s_l;
-    for (int c = tid; c < p.head_dim; c += blockDim.x) {
-        float a = 0.0f;
-        for (int r = 0; r < p.world; r++) {
+    float mr[EX_MAX_WORLD], lr[EX_MAX_WORLD], ar[EX_MAX_WORLD];
+    const int c = tid;  // head_dim <= 128 = blockDim.x (checked on the host)
+#pragma unroll
+    for (int r = 0; r < EX_MAX_WORLD; r++) {
+        if (r < p.world) {
             const float *rp = rec_of(r);
-            if (ld_relaxed_sys(rp + p.head_dim + 1) > 0.0f) a = fmaf(expf(ld_relaxed_sys(rp + p.head_dim) - M), ld_relaxed_sys(rp + c), a);
+            mr[r] = ld_relaxed_sys(rp + p.head_dim);
+            lr[r] = ld_relaxed_sys(rp + p.head_dim + 1);
+            ar[r] = c < p.head_dim ? ld_relaxed_sys(rp + c) : 0.0f;
         }
-        p.out[(long long)h * p.head_dim + c] = L > 0.0f ? a / L : 0.0f;
     }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < EX_MAX_WORLD; r++)
+        if (r < p.world) M = fmaxf(M, mr[r]);
+    float L = 0.0f, a = 0.0f;
+#pragma unroll
+    for (int r = 0; r < EX_MAX_WORLD; r++) {
+        if (r < p.world && lr[r] > 0.0f) {
+            const float e = expf(mr[r] - M);
+            L += lr[r] * e;
+            a = fmaf(e, ar[r], a);
+        }
+    }
+    if (c < p.head_dim) p.out[(long long)h * p.head_dim + c] = L > 0.0f ? a / L : 0.0f;
 }
 
 }  // namespace
@@ -203,8 +204,8 @@ extern "C" int tqk_ipc_close_handle(void *ptr) {
 
 extern "C" int tqk_exchange_merge(int n_heads, int head_dim, int world, int rank, void *const *mailboxes, int epoch,
                                   float *out, tqk_stream_t stream) {
-    if (!out || !mailboxes || n_heads <= 0 || head_dim <= 0 || world < 1 || world > EX_MAX_WORLD || rank < 0 ||
-        rank >= world || epoch < 1)
+    if (!out || !mailboxes || n_heads <= 0 || head_dim <= 0 || head_dim > 128 || world < 1 || world > EX_MAX_WORLD ||
+        rank < 0 || rank >= world || epoch < 1)
         return fail(TQK_EINVAL, "tqk_exchange_merge: bad arguments");
     int rc = ensure_device();
     if (rc) return rc;
