@@ -290,6 +290,9 @@ class Config4:
         self.launches_per_step = 1 if world == 1 else 2  # decode (+ exchange-merge, or merge after NCCL)
         self.exchange = exchange
         self.peer = shard.PeerExchange(dist, tqk, n_q, hd) if world > 1 and exchange == "p2p" else None
+        self.e2e_api = ("tqk_decode_q8 (C ABI, log-sum-exp partials of this rank's range) + tqk_exchange_merge "
+                        if self.peer is not None else "tqk_decode_q8 (C ABI) ") + \
+            "with pinned host q in and the attention output out, stream-synchronised every step"
         self.h_q = self.q.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
         self.h2d = self.h_q.numel() * 4
