@@ -144,3 +144,37 @@ def test_exchange_merge_single_rank(cuda):
         assert tqk.device_status() == 0
     finally:
         tqk.peer_buffer_free(box)
+
+
+def test_exchange_wait_times_out_without_peer(cuda):
+    """Failure detection without a fault: a two-rank exchange whose peer never
+    raises its flag (the "peer" mailbox is a second local buffer nobody writes).
+    The kernel's bounded wait gives up after about a second, records the timeout
+    in the device error word, leaves the output unwritten and returns; the
+    context stays usable and the next exchange succeeds."""
+    import time
+
+    import torch
+    from tailorquantkernel_b200 import tqk
+    nq, hd = 64, 128
+    nbytes = tqk.tqk_exchange_mailbox_bytes(2, nq, hd)
+    boxes = [tqk.peer_buffer_alloc(nbytes), tqk.peer_buffer_alloc(nbytes)]
+    solo = tqk.peer_buffer_alloc(tqk.tqk_exchange_mailbox_bytes(1, nq, hd))
+    try:
+        assert tqk.device_status(clear=True) == 0
+        out = torch.full((nq * hd,), float("nan"), device="cuda")
+        t0 = time.time()
+        tqk.exchange_merge(nq, hd, 2, 0, boxes, 1, out)
+        torch.cuda.synchronize()
+        waited = time.time() - t0
+        assert 0.5 < waited < 30, waited
+        assert tqk.device_status(clear=True) == 1  # the timeout code of the device error word
+        assert torch.isnan(out).all()  # nothing merged
+        # recovery: a one-rank exchange over a zeroed mailbox (l = 0 everywhere) writes zeros
+        tqk.exchange_merge(nq, hd, 1, 0, [solo], 1, out)
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(out).item() == 0
+        assert tqk.device_status() == 0
+    finally:
+        for b in boxes + [solo]:
+            tqk.peer_buffer_free(b)
