@@ -19,9 +19,11 @@
 //         TMEM) and four kind::f16 MMAs (M=128, N=128, K=16) of P against
 //         V_hi and V_lo accumulating O in TMEM.  Its shared-memory
 //         descriptors are built once; each MMA adds a constant offset;
-//       - four softmax warps per Q tile, one thread per query row, copy the
-//         row's block dots out of TMEM and release S at once, so the MMA warp
-//         computes the next step's S while they work.  They combine the dots
+//       - eight softmax warps per Q tile, two threads per query row (each
+//         takes 16 keys of a step and 64 columns of O; the pair shares its
+//         row maximum through shared memory), copy the row's block dots out
+//         of TMEM and release S at once, so the MMA warp computes the next
+//         step's S while they work.  They combine the dots
 //         with the Q8 scales as
 //         score = sum_b (float)dot_b * (qd_b*kd_b) * scale (model/attn_q8.c:24-31)
 //         with packed fp32 fused multiply-adds (scale and log2(e) folded into
@@ -51,7 +53,10 @@ constexpr int PF_HD = 128;
 constexpr int PF_NB = PF_HD / QK;            // 4 Q8 blocks per row
 constexpr int PF_ROW = PF_NB * BLOCK_BYTES;  // 144-byte cache row
 constexpr int PF_STAGES = 4;
-constexpr int PF_SM_WARPS = 4 * PF_QT;         // softmax warps (one thread per query row)
+constexpr int PF_TPR = 2;                      // softmax threads per query row
+constexpr int PF_KH = PF_KT / PF_TPR;          // keys of a step per thread
+constexpr int PF_OH = PF_HD / PF_TPR;          // O columns per thread
+constexpr int PF_SM_WARPS = 4 * PF_TPR * PF_QT;  // softmax warps
 constexpr int PF_TMA_WARP = PF_SM_WARPS;
 constexpr int PF_MMA_WARP = PF_SM_WARPS + 1;
 constexpr int PF_THREADS = 32 * (PF_SM_WARPS + 2);
@@ -76,7 +81,10 @@ constexpr int OFF_QC = OFF_RING + PF_STAGES * ST_BYTES;       // int8 Q: [tile][
 constexpr int QC_TILE = PF_NB * PF_M * 32;                    // 16 KB
 constexpr int OFF_PC = OFF_QC + PF_QT * QC_TILE;              // fp16 P: [tile][buf][128 rows x 32 keys], K-major
 constexpr int PC_BUF = PF_M * PF_KT * 2;                      // 8 KB
-constexpr int OFF_BAR = OFF_PC + PF_QT * 2 * PC_BUF;
+constexpr int OFF_QD = OFF_PC + PF_QT * 2 * PC_BUF;           // float qd [tile][row][block]
+constexpr int OFF_MX = OFF_QD + PF_QT * PF_M * PF_NB * 4;     // float [step parity][tile][half][row]: row maxima
+constexpr int OFF_SL = OFF_MX + 2 * PF_QT * PF_TPR * PF_M * 4;  // float [tile][half][row]: row sums
+constexpr int OFF_BAR = OFF_SL + PF_QT * PF_TPR * PF_M * 4;
 // full[4] empty[4] s_full[tile] s_free[tile] p_full[tile][buf] pv_done[tile] o_done.  P has a barrier
 // per buffer: the softmax can finish step j+1 before the MMA warp looks at step j, and two completed
 // phases on one barrier would be indistinguishable to a parity wait.
@@ -221,9 +229,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         }
         for (int t = 0; t < PF_QT; t++) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&s_free[t], 4);  // one arrival per softmax warp of the tile
-            mbar_init(&p_full[2 * t], 4);
-            mbar_init(&p_full[2 * t + 1], 4);
+            mbar_init(&s_free[t], 4 * PF_TPR);  // one arrival per softmax warp of the tile
+            mbar_init(&p_full[2 * t], 4 * PF_TPR);
+            mbar_init(&p_full[2 * t + 1], 4 * PF_TPR);
             mbar_init(&pv_done[t], 1);
         }
         mbar_init(o_done, 1);
@@ -231,13 +239,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
     }
     if (warp == 0) tmem_alloc(tmem_slot, PF_TMEM_COLS);
 
-    // softmax thread (qt, r): row r of Q tile qt
-    const int qt = warp >> 2, r = tid & (PF_M - 1);
+    // softmax thread (qt, hf, r): row r of Q tile qt, half hf of every step's keys and of O's columns
+    const int qt = warp / (4 * PF_TPR), hf = (warp >> 2) % PF_TPR, r = (warp & 3) * 32 + lane;
     const int tq0 = tok0 + qt * T;
     const int token = tq0 + r / G;
     const bool valid_row = warp < PF_SM_WARPS && token <= tok_last;
     const int head = kvh * G + r % G;
-    pf2 qd2[PF_NB];  // qd * scale * log2(e): scores come out in log2 units
+    float *const sqd = reinterpret_cast<float *>(smem + OFF_QD);
     if (warp < PF_SM_WARPS) {
         // quantise the row's q (quant_x.c:12-34) into the int8 A operand; rows past the chunk get
         // zeros (their scores are 0 and they are never written)
@@ -245,7 +253,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             p.q + ((long long)(valid_row ? token : tok0) * (p.n_kv * G) + head) * PF_HD);
         const float qs = __fmul_rn(p.scale, 1.4426950408889634f);
 #pragma unroll
-        for (int b = 0; b < PF_NB; b++) {
+        for (int bb = 0; bb < PF_NB / PF_TPR; bb++) {
+            const int b = hf * (PF_NB / PF_TPR) + bb;  // this thread's share of the row's blocks
             float x[QK];
 #pragma unroll
             for (int i = 0; i < QK / 4; i++) {
@@ -266,8 +275,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
 #pragma unroll
                 for (int i = 0; i < 8; i++) w[i] = 0u;
             }
-            const float dq = valid_row ? d * qs : 0.0f;
-            qd2[b] = pk(dq, dq);
+            sqd[(qt * PF_M + r) * PF_NB + b] = valid_row ? d * qs : 0.0f;
             uint8_t *dst = qc + qt * QC_TILE + b * PF_M * 32;
             *reinterpret_cast<uint4 *>(dst + qk_off(r, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
             *reinterpret_cast<uint4 *>(dst + qk_off(r, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
@@ -363,70 +371,78 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
         }
         __syncwarp();
     } else {
-        // ---- softmax: thread r of tile qt owns TMEM lane r of S_qt and O_qt
+        // ---- softmax: threads (hf = 0, 1) of row r of tile qt share TMEM lane r of S_qt and O_qt
         const int limit = p.pos0 + token;  // last key the row may see (causal)
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-        const uint32_t t_s = tmem + lane_base + qt * S_COLS;
-        const uint32_t t_o = tmem + lane_base + TM_O + qt * PF_HD;
-        float m = -INFINITY, l = 0.0f;  // running max (log2 units) and sum
+        const uint32_t t_s = tmem + lane_base + qt * S_COLS + hf * PF_KH;
+        const uint32_t t_o = tmem + lane_base + TM_O + qt * PF_HD + hf * PF_OH;
+        const int pair_bar = 1 + qt * 4 + (warp & 3);  // named barrier of the row's two warps
+        float *const smx = reinterpret_cast<float *>(smem + OFF_MX);
+        float *const ssl = reinterpret_cast<float *>(smem + OFF_SL);
+        pf2 qd2[PF_NB];  // qd * scale * log2(e): scores come out in log2 units
+#pragma unroll
+        for (int b = 0; b < PF_NB; b++) {
+            const float dq = sqd[(qt * PF_M + r) * PF_NB + b];
+            qd2[b] = pk(dq, dq);
+        }
+        float m = -INFINITY, l = 0.0f;  // running max (log2 units, the same in both threads) and partial sum
 
         for (int j = 0; j < n_tiles; j++) {
             if (!mbar_wait_bounded(&s_full[qt], (uint32_t)(j & 1), bad ? PF_DRAIN_NS : PF_WAIT_NS, p.err)) bad = true;
             tc_fence_after();
-            const float *kd = reinterpret_cast<const float *>(smem + OFF_RING + (j % PF_STAGES) * ST_BYTES + ST_KD);
+            const float *kd = reinterpret_cast<const float *>(smem + OFF_RING + (j % PF_STAGES) * ST_BYTES + ST_KD) +
+                              hf * PF_KH;
+            const int key0 = j * PF_KT + hf * PF_KH;  // this thread's first key of the step
             const bool diag = j * PF_KT + PF_KT - 1 > p.pos0 + tq0;  // the step reaches past some row's last key
 
-            // scores of the row's 32 keys (the reference's per-block combine), log2 units; S is
-            // released to the MMA warp as soon as its second half is in registers
-            float s[PF_KT];
+            // this thread's 16 scores (the reference's per-block combine), log2 units; S is released
+            // to the MMA warp as soon as it is in registers
+            uint32_t dv[PF_NB][16];
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                uint32_t dv[PF_NB][16];
+            for (int b = 0; b < PF_NB; b++) tmem_ld16(t_s + b * PF_KT, dv[b]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_release(&s_free[qt]);
+            float s[PF_KH];
 #pragma unroll
-                for (int b = 0; b < PF_NB; b++) tmem_ld16(t_s + b * PF_KT + h * 16, dv[b]);
-                tmem_wait_ld();
-                if (h == 1) {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_release(&s_free[qt]);
-                }
+            for (int i2 = 0; i2 < PF_KH / 2; i2++) {
+                pf2 acc = mul2p(pk(__int2float_rn((int)dv[0][2 * i2]), __int2float_rn((int)dv[0][2 * i2 + 1])),
+                                mul2p(qd2[0], *reinterpret_cast<const pf2 *>(kd + 2 * i2)));
 #pragma unroll
-                for (int i2 = 0; i2 < 8; i2++) {
-                    const int kk = h * 16 + 2 * i2;
-                    pf2 acc = mul2p(pk(__int2float_rn((int)dv[0][2 * i2]), __int2float_rn((int)dv[0][2 * i2 + 1])),
-                                    mul2p(qd2[0], *reinterpret_cast<const pf2 *>(kd + kk)));
-#pragma unroll
-                    for (int b = 1; b < PF_NB; b++)
-                        acc = fma2p(pk(__int2float_rn((int)dv[b][2 * i2]), __int2float_rn((int)dv[b][2 * i2 + 1])),
-                                    mul2p(qd2[b], *reinterpret_cast<const pf2 *>(kd + b * PF_KT + kk)), acc);
-                    upk(acc, s[kk], s[kk + 1]);
-                }
+                for (int b = 1; b < PF_NB; b++)
+                    acc = fma2p(pk(__int2float_rn((int)dv[b][2 * i2]), __int2float_rn((int)dv[b][2 * i2 + 1])),
+                                mul2p(qd2[b], *reinterpret_cast<const pf2 *>(kd + b * PF_KT + 2 * i2)), acc);
+                upk(acc, s[2 * i2], s[2 * i2 + 1]);
             }
             if (diag) {
 #pragma unroll
-                for (int kk = 0; kk < PF_KT; kk++)
-                    if (j * PF_KT + kk > limit) s[kk] = -INFINITY;
+                for (int kk = 0; kk < PF_KH; kk++)
+                    if (key0 + kk > limit) s[kk] = -INFINITY;
             }
-            // tree maximum of the 32 scores
-            float mx[PF_KT / 2];
+            // tree maximum of the 16 scores, then the row's maximum with the partner thread's
+            float mx[PF_KH / 2];
 #pragma unroll
-            for (int kk = 0; kk < PF_KT / 2; kk++) mx[kk] = fmaxf(s[2 * kk], s[2 * kk + 1]);
+            for (int kk = 0; kk < PF_KH / 2; kk++) mx[kk] = fmaxf(s[2 * kk], s[2 * kk + 1]);
 #pragma unroll
-            for (int w2 = PF_KT / 4; w2 >= 1; w2 >>= 1)
+            for (int w2 = PF_KH / 4; w2 >= 1; w2 >>= 1)
 #pragma unroll
                 for (int kk = 0; kk < w2; kk++) mx[kk] = fmaxf(mx[kk], mx[kk + w2]);
-            const float mt = mx[0];
+            float *mxs = smx + ((j & 1) * PF_QT + qt) * PF_TPR * PF_M;  // by step parity: no overwrite before read
+            mxs[hf * PF_M + r] = mx[0];
+            asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "n"(64) : "memory");
+            const float mt = fmaxf(mx[0], mxs[(1 - hf) * PF_M + r]);
             // raise the running max lazily: only when it grows by more than 8 (P stays <= 2^8)
             const bool raise = mt > m + 8.0f;
             const float m_new = raise ? mt : m;
             const float factor = raise ? ex2f(m - m_new) : 1.0f;
             if (j > 0 && __any_sync(0xffffffffu, raise && factor != 1.0f)) {
-                // PV_qt(j-1) may still run: wait for it before rescaling O
+                // PV_qt(j-1) may still run: wait for it before rescaling this thread's half of O
                 if (!mbar_wait_bounded(&pv_done[qt], (uint32_t)((j - 1) & 1), bad ? PF_DRAIN_NS : PF_WAIT_NS, p.err))
                     bad = true;
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < PF_HD / 16; c++) {
+                for (int c = 0; c < PF_OH / 16; c++) {
                     uint32_t ov[16];
                     tmem_ld16(t_o + c * 16, ov);
                     tmem_wait_ld();
@@ -439,10 +455,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             l *= factor;
             m = m_new;
             const pf2 neg_m = pk(-m, -m), one2 = pk(1.0f, 1.0f);
-            uint32_t ph[PF_KT / 2];
+            uint32_t ph[PF_KH / 2];
             pf2 sum2 = pk(0.0f, 0.0f);
 #pragma unroll
-            for (int i2 = 0; i2 < PF_KT / 2; i2++) {
+            for (int i2 = 0; i2 < PF_KH / 2; i2++) {
                 float a, c;
                 upk(fma2p(pk(s[2 * i2], s[2 * i2 + 1]), one2, neg_m), a, c);
                 const pf2 e2 = pk(ex2f(a), ex2f(c));
@@ -456,8 +472,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             l += sa + sb;
             uint8_t *pb = pc + (2 * qt + (j & 1)) * PC_BUF;
 #pragma unroll
-            for (int kc = 0; kc < 4; kc++)
-                *reinterpret_cast<uint4 *>(pb + p_off(r, kc)) =
+            for (int kc = 0; kc < PF_KH / 8; kc++)
+                *reinterpret_cast<uint4 *>(pb + p_off(r, hf * (PF_KH / 8) + kc)) =
                     make_uint4(ph[4 * kc], ph[4 * kc + 1], ph[4 * kc + 2], ph[4 * kc + 3]);
             fence_proxy_async();  // P -> the tensor core
             tc_fence_before();    // the O rescale is done
@@ -465,13 +481,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             if (lane == 0) mbar_arrive_release(&p_full[2 * qt + (j & 1)]);
         }
 
-        // ---- epilogue: O / l
+        // ---- epilogue: O / (the two threads' partial sums)
+        ssl[(qt * PF_TPR + hf) * PF_M + r] = l;
         if (!mbar_wait_bounded(o_done, 0u, bad ? PF_DRAIN_NS : PF_WAIT_NS, p.err)) bad = true;
         tc_fence_after();
-        const float inv_l = 1.0f / l;
-        float *dst = p.out + ((long long)token * (p.n_kv * G) + head) * PF_HD;
+        asm volatile("bar.sync %0, %1;" ::"r"(pair_bar), "n"(64) : "memory");
+        const float inv_l = 1.0f / (ssl[(qt * PF_TPR) * PF_M + r] + ssl[(qt * PF_TPR + 1) * PF_M + r]);
+        float *dst = p.out + ((long long)token * (p.n_kv * G) + head) * PF_HD + hf * PF_OH;
 #pragma unroll
-        for (int c = 0; c < PF_HD / 16; c++) {
+        for (int c = 0; c < PF_OH / 16; c++) {
             uint32_t ov[16];
             tmem_ld16(t_o + c * 16, ov);
             tmem_wait_ld();
