@@ -308,6 +308,12 @@ TQK_API int tqk_append_attend_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, i
  * Chunked causal prefill (attention_layer_batch's append+attend loop, reference
  * model/attention_layer.c:221-236): appends n tokens at pos0..pos0+n-1, then
  * token i attends over positions <= pos0+i.  q/out [n][n_q][hd], k/v [n][n_kv][hd].
+ * For head_dim 128 and 1, 2, 4 or 8 q heads per kv head the attention runs on
+ * the tensor cores after the cache rows 0 .. pos0+n-1 are staged as MMA
+ * operands in a library-owned buffer per (device, stream), allocated on the
+ * first call and grown when a call needs more: n_kv * ceil((pos0+n)/32) *
+ * 20992 bytes (21.5 MB for 8 kv heads and 4096 positions).  Other shapes use
+ * the decode kernel, one item per new token.
  */
 TQK_API int tqk_prefill_q8(tqk_block_q8 *k_plane, tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
                    int head_dim, int max_tokens, int pos0, int n, const float *q, const float *k,
