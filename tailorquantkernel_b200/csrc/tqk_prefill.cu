@@ -156,6 +156,8 @@ __device__ __forceinline__ pf2 add2p(pf2 a, pf2 b) {
 __global__ void __launch_bounds__(256) stage_kv_tiles_kernel(const uint8_t *k, const uint8_t *v, int max_tokens,
                                                              int n_keys, long long tiles, uint8_t *stage) {
     const int j = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+    // the attention kernel may start its prologue now; it reads the images only after this grid ends
+    grid_dependents_launch();
     const long long head = (long long)h * max_tokens * PF_ROW;
     uint8_t *dst = stage + ((long long)h * tiles + j) * ST_BYTES;
     const int key0 = j * PF_KT;
@@ -291,6 +293,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
     if (warp == PF_TMA_WARP) {
         // ---- producer: staged tile images into the ring
         if (lane == 0) {
+            // launched with programmatic stream serialization behind the staging kernel: the
+            // images are complete once it has finished (q, read in the prologue, was complete
+            // before the staging kernel started)
+            grid_dependency_wait();
             const uint8_t *src = p.stage + (long long)kvh * p.tiles * ST_BYTES;
             int issued = 0;
             for (int j = 0; j < n_tiles; j++) {
@@ -527,8 +533,7 @@ int launch_prefill(const PrefillParams &p, cudaStream_t stream) {
     }
     constexpr int T = PF_M / G;
     const dim3 grid((unsigned)p.n_kv, (unsigned)((p.n + PF_QT * T - 1) / (PF_QT * T)));
-    prefill_q8_tc_kernel<G><<<grid, PF_THREADS, PF_SMEM, stream>>>(p);
-    return check_launch("prefill_q8_tc_kernel");
+    return launch_pdl(prefill_q8_tc_kernel<G>, grid, dim3(PF_THREADS), PF_SMEM, stream, p);
 }
 
 }  // namespace

@@ -49,19 +49,21 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float *__restr
 }
 
 // Append n tokens at pos0..pos0+n-1.  Block index decomposition (fastest first):
-// b (block within the row), h (kv head), kv (0 = K, 1 = V), i (token).
+// b (block within the row), h (kv head), kv (0 = K, 1 = V), i (token).  Idx is
+// the index type: 32-bit whenever the block count fits, so the decomposition
+// needs no 64-bit divisions.
+template <typename Idx>
 __global__ void __launch_bounds__(256) store_kv_kernel(const float *__restrict__ k, const float *__restrict__ v,
                                                        uint8_t *__restrict__ kp, uint8_t *__restrict__ vp, int n_kv,
-                                                       int nb, int max_tokens, int pos0, long long n_blocks) {
-    const long long gt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long blk = gt >> 3;
+                                                       int nb, int max_tokens, int pos0, Idx n_blocks) {
+    const Idx blk = (Idx)(((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3);
     if (blk >= n_blocks) return;
-    const int b = (int)(blk % nb);
-    long long r = blk / nb;
-    const int h = (int)(r % n_kv);
-    r /= n_kv;
+    const int b = (int)(blk % (Idx)nb);
+    Idx r = blk / (Idx)nb;
+    const int h = (int)(r % (Idx)n_kv);
+    r /= (Idx)n_kv;
     const int kv = (int)(r & 1);
-    const long long i = r >> 1;
+    const long long i = (long long)(r >> 1);
     const int hd = nb * QK;
     const float *src = (kv ? v : k) + (i * n_kv + h) * (long long)hd + b * QK;
     uint8_t *plane = kv ? vp : kp;
@@ -99,9 +101,14 @@ extern "C" int tqk_store_kv_q8_batch(tqk_block_q8 *k_plane, tqk_block_q8 *v_plan
     const int nb = head_dim / QK;
     const long long n_blocks = (long long)n * 2 * n_kv_heads * nb;
     const unsigned grid = (unsigned)((n_blocks * 8 + 255) / 256);
-    store_kv_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(k, v, reinterpret_cast<uint8_t *>(k_plane),
-                                                            reinterpret_cast<uint8_t *>(v_plane), n_kv_heads, nb,
-                                                            max_tokens, pos0, n_blocks);
+    if (n_blocks * 8 <= 0x7fffffffLL)
+        store_kv_kernel<unsigned><<<grid, 256, 0, (cudaStream_t)stream>>>(
+            k, v, reinterpret_cast<uint8_t *>(k_plane), reinterpret_cast<uint8_t *>(v_plane), n_kv_heads, nb,
+            max_tokens, pos0, (unsigned)n_blocks);
+    else
+        store_kv_kernel<long long><<<grid, 256, 0, (cudaStream_t)stream>>>(
+            k, v, reinterpret_cast<uint8_t *>(k_plane), reinterpret_cast<uint8_t *>(v_plane), n_kv_heads, nb,
+            max_tokens, pos0, n_blocks);
     return check_launch("store_kv_kernel");
 }
 
