@@ -199,9 +199,16 @@ class Config2:
                        rope_cos=self.rope_cos, rope_sin=self.rope_sin, rope_item_stride=hd // 2)
         else:
             q = rope_np(q, hd, pos, 500000.0)
-        self.q = torch.from_numpy(q).cuda()
-        self.k_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
-        self.v_new = torch.randn(layers, n_kv * hd, device="cuda", generator=g)
+        # q, k_new and v_new are views of one device buffer, so the end-to-end leg moves a step's
+        # inputs with a single host-to-device copy
+        nq_f, nkv_f = layers * n_q * hd, layers * n_kv * hd
+        self.inbuf = torch.empty(nq_f + 2 * nkv_f, device="cuda")
+        self.q = self.inbuf[:nq_f].view(layers, n_q * hd)
+        self.q.copy_(torch.from_numpy(q).reshape(layers, n_q * hd))
+        self.k_new = self.inbuf[nq_f:nq_f + nkv_f].view(layers, n_kv * hd)
+        self.v_new = self.inbuf[nq_f + nkv_f:].view(layers, n_kv * hd)
+        self.k_new.copy_(torch.randn(layers, n_kv * hd, device="cuda", generator=g))
+        self.v_new.copy_(torch.randn(layers, n_kv * hd, device="cuda", generator=g))
         self.out = torch.empty(layers, n_q * hd, device="cuda")
         self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
                                     item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
@@ -214,11 +221,9 @@ class Config2:
         self.tokens_per_step = 1
         self.launches_per_step = 1
         # pinned host buffers of the end-to-end leg
-        self.h_q = self.q.cpu().pin_memory()
-        self.h_k = self.k_new.cpu().pin_memory()
-        self.h_v = self.v_new.cpu().pin_memory()
+        self.h_in = self.inbuf.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
-        self.h2d = self.h_q.numel() * 4 + self.h_k.numel() * 4 + self.h_v.numel() * 4
+        self.h2d = self.h_in.numel() * 4
         self.d2h = self.h_out.numel() * 4
 
     def step(self):
@@ -227,9 +232,7 @@ class Config2:
     def step_e2e(self):
         import torch
         s = torch.cuda.current_stream()
-        self.q.copy_(self.h_q, non_blocking=True)
-        self.k_new.copy_(self.h_k, non_blocking=True)
-        self.v_new.copy_(self.h_v, non_blocking=True)
+        self.inbuf.copy_(self.h_in, non_blocking=True)  # q, k_new and v_new of the step
         self.tqk.decode(self.args)
         self.h_out.copy_(self.out, non_blocking=True)
         s.synchronize()
