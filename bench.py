@@ -11,10 +11,13 @@ One step = one token: for every layer the fused kernel appends the new K/V row
 tqk_decode_q8.  K/V per step is 302 MB, larger than the 126 MB L2, so no flush
 is needed between steps.
 
-For N > 1 (torchrun, one process per GPU) every rank decodes its own sequence
-(batch sharding, no collective): weak scaling, value = all ranks' tokens / the
-slowest rank's time.  The timed region is about 2 s by default so that the
-clock sampler sees it several times.
+For N > 1 (torchrun, one process per GPU) the same token is divided by kv-head
+group: rank r attends to kv heads [r*8/N, (r+1)*8/N) of every layer (with
+their q heads) and tqk_exchange_gather assembles the whole output on every rank
+over peer memory: strong scaling, value = tokens / the slowest rank's time.
+Each rank then rotates over N copies of its cache slice, so that its working
+set stays 302 MB (larger than L2).  The timed region is about 2 s by default so
+that the clock sampler sees it several times.
 
 Rank 0 prints one JSON line.  --impl reference times the reference's own CPU
 code for the same workload (oracle/_ref/libtqref_avx2.so: the reference's AVX2
@@ -165,26 +168,57 @@ def barrier(dist):
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
-class Config2:
-    """Llama-3-8B-shaped decode: L layers of one sequence, fused append + attention."""
-    name = "config2"
-    scaling = "weak"  # every rank decodes its own sequence
+def describe_config2(layers, n_q, n_kv, hd, pos, prologue=False):
+    """config entry of config 2 (shared by our arm and the reference arm)."""
+    row = hd // QK * BB
+    kv_bytes = 2 * layers * n_kv * (pos + 1) * row
+    pro = (", q/k RMSNorm + RoPE(500000) fused into the launch (Qwen3-style prologue)" if prologue
+           else ", RoPE(500000) q")
+    return {"workload": f"config2: Llama-3-8B-shaped Q8 GQA decode, all {layers} layers, {n_q} q / {n_kv} kv heads, "
+                        f"head_dim {hd}, context {pos} + 1 appended token (n={pos + 1})" + pro,
+            "layers": layers, "seq_len": pos + 1, "kv_bytes_per_token": kv_bytes,
+            "l2": f"no flush: inputs larger than L2 ({kv_bytes / 1e6:.0f} MB of K/V per step vs 126 MB L2)"
+                  if kv_bytes > 126e6 else f"{kv_bytes / 1e6:.1f} MB of K/V per step (smaller than L2)"}
 
-    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096, prologue=False):
+
+class Config2:
+    """Llama-3-8B-shaped decode: L layers of one sequence, fused append + attention.
+
+    One GPU: one tqk_decode_q8 launch over all layers (32 items of 8 kv heads).
+    N GPUs: the kv-head-group split.  Rank r holds kv heads head_range(8, r, N)
+    of every layer (its slice of each layer's cache, with their q heads): its
+    own launch over those heads, then tqk_exchange_gather, which gives every
+    rank the whole output [layers][32 q heads][head_dim] over peer memory.
+    The rank's slice is laid out [layers * per][max_tokens][nb], viewed as
+    items of two kv heads, so the packed two-heads-per-CTA kernel runs at
+    every N (at N = 8 an item is one kv head of two consecutive layers)."""
+    name = "config2"
+    scaling = "strong"  # one token of one sequence; N GPUs divide its kv heads
+
+    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, pos=4096, prologue=False, rank=0, world=1,
+                 dist=None):
         import torch
-        from tailorquantkernel_b200 import tqk
-        self.tqk = tqk
+        from tailorquantkernel_b200 import shard, tqk
+        self.tqk, self.world, self.rank = tqk, world, rank
         self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
         self.prologue = prologue
         self.mt = pos + 1
         self.nb = hd // QK
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        shape = (layers, n_kv, self.mt, hd)
+        group = n_q // n_kv
+        kvh0, per = shard.head_range(n_kv, rank, world)
+        if prologue and world > 1:
+            raise SystemExit("--prologue runs on one GPU only")
+        self.per = per
+        # on N GPUs each rank holds 1/N of the cache, less than L2 for N >= 4: it rotates over N
+        # copies of its slice, one per step, so that its working set stays the whole cache's size
+        self.copies = world
+        g = torch.Generator(device="cuda").manual_seed(seed + rank)
+        shape = (self.copies, layers, per, self.mt, hd)
         # setup (untimed): N(0,1) K/V quantised by the device quantiser into the cache
         self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         rng = np.random.default_rng(seed)
-        q = rng.standard_normal((layers, n_q * hd), dtype=np.float32)
+        q = rng.standard_normal((layers, n_q * hd), dtype=np.float32)  # the same q at every N
         pro = {}
         if prologue:
             # Qwen3-style layer: per-layer q/k RMSNorm weights and the RoPE table of position pos,
@@ -199,60 +233,107 @@ class Config2:
                        rope_cos=self.rope_cos, rope_sin=self.rope_sin, rope_item_stride=hd // 2)
         else:
             q = rope_np(q, hd, pos, 500000.0)
+        q = q.reshape(layers, n_q, hd)[:, kvh0 * group:(kvh0 + per) * group].reshape(layers, per * group * hd)
         # q, k_new and v_new are views of one device buffer, so the end-to-end leg moves a step's
         # inputs with a single host-to-device copy
-        nq_f, nkv_f = layers * n_q * hd, layers * n_kv * hd
+        lq, lkv = per * group * hd, per * hd
+        nq_f, nkv_f = layers * lq, layers * lkv
         self.inbuf = torch.empty(nq_f + 2 * nkv_f, device="cuda")
-        self.q = self.inbuf[:nq_f].view(layers, n_q * hd)
-        self.q.copy_(torch.from_numpy(q).reshape(layers, n_q * hd))
-        self.k_new = self.inbuf[nq_f:nq_f + nkv_f].view(layers, n_kv * hd)
-        self.v_new = self.inbuf[nq_f + nkv_f:].view(layers, n_kv * hd)
-        self.k_new.copy_(torch.randn(layers, n_kv * hd, device="cuda", generator=g))
-        self.v_new.copy_(torch.randn(layers, n_kv * hd, device="cuda", generator=g))
-        self.out = torch.empty(layers, n_q * hd, device="cuda")
-        self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
-                                    item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
-                                    q_item_stride=n_q * hd, out_item_stride=n_q * hd, k_new=self.k_new,
-                                    v_new=self.v_new, kv_new_item_stride=n_kv * hd, **pro)
-        # algorithmic bytes of one step: K/V rows read + the appended Q8 rows written
-        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * self.nb * BB
-        self.append_bytes = 2 * layers * n_kv * self.nb * BB
-        self.bytes_per_step = self.kv_bytes + self.append_bytes
+        self.q = self.inbuf[:nq_f].view(layers, lq)
+        self.q.copy_(torch.from_numpy(np.ascontiguousarray(q)))
+        self.k_new = self.inbuf[nq_f:nq_f + nkv_f].view(layers, lkv)
+        self.v_new = self.inbuf[nq_f + nkv_f:].view(layers, lkv)
+        self.k_new.copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.v_new.copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.out = torch.empty(layers, n_q * hd, device="cuda")  # the whole output, on every rank
+        if world == 1:
+            self.gather = None
+            self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
+                                        item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
+                                        q_item_stride=n_q * hd, out_item_stride=n_q * hd, k_new=self.k_new,
+                                        v_new=self.v_new, kv_new_item_stride=n_kv * hd, **pro)
+        else:
+            self.gather = shard.PeerGather(dist, tqk, layers, lq)
+            self.args_by = {}  # (copy, epoch parity) -> decode arguments
+            for c in range(self.copies):
+                for parity in (0, 1):
+                    slot = tqk.gather_slot(self.gather.local, layers, lq, 2 - parity)  # epoch 2 - parity
+                    self.args_by[c, parity] = shard.head_split_args(
+                        tqk, self.kp[c], self.vp[c], layers, n_q, n_kv, hd, self.mt, world, self.q, slot,
+                        len0=pos + 1, k_new=self.k_new, v_new=self.v_new)
+            self.kernel_count = 0
+        # algorithmic bytes of one step on this rank: K/V rows read + the appended Q8 rows written
+        self.kv_bytes = 2 * layers * n_kv * (pos + 1) * self.nb * BB   # the whole job
+        self.bytes_per_step = 2 * layers * per * (pos + 1) * self.nb * BB + 2 * layers * per * self.nb * BB
         self.tokens_per_step = 1
-        self.launches_per_step = 1
-        # pinned host buffers of the end-to-end leg
+        self.launches_per_step = 1 if world == 1 else 2  # decode (+ the gather)
+        # pinned host buffers of the end-to-end leg: every rank copies its inputs in, rank 0 the
+        # whole output out (the job's bytes are the sums over ranks)
         self.h_in = self.inbuf.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
-        self.h2d = self.h_in.numel() * 4
+        self.h2d = (nq_f + 2 * nkv_f) * 4 * world
         self.d2h = self.h_out.numel() * 4
+        self.e2e_api = ("tqk_decode_q8 (C ABI) with pinned host q, k and v in and the attention output out, "
+                        "stream-synchronised every step" if world == 1 else
+                        "per rank: its q/k/v slice in from pinned host memory, tqk_decode_q8 over its kv heads + "
+                        "tqk_exchange_gather; rank 0 copies the whole output out; stream-synchronised every step")
 
     def step(self):
-        self.tqk.decode(self.args)
+        if self.gather is None:
+            self.tqk.decode(self.args)
+            return
+        e = self.gather.epoch + 1
+        self.gather.begin()
+        self.tqk.decode(self.args_by[e % self.copies, e & 1])
+        self.gather.end(self.out)
+
+    def kernel_step(self):
+        """The decode launch of a step alone (its bytes are this rank's share), for the roofline."""
+        self.kernel_count += 1
+        self.tqk.decode(self.args_by[self.kernel_count % self.copies, self.kernel_count & 1])
 
     def step_e2e(self):
         import torch
         s = torch.cuda.current_stream()
         self.inbuf.copy_(self.h_in, non_blocking=True)  # q, k_new and v_new of the step
-        self.tqk.decode(self.args)
-        self.h_out.copy_(self.out, non_blocking=True)
+        self.step()
+        if self.rank == 0:
+            self.h_out.copy_(self.out, non_blocking=True)
         s.synchronize()
 
     def describe(self):
-        pro = (", q/k RMSNorm + RoPE(500000) fused into the launch (Qwen3-style prologue)" if self.prologue
-               else ", RoPE(500000) q")
-        return {"workload": "config2: Llama-3-8B-shaped Q8 GQA decode, all 32 layers, 32 q / 8 kv heads, "
-                            "head_dim 128, context 4096 + 1 appended token (n=4097)" + pro,
-                "layers": self.L, "seq_len": self.pos + 1, "kv_bytes_per_token": self.kv_bytes,
-                "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
+        return describe_config2(self.L, self.nq, self.nkv, self.hd, self.pos, self.prologue)
 
-    @staticmethod
-    def parallelism(world):
-        return "batch-sharded: one sequence per GPU, no collective" if world > 1 else "single GPU"
+    def per_rank(self):
+        return {"kv_heads_per_layer": self.per, "cache_copies_rotated": self.copies}
+
+    def parallelism(self, world):
+        if world == 1:
+            return "single GPU"
+        group = self.nq // self.nkv
+        return (f"kv-head-group split over {world} GPUs: {self.per} kv head(s) and their {self.per * group} q heads "
+                f"of every layer per GPU, outputs gathered over peer memory (tqk_exchange_gather)")
+
+    def close(self):
+        if self.gather is not None:
+            self.gather.close()
+            self.gather = None
 
     # the reference's CPU path on the same workload (host planes)
     def host_planes(self):
-        return self.kp.cpu().numpy(), self.vp.cpu().numpy(), self.q.cpu().numpy(), \
+        if self.world != 1:
+            raise RuntimeError("the CPU baseline runs at N = 1")
+        return self.kp[0].cpu().numpy(), self.vp[0].cpu().numpy(), self.q.cpu().numpy(), \
             self.k_new.cpu().numpy(), self.v_new.cpu().numpy()
+
+
+def describe_config4(n_q, n_kv, hd, n):
+    kv_bytes = 2 * n_kv * n * (hd // QK) * BB
+    return {"workload": f"config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, {n_q} q / {n_kv} kv "
+                        f"heads, head_dim {hd}, context {n}",
+            "layers": 1, "seq_len": n, "kv_bytes_per_token": kv_bytes,
+            "l2": f"no flush: inputs larger than L2 ({kv_bytes / 1e6:.0f} MB of K/V per step vs 126 MB L2)"
+                  if kv_bytes > 126e6 else f"{kv_bytes / 1e6:.1f} MB of K/V per step (smaller than L2)"}
 
 
 class Config4:
@@ -276,8 +357,12 @@ class Config4:
         self.mt, self.pos = n, n - 1
         self.nb = hd // QK
         self.start, self.n_local = shard.seq_range(n, rank, world)
+        # on N GPUs a rank's range is 1/N of the cache: it rotates over N copies of it, one per step, so
+        # that its working set stays the whole cache's size (larger than L2)
+        self.copies = world
+        self.count = 0
         g = torch.Generator(device="cuda").manual_seed(seed + rank)
-        shape = (n_kv, max(self.n_local, 1), hd)
+        shape = (self.copies, n_kv, max(self.n_local, 1), hd)
         self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
         gq = torch.Generator(device="cuda").manual_seed(seed)  # the same q on every rank
@@ -304,12 +389,23 @@ class Config4:
     def step(self):
         if self.world == 1:
             self.tqk.decode(self.args)
-        elif self.peer is not None:
-            self.shard.seqsplit_attend_p2p(self.peer, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
-                                           self.n_local, self.q, self.out)
+            return
+        self.count += 1
+        kp, vp = self.kp[self.count % self.copies], self.vp[self.count % self.copies]
+        if self.peer is not None:
+            self.shard.seqsplit_attend_p2p(self.peer, self.tqk, kp, vp, self.nq, self.nkv, self.hd, self.n_local,
+                                           self.q, self.out)
         else:
-            self.shard.seqsplit_attend(self.dist, self.tqk, self.kp, self.vp, self.nq, self.nkv, self.hd,
-                                       self.n_local, self.q, self.out, self.partial, gathered=self.gathered)
+            self.shard.seqsplit_attend(self.dist, self.tqk, kp, vp, self.nq, self.nkv, self.hd, self.n_local, self.q,
+                                       self.out, self.partial, gathered=self.gathered)
+
+    def kernel_step(self):
+        """This rank's decode launch alone (partials of its range), for the roofline."""
+        self.count += 1
+        c = self.count % self.copies
+        args = self.tqk.decode_args(self.kp[c], self.vp[c], self.nq, self.nkv, self.hd, max(self.n_local, 1), self.q,
+                                    self.partial, len0=self.n_local, out_mode=self.tqk.OUT_PARTIAL)
+        self.tqk.decode(args)
 
     def step_e2e(self):
         import torch
@@ -320,11 +416,10 @@ class Config4:
         s.synchronize()
 
     def describe(self):
-        return {"workload": "config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, 64 q / 8 kv heads, "
-                            "head_dim 128, context 131072",
-                "layers": 1, "seq_len": self.n, "kv_bytes_per_token": self.kv_bytes,
-                "tokens_per_rank": self.n_local,
-                "l2": "no flush: inputs larger than L2 (302 MB of K/V per step vs 126 MB L2)"}
+        return describe_config4(self.nq, self.nkv, self.hd, self.n)
+
+    def per_rank(self):
+        return {"tokens_per_rank": self.n_local, "cache_copies_rotated": self.copies}
 
     def parallelism(self, world):
         if world == 1:
@@ -355,6 +450,15 @@ def rope_np(x, hd, pos, theta):
     return h.astype(np.float32).reshape(x.shape)
 
 
+def describe_config3(all_lens, lo, mt, n_q, n_kv, hd):
+    kv_bytes = 2 * n_kv * int(np.sum(all_lens)) * (hd // QK) * BB
+    return {"workload": f"config3: ragged batched Q8 GQA decode, {len(all_lens)} sequences, lengths U[{lo}, {mt}] "
+                        f"(sum {int(np.sum(all_lens))}), {n_q} q / {n_kv} kv heads, head_dim {hd}, 1% x8 outliers",
+            "layers": 1, "batch": len(all_lens), "kv_bytes_per_step": kv_bytes,
+            "l2": f"no flush: inputs larger than L2 ({kv_bytes / 1e6:.0f} MB of K/V per step vs 126 MB L2)"
+                  if kv_bytes > 126e6 else f"{kv_bytes / 1e6:.1f} MB of K/V per step (smaller than L2)"}
+
+
 class Config3:
     """Ragged batched decode: 64 sequences, lengths uniform
     in [512, 8192], 32 q / 8 kv heads, head_dim 128, K/V ~ N(0,1) with 1% of
@@ -366,14 +470,14 @@ class Config3:
     scaling = "strong"  # the batch of 64 is fixed; each rank takes a share
     B = 64
 
-    def __init__(self, seed: int, rank: int = 0, world: int = 1, n_q=32, n_kv=8, hd=128, mt=8192):
+    def __init__(self, seed: int, rank: int = 0, world: int = 1, n_q=32, n_kv=8, hd=128, mt=8192, lo=512):
         import torch
         from tailorquantkernel_b200 import shard, tqk
         self.tqk = tqk
-        self.L, self.nq, self.nkv, self.hd, self.mt = 1, n_q, n_kv, hd, mt
+        self.L, self.nq, self.nkv, self.hd, self.mt, self.lo = 1, n_q, n_kv, hd, mt, lo
         self.nb = hd // QK
         rng = np.random.default_rng(seed)
-        self.all_lens = rng.integers(512, mt + 1, self.B).astype(np.int32)
+        self.all_lens = rng.integers(lo, mt + 1, self.B).astype(np.int32)
         self.mine = shard.batch_shard(self.all_lens, world)[rank]
         lens = self.all_lens[self.mine]
         nloc = len(self.mine)
@@ -388,35 +492,48 @@ class Config3:
         self.lens = torch.from_numpy(lens).cuda()
         self.q = torch.randn(nloc, n_q * hd, device="cuda", generator=g)
         self.out = torch.empty(nloc, n_q * hd, device="cuda")
-        self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, mt, self.q, self.out, n_items=nloc,
-                                    item_stride_blocks=n_kv * mt * self.nb, lens=self.lens,
-                                    max_len=int(lens.max()), q_item_stride=n_q * hd, out_item_stride=n_q * hd)
         self.kv_bytes = 2 * n_kv * int(self.all_lens.sum()) * self.nb * BB  # the whole batch
         self.bytes_per_step = 2 * n_kv * int(lens.sum()) * self.nb * BB   # this rank's decode kernel
+        # a rank's share of the batch can be smaller than L2: it then rotates over copies of its planes,
+        # one per step, so that at least twice L2's 126 MB is read between two reads of the same bytes
+        self.copies = 1 if world == 1 else max(1, -(-252_000_000 // max(self.bytes_per_step, 1)))
+        kps, vps = [self.kp], [self.vp]
+        for _ in range(self.copies - 1):
+            kps.append(self.kp.clone())
+            vps.append(self.vp.clone())
+        self.kps, self.vps = kps, vps
+        self.all_args = [tqk.decode_args(kps[c], vps[c], n_q, n_kv, hd, mt, self.q, self.out, n_items=nloc,
+                                         item_stride_blocks=n_kv * mt * self.nb, lens=self.lens,
+                                         max_len=int(lens.max()), q_item_stride=n_q * hd, out_item_stride=n_q * hd)
+                         for c in range(self.copies)]
+        self.args = self.all_args[0]
+        self.count = 0
         self.tokens_per_step = self.B  # for the whole job: each step is one token of every sequence
         self.launches_per_step = 1
+        self.e2e_api = ("tqk_decode_q8 (C ABI, ragged device lengths) with the rank's sequences' pinned host q in "
+                        "and their attention outputs out, stream-synchronised every step")
         self.h_q = self.q.cpu().pin_memory()
         self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
         self.h2d = self.h_q.numel() * 4
         self.d2h = self.h_out.numel() * 4
 
     def step(self):
-        self.tqk.decode(self.args)
+        self.count += 1
+        self.tqk.decode(self.all_args[self.count % self.copies])
 
     def step_e2e(self):
         import torch
         s = torch.cuda.current_stream()
         self.q.copy_(self.h_q, non_blocking=True)
-        self.tqk.decode(self.args)
+        self.step()
         self.h_out.copy_(self.out, non_blocking=True)
         s.synchronize()
 
     def describe(self):
-        return {"workload": "config3: ragged batched Q8 GQA decode, 64 sequences, lengths U[512, 8192] "
-                            f"(sum {int(self.all_lens.sum())}), 32 q / 8 kv heads, head_dim 128, 1% x8 outliers",
-                "layers": 1, "batch": self.B, "sequences_per_rank": len(self.mine),
-                "kv_bytes_per_step": self.kv_bytes,
-                "l2": "no flush: inputs larger than L2 (628 MB of K/V per step vs 126 MB L2)"}
+        return describe_config3(self.all_lens, self.lo, self.mt, self.nq, self.nkv, self.hd)
+
+    def per_rank(self):
+        return {"sequences_per_rank": len(self.mine), "cache_copies_rotated": self.copies}
 
     @staticmethod
     def parallelism(world):
@@ -424,6 +541,19 @@ class Config3:
 
     def host_planes(self):
         raise NotImplementedError("the CPU baseline of config 3 uses HostConfig3")
+
+
+def prefill_flops(n_q, hd, pos0, n):
+    """2*2*head_dim FLOPs (QK^T and PV) per (query head, visible key) of a causal chunk."""
+    pairs = n * pos0 + n * (n + 1) // 2
+    return n_q * pairs * 2 * 2 * hd
+
+
+def describe_config5(n_q, n_kv, hd, pos0, n):
+    return {"workload": f"config5: chunked causal prefill, {n} new tokens at positions {pos0}..{pos0 + n - 1} over a "
+                        f"{pos0}-position Q8 cache, {n_q} q / {n_kv} kv heads, head_dim {hd}",
+            "tokens_per_step": n, "flops_per_step": prefill_flops(n_q, hd, pos0, n),
+            "l2": "the Q8 K/V of a kv head is L2-resident by design; timed back to back"}
 
 
 class Config5:
@@ -435,7 +565,6 @@ class Config5:
     name = "config5"
     scaling = "weak"  # replicas: every rank prefills its own sequence
     bound = "tensor"
-    FLOPS = 103095992320  # 32 heads x (2048*2048 + 2048*2049/2) key pairs x 2*2*128
     e2e_steps = 50        # each end-to-end step moves 82 MB over PCIe
 
     def __init__(self, seed: int, n_q=32, n_kv=8, hd=128, pos0=2048, n=2048):
@@ -443,6 +572,7 @@ class Config5:
         from tailorquantkernel_b200 import tqk
         self.tqk = tqk
         self.L, self.nq, self.nkv, self.hd, self.pos0, self.n = 1, n_q, n_kv, hd, pos0, n
+        self.FLOPS = prefill_flops(n_q, hd, pos0, n)  # 103,095,992,320 at the default shape
         self.mt = pos0 + n
         self.nb = hd // QK
         g = torch.Generator(device="cuda").manual_seed(seed)
@@ -483,10 +613,7 @@ class Config5:
         s.synchronize()
 
     def describe(self):
-        return {"workload": "config5: chunked causal prefill, 2048 new tokens at positions 2048..4095 over a "
-                            "2048-position Q8 cache, 32 q / 8 kv heads, head_dim 128",
-                "tokens_per_step": self.n, "flops_per_step": self.FLOPS,
-                "l2": "the 2.4 MB of Q8 K/V per kv head is L2-resident by design; timed back to back"}
+        return describe_config5(self.nq, self.nkv, self.hd, self.pos0, self.n)
 
     @staticmethod
     def parallelism(world):
@@ -505,6 +632,20 @@ def q8_weight_rows_np(rng, rows: int, cols: int) -> np.ndarray:
     w[:, :, 4:] = rng.integers(-127, 128, (rows, nb, QK), dtype=np.int8).view(np.uint8)
     w[:, :, :4] = rng.uniform(0.002, 0.02, (rows, nb)).astype(np.float32).view(np.uint8).reshape(rows, nb, 4)
     return w.reshape(rows, nb * BB)
+
+
+def describe_config6(layers, n_q, n_kv, hd, hidden, pos):
+    row = hd // QK * BB
+    q_dim, kv_dim = n_q * hd, n_kv * hd
+    wbytes = layers * (q_dim * hidden + 2 * kv_dim * hidden + hidden * q_dim) // QK * BB
+    kv_bytes = 2 * layers * n_kv * (pos + 1) * row
+    return {"workload": f"config6: Llama-3-8B-shaped attention stack, one token through {layers} attention layers "
+                        f"(Q8 wq/wk/wv/wo, q/k RMSNorm + RoPE(500000), Q8 cache append at {pos} and attention "
+                        f"over {pos + 1} positions, output projection), each layer's output feeding the next",
+            "layers": layers, "seq_len": pos + 1, "hidden": hidden,
+            "weight_bytes_per_token": wbytes, "kv_bytes_per_token": kv_bytes,
+            "l2": f"no flush: inputs larger than L2 ({(wbytes + kv_bytes) / 1e9:.2f} GB per step vs 126 MB L2)"
+                  if wbytes + kv_bytes > 126e6 else "smaller than L2"}
 
 
 class Config6:
@@ -588,12 +729,7 @@ class Config6:
         self.stream.synchronize()
 
     def describe(self):
-        return {"workload": "config6: Llama-3-8B-shaped attention stack, one token through 32 attention layers "
-                            "(Q8 wq/wk/wv/wo, q/k RMSNorm + RoPE(500000), Q8 cache append at 4096 and attention "
-                            "over 4097 positions, output projection), each layer's output feeding the next",
-                "layers": self.L, "seq_len": self.pos + 1, "hidden": self.hidden,
-                "weight_bytes_per_token": self.weight_bytes, "kv_bytes_per_token": self.kv_bytes,
-                "l2": "no flush: inputs larger than L2 (1.81 GB per step vs 126 MB L2)"}
+        return describe_config6(self.L, self.nq, self.nkv, self.hd, self.hidden, self.pos)
 
     @staticmethod
     def parallelism(world):
@@ -626,9 +762,7 @@ class HostConfig6:
         self.bytes_per_step = wbytes + self.kv_bytes + 2 * layers * n_kv * row
 
     def describe(self):
-        return {"workload": "config6: Llama-3-8B-shaped attention stack, one token through 32 attention layers "
-                            "(the reference's attention_layer, Q8 weights, Q8 cache at 4096)",
-                "layers": self.L, "seq_len": self.pos + 1, "hidden": self.hidden}
+        return describe_config6(self.L, self.nq, self.nkv, self.hd, self.hidden, self.pos)
 
 
 def reference_layers_seconds(orc, wl, budget_s: float, max_tokens: int | None = None, min_tokens: int = 2):
@@ -674,7 +808,7 @@ class HostConfig2:
         return self.kp, self.vp, self.q, self.k_new, self.v_new
 
     def describe(self):
-        return Config2.describe(self)
+        return describe_config2(self.L, self.nq, self.nkv, self.hd, self.pos)
 
 
 class HostConfig3:
@@ -683,10 +817,10 @@ class HostConfig3:
     bounded sample the CPU baseline times."""
     name = "config3"
 
-    def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, mt=8192, sample=4):
-        self.L, self.nq, self.nkv, self.hd, self.mt = 1, n_q, n_kv, hd, mt
+    def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, mt=8192, lo=512, sample=4):
+        self.L, self.nq, self.nkv, self.hd, self.mt, self.lo = 1, n_q, n_kv, hd, mt, lo
         rng = np.random.default_rng(seed)
-        self.all_lens = rng.integers(512, mt + 1, Config3.B).astype(np.int32)
+        self.all_lens = rng.integers(lo, mt + 1, Config3.B).astype(np.int32)
         self.sample = list(range(sample))
         self.sample_lens = self.all_lens[:sample]
         row = hd // QK * BB
@@ -703,8 +837,7 @@ class HostConfig3:
         self.n = 1
 
     def describe(self):
-        return {"workload": "config3: ragged batched Q8 GQA decode, 64 sequences, lengths U[512, 8192], "
-                            "32 q / 8 kv heads, head_dim 128, 1% x8 outliers"}
+        return describe_config3(self.all_lens, self.lo, self.mt, self.nq, self.nkv, self.hd)
 
 
 class HostConfig4:
@@ -728,18 +861,16 @@ class HostConfig4:
         return self.kp, self.vp, self.q, None, None
 
     def describe(self):
-        return {"workload": "config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, 64 q / 8 kv heads, "
-                            "head_dim 128, context 131072",
-                "layers": 1, "seq_len": self.n, "kv_bytes_per_token": self.kv_bytes}
+        return describe_config4(self.nq, self.nkv, self.hd, self.n)
 
 
 class HostConfig5:
     """Config 5 built on the host only, for the reference arm."""
     name = "config5"
-    FLOPS = Config5.FLOPS
 
     def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, pos0=2048, n=2048):
         self.L, self.nq, self.nkv, self.hd, self.pos0, self.n = 1, n_q, n_kv, hd, pos0, n
+        self.FLOPS = prefill_flops(n_q, hd, pos0, n)
         self.mt = pos0 + n
         rng = np.random.default_rng(seed)
         row = hd // QK * BB
@@ -758,7 +889,7 @@ class HostConfig5:
         return self.kp, self.vp, self.q, self.k_new, self.v_new
 
     def describe(self):
-        return Config5.describe(self)
+        return describe_config5(self.nq, self.nkv, self.hd, self.pos0, self.n)
 
 
 # ---------------------------------------------------------------------------
@@ -823,37 +954,62 @@ def reference_prefill_token_seconds(orc, wl, budget_s: float, sample: int = 32, 
     return statistics.median(times), len(times) * sample, threads
 
 
+# --tiny: shapes small enough for the CPU test of the reference arm (tests/test_bench_cpu.py);
+# never a benchmark line
+TINY = {2: dict(layers=2, pos=255), 3: dict(mt=256, lo=64), 4: dict(n=2048), 5: dict(pos0=64, n=64),
+        6: dict(layers=2, hidden=512, pos=255)}
+SCALING = {2: "strong", 3: "strong", 4: "strong", 5: "weak", 6: "weak"}
+
+
+def global_batch(config: int, world: int) -> int:
+    """Sequences in flight in one step of the whole job: config 3 is a batch of 64, configs 2 and 4 one
+    sequence divided over the GPUs, configs 5 and 6 one sequence per GPU (replicas)."""
+    return {2: 1, 3: Config3.B, 4: 1}.get(config, world)
+
+
 def run_reference(args):
     rank, local, world = dist_init(args.gpus)
     if rank != 0:
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
+    shape = TINY[args.config] if args.tiny else {}
     if args.config == 6:
-        wl = HostConfig6(orc, seed=6000)
+        wl = HostConfig6(orc, seed=6000, **shape)
         reference_layers_seconds(orc, wl, 0.0, max_tokens=1, min_tokens=1)
         sec, n, threads = reference_layers_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
                                                    min_tokens=min(args.steps, 3))
+        sample = f"{n} whole tokens through the reference's attention_layer x {wl.L}, median per token"
     elif args.config == 5:
-        wl = HostConfig5(orc, seed=5000)
+        wl = HostConfig5(orc, seed=5000, **shape)
         sec, n, threads = reference_prefill_token_seconds(orc, wl, args.ref_seconds)
+        sample = (f"{n} tokens: the first 32 tokens of the chunk through the reference's append + causal "
+                  f"attention, repeated, median per token")
     elif args.config == 3:
-        wl = HostConfig3(orc, seed=3000)
+        wl = HostConfig3(orc, seed=3000, **shape)
         sec, n, threads = reference_ragged_seconds(orc, wl, args.ref_seconds)
+        sample = (f"{n} sequence-tokens of config 3 (the first 4 sequences through the reference's attend_q8), "
+                  f"median, scaled to the batch's mean length")
     else:
-        wl = HostConfig2(orc, seed=1000) if args.config == 2 else HostConfig4(orc, seed=4000)
-        # bounded: at most --steps whole tokens, stopping after ~60 s of CPU work
+        wl = HostConfig2(orc, seed=1000, **shape) if args.config == 2 else HostConfig4(orc, seed=4000, **shape)
+        # bounded: at most --steps whole tokens, stopping after --ref-seconds of CPU work
         reference_token_seconds(orc, wl, 0.0, max_tokens=args.warmup, min_tokens=args.warmup)
         sec, n, threads = reference_token_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
                                                   min_tokens=min(args.steps, 3))
+        sample = (f"{n} whole tokens of {wl.name} ({wl.L} layer(s) of "
+                  f"{'store_kv + ' if args.config == 2 else ''}attend_q8), median per token")
+    # sec is the CPU time of one token: of one sequence at the batch's mean length for config 3 (whose
+    # step is one token of each of its 64 sequences), of one chunk token for config 5 (whose step is
+    # the whole chunk), of the whole step otherwise
     value = 1.0 / sec
-    scaling = "strong" if args.config in (3, 4) else "weak"
+    per_step = sec * (Config3.B if args.config == 3 else wl.n if args.config == 5 else 1)
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": scaling,
-            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "impl": "reference",
-            "config": {**wl.describe(), "global_batch": 1, "parallelism": "reference CPU (OpenMP over kv heads)"},
+            "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+            "scaling": SCALING[args.config], "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
+            "impl": "reference",
+            "config": {**wl.describe(), "global_batch": global_batch(args.config, 1),
+                       "parallelism": "reference CPU (its OpenMP over kv heads, all host threads)"},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
-                             "sample": f"{n} whole tokens of {wl.name} ({wl.L} layer(s)), median per token, "
-                                       f"~{args.ref_seconds:.0f} s budget"},
+                             "sample": sample + f", ~{args.ref_seconds:.0f} s budget"},
             "hbm_gbs_equivalent": (wl.bytes_per_step / Config3.B if args.config == 3 else wl.bytes_per_step)
                                   / sec / 1e9 * (wl.n if args.config == 5 else 1),
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -872,16 +1028,17 @@ def run_ours(args):
     from tailorquantkernel_b200 import tqk
     peak, peak_kind = _peaks()
 
+    shape = TINY[args.config] if args.tiny else {}
     if args.config == 2:
-        wl = Config2(seed=1000 + rank, prologue=args.prologue)
+        wl = Config2(seed=1000, prologue=args.prologue, rank=rank, world=world, dist=dist, **shape)
     elif args.config == 3:
-        wl = Config3(seed=3000, rank=rank, world=world)
+        wl = Config3(seed=3000, rank=rank, world=world, **shape)
     elif args.config == 4:
-        wl = Config4(seed=4000, rank=rank, world=world, dist=dist, exchange=args.exchange)
+        wl = Config4(seed=4000, rank=rank, world=world, dist=dist, exchange=args.exchange, **shape)
     elif args.config == 6:
-        wl = Config6(seed=6000 + rank)
+        wl = Config6(seed=6000 + rank, **shape)
     else:
-        wl = Config5(seed=5000 + rank)
+        wl = Config5(seed=5000 + rank, **shape)
     stream = torch.cuda.current_stream()
     for _ in range(max(args.warmup, 3)):
         wl.step()
@@ -898,6 +1055,23 @@ def run_ours(args):
     t_local = ev0.elapsed_time(ev1) / 1e3
     t = max_over_ranks(dist, t_local)
     status = tqk.device_status()
+
+    # the dominant kernel's own launch time: the step itself on one GPU; on several GPUs (where a
+    # step adds the gather or the exchange) the same decode launches timed alone, after the
+    # timed region, on the stream they run on
+    if world > 1 and hasattr(wl, "kernel_step"):
+        for _ in range(3):
+            wl.kernel_step()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(args.steps):
+            wl.kernel_step()
+        k1.record(stream)
+        k1.synchronize()
+        kernel_s = k0.elapsed_time(k1) / 1e3 / args.steps
+    else:
+        kernel_s = t_local / args.steps
+    kernel_s = max_over_ranks(dist, kernel_s)
 
     # end to end through the C ABI with host buffers (pinned H2D of q/k/v, D2H of out)
     e2e_steps = min(args.steps, getattr(wl, "e2e_steps", args.steps))
@@ -940,9 +1114,7 @@ def run_ours(args):
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        # the decode kernel's share of a step: one launch per step (config 4 at N > 1 adds the
-        # all-gather and the merge, so this per-step figure understates the kernel's rate there)
-        per_launch = t_local / args.steps
+        per_launch = kernel_s
         if getattr(wl, "bound", "hbm") == "tensor":
             tpeak, tpeak_kind = _tensor_peak()
             achieved = wl.FLOPS / per_launch / 1e12
@@ -959,6 +1131,9 @@ def run_ours(args):
                         "traffic": _traffic_from_profile(("layers_" if wl.name == "config6" else "decode_q8_")
                                                          + wl.name)}
         jobs = world if wl.scaling == "weak" else 1  # weak: every rank runs its own sequence
+        if world > 1:
+            roofline["note"] = ("the slowest rank's decode launch timed alone (without the step's gather or "
+                                "exchange); bytes are that rank's share")
         line = {
             "metric": METRIC,
             "value": jobs * args.steps * wl.tokens_per_step / t,
@@ -968,14 +1143,14 @@ def run_ours(args):
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "int8+fp32",
             "data": getattr(wl, "data", "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q"),
-            "config": {**wl.describe(), "global_batch": jobs, "parallelism": wl.parallelism(world)},
+            "config": {**wl.describe(), "global_batch": global_batch(args.config, world),
+                       "parallelism": wl.parallelism(world)},
+            **({"per_gpu": wl.per_rank()} if hasattr(wl, "per_rank") else {}),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": jobs * e2e_steps * wl.tokens_per_step / t_e2e, "unit": "tokens/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h,
-                    "api": getattr(wl, "e2e_api", "tqk_decode_q8 (C ABI) with pinned host inputs (q, and the "
-                                                  "appended k/v for config 2) in and the attention output out, "
-                                                  "stream-synchronised every step")},
+                    "api": wl.e2e_api},
             "gpu_launches": args.steps * wl.launches_per_step,
             **({"hbm_gbs": achieved} if roofline["bound"] == "hbm" else {}),
             "clocks": clk.summary(),
@@ -1001,6 +1176,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="config 4 on several GPUs: the partials' exchange over peer memory or by NCCL")
+    ap.add_argument("--tiny", action="store_true",
+                    help="shrunken shapes for the CPU test of the reference arm and quick GPU checks; not a "
+                         "benchmark of the configs")
     ap.add_argument("--prologue", action="store_true",
                     help="config 2 with the q/k RMSNorm + RoPE prologue fused into the decode launch")
     args = ap.parse_args()

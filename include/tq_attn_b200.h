@@ -113,7 +113,14 @@ TQ_B200_API int tq_attn_validate_cache(const tq_kv_cache *cache);
 
 /* model/attention_layer.c:169-194 (model_ops.h:119-121).  Returns -1 for pos
  * outside [0, max_tokens) before touching anything; a GPU failure returns a
- * tqk status (< -1) instead of aborting. */
+ * tqk status (< -1) instead of aborting.  Every Q8 call ends by reading the
+ * device's sticky error word in stream order: a kernel wait that gave up
+ * (TQK_ETIMEOUT, -25) or a clamped device length (TQK_EDEVLEN, -27) is
+ * returned, the word is cleared, the host cache planes are left without the
+ * new rows and the device mirror is marked stale, so that calling again at
+ * the same position recomputes from the host planes.  The same holds for
+ * attention_layer_batch; the void entry points below report it through
+ * tq_b200_last_status and fill their outputs with NaN. */
 TQ_B200_API int attention_layer(const tq_attn_weights *w, const tq_attn_config *cfg, tq_kv_cache *cache, int pos,
                                 const float *xn, float *scores, float *out);
 

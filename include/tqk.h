@@ -49,6 +49,7 @@ typedef void *tqk_stream_t; /* a cudaStream_t */
 #define TQK_ENODEV         -24  /* no usable CUDA device */
 #define TQK_ETIMEOUT       -25  /* a device-side bounded wait gave up (see tqk_device_status) */
 #define TQK_EUNSUPPORTED   -26  /* head_dim > 256 or another shape outside the kernels' range */
+#define TQK_EDEVLEN        -27  /* a length read from device memory was outside [0, max_tokens] (clamped) */
 
 TQK_API const char *tqk_status_string(int status);
 /* Text of the last failure on the calling host thread ("" if none). */
@@ -60,6 +61,16 @@ TQK_API const char *tqk_version(void);
  * current device: 0 when no kernel reported a timeout or bad input.  Synchronises
  * the device.  The kernels set it instead of trapping. */
 TQK_API int tqk_device_status(int *device_error, int clear);
+/* Enqueues on `stream` a copy of the current device's error word into
+ * *host_dst (pinned host memory for a truly asynchronous copy); read it after
+ * synchronising the stream.  It shows what every kernel that finished before
+ * the copy in stream order recorded (and whatever other streams' kernels
+ * recorded by then: the word is per device).  Clear it with
+ * tqk_device_status(&v, 1). */
+TQK_API int tqk_device_status_async(int *host_dst, tqk_stream_t stream);
+/* The status code of a device error word value: TQK_OK for 0, TQK_ETIMEOUT for
+ * a bounded wait that gave up, TQK_EDEVLEN for a clamped device length. */
+TQK_API int tqk_device_error_status(int device_error);
 
 /* ---------------------------------------------------------------------------
  * Quantiser.  Replaces quantize_row_q8 (reference kernel/quant_x.c:12-34) for
@@ -195,8 +206,12 @@ TQK_API int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t work
  * instance a runtime whose memory is fully reserved up front.  The split
  * tickets and partials live in fixed static device arrays of this library
  * (tickets for 16384 units, 4 MiB of partials, present from module load); nothing else
- * is allocated, not even the device error word.  Same arguments, results and
- * automatic split as tqk_decode_q8.
+ * is allocated, not even the device error word.  Same arguments as
+ * tqk_decode_q8, and the same automatic split for equal lengths.  For a ragged
+ * batch it always takes the fixed split, never tqk_decode_q8's balanced
+ * schedule: the split merge then combines in another order, so the output
+ * agrees with tqk_decode_q8's within the decode tolerance rather than bit for
+ * bit, and ragged batches may run slower.
  *   - Calls whose split needs more than 16384 (item, head unit) pairs or more
  *     than 4 MiB of partials fail with TQK_EWORKSPACE; use tqk_decode_q8 with
  *     a workspace, or a larger split_tokens.
@@ -342,10 +357,14 @@ TQK_API int tqk_merge_partials(const float *parts, int n_parts, int64_t part_str
  *      mailboxes[r] is rank r's mailbox as mapped in this process
  *      (mailboxes[rank] = the local one).
  * The kernel raises this rank's flag in every peer's mailbox, waits for every
- * peer's flag of this epoch (1 s limit: TQK_ETIMEOUT in tqk_device_status,
- * output left unwritten), reads the peers' records over NVLink and writes the
+ * peer's flag of this epoch, reads the peers' records over NVLink and writes the
  * merged output (tqk_merge_partials' arithmetic).  All ranks must make the
  * same calls with the same epoch sequence, each rank on one stream; world <= 8.
+ * The wait has a 1 s limit per block of the kernel: when it runs out,
+ * tqk_device_status reports TQK_ETIMEOUT and the output is undefined (blocks
+ * whose flags arrived in time merged, the others did not).  The mailboxes'
+ * flags are then out of step: free them and set up the exchange again (new
+ * zeroed mailboxes, epochs from 1) before the next step.
  */
 #define TQK_IPC_HANDLE_BYTES 64
 TQK_API size_t tqk_exchange_mailbox_bytes(int world, int n_heads, int head_dim);
@@ -357,6 +376,24 @@ TQK_API int tqk_ipc_open_handle(const unsigned char *handle, void **ptr);
 TQK_API int tqk_ipc_close_handle(void *ptr);
 TQK_API int tqk_exchange_merge(int n_heads, int head_dim, int world, int rank, void *const *mailboxes, int epoch,
                        float *out, tqk_stream_t stream);
+
+/* The kv-head-group split's gather over peer memory (the multi-GPU form of
+ * attend_q8's loop over kv heads, reference model/attention_layer.c:134-149,
+ * whose one CPU needs no such step).  Each rank attends to its own kv heads
+ * and their q heads for every layer, and every rank needs the whole output.
+ * Same mailboxes, IPC set-up, epochs, flags and timeout as tqk_exchange_merge;
+ * the mailbox is tqk_gather_mailbox_bytes(world, n_groups, chunk_floats) bytes
+ * and per step with epoch e:
+ *   1. the rank writes its [n_groups][chunk_floats] floats (for instance the
+ *      decode's output, [layers][its q heads][head_dim]) at byte offset
+ *      tqk_gather_slot_offset(n_groups, chunk_floats, e) of its own mailbox;
+ *   2. tqk_exchange_gather(...) then writes out[g][r][:] = rank r's group g,
+ *      out being [n_groups][world][chunk_floats] (16-byte aligned).
+ * chunk_floats % 4 == 0 and world * chunk_floats <= 8192; n_groups <= 65535. */
+TQK_API size_t tqk_gather_mailbox_bytes(int world, int n_groups, int chunk_floats);
+TQK_API size_t tqk_gather_slot_offset(int n_groups, int chunk_floats, int epoch);
+TQK_API int tqk_exchange_gather(int n_groups, int chunk_floats, int world, int rank, void *const *mailboxes,
+                                int epoch, float *out, tqk_stream_t stream);
 
 #ifdef __cplusplus
 }

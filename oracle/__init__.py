@@ -58,7 +58,8 @@ def available(kind: str) -> bool:
 def build(reference: str | None = None) -> None:
     """make -C oracle [ref]: the restatement always, the reference builds when its tree exists."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    ref = reference or os.environ.get("TQK_REFERENCE", "/root/reference")
+    ref = reference or os.environ.get("TQK_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                        "reference")
     if os.path.isdir(ref):
         subprocess.run(["make", "-s", "-C", HERE, f"REF={ref}", "ref"], check=True)
 

@@ -100,7 +100,8 @@ def build_oracle(verbose: bool = False) -> None:
     reference builds when the reference tree is present on this machine."""
     oracle = os.path.join(ROOT, "oracle")
     _run(["make", "-s", "-C", oracle, "all"], verbose)
-    ref = os.environ.get("TQK_REFERENCE", "/root/reference")
+    # the reference tree: $TQK_REFERENCE, else a "reference" directory beside the repository
+    ref = os.environ.get("TQK_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
     if os.path.isdir(ref):
         _run(["make", "-s", "-C", oracle, f"REF={ref}", "ref"], verbose)
         if os.path.exists(os.path.join(PKG, "libtq_attn_b200.so")):

@@ -67,6 +67,7 @@ static struct {
     size_t hstage_bytes;
     mirror *mirrors;
     wreg *wregs;
+    int *herr;   /* pinned host copy of the device error word */
 } G;
 
 static pthread_mutex_t g_mu = PTHREAD_MUTEX_INITIALIZER;
@@ -106,8 +107,30 @@ static int ctx_ready(void) {
         CU(cudaGetDevice(&dev), "cudaGetDevice");
     }
     CU(cudaStreamCreateWithFlags(&G.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    CU(cudaHostAlloc((void **)&G.herr, sizeof(int), cudaHostAllocDefault), "cudaHostAlloc");
+    *G.herr = 0;
     G.device = dev;
     G.ready = 1;
+    return 0;
+}
+
+/* Ends a call's queued work: enqueues the read of the device error word behind
+ * it, synchronises the stream and maps a recorded device failure (a bounded
+ * wait that gave up, a clamped length) to its negative status, clearing the
+ * word so that the next call starts clean.  Returns 0 when the call's results
+ * can be used.  The word is per device, so a failure that another stream's
+ * kernel recorded before this call's work finished is reported here too. */
+static int finish(const char *what) {
+    int rc = tqk_device_status_async(G.herr, G.stream);
+    if (rc) return tqk_fail(rc, what);
+    CU(cudaStreamSynchronize(G.stream), what);
+    const int word = *G.herr;
+    if (word) {
+        int dummy = 0;
+        tqk_device_status(&dummy, 1);
+        *G.herr = 0;
+        return tqk_fail(tqk_device_error_status(word), what);
+    }
     return 0;
 }
 
@@ -273,7 +296,7 @@ static int q8_append_attend(tq_kv_cache *cache, const tq_attn_config *cfg, int p
     CU(cudaMemcpy2DAsync(h + off_rv, (size_t)n * row, (const unsigned char *)m->dv + (size_t)pos0 * row, pitch,
                          (size_t)n * row, (size_t)cfg->n_kv_heads, cudaMemcpyDeviceToHost, G.stream),
        "download V rows");
-    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    if ((rc = finish("append + attention"))) return rc;  /* m->synced stays -1: the next call re-uploads */
     memcpy(attn, h + off_out, out_bytes);
     for (int kvh = 0; kvh < cfg->n_kv_heads; kvh++) {
         const size_t dst = ((size_t)kvh * cache->max_tokens + pos0) * row;
@@ -530,7 +553,7 @@ static int device_layers(const wreg *r, tq_kv_cache *cache, const tq_attn_config
     CU(cudaMemcpy2DAsync(h + h_rv, (size_t)n * row, (const unsigned char *)m->dv + (size_t)pos0 * row, pitch,
                          (size_t)n * row, (size_t)cfg->n_kv_heads, cudaMemcpyDeviceToHost, G.stream),
        "download V rows");
-    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    if ((rc = finish("device attention layer"))) return rc;  /* m->synced stays -1: the next call re-uploads */
     memcpy(out, h + h_out, x_bytes);
     for (int kvh = 0; kvh < cfg->n_kv_heads; kvh++) {
         const size_t dst = ((size_t)kvh * cache->max_tokens + pos0) * row;
@@ -729,7 +752,7 @@ static int head_q8_impl(const float *q, block_q8 *q_q8, const block_q8 *k_cache,
     CU(cudaMemcpyAsync(q_q8, d + o_qq, nb * blk, cudaMemcpyDeviceToHost, G.stream), "download q_q8");
     if (n > 0) CU(cudaMemcpyAsync(scores, d + o_s, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, G.stream), "download scores");
     CU(cudaMemcpyAsync(out, d + o_o, head_dim * sizeof(float), cudaMemcpyDeviceToHost, G.stream), "download out");
-    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    if ((rc = finish("attention_head_q8"))) return rc;
     return set_status(0);
 }
 
@@ -758,7 +781,7 @@ static int scores_impl(const block_q8 *q, int g, const block_q8 *k, int n, int n
         return tqk_fail(rc, "tqk_attn_scores_q8");
     CU(cudaMemcpy2DAsync(scores, stride * sizeof(float), d + o_s, (size_t)n * sizeof(float), (size_t)n * sizeof(float),
                          (size_t)g, cudaMemcpyDeviceToHost, G.stream), "download scores");
-    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    if ((rc = finish("attn_scores_q8"))) return rc;
     return set_status(0);
 }
 
@@ -791,7 +814,7 @@ static int accum_impl(const float *w, size_t w_stride, int g, const block_q8 *v,
         return tqk_fail(rc, "tqk_attn_accum_q8");
     CU(cudaMemcpy2DAsync(out, out_stride * sizeof(float), d + o_o, (size_t)hd * sizeof(float), (size_t)hd * sizeof(float),
                          (size_t)g, cudaMemcpyDeviceToHost, G.stream), "download out");
-    CU(cudaStreamSynchronize(G.stream), "synchronize");
+    if ((rc = finish("attn_accum_q8"))) return rc;
     return set_status(0);
 }
 

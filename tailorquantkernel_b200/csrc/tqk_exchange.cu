@@ -21,6 +21,11 @@
 // epoch e only at epoch e+2, after its exchange of epoch e+1 has seen every
 // peer's flag e+1, which each peer raises only once it has finished merging
 // epoch e.  No TMA, no multicast, no NVLS: plain loads and stores.
+//
+// tqk_exchange_gather runs the same protocol for the kv-head-group split of
+// one sequence (the decode's q heads divided over the ranks by kv head): each
+// rank's slot holds its output heads of every layer, and the kernel
+// concatenates every rank's slice into the full output instead of merging.
 #include "tqk_internal.h"
 
 #include <cstring>
@@ -38,13 +43,21 @@ struct MailboxLayout {
     size_t bytes;
 };
 
-MailboxLayout mailbox_layout(int world, int n_heads, int head_dim) {
+// Layout of a mailbox whose two parity slots hold slot_floats floats each,
+// followed by the flags int[2][world] (every part 256-byte aligned).
+MailboxLayout mailbox_layout_floats(int world, size_t slot_floats) {
     MailboxLayout m{};
-    m.rec = (size_t)head_dim + 2;
-    m.slot = (size_t)n_heads * m.rec;
+    m.rec = 0;
+    m.slot = slot_floats;
     const size_t data = 2 * m.slot * sizeof(float);
     m.flags_off = (data + 255) & ~(size_t)255;
     m.bytes = m.flags_off + (((size_t)2 * world * sizeof(int) + 255) & ~(size_t)255);
+    return m;
+}
+
+MailboxLayout mailbox_layout(int world, int n_heads, int head_dim) {
+    MailboxLayout m = mailbox_layout_floats(world, (size_t)n_heads * ((size_t)head_dim + 2));
+    m.rec = (size_t)head_dim + 2;
     return m;
 }
 
@@ -72,28 +85,27 @@ __device__ __forceinline__ float ld_relaxed_sys(const float *p) {
     return v;
 }
 
-__global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParams p) {
-    const int h = blockIdx.x, tid = threadIdx.x;
-    const int rec = p.head_dim + 2, par = p.epoch & 1;
+// Raises this rank's flag of the epoch in every peer's mailbox (block 0) and
+// waits, in thread 0 of every block, until every peer's flag of the epoch has
+// arrived in the local mailbox (1 s limit: DEVERR_TIMEOUT, returns false).
+// Called after grid_dependency_wait, so this rank's slot is complete.
+__device__ bool raise_and_wait_flags(float *const *mbox, int world, int rank, int epoch, long long flags_off,
+                                     int *err) {
     __shared__ int s_ok;
-
-    // launched with programmatic stream serialization: the records come from the decode grid before
-    grid_dependency_wait();
-    // this rank's records of the epoch are in its slot: tell every peer
-    if (h == 0 && tid < p.world && tid != p.rank) {
-        int *flags = reinterpret_cast<int *>(reinterpret_cast<char *>(p.mbox[tid]) + p.flags_off);
-        st_release_sys(flags + par * p.world + p.rank, p.epoch);
+    const int tid = threadIdx.x, par = epoch & 1;
+    if (blockIdx.x == 0 && tid < world && tid != rank) {
+        int *flags = reinterpret_cast<int *>(reinterpret_cast<char *>(mbox[tid]) + flags_off);
+        st_release_sys(flags + par * world + rank, epoch);
     }
     if (tid == 0) {
-        // wait until every peer's records of this epoch are in its slot
-        const int *flags = reinterpret_cast<const int *>(reinterpret_cast<const char *>(p.mbox[p.rank]) + p.flags_off);
+        const int *flags = reinterpret_cast<const int *>(reinterpret_cast<const char *>(mbox[rank]) + flags_off);
         int ok = 1;
-        const uint64_t t0 = p.world > 1 ? globaltimer_ns() : 0;
-        for (int peer = 0; peer < p.world && ok; peer++) {
-            if (peer == p.rank) continue;
-            for (uint32_t it = 0; ld_acquire_sys(flags + par * p.world + peer) != p.epoch; it++) {
+        const uint64_t t0 = world > 1 ? globaltimer_ns() : 0;
+        for (int peer = 0; peer < world && ok; peer++) {
+            if (peer == rank) continue;
+            for (uint32_t it = 0; ld_acquire_sys(flags + par * world + peer) != epoch; it++) {
                 if ((it & 63u) == 63u && globaltimer_ns() - t0 > EX_WAIT_NS) {
-                    record_error(p.err, DEVERR_TIMEOUT);
+                    record_error(err, DEVERR_TIMEOUT);
                     ok = 0;
                     break;
                 }
@@ -103,7 +115,17 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParam
         s_ok = ok;
     }
     __syncthreads();
-    if (!s_ok) return;
+    return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParams p) {
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const int rec = p.head_dim + 2, par = p.epoch & 1;
+
+    // launched with programmatic stream serialization: the records come from the decode grid before
+    grid_dependency_wait();
+    // this rank's records of the epoch are in its slot: tell every peer, then wait for theirs
+    if (!raise_and_wait_flags(p.mbox, p.world, p.rank, p.epoch, p.flags_off, p.err)) return;
 
     // ---- merge head h: out = sum_r acc_r e^(m_r - M) / sum_r l_r e^(m_r - M), M = max_r m_r
     //      (tqk_merge_partials' arithmetic).  Every thread issues all its loads of the ranks'
@@ -135,6 +157,56 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParam
         }
     }
     if (c < p.head_dim) p.out[(long long)h * p.head_dim + c] = L > 0.0f ? a / L : 0.0f;
+}
+
+struct GatherParams {
+    float *mbox[EX_MAX_WORLD];  // every rank's mailbox as mapped in this process (mbox[rank] is local)
+    float *out;                 // [n_groups][world][chunk]
+    int world, rank, n_groups, chunk;
+    int epoch;
+    long long slot, flags_off;
+    int *err;
+};
+
+__device__ __forceinline__ float4 ld_relaxed_sys_v4(const float4 *p) {
+    float4 v;
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// All-gather of the kv-head-group split: rank r's slot of the epoch holds
+// [n_groups][chunk] floats (its head slice of every layer); out[g][r][:] =
+// slot_r[g][:] on every rank.  Block g copies group g of every rank; each
+// thread issues the loads of all its float4 columns before it stores any, so
+// the peers' slices cost one NVLink round trip.  chunk % 4 == 0 (host-checked).
+constexpr int GATHER_THREADS = 256;
+constexpr int GATHER_MAX_V4 = 8;  // float4 per thread: world * chunk <= 8192 floats per group
+
+__global__ void __launch_bounds__(GATHER_THREADS) exchange_gather_kernel(const GatherParams p) {
+    grid_dependency_wait();
+    if (!raise_and_wait_flags(p.mbox, p.world, p.rank, p.epoch, p.flags_off, p.err)) return;
+    const int g = blockIdx.x, tid = threadIdx.x, par = p.epoch & 1;
+    const int c4 = p.chunk >> 2, total = p.world * c4;
+    float4 v[GATHER_MAX_V4];
+#pragma unroll
+    for (int k = 0; k < GATHER_MAX_V4; k++) {
+        const int i = tid + k * GATHER_THREADS;
+        if (i < total) {
+            const int r = i / c4, c = i - r * c4;
+            const float4 *src = reinterpret_cast<const float4 *>(p.mbox[r] + (long long)par * p.slot +
+                                                                 (long long)g * p.chunk) + c;
+            v[k] = ld_relaxed_sys_v4(src);
+        }
+    }
+    float4 *dst = reinterpret_cast<float4 *>(p.out + (long long)g * p.world * p.chunk);
+#pragma unroll
+    for (int k = 0; k < GATHER_MAX_V4; k++) {
+        const int i = tid + k * GATHER_THREADS;
+        if (i < total) dst[i] = v[k];
+    }
 }
 
 }  // namespace
@@ -226,4 +298,45 @@ extern "C" int tqk_exchange_merge(int n_heads, int head_dim, int world, int rank
     p.flags_off = (long long)m.flags_off;
     p.err = device_info()->err_word;
     return launch_pdl(exchange_merge_kernel, dim3((unsigned)n_heads), dim3(128), 0, (cudaStream_t)stream, p);
+}
+
+extern "C" size_t tqk_gather_mailbox_bytes(int world, int n_groups, int chunk_floats) {
+    if (world < 1 || world > EX_MAX_WORLD || n_groups <= 0 || chunk_floats <= 0) return 0;
+    return mailbox_layout_floats(world, (size_t)n_groups * chunk_floats).bytes;
+}
+
+extern "C" size_t tqk_gather_slot_offset(int n_groups, int chunk_floats, int epoch) {
+    if (n_groups <= 0 || chunk_floats <= 0 || epoch < 1) return 0;
+    return (size_t)(epoch & 1) * (size_t)n_groups * chunk_floats * sizeof(float);
+}
+
+extern "C" int tqk_exchange_gather(int n_groups, int chunk_floats, int world, int rank, void *const *mailboxes,
+                                   int epoch, float *out, tqk_stream_t stream) {
+    if (!out || !mailboxes || n_groups <= 0 || n_groups > 65535 || chunk_floats <= 0 || world < 1 ||
+        world > EX_MAX_WORLD || rank < 0 || rank >= world || epoch < 1)
+        return fail(TQK_EINVAL, "tqk_exchange_gather: bad arguments");
+    if (chunk_floats % 4 || (long long)world * chunk_floats > (long long)GATHER_MAX_V4 * GATHER_THREADS * 4)
+        return fail(TQK_EUNSUPPORTED, "tqk_exchange_gather: chunk_floats must be a multiple of 4 and "
+                                      "world * chunk_floats at most 8192");
+    if (reinterpret_cast<uintptr_t>(out) & 15) return fail(TQK_EALIGN, "tqk_exchange_gather: out must be 16-byte aligned");
+    int rc = ensure_device();
+    if (rc) return rc;
+    const MailboxLayout m = mailbox_layout_floats(world, (size_t)n_groups * chunk_floats);
+    GatherParams p{};
+    for (int r = 0; r < world; r++) {
+        if (!mailboxes[r] || (reinterpret_cast<uintptr_t>(mailboxes[r]) & 255))
+            return fail(TQK_EALIGN, "tqk_exchange_gather: every mailbox must be a whole tqk_peer_buffer_alloc buffer");
+        p.mbox[r] = static_cast<float *>(mailboxes[r]);
+    }
+    p.out = out;
+    p.world = world;
+    p.rank = rank;
+    p.n_groups = n_groups;
+    p.chunk = chunk_floats;
+    p.epoch = epoch;
+    p.slot = (long long)m.slot;
+    p.flags_off = (long long)m.flags_off;
+    p.err = device_info()->err_word;
+    return launch_pdl(exchange_gather_kernel, dim3((unsigned)n_groups), dim3(GATHER_THREADS), 0, (cudaStream_t)stream,
+                      p);
 }

@@ -133,6 +133,7 @@ extern "C" const char *tqk_status_string(int status) {
         case TQK_ENODEV: return "no CUDA device";
         case TQK_ETIMEOUT: return "device wait timed out";
         case TQK_EUNSUPPORTED: return "unsupported shape";
+        case TQK_EDEVLEN: return "a device-side length was outside [0, max_tokens] and was clamped";
         default: return "unknown status";
     }
 }
@@ -156,6 +157,26 @@ extern "C" int tqk_device_status(int *device_error, int clear) {
     }
     if (device_error) *device_error = v;
     return TQK_OK;
+}
+
+extern "C" int tqk_device_status_async(int *host_dst, tqk_stream_t stream) {
+    if (!host_dst) return fail(TQK_EINVAL, "tqk_device_status_async: NULL destination");
+    int rc = ensure_device();
+    if (rc) return rc;
+    const DeviceInfo *d = device_info();
+    if (!d) return fail(TQK_ENODEV, "tqk_device_status_async: no device state");
+    const cudaError_t e = cudaMemcpyAsync(host_dst, d->err_word, sizeof(int), cudaMemcpyDeviceToHost,
+                                          (cudaStream_t)stream);
+    return e == cudaSuccess ? TQK_OK : fail_cuda(e, "tqk_device_status_async");
+}
+
+extern "C" int tqk_device_error_status(int device_error) {
+    switch (device_error) {
+        case 0: return TQK_OK;
+        case DEVERR_TIMEOUT: return TQK_ETIMEOUT;
+        case DEVERR_BADLEN: return TQK_EDEVLEN;
+        default: return TQK_ECUDA;
+    }
 }
 
 extern "C" int tqk_workspace_init(void *workspace, size_t bytes, tqk_stream_t stream) {

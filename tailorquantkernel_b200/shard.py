@@ -55,6 +55,42 @@ def head_range(n_kv: int, rank: int, world: int) -> Tuple[int, int]:
     return rank * per, per
 
 
+def head_split_args(tqk, k_local, v_local, n_layers: int, n_q: int, n_kv: int, head_dim: int, max_tokens: int,
+                    world: int, q_local, out_local, *, len0: int, k_new=None, v_new=None):
+    """Decode arguments of one rank's share of the kv-head-group split of n_layers
+    layers (the reference's per-kv-head loop of attend_q8,
+    model/attention_layer.c:134-149, divided over GPUs).
+
+    The rank holds per = n_kv / world kv heads of every layer, with their
+    per * group q heads (group = n_q / n_kv):
+      k_local / v_local: Q8 planes [n_layers * per][max_tokens][head_dim/32];
+      q_local, out_local: [n_layers][per * group][head_dim] floats;
+      k_new / v_new (optional fused append at len0 - 1): [n_layers][per][head_dim].
+    The share is handed to the kernel as items of two kv heads -- one kv head of
+    two consecutive layers when per == 1 -- so that the kernel that packs two kv
+    heads per CTA runs at every world size; the output layout does not change."""
+    if n_kv % world or n_q % n_kv:
+        raise ValueError(f"{n_q} q / {n_kv} kv heads do not split over {world} ranks")
+    per, group = n_kv // world, n_q // n_kv
+    heads = n_layers * per
+    kv_item = 2 if heads % 2 == 0 else 1
+    nb = head_dim // 32
+    return tqk.decode_args(k_local, v_local, kv_item * group, kv_item, head_dim, max_tokens, q_local, out_local,
+                           n_items=heads // kv_item, item_stride_blocks=kv_item * max_tokens * nb, len0=len0,
+                           q_item_stride=kv_item * group * head_dim, out_item_stride=kv_item * group * head_dim,
+                           k_new=k_new, v_new=v_new, kv_new_item_stride=kv_item * head_dim)
+
+
+def head_split_slice(x, n_layers: int, n_heads: int, head_dim: int, rank: int, world: int):
+    """Rank `rank`'s heads of a per-layer head-major array x [n_layers][n_heads * head_dim] (numpy
+    or torch): [n_layers][n_heads/world * head_dim], contiguous.  For q (n_heads = n_q) this is the
+    q heads of the rank's kv heads; for k_new / v_new (n_heads = n_kv) its kv heads."""
+    per = n_heads // world
+    y = x.reshape(n_layers, n_heads, head_dim)[:, rank * per:(rank + 1) * per]
+    y = y.reshape(n_layers, per * head_dim)
+    return y.contiguous() if hasattr(y, "contiguous") else y.copy()
+
+
 def batch_shard(lens: Sequence[int], world: int) -> List[List[int]]:
     """Sequences of a ragged batch per rank, balanced by total length: longest
     first, each to the currently lightest rank (ties to the lower rank).  Every
@@ -104,21 +140,17 @@ def seqsplit_attend(dist, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: 
     return out
 
 
-class PeerExchange:
-    """The sequence split's exchange step over peer memory for ranks on the GPUs of
-    one box: one mailbox per rank (tqk_peer_buffer_alloc), mapped in every other
-    rank through CUDA IPC handles swapped once with torch.distributed.  Per step:
-    begin() gives the slot this rank's partial records go to, end() launches
-    tqk_exchange_merge.  Every rank must run the same steps in the same order;
-    close() unmaps and frees."""
+class _PeerMailboxes:
+    """One mailbox per rank (tqk_peer_buffer_alloc, `nbytes` bytes), mapped in every
+    other rank through CUDA IPC handles swapped once with torch.distributed, and
+    the epoch counter of the flag protocol that tqk_exchange_merge and
+    tqk_exchange_gather share.  close() frees everything once every rank has
+    finished its last step."""
 
-    def __init__(self, dist, tqk, n_heads: int, head_dim: int, group=None):
+    def __init__(self, dist, tqk, nbytes: int, group=None):
         import torch
-        self.tqk, self.n_heads, self.head_dim = tqk, n_heads, head_dim
+        self.tqk, self.dist, self.group = tqk, dist, group
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
-        nbytes = tqk.tqk_exchange_mailbox_bytes(self.world, n_heads, head_dim)
-        if nbytes == 0:
-            raise ValueError(f"no mailbox layout for world {self.world}, {n_heads} heads of {head_dim}")
         self.local = tqk.peer_buffer_alloc(nbytes)
         handles = [None] * self.world
         dist.all_gather_object(handles, tqk.ipc_get_handle(self.local), group=group)
@@ -135,6 +167,38 @@ class PeerExchange:
         torch.cuda.synchronize()
         dist.barrier(group=group)  # every mailbox is zeroed and mapped before the first step
 
+    def close(self):
+        """Unmaps the peers' mailboxes and frees this rank's.  A peer's last step
+        reads this rank's mailbox over NVLink after it has seen this rank's flag,
+        which can be after this rank has finished its own step: so every rank
+        first waits for its own work and then for every other rank (a barrier)
+        before anything is unmapped or freed.  Every rank must call close()."""
+        import torch
+        if self.local is None:
+            return
+        torch.cuda.synchronize()
+        self.dist.barrier(group=self.group)
+        for ptr in self.opened:
+            self.tqk.ipc_close_handle(ptr)
+        self.opened = []
+        self.tqk.peer_buffer_free(self.local)
+        self.local = None
+
+
+class PeerExchange(_PeerMailboxes):
+    """The sequence split's exchange step over peer memory for ranks on the GPUs of
+    one box.  Per step: begin() gives the slot this rank's partial records go to,
+    end() launches tqk_exchange_merge.  Every rank must run the same steps in the
+    same order, and close() on every rank at the end."""
+
+    def __init__(self, dist, tqk, n_heads: int, head_dim: int, group=None):
+        self.n_heads, self.head_dim = n_heads, head_dim
+        world = dist.get_world_size(group)
+        nbytes = tqk.tqk_exchange_mailbox_bytes(world, n_heads, head_dim)
+        if nbytes == 0:
+            raise ValueError(f"no mailbox layout for world {world}, {n_heads} heads of {head_dim}")
+        super().__init__(dist, tqk, nbytes, group)
+
     def begin(self) -> int:
         """Starts the next step: the device address its partial records must be written to."""
         self.epoch += 1
@@ -146,15 +210,30 @@ class PeerExchange:
                                 stream=stream)
         return out
 
-    def close(self):
-        import torch
-        torch.cuda.synchronize()
-        for ptr in self.opened:
-            self.tqk.ipc_close_handle(ptr)
-        self.opened = []
-        if self.local:
-            self.tqk.peer_buffer_free(self.local)
-            self.local = None
+
+class PeerGather(_PeerMailboxes):
+    """The kv-head-group split's gather over peer memory: each rank attends to its
+    kv heads (and their q heads) of every layer and writes its output slice,
+    [n_groups][chunk_floats] floats, to the slot begin() returns; end() launches
+    tqk_exchange_gather, after which out is [n_groups][world][chunk_floats] on
+    every rank (for the decode: [layers][n_q_heads][head_dim])."""
+
+    def __init__(self, dist, tqk, n_groups: int, chunk_floats: int, group=None):
+        self.n_groups, self.chunk = n_groups, chunk_floats
+        world = dist.get_world_size(group)
+        nbytes = tqk.tqk_gather_mailbox_bytes(world, n_groups, chunk_floats)
+        if nbytes == 0:
+            raise ValueError(f"no gather mailbox for world {world}, {n_groups} groups of {chunk_floats} floats")
+        super().__init__(dist, tqk, nbytes, group)
+
+    def begin(self) -> int:
+        self.epoch += 1
+        return self.tqk.gather_slot(self.local, self.n_groups, self.chunk, self.epoch)
+
+    def end(self, out, stream=None):
+        self.tqk.exchange_gather(self.n_groups, self.chunk, self.world, self.rank, self.mailboxes, self.epoch, out,
+                                 stream=stream)
+        return out
 
 
 def seqsplit_attend_p2p(exchange: PeerExchange, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: int,

@@ -33,6 +33,7 @@ ECUDA = -23
 ENODEV = -24
 ETIMEOUT = -25
 EUNSUPPORTED = -26
+EDEVLEN = -27
 
 OUT_NORMALIZED = 0
 OUT_PARTIAL = 1
@@ -79,6 +80,8 @@ tqk_status_string = _sig("tqk_status_string", [_i], ctypes.c_char_p)
 tqk_last_error = _sig("tqk_last_error", [], ctypes.c_char_p)
 tqk_version = _sig("tqk_version", [], ctypes.c_char_p)
 tqk_device_status = _sig("tqk_device_status", [ctypes.POINTER(_i), _i])
+tqk_device_status_async = _sig("tqk_device_status_async", [_vp, _vp])
+tqk_device_error_status = _sig("tqk_device_error_status", [_i])
 tqk_quantize_rows_q8 = _sig("tqk_quantize_rows_q8", [_vp, _vp, _i, _i, _vp])
 tqk_store_kv_q8 = _sig("tqk_store_kv_q8", [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_store_kv_q8_batch = _sig("tqk_store_kv_q8_batch", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
@@ -139,10 +142,14 @@ tqk_ipc_open_handle = _sig("tqk_ipc_open_handle", [ctypes.c_char_p, ctypes.POINT
 tqk_ipc_close_handle = _sig("tqk_ipc_close_handle", [_vp])
 tqk_exchange_slot_offset = _sig("tqk_exchange_slot_offset", [_i, _i, _i], _sz)
 tqk_exchange_merge = _sig("tqk_exchange_merge", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+tqk_gather_mailbox_bytes = _sig("tqk_gather_mailbox_bytes", [_i, _i, _i], _sz)
+tqk_gather_slot_offset = _sig("tqk_gather_slot_offset", [_i, _i, _i], _sz)
+tqk_exchange_gather = _sig("tqk_exchange_gather", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
 IPC_HANDLE_BYTES = 64
 
 EXPORTED = [
-    "tqk_status_string", "tqk_last_error", "tqk_version", "tqk_device_status",
+    "tqk_status_string", "tqk_last_error", "tqk_version", "tqk_device_status", "tqk_device_status_async",
+    "tqk_device_error_status",
     "tqk_quantize_rows_q8", "tqk_store_kv_q8", "tqk_store_kv_q8_batch",
     "tqk_attn_scores_q8", "tqk_attn_accum_q8", "tqk_softmax_rows",
     "tqk_decode_workspace_size", "tqk_workspace_init", "tqk_decode_q8",
@@ -153,6 +160,7 @@ EXPORTED = [
     "tqk_exchange_mailbox_bytes", "tqk_exchange_slot_offset", "tqk_peer_buffer_alloc", "tqk_peer_buffer_free",
     "tqk_ipc_get_handle",
     "tqk_ipc_open_handle", "tqk_ipc_close_handle", "tqk_exchange_merge",
+    "tqk_gather_mailbox_bytes", "tqk_gather_slot_offset", "tqk_exchange_gather",
 ]
 
 
@@ -403,6 +411,18 @@ def exchange_merge(n_heads, head_dim, world, rank, mailboxes, epoch, out, stream
     arr = (_vp * len(mailboxes))(*mailboxes)
     check(tqk_exchange_merge(n_heads, head_dim, world, rank, arr, epoch, _ptr(out), _stream(stream)),
           "tqk_exchange_merge")
+
+
+def exchange_gather(n_groups, chunk_floats, world, rank, mailboxes, epoch, out, stream=None):
+    """tqk_exchange_gather: out[g][r][:] = rank r's group g of the epoch, on every rank."""
+    arr = (_vp * len(mailboxes))(*mailboxes)
+    check(tqk_exchange_gather(n_groups, chunk_floats, world, rank, arr, epoch, _ptr(out), _stream(stream)),
+          "tqk_exchange_gather")
+
+
+def gather_slot(mailbox: int, n_groups: int, chunk_floats: int, epoch: int) -> int:
+    """Address of the epoch's slot in a gather mailbox."""
+    return mailbox + tqk_gather_slot_offset(n_groups, chunk_floats, epoch)
 
 
 def exchange_slot(mailbox: int, n_heads: int, head_dim: int, epoch: int) -> int:

@@ -123,3 +123,68 @@ def test_registered_weights_run_the_layer_on_the_device(cuda, fmt):
     assert np.abs(out - want).max() <= 1e-3 * np.abs(want).max()
     lib.tq_kv_cache_free.argtypes = [ctypes.c_void_p]
     lib.tq_kv_cache_free(ctypes.byref(cache))
+
+
+def test_device_error_word_reaches_the_dropin_caller(cuda):
+    """A failure that a kernel records in the device error word (here a bounded wait that
+    gave up, made without any fault: a two-rank exchange whose peer never raises its flag)
+    comes back from the next drop-in attention_layer call as TQK_ETIMEOUT, with the host
+    cache rows untouched; the word is cleared and the call after that succeeds, bit-exact
+    in the appended rows and within the layer tolerance in the output."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import oracle
+    from _cases import layer_inputs
+    from tailorquantkernel_b200 import tqk
+    if not os.path.exists(HARNESS):
+        pytest.skip("oracle/_ref/libtqref_dropin.so not built (needs the reference tree at build time)")
+    lib = ctypes.CDLL(HARNESS)
+    port = oracle.Oracle("port")
+    seed, nq, nkv, hd, hidden, mt, pos, theta, eps = LAYER
+    fmt = "8"
+    w, qn, kn, kp, vp_, xn = layer_inputs(seed, nq, nkv, hd, hidden, mt, pos, fmt, port)
+    aw, cfg = _layer_structs(oracle, w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps)
+    cache = oracle._TqKvCache()
+    lib.tq_kv_cache_init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
+    assert lib.tq_kv_cache_init(ctypes.byref(cache), 1, ctypes.byref(cfg), mt) == 0
+    ctypes.memmove(cache.k_q8, kp.ctypes.data, kp.nbytes)
+    ctypes.memmove(cache.v_q8, vp_.ctypes.data, vp_.nbytes)
+    host_k = np.ctypeslib.as_array(ctypes.cast(cache.k_q8, ctypes.POINTER(ctypes.c_uint8)), shape=kp.shape)
+    fn = lib.attention_layer
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_void_p]
+    scores = np.zeros(nq * mt, np.float32)
+    out = np.zeros(hidden, np.float32)
+    # the drop-in's first call binds its context; then the error word is set by a timed-out wait
+    assert fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos, xn.ctypes.data, scores.ctypes.data,
+              out.ctypes.data) == 0
+    kp_ref, vp_ref = kp.copy(), vp_.copy()
+    port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp_ref, vp_ref, mt, pos, xn)
+    nbytes = tqk.tqk_exchange_mailbox_bytes(2, nq, hd)
+    boxes = [tqk.peer_buffer_alloc(nbytes), tqk.peer_buffer_alloc(nbytes)]
+    try:
+        assert tqk.device_status(clear=True) == 0
+        junk = torch.empty(nq * hd, device="cuda")
+        tqk.exchange_merge(nq, hd, 2, 0, boxes, 1, junk)
+        torch.cuda.synchronize()
+        row_before = host_k[:, pos + 1].copy()
+        x = np.random.default_rng(3).standard_normal(hidden, dtype=np.float32)
+        rc = fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos + 1, x.ctypes.data, scores.ctypes.data,
+                out.ctypes.data)
+        assert rc == tqk.ETIMEOUT, rc
+        assert np.array_equal(host_k[:, pos + 1], row_before)  # no rows written back
+        assert tqk.device_status() == 0  # the drop-in cleared the word
+        out[:] = np.nan
+        assert fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos + 1, x.ctypes.data,
+                  scores.ctypes.data, out.ctypes.data) == 0
+        want = port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp_ref, vp_ref, mt, pos + 1, x)
+        assert np.array_equal(host_k[:, pos + 1], kp_ref[:, pos + 1])
+        assert np.abs(out - want).max() <= 1e-3 * np.abs(want).max()
+    finally:
+        for b in boxes:
+            tqk.peer_buffer_free(b)
+        lib.tq_kv_cache_free.argtypes = [ctypes.c_void_p]
+        lib.tq_kv_cache_free(ctypes.byref(cache))

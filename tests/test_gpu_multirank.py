@@ -178,3 +178,172 @@ def test_exchange_wait_times_out_without_peer(cuda):
     finally:
         for b in boxes + [solo]:
             tqk.peer_buffer_free(b)
+
+
+def _rank_main_heads(rank, world, port, result_dir):
+    """kv-head-group split of a 3-layer decode (bench config 2's multi-GPU path) on `world` GPUs:
+    each rank appends and attends for its kv heads of every layer, tqk_exchange_gather assembles
+    the output; two steps at consecutive positions with different q / k / v."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    from tailorquantkernel_b200 import shard, tqk
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    pg = None
+    try:
+        port_ = oracle.Oracle("port")
+        layers, nq, nkv, hd, pos, steps = 3, 32, 8, 128, 700, 2
+        mt, per, group = pos + steps, nkv // world, nq // nkv
+        rng = np.random.default_rng(90)  # the same full problem on every rank
+        kf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+        vf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+        kf[:, :, pos:] = 0.0
+        vf[:, :, pos:] = 0.0
+        kp_full, vp_full = port_.quantize_rows(kf), port_.quantize_rows(vf)  # [L][nkv][mt][row]
+        qs = rng.standard_normal((steps, layers, nq * hd), dtype=np.float32)
+        ks = rng.standard_normal((steps, layers, nkv * hd), dtype=np.float32)
+        vs = rng.standard_normal((steps, layers, nkv * hd), dtype=np.float32)
+        lo = rank * per
+        kl = torch.from_numpy(np.ascontiguousarray(kp_full[:, lo:lo + per])).cuda()
+        vl = torch.from_numpy(np.ascontiguousarray(vp_full[:, lo:lo + per])).cuda()
+        pg = shard.PeerGather(dist, tqk, layers, per * group * hd)
+        outs = []
+        for s in range(steps):
+            q = torch.from_numpy(shard.head_split_slice(qs[s], layers, nq, hd, rank, world)).cuda()
+            k = torch.from_numpy(shard.head_split_slice(ks[s], layers, nkv, hd, rank, world)).cuda()
+            v = torch.from_numpy(shard.head_split_slice(vs[s], layers, nkv, hd, rank, world)).cuda()
+            out = torch.full((layers, nq * hd), float("nan"), device="cuda")
+            slot = pg.begin()
+            tqk.decode(shard.head_split_args(tqk, kl, vl, layers, nq, nkv, hd, mt, world, q, slot, len0=pos + s + 1,
+                                             k_new=k, v_new=v))
+            pg.end(out)
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
+        refs = []
+        for s in range(steps):
+            ref = np.empty((layers, nq * hd), np.float32)
+            for layer in range(layers):
+                assert port_.store_kv(kp_full[layer], vp_full[layer], nkv, hd, mt, pos + s, ks[s, layer],
+                                      vs[s, layer]) == 0
+                ref[layer] = port_.attend(kp_full[layer], vp_full[layer], nq, nkv, hd, mt, pos + s, qs[s, layer])
+            refs.append(ref)
+        rows_ok = np.array_equal(kl.cpu().numpy(), kp_full[:, lo:lo + per]) and \
+            np.array_equal(vl.cpu().numpy(), vp_full[:, lo:lo + per])
+        np.save(os.path.join(result_dir, f"heads_rank{rank}.npy"), np.stack([np.stack(outs), np.stack(refs)]))
+        with open(os.path.join(result_dir, f"heads_rank{rank}.txt"), "w") as f:
+            f.write(f"{int(rows_ok)} {tqk.device_status()}")
+    finally:
+        if pg is not None:
+            pg.close()
+        dist.destroy_process_group()
+
+
+def test_head_split_gather_two_gpus(cuda, tmp_path):
+    """The kv-head-group split over 2 GPUs against the oracle: every rank's gathered output of
+    every layer and step within the attention tolerance of the oracle's store_kv + attend_q8,
+    and each rank's appended cache rows bit-exact."""
+    import torch
+    import torch.multiprocessing as mp
+    from _cases import tolerance_ok
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_rank_main_heads, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        rows_ok, status = (int(x) for x in open(tmp_path / f"heads_rank{r}.txt").read().split())
+        assert rows_ok == 1 and status == 0, (r, rows_ok, status)
+        got, ref = np.load(tmp_path / f"heads_rank{r}.npy")
+        for s in range(got.shape[0]):
+            ok, max_abs, rel = tolerance_ok(got[s], ref[s])
+            assert ok, f"rank {r} step {s}: max abs {max_abs:.3g} rel {rel:.3g}"
+
+
+def test_head_split_single_gpu_matches_oracle(cuda):
+    """The head-split item layout (two kv heads per item, spanning layers when a rank holds one
+    kv head per layer) on one GPU, for the shares of 2, 4 and 8 ranks emulated one after the
+    other, with a world-1 gather: each share's output equals the oracle's heads of it."""
+    import torch
+
+    import oracle
+    from _cases import tolerance_ok
+    from tailorquantkernel_b200 import shard, tqk
+    port_ = oracle.Oracle("port")
+    layers, nq, nkv, hd, pos = 4, 32, 8, 128, 300
+    mt = pos + 1
+    rng = np.random.default_rng(91)
+    kf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+    vf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+    kf[:, :, pos:] = 0.0
+    vf[:, :, pos:] = 0.0
+    kp_full, vp_full = port_.quantize_rows(kf), port_.quantize_rows(vf)
+    q = rng.standard_normal((layers, nq * hd), dtype=np.float32)
+    k = rng.standard_normal((layers, nkv * hd), dtype=np.float32)
+    v = rng.standard_normal((layers, nkv * hd), dtype=np.float32)
+    ref = np.empty((layers, nq * hd), np.float32)
+    kp_ref, vp_ref = kp_full.copy(), vp_full.copy()
+    for layer in range(layers):
+        assert port_.store_kv(kp_ref[layer], vp_ref[layer], nkv, hd, mt, pos, k[layer], v[layer]) == 0
+        ref[layer] = port_.attend(kp_ref[layer], vp_ref[layer], nq, nkv, hd, mt, pos, q[layer])
+    for world in (2, 4, 8):
+        per, group = nkv // world, nq // nkv
+        for rank in range(world):
+            lo = rank * per
+            kl = torch.from_numpy(np.ascontiguousarray(kp_full[:, lo:lo + per])).cuda()
+            vl = torch.from_numpy(np.ascontiguousarray(vp_full[:, lo:lo + per])).cuda()
+            ql = torch.from_numpy(shard.head_split_slice(q, layers, nq, hd, rank, world)).cuda()
+            kn = torch.from_numpy(shard.head_split_slice(k, layers, nkv, hd, rank, world)).cuda()
+            vn = torch.from_numpy(shard.head_split_slice(v, layers, nkv, hd, rank, world)).cuda()
+            chunk = per * group * hd
+            box = tqk.peer_buffer_alloc(tqk.tqk_gather_mailbox_bytes(1, layers, chunk))
+            try:
+                out = torch.full((layers, chunk), float("nan"), device="cuda")
+                slot = tqk.gather_slot(box, layers, chunk, 1)
+                tqk.decode(shard.head_split_args(tqk, kl, vl, layers, nq, nkv, hd, mt, world, ql, slot, len0=pos + 1,
+                                                 k_new=kn, v_new=vn))
+                tqk.exchange_gather(layers, chunk, 1, 0, [box], 1, out)
+                torch.cuda.synchronize()
+            finally:
+                tqk.peer_buffer_free(box)
+            want = shard.head_split_slice(ref, layers, nq, hd, rank, world)
+            ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), want)
+            assert ok, f"world {world} rank {rank}: max abs {max_abs:.3g} rel {rel:.3g}"
+            assert np.array_equal(kl.cpu().numpy(), kp_ref[:, lo:lo + per])
+            assert np.array_equal(vl.cpu().numpy(), vp_ref[:, lo:lo + per])
+    assert tqk.device_status() == 0
+
+
+def test_gather_wait_times_out_without_peer(cuda):
+    """tqk_exchange_gather's bounded wait, as the exchange's: a two-rank gather whose peer
+    mailbox nobody writes gives up after about a second, records the timeout and returns;
+    a one-rank gather afterwards works."""
+    import time
+
+    import torch
+    from tailorquantkernel_b200 import tqk
+    groups, chunk = 4, 256
+    boxes = [tqk.peer_buffer_alloc(tqk.tqk_gather_mailbox_bytes(2, groups, chunk)) for _ in range(2)]
+    solo = tqk.peer_buffer_alloc(tqk.tqk_gather_mailbox_bytes(1, groups, chunk))
+    try:
+        assert tqk.device_status(clear=True) == 0
+        out = torch.full((groups, 2 * chunk), float("nan"), device="cuda")
+        t0 = time.time()
+        tqk.exchange_gather(groups, chunk, 2, 0, boxes, 1, out)
+        torch.cuda.synchronize()
+        assert 0.5 < time.time() - t0 < 30
+        assert tqk.device_status(clear=True) == 1
+        assert torch.isnan(out).all()
+        out1 = torch.full((groups, chunk), float("nan"), device="cuda")
+        tqk.exchange_gather(groups, chunk, 1, 0, [solo], 1, out1)  # a zeroed slot gathers zeros
+        torch.cuda.synchronize()
+        assert torch.count_nonzero(out1).item() == 0
+        with pytest.raises(tqk.TQKError):
+            tqk.exchange_gather(groups, 3, 1, 0, [solo], 1, out1)  # chunk not a multiple of 4
+        assert tqk.device_status() == 0
+    finally:
+        for b in boxes + [solo]:
+            tqk.peer_buffer_free(b)

@@ -116,3 +116,119 @@ def test_two_gloo_ranks_sequence_split(tmp_path, n):
     for r in range(world):
         got = np.load(tmp_path / f"rank{r}.npy")
         np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12)
+
+
+# ---------------------------------------------------------------------------
+# kv-head-group split (bench config 2 on N GPUs): layout and gather
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_head_split_items_keep_the_gqa_mapping(world):
+    """shard.head_split_args hands a rank's kv heads of every layer to the kernel as items of two
+    kv heads.  Walking the items the way the kernel does (item i, kv head j of the item, q head h of
+    the item -> kv head h // group) must visit every (layer, q head) of the rank exactly once, each
+    paired with its own layer's kv head h_global // group, at the offsets the planes, q, out and the
+    appended rows really have."""
+    from tailorquantkernel_b200 import tqk
+    layers, nq, nkv, hd, mt = 32, 32, 8, 128, 4097
+    group, nb, per = nq // nkv, hd // 32, nkv // world
+    a = shard.head_split_args(tqk, 1 << 20, 1 << 21, layers, nq, nkv, hd, mt, world, 1 << 22, 1 << 23, len0=mt,
+                              k_new=1 << 24, v_new=1 << 25)
+    assert a.n_kv_heads * a.n_items == layers * per and a.n_q_heads == a.n_kv_heads * group
+    assert a.max_tokens == mt and a.len0 == mt and a.head_dim == hd
+    seen = set()
+    for rank in range(world):
+        for i in range(a.n_items):
+            for h in range(a.n_q_heads):
+                kvh = h // group  # the kernel's GQA rule inside an item
+                plane_row = (i * a.item_stride) // (mt * nb) + kvh          # kv-head row of the rank's planes
+                q_row = (i * a.q_item_stride) // hd + h                     # q-head row of the rank's q / out
+                assert a.q_item_stride == a.out_item_stride
+                assert (i * a.kv_new_item_stride) // hd + kvh == plane_row  # appended row of that kv head
+                layer, local_kv = divmod(plane_row, per)
+                q_layer, local_q = divmod(q_row, per * group)
+                assert q_layer == layer and local_q // group == local_kv
+                seen.add((rank, layer, rank * per * group + local_q))
+    assert len(seen) == world * layers * per * group == layers * nq  # every (layer, q head) of the job once
+
+
+def _rank_main_heads(rank, world, port, result_dir):
+    """float64 attention of this rank's kv heads (every layer), gathered with gloo into the
+    [layers][world][chunk] layout tqk_exchange_gather writes."""
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layers, nq, nkv, hd, n = 3, 8, 4, 16, 50
+        rng = np.random.default_rng(12)
+        q = rng.standard_normal((layers, nq * hd))
+        k = rng.standard_normal((layers, nkv, n, hd))
+        v = rng.standard_normal((layers, nkv, n, hd))
+        per, group = nkv // world, nq // nkv
+        ql = shard.head_split_slice(q, layers, nq, hd, rank, world).reshape(layers, per * group, hd)
+        lo = rank * per
+        local = np.empty((layers, per * group * hd))
+        for layer in range(layers):
+            rec = _attention_partial(ql[layer], k[layer, lo:lo + per], v[layer, lo:lo + per], 0, n, hd ** -0.5)
+            local[layer] = (rec[:, :hd] / rec[:, hd + 1:hd + 2]).reshape(-1)
+        parts = [torch.empty(layers, per * group * hd, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(local))
+        out = torch.stack(parts, 1).reshape(layers, nq * hd)  # out[g][r][:] = rank r's group g
+        np.save(os.path.join(result_dir, f"heads{rank}.npy"), out.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_head_split(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_rank_main_heads, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    layers, nq, nkv, hd, n = 3, 8, 4, 16, 50
+    rng = np.random.default_rng(12)
+    q = rng.standard_normal((layers, nq * hd))
+    k = rng.standard_normal((layers, nkv, n, hd))
+    v = rng.standard_normal((layers, nkv, n, hd))
+    ref = np.empty((layers, nq * hd))
+    for layer in range(layers):
+        rec = _attention_partial(q[layer].reshape(nq, hd), k[layer], v[layer], 0, n, hd ** -0.5)
+        ref[layer] = (rec[:, :hd] / rec[:, hd + 1:hd + 2]).reshape(-1)
+    for r in range(world):
+        np.testing.assert_allclose(np.load(tmp_path / f"heads{r}.npy"), ref, rtol=1e-12, atol=1e-12)
+
+
+# ---------------------------------------------------------------------------
+# failure detection on the host: a rank that leaves between steps
+# ---------------------------------------------------------------------------
+def _rank_main_leaver(rank, world, port, result_dir):
+    """Rank 1 runs one step and then leaves (returns without taking part in the next step's
+    collective, as a crashed or killed rank would); rank 0's next exchange must end with an
+    error within the process group's short timeout instead of waiting for good."""
+    import time
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    q, k, v = _problem(200)
+    s, ln = shard.seq_range(200, rank, world)
+    local = torch.from_numpy(_attention_partial(q, k, v, s, s + ln, 128 ** -0.5).reshape(-1))
+    shard.gather_partials(dist, local)  # step 1: every rank
+    if rank == 1:
+        return  # leaves between steps, with nothing in flight
+    t0 = time.time()
+    try:
+        shard.gather_partials(dist, local)  # step 2: the peer never joins
+        outcome = "completed"
+    except Exception as e:  # noqa: BLE001  (gloo raises RuntimeError / DistBackendError)
+        outcome = f"error {type(e).__name__}"
+    with open(os.path.join(result_dir, "leaver.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.time() - t0:.2f}\n")
+
+
+def test_rank_leaving_between_steps_errors_instead_of_hanging(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_rank_main_leaver, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    outcome, waited = open(tmp_path / "leaver.txt").read().split("\n")[:2]
+    assert outcome.startswith("error"), outcome
+    assert float(waited) < 60.0
