@@ -377,6 +377,52 @@ TQK_API int tqk_ipc_close_handle(void *ptr);
 TQK_API int tqk_exchange_merge(int n_heads, int head_dim, int world, int rank, void *const *mailboxes, int epoch,
                        float *out, tqk_stream_t stream);
 
+/* The kv-head-group split with its gather fused into the decode (the
+ * multi-GPU form of attend_q8's loop over kv heads, reference
+ * model/attention_layer.c:134-149; the reference's one CPU has no such step).
+ * Rank `rank` of `world` decodes its share of the kv heads of every layer
+ * (arguments as for tqk_decode_q8, normalised output only), and every unit's
+ * finishing CTA writes the unit's output heads straight into every rank's
+ * buffer -- over NVLink for the peers -- as {value bits, epoch} pairs of 8
+ * bytes, each one store, so that a reader that sees a pair's epoch sees its
+ * value: no fence and no flag is needed (a system-scope fence per unit, or
+ * even per launch, costs several microseconds on this path).
+ *   out[r]: rank r's pair buffer as mapped in this process (r == rank: the
+ *     local one), 8-byte aligned, [n_groups][world][chunk_heads][head_dim]
+ *     pairs, where the rank's local flat q head f = item * n_q_heads + h lands
+ *     in group f / chunk_heads at position f % chunk_heads of the rank's chunk
+ *     (for the split of a layer stack: a group is a layer, chunk_heads the
+ *     rank's q heads per layer, and the buffer is [layers][n_q_total][hd]);
+ *   epoch: the step's number, >= 1, written with every value.
+ * tqk_gather_collect then turns the local pairs into the plain output once
+ * every pair shows the epoch.  Buffers must be reachable from this device
+ * (tqk_peer_buffer_alloc + tqk_ipc_open_handle).  Never uses the balanced
+ * schedule (equal lengths use the fixed split anyway).  A caller that reuses
+ * a buffer across steps must make sure no rank's next step writes it before
+ * every rank has collected it: pair buffers double-buffered by step parity
+ * are enough, since a rank's step e + 2 starts only after it has collected
+ * step e + 1, which needs every rank's step e + 1 pairs, which each rank
+ * writes only after it has collected step e (shard.py, PeerHeadSplit). */
+typedef struct {
+    int world, rank;                  /* world <= 8 */
+    void *out[8];
+    int chunk_heads;
+    int epoch;
+} tqk_gather_dst;
+TQK_API int tqk_decode_q8_gather(const tqk_decode_args *a, const tqk_gather_dst *g, void *workspace,
+                                 size_t workspace_bytes, tqk_stream_t stream);
+/* Head units (the kernels' unit of work) of a tqk_decode_q8_gather call with
+ * these arguments. */
+TQK_API int tqk_decode_unit_count(const tqk_decode_args *a, int *units);
+/* Waits on the stream until each of the n {value bits, epoch} pairs at `pairs`
+ * (device memory, 8-byte aligned) shows `epoch`, and writes the values to
+ * out[0..n).  Each thread waits at most 1 s in all, then records TQK_ETIMEOUT
+ * in the device error word and leaves the value it has (out is then
+ * undefined).  At its end it also waits for the kernel launched before it on
+ * the stream to complete, so that the next launch may reuse that kernel's
+ * workspace. */
+TQK_API int tqk_gather_collect(const void *pairs, size_t n, int epoch, float *out, tqk_stream_t stream);
+
 /* The kv-head-group split's gather over peer memory (the multi-GPU form of
  * attend_q8's loop over kv heads, reference model/attention_layer.c:134-149,
  * whose one CPU needs no such step).  Each rank attends to its own kv heads

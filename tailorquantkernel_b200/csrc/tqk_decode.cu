@@ -30,8 +30,26 @@ constexpr int DEC_THREADS = 128;
 constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_T = 64;          // tokens per tile
 constexpr int MAX_SPLITS = 128;    // bound on splits per (item, kv head)
-constexpr int MERGE_GROUP = 8;     // splits merged per first-level group
-constexpr int TICKETS_PER_UNIT = 1 + MAX_SPLITS / MERGE_GROUP;  // final ticket + one per group
+constexpr int MERGE_GROUP = 16;    // up to 16 splits merge in one level; more in groups of 16
+// ints per (item, head unit) in the ticket region: the final ticket and one per
+// group; the stride is kept at 17 so that caller workspaces keep their layout
+constexpr int TICKETS_PER_UNIT = 17;
+static_assert(1 + (MAX_SPLITS + MERGE_GROUP - 1) / MERGE_GROUP <= TICKETS_PER_UNIT, "ticket block too small");
+
+// Number of splits of an item of len tokens at split tokens per split: the
+// whole splits, plus one for a remainder above a quarter split; a smaller
+// remainder joins the last whole split, so that no CTA is spent on a sliver
+// (4097 tokens at 256 per split are 16 splits, the last of 257 tokens, not
+// 17).  Non-decreasing in len.  Split s covers [s*split, s*split + split),
+// the last one [s*split, len).
+__host__ __device__ __forceinline__ int n_splits_of(int len, int split) {
+    if (len <= 0) return 0;
+    const int n = len / split, rem = len - n * split;
+    return n == 0 ? 1 : n + (rem > split / 4 ? 1 : 0);
+}
+__host__ __device__ __forceinline__ int split_end(int s, int n_splits, int split, int len) {
+    return s == n_splits - 1 ? len : (s + 1) * split;
+}
 constexpr uint64_t WAIT_NS = 1000000000ull;   // 1 s bound on any mbarrier wait
 constexpr uint64_t DRAIN_NS = 20000000ull;    // 20 ms bound when draining after a timeout
 
@@ -62,7 +80,29 @@ struct DecodeParams {
     int *counters;               // tickets: [n_items][pairs][TICKETS_PER_UNIT]; balanced: [..][tickets_per_unit]
     int *err;
     int tickets_per_unit;        // balanced schedule only
+    // fused gather of the kv-head-group split (tqk_decode_q8_gather; g_world == 0: off).  The
+    // normalised output of local flat q head f = item * n_q_heads + qh goes to every rank r's
+    // buffer g_out[r] at [f / g_chunk][g_rank][f % g_chunk][HD] as {value bits, g_epoch} pairs,
+    // each written by one 8-byte store, so a reader that sees the epoch sees the value.
+    int g_world, g_rank, g_chunk, g_epoch;
+    uint2 *g_out[8];
 };
+
+// One element of the call's normalised output: head qh (of the item) column c.
+template <int HD>
+__device__ __forceinline__ void store_out(const DecodeParams &p, float *out_item, int item, int qh, int c, float v) {
+    if (p.g_world == 0) {
+        out_item[(long long)qh * HD + c] = v;
+        return;
+    }
+    const long long f = (long long)item * (p.n_kv * p.group) + qh;
+    const long long grp = f / p.g_chunk, w = f - grp * p.g_chunk;
+    const long long off = ((grp * p.g_world + p.g_rank) * p.g_chunk + w) * HD + c;
+    for (int r = 0; r < p.g_world; r++)  // one 8-byte store per rank, over NVLink for the peers
+        asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p.g_out[r] + off), "r"(__float_as_uint(v)),
+                     "r"(p.g_epoch)
+                     : "memory");
+}
 
 template <int NB>
 constexpr int stages_for() { return NB >= 8 ? 2 : 3; }
@@ -195,7 +235,7 @@ __device__ __forceinline__ bool last_arrival(int *ticket, int n, int tid, int *f
 template <int HD, int GROWS, int NT, int BAR>
 __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, int first, int stride, int n, int G,
                                             int tid, float *wts, float *ms, float *ls, bool to_part, float *out_item,
-                                            int qh0) {
+                                            int item, int qh0) {
     constexpr int RS = HD + 2;
     constexpr int EPT = (GROWS * HD + NT - 1) / NT;
     constexpr int KB = EPT >= 64 ? 1 : 64 / EPT;  // slots per batch of loads in flight
@@ -262,7 +302,7 @@ __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, in
             d[c] = a[e];
             if (c == 0) { d[HD] = ms[g]; d[HD + 1] = ls[g]; }
         } else if (p.out_mode == TQK_OUT_NORMALIZED) {
-            out_item[(long long)(qh0 + g) * HD + c] = a[e] / ls[g];
+            store_out<HD>(p, out_item, item, qh0 + g, c, a[e] / ls[g]);
         } else {
             float *o = out_item + (long long)(qh0 + g) * RS;
             o[c] = a[e];
@@ -286,15 +326,15 @@ __device__ __forceinline__ void merge_slots(const DecodeParams &p, float *pb, in
 // ticket block ([0] final, [1 + i] group i).
 template <int HD, int GROWS, int NT, int BAR, typename AccFn>
 __device__ __forceinline__ void finish_split_at(const DecodeParams &p, int tid, float *pb, int *tickets, int s,
-                                                int n_splits, int qh0, int G, float *out_item, AccFn acc, float *ms,
-                                                float *ls, float *wts, int *flag) {
+                                                int n_splits, int item, int qh0, int G, float *out_item, AccFn acc,
+                                                float *ms, float *ls, float *wts, int *flag) {
     const bool single = n_splits == 1;
     for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, c = i - g * HD;
         const float a = acc(g, c);
         if (single) {
             if (p.out_mode == TQK_OUT_NORMALIZED) {
-                out_item[(long long)(qh0 + g) * HD + c] = a / ls[g];
+                store_out<HD>(p, out_item, item, qh0 + g, c, a / ls[g]);
             } else {
                 float *o = out_item + (long long)(qh0 + g) * (HD + 2);
                 o[c] = a;
@@ -312,14 +352,15 @@ __device__ __forceinline__ void finish_split_at(const DecodeParams &p, int tid, 
         const int gi = s / MERGE_GROUP, first = gi * MERGE_GROUP;
         const int gsz = min(MERGE_GROUP, n_splits - first);
         if (!last_arrival<BAR, NT>(tickets + 1 + gi, gsz, tid, flag)) return;
-        merge_slots<HD, GROWS, NT, BAR>(p, pb, first, 1, gsz, G, tid, wts, ms, ls, true, out_item, qh0);
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, first, 1, gsz, G, tid, wts, ms, ls, true, out_item, item, qh0);
         if (tid == 0) tickets[1 + gi] = 0;
         const int n_groups = (n_splits + MERGE_GROUP - 1) / MERGE_GROUP;
         if (!last_arrival<BAR, NT>(tickets, n_groups, tid, flag)) return;
-        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, MERGE_GROUP, n_groups, G, tid, wts, ms, ls, false, out_item, qh0);
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, MERGE_GROUP, n_groups, G, tid, wts, ms, ls, false, out_item, item,
+                                        qh0);
     } else {
         if (!last_arrival<BAR, NT>(tickets, n_splits, tid, flag)) return;
-        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, 1, n_splits, G, tid, wts, ms, ls, false, out_item, qh0);
+        merge_slots<HD, GROWS, NT, BAR>(p, pb, 0, 1, n_splits, G, tid, wts, ms, ls, false, out_item, item, qh0);
     }
     if (tid == 0) tickets[0] = 0;  // ready for the next launch
 }
@@ -332,8 +373,8 @@ __device__ __forceinline__ void finish_split(const DecodeParams &p, int tid, int
                                              float *wts, int *flag) {
     const long long unit = (long long)item * p.pairs + pair;
     finish_split_at<HD, GROWS, NT, BAR>(p, tid, p.part + unit * p.max_splits * GROWS * (HD + 2),
-                                        p.counters + unit * TICKETS_PER_UNIT, s, n_splits, qh0, G, out_item, acc, ms,
-                                        ls, wts, flag);
+                                        p.counters + unit * TICKETS_PER_UNIT, s, n_splits, item, qh0, G, out_item, acc,
+                                        ms, ls, wts, flag);
 }
 
 template <int NB, int GMAX>
@@ -364,11 +405,10 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
         len = len < 0 ? 0 : p.max_tokens;
     }
-    int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
+    int n_splits = n_splits_of(len, p.split_tokens);
     if (n_splits > p.max_splits) {  // a device length above the max_len the grid was sized for
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
-        n_splits = p.max_splits;
-        len = p.max_splits * p.split_tokens;
+        n_splits = p.max_splits;    // the last split then runs to len (<= max_tokens)
     }
     const int s = blockIdx.x;
     if (s >= (n_splits > 0 ? n_splits : 1)) return;
@@ -379,7 +419,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
         for (int i = tid; i < G * HD; i += DEC_THREADS) {
             const int g = i / HD, c = i - g * HD;
             if (p.out_mode == TQK_OUT_NORMALIZED) {
-                out_item[(long long)(qh0 + g) * HD + c] = 0.0f;
+                store_out<HD>(p, out_item, item, qh0 + g, c, 0.0f);
             } else {
                 float *o = out_item + (long long)(qh0 + g) * (HD + 2);
                 o[c] = 0.0f;
@@ -390,7 +430,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_q8_kernel(const DecodePara
     }
 
     const int t_begin = s * p.split_tokens;
-    const int t_end = min(len, t_begin + p.split_tokens);
+    const int t_end = split_end(s, n_splits, p.split_tokens, len);
     const int n_tiles = (t_end - t_begin + DEC_T - 1) / DEC_T;
     const long long head_off = (long long)kvh * p.max_tokens * ROW;
     const uint8_t *kbase = p.k + (long long)item * p.item_stride + head_off;
@@ -868,7 +908,7 @@ size_t counters_region(int n_items, int units) {
     return b;
 }
 
-int make_plan(const tqk_decode_args *a, Plan *pl) {
+int make_plan(const tqk_decode_args *a, Plan *pl, bool gather = false) {
     if (!a) return fail(TQK_EINVAL, "decode: NULL args");
     if (a->n_items <= 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0 || a->head_dim <= 0 || a->max_tokens <= 0)
         return fail(TQK_EINVAL, "decode: non-positive shape");
@@ -922,7 +962,7 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
         // the balanced schedule pays a segment switch mid-run; it wins where the
         // fixed split cannot even out the work: unequal lengths across items
         const bool ragged = a->n_items > 1 && (a->lens != nullptr || a->len_step != 0);
-        const bool balanced = pl->pack && ragged && a->n_items <= BAL_MAX_ITEMS;
+        const bool balanced = !gather && pl->pack && ragged && a->n_items <= BAL_MAX_ITEMS;
         int occ = 0;
         DecodeParams dummy{};
         const int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ, balanced)
@@ -961,9 +1001,9 @@ int make_plan(const tqk_decode_args *a, Plan *pl) {
     }
     split = ((split + DEC_T - 1) / DEC_T) * DEC_T;
     if (split < DEC_T) split = DEC_T;
-    while ((max_len + split - 1) / split > MAX_SPLITS) split += DEC_T;
+    while (n_splits_of(max_len, split) > MAX_SPLITS) split += DEC_T;
     pl->split_tokens = split;
-    pl->max_splits = max_len > 0 ? (max_len + split - 1) / split : 1;
+    pl->max_splits = max_len > 0 ? n_splits_of(max_len, split) : 1;
     if (pl->max_splits > 1) {
         pl->counters_bytes = counters_region(a->n_items, pl->pairs);
         pl->part_bytes = (size_t)a->n_items * pl->pairs * pl->max_splits * pl->gmax * (a->head_dim + 2) * sizeof(float);
@@ -1028,10 +1068,14 @@ extern "C" int tqk_decode_workspace_size(const tqk_decode_args *a, size_t *bytes
     return TQK_OK;
 }
 
-extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes,
-                             tqk_stream_t stream) {
+namespace tqk {
+namespace {
+
+// tqk_decode_q8 and tqk_decode_q8_gather: the plan, the scratch and the launch.
+int decode_impl(const tqk_decode_args *a, const tqk_gather_dst *gd, void *workspace, size_t workspace_bytes,
+                tqk_stream_t stream) {
     Plan pl;
-    int rc = make_plan(a, &pl);  // validates before touching the device
+    int rc = make_plan(a, &pl, gd != nullptr);  // validates before touching the device
     if (rc) return rc;
     rc = ensure_device();
     if (rc) return rc;
@@ -1056,10 +1100,50 @@ extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t w
     p.counters = counters;
     p.part = part;
     p.err = device_info()->err_word;
+    if (gd) {
+        p.g_world = gd->world;
+        p.g_rank = gd->rank;
+        p.g_chunk = gd->chunk_heads;
+        p.g_epoch = gd->epoch;
+        for (int r = 0; r < gd->world; r++) p.g_out[r] = reinterpret_cast<uint2 *>(gd->out[r]);
+    }
     if (pl.balanced) return dispatch_pack(pl.nb, p, dim3((unsigned)pl.bal_ctas), st, nullptr, true);
     const dim3 grid((unsigned)pl.max_splits, (unsigned)pl.pairs, (unsigned)a->n_items);
     if (pl.pack) return dispatch_pack(pl.nb, p, grid, st, nullptr);
     return pl.mma ? dispatch_mma(pl.nb, pl.gmax, p, grid, st, nullptr) : dispatch(pl.nb, pl.gmax, p, grid, st, nullptr);
+}
+
+}  // namespace
+}  // namespace tqk
+
+extern "C" int tqk_decode_q8(const tqk_decode_args *a, void *workspace, size_t workspace_bytes,
+                             tqk_stream_t stream) {
+    return decode_impl(a, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int tqk_decode_unit_count(const tqk_decode_args *a, int *units) {
+    if (!units) return fail(TQK_EINVAL, "tqk_decode_unit_count: NULL units");
+    Plan pl;
+    int rc = make_plan(a, &pl, true);
+    if (rc) return rc;
+    *units = a->n_items * pl.pairs;
+    return TQK_OK;
+}
+
+extern "C" int tqk_decode_q8_gather(const tqk_decode_args *a, const tqk_gather_dst *g, void *workspace,
+                                    size_t workspace_bytes, tqk_stream_t stream) {
+    if (!a || !g) return fail(TQK_EINVAL, "tqk_decode_q8_gather: NULL arguments");
+    if (g->world < 1 || g->world > 8 || g->rank < 0 || g->rank >= g->world || g->chunk_heads <= 0)
+        return fail(TQK_EINVAL, "tqk_decode_q8_gather: bad world, rank or chunk_heads");
+    if (a->out_mode != TQK_OUT_NORMALIZED)
+        return fail(TQK_EINVAL, "tqk_decode_q8_gather: the gather carries normalised outputs only");
+    if (((long long)a->n_items * a->n_q_heads) % g->chunk_heads)
+        return fail(TQK_EINVAL, "tqk_decode_q8_gather: n_items * n_q_heads must be a multiple of chunk_heads");
+    if (g->epoch < 1) return fail(TQK_EINVAL, "tqk_decode_q8_gather: epochs count from 1");
+    for (int r = 0; r < g->world; r++)
+        if (!g->out[r] || (reinterpret_cast<uintptr_t>(g->out[r]) & 7))
+            return fail(TQK_EALIGN, "tqk_decode_q8_gather: every rank needs an 8-byte aligned output buffer");
+    return decode_impl(a, g, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

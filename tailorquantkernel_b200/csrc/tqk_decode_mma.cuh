@@ -386,11 +386,10 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
         len = len < 0 ? 0 : p.max_tokens;
     }
-    int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
-    if (n_splits > p.max_splits) {
+    int n_splits = n_splits_of(len, p.split_tokens);
+    if (n_splits > p.max_splits) {  // a device length above the max_len the grid was sized for
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
-        n_splits = p.max_splits;
-        len = p.max_splits * p.split_tokens;
+        n_splits = p.max_splits;    // the last split then runs to len (<= max_tokens)
     }
     const int s = blockIdx.x;
     if (s >= (n_splits > 0 ? n_splits : 1)) return;
@@ -401,7 +400,7 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
         for (int i = tid; i < G * HD; i += MMA_THREADS) {
             const int g = i / HD, c = i - g * HD;
             if (p.out_mode == TQK_OUT_NORMALIZED) {
-                out_item[(long long)(qh0 + g) * HD + c] = 0.0f;
+                store_out<HD>(p, out_item, item, qh0 + g, c, 0.0f);
             } else {
                 float *o = out_item + (long long)(qh0 + g) * (HD + 2);
                 o[c] = 0.0f;
@@ -412,7 +411,7 @@ __global__ void __launch_bounds__(MMA_THREADS) decode_q8_mma_kernel(const Decode
     }
 
     const int t_begin = s * p.split_tokens;
-    const int t_end = min(len, t_begin + p.split_tokens);
+    const int t_end = split_end(s, n_splits, p.split_tokens, len);
     const int n_tiles = (t_end - t_begin + MMA_T - 1) / MMA_T;
     const long long head_off = (long long)kvh * p.max_tokens * ROW;
     const uint8_t *kbase = p.k + (long long)item * p.item_stride + head_off;

@@ -449,11 +449,10 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
         len = len < 0 ? 0 : p.max_tokens;
     }
-    int n_splits = (len + p.split_tokens - 1) / p.split_tokens;
-    if (n_splits > p.max_splits) {
+    int n_splits = n_splits_of(len, p.split_tokens);
+    if (n_splits > p.max_splits) {  // a device length above the max_len the grid was sized for
         if (tid == 0) record_error(p.err, DEVERR_BADLEN);
-        n_splits = p.max_splits;
-        len = p.max_splits * p.split_tokens;
+        n_splits = p.max_splits;    // the last split then runs to len (<= max_tokens)
     }
     const int s = blockIdx.x;
     if (s >= (n_splits > 0 ? n_splits : 1)) return;
@@ -464,7 +463,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         for (int i = tid; i < G * HD; i += PK_THREADS) {
             const int g = i / HD, c = i - g * HD;
             if (p.out_mode == TQK_OUT_NORMALIZED) {
-                out_item[(long long)(qh0 + g) * HD + c] = 0.0f;
+                store_out<HD>(p, out_item, item, qh0 + g, c, 0.0f);
             } else {
                 float *o = out_item + (long long)(qh0 + g) * (HD + 2);
                 o[c] = 0.0f;
@@ -475,7 +474,7 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     }
 
     const int t_begin = s * p.split_tokens;
-    const int t_end = min(len, t_begin + p.split_tokens);
+    const int t_end = split_end(s, n_splits, p.split_tokens, len);
     const int n_tiles = (t_end - t_begin + PK_T - 1) / PK_T;
     const long long head_bytes = (long long)p.max_tokens * ROW;
     const long long off_a = (long long)item * p.item_stride + (long long)kvh_a * head_bytes;
@@ -842,7 +841,8 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_bal_ke
         int *tickets = p.counters + unit * p.tickets_per_unit;
         float *out_item = p.out + (long long)sg.item * p.out_item_stride;
         auto acc_of = [&](int gg, int cc) { return red.acc<L::RED_STRIDE>(gg, cc); };
-        finish_split_at<HD, G, PK_WARPS * 32, 1>(p, tid, pb, tickets, cn - c0, c1 - c0 + 1, 2 * sg.pair * p.group, G,
+        finish_split_at<HD, G, PK_WARPS * 32, 1>(p, tid, pb, tickets, cn - c0, c1 - c0 + 1, sg.item,
+                                                 2 * sg.pair * p.group, G,
                                                  out_item, acc_of, red.fm(), red.fl(), red.red, flag);
         gt = sg.ubase + sg.lt1;
         if (gt >= g1n) break;

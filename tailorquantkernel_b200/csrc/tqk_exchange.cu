@@ -209,6 +209,49 @@ __global__ void __launch_bounds__(GATHER_THREADS) exchange_gather_kernel(const G
     }
 }
 
+__device__ __forceinline__ uint2 ld_relaxed_sys_v2(const uint2 *p) {
+    uint2 v;
+    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// tqk_gather_collect: every thread loads its {value, epoch} pairs, re-reads a
+// pair (bounded: 1 s in all) until it shows the step's epoch, and writes the
+// value.  Then the grid waits for the kernel before it on the stream (the
+// decode that wrote this rank's own pairs) to complete, so that the stream's
+// next kernel may reuse that decode's workspace.
+constexpr int COLLECT_THREADS = 256, COLLECT_PER = 4;
+
+__global__ void __launch_bounds__(COLLECT_THREADS) gather_collect_kernel(const uint2 *pairs, long long n, int epoch,
+                                                                        float *out, int *err) {
+    const long long base = (long long)blockIdx.x * COLLECT_THREADS * COLLECT_PER + threadIdx.x;
+    uint2 v[COLLECT_PER];
+#pragma unroll
+    for (int k = 0; k < COLLECT_PER; k++) {
+        const long long i = base + (long long)k * COLLECT_THREADS;
+        if (i < n) v[k] = ld_relaxed_sys_v2(pairs + i);
+    }
+    bool ok = true;
+    uint64_t t0 = 0;
+#pragma unroll
+    for (int k = 0; k < COLLECT_PER; k++) {
+        const long long i = base + (long long)k * COLLECT_THREADS;
+        if (i >= n) continue;
+        for (uint32_t it = 0; ok && v[k].y != (uint32_t)epoch; it++) {
+            if (t0 == 0) t0 = globaltimer_ns();
+            if ((it & 15u) == 15u && globaltimer_ns() - t0 > EX_WAIT_NS) {
+                record_error(err, DEVERR_TIMEOUT);
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+            v[k] = ld_relaxed_sys_v2(pairs + i);
+        }
+        out[i] = __uint_as_float(v[k].x);
+    }
+    grid_dependency_wait();
+}
+
 }  // namespace
 }  // namespace tqk
 
@@ -339,4 +382,17 @@ extern "C" int tqk_exchange_gather(int n_groups, int chunk_floats, int world, in
     p.err = device_info()->err_word;
     return launch_pdl(exchange_gather_kernel, dim3((unsigned)n_groups), dim3(GATHER_THREADS), 0, (cudaStream_t)stream,
                       p);
+}
+
+extern "C" int tqk_gather_collect(const void *pairs, size_t n, int epoch, float *out, tqk_stream_t stream) {
+    if (!pairs || !out || (reinterpret_cast<uintptr_t>(pairs) & 7) || epoch < 1)
+        return fail(TQK_EINVAL, "tqk_gather_collect: bad pairs, out or epoch");
+    if (n == 0) return TQK_OK;
+    int rc = ensure_device();
+    if (rc) return rc;
+    const long long per_block = (long long)COLLECT_THREADS * COLLECT_PER;
+    const long long blocks = ((long long)n + per_block - 1) / per_block;
+    if (blocks > 0x7fffffffLL) return fail(TQK_EINVAL, "tqk_gather_collect: n too large");
+    return launch_pdl(gather_collect_kernel, dim3((unsigned)blocks), dim3(COLLECT_THREADS), 0, (cudaStream_t)stream,
+                      static_cast<const uint2 *>(pairs), (long long)n, epoch, out, device_info()->err_word);
 }

@@ -236,6 +236,38 @@ class PeerGather(_PeerMailboxes):
         return out
 
 
+class PeerHeadSplit(_PeerMailboxes):
+    """The kv-head-group split with the gather fused into the decode
+    (tqk_decode_q8_gather).  Every rank's peer buffer holds two pair buffers
+    by step parity, [n_groups][world][chunk_heads][head_dim] {value, epoch}
+    pairs each.  A step decodes this rank's heads, the decode writing every
+    unit's output into every rank's pair buffer of the step's parity, then
+    tqk_gather_collect waits until every local pair shows the step's epoch and
+    writes the plain output [n_groups][world * chunk_heads * head_dim] floats.
+    Parity buffers make the reuse safe: a rank's step e + 2 writes a buffer
+    only after it has collected its step e + 1, which needs every rank's pairs
+    of e + 1, which each rank writes only after it has collected step e."""
+
+    def __init__(self, dist, tqk, n_groups: int, chunk_heads: int, head_dim: int, group=None):
+        import torch
+        world = dist.get_world_size(group)
+        self.n_groups, self.chunk_heads, self.head_dim = n_groups, chunk_heads, head_dim
+        self.n = n_groups * world * chunk_heads * head_dim
+        self.pair_bytes = (self.n * 8 + 255) // 256 * 256
+        super().__init__(dist, tqk, 2 * self.pair_bytes, group)
+        self.out = torch.empty(n_groups, world * chunk_heads * head_dim, device="cuda")
+
+    def step(self, args, workspace=None, stream=None):
+        """One step: returns the output tensor (ready once the stream reaches this point)."""
+        self.epoch += 1
+        off = (self.epoch & 1) * self.pair_bytes
+        dst = self.tqk.gather_dst(self.world, self.rank, [m + off for m in self.mailboxes], self.chunk_heads,
+                                  self.epoch)
+        self.tqk.decode_gather(args, dst, workspace=workspace, stream=stream)
+        self.tqk.gather_collect(self.local + off, self.n, self.epoch, self.out, stream=stream)
+        return self.out
+
+
 def seqsplit_attend_p2p(exchange: PeerExchange, tqk, k_local, v_local, n_q: int, n_kv: int, head_dim: int,
                         n_local: int, q, out, stream=None):
     """seqsplit_attend with the exchange over peer memory: decode of this rank's

@@ -142,6 +142,15 @@ tqk_ipc_open_handle = _sig("tqk_ipc_open_handle", [ctypes.c_char_p, ctypes.POINT
 tqk_ipc_close_handle = _sig("tqk_ipc_close_handle", [_vp])
 tqk_exchange_slot_offset = _sig("tqk_exchange_slot_offset", [_i, _i, _i], _sz)
 tqk_exchange_merge = _sig("tqk_exchange_merge", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+class GatherDst(ctypes.Structure):
+    """Mirror of tqk_gather_dst (include/tqk.h)."""
+    _fields_ = [("world", _i), ("rank", _i), ("out", _vp * 8), ("chunk_heads", _i), ("epoch", _i)]
+
+
+tqk_decode_q8_gather = _sig("tqk_decode_q8_gather", [ctypes.POINTER(DecodeArgs), ctypes.POINTER(GatherDst), _vp, _sz,
+                                                      _vp])
+tqk_decode_unit_count = _sig("tqk_decode_unit_count", [ctypes.POINTER(DecodeArgs), ctypes.POINTER(_i)])
+tqk_gather_collect = _sig("tqk_gather_collect", [_vp, _sz, _i, _vp, _vp])
 tqk_gather_mailbox_bytes = _sig("tqk_gather_mailbox_bytes", [_i, _i, _i], _sz)
 tqk_gather_slot_offset = _sig("tqk_gather_slot_offset", [_i, _i, _i], _sz)
 tqk_exchange_gather = _sig("tqk_exchange_gather", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
@@ -161,6 +170,7 @@ EXPORTED = [
     "tqk_ipc_get_handle",
     "tqk_ipc_open_handle", "tqk_ipc_close_handle", "tqk_exchange_merge",
     "tqk_gather_mailbox_bytes", "tqk_gather_slot_offset", "tqk_exchange_gather",
+    "tqk_decode_q8_gather", "tqk_decode_unit_count", "tqk_gather_collect",
 ]
 
 
@@ -418,6 +428,51 @@ def exchange_gather(n_groups, chunk_floats, world, rank, mailboxes, epoch, out, 
     arr = (_vp * len(mailboxes))(*mailboxes)
     check(tqk_exchange_gather(n_groups, chunk_floats, world, rank, arr, epoch, _ptr(out), _stream(stream)),
           "tqk_exchange_gather")
+
+
+def gather_dst(world: int, rank: int, outs, chunk_heads: int, epoch: int) -> GatherDst:
+    """tqk_gather_dst: every rank's pair buffer as mapped in this process, for the step `epoch` (>= 1)."""
+    d = GatherDst()
+    d.world, d.rank, d.chunk_heads, d.epoch = world, rank, chunk_heads, epoch
+    for r in range(world):
+        d.out[r] = outs[r]
+    return d
+
+
+def decode_gather(args: DecodeArgs, dst: GatherDst, workspace=None, stream=None) -> None:
+    """tqk_decode_q8_gather: the decode with every unit's output pushed to every rank's buffer."""
+    ws = _ptr(workspace) if workspace is not None else None
+    nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(tqk_decode_q8_gather(ctypes.byref(args), ctypes.byref(dst), ws, nbytes, _stream(stream)),
+          "tqk_decode_q8_gather")
+
+
+def decode_unit_count(args: DecodeArgs) -> int:
+    n = _i(0)
+    check(tqk_decode_unit_count(ctypes.byref(args), ctypes.byref(n)), "tqk_decode_unit_count")
+    return n.value
+
+
+def gather_collect(pairs: int, n: int, epoch: int, out, stream=None) -> None:
+    """tqk_gather_collect: waits until the n {value, epoch} pairs at device address `pairs` show the
+    epoch and writes the values to out."""
+    check(tqk_gather_collect(pairs, n, epoch, _ptr(out), _stream(stream)), "tqk_gather_collect")
+
+
+class _DeviceArray:
+    """A raw device address seen through __cuda_array_interface__ (torch.as_tensor views it without a copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_array(ptr: int, shape, dtype="float32"):
+    """A torch CUDA tensor viewing `shape` elements at device address ptr (memory owned elsewhere, for
+    instance a tqk_peer_buffer_alloc buffer)."""
+    import torch
+    typestr = {"float32": "<f4", "uint8": "|u1", "int32": "<i4", "int64": "<i8"}[dtype]
+    return torch.as_tensor(_DeviceArray(ptr, shape, typestr), device="cuda")
 
 
 def gather_slot(mailbox: int, n_groups: int, chunk_floats: int, epoch: int) -> int:

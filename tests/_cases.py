@@ -115,7 +115,12 @@ def head_inputs(hd: int, n: int, seed: int):
     return q, kf, vf
 
 
-def prefill_inputs(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, pos0: int, n: int):
+def prefill_inputs(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, pos0: int, n: int,
+                   qk_scale: float = 1.0, outlier_frac: float = 0.0):
+    """One attention_layer_batch chunk (model/attention_layer.c:221-236): cache rows [0, pos0) and n
+    new tokens' q, k, v.  qk_scale multiplies q and every K row (the reference's large-score case,
+    tools/test_model.c:725-728, uses 30); outlier_frac of the K and V entries are x8 (config 3's
+    outlier blocks)."""
     rng = np.random.default_rng(seed)
     kf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
     vf = rng.standard_normal((n_kv, max_tokens, hd), dtype=np.float32)
@@ -124,6 +129,12 @@ def prefill_inputs(seed: int, n_q: int, n_kv: int, hd: int, max_tokens: int, pos
     qn = rng.standard_normal((n, n_q * hd), dtype=np.float32)
     kn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
     vn = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+    if qk_scale != 1.0:
+        s = np.float32(qk_scale)
+        kf, qn, kn = kf * s, qn * s, kn * s
+    if outlier_frac > 0.0:
+        for a in (kf, vf, kn, vn):
+            a *= np.where(rng.random(a.shape) < outlier_frac, np.float32(8.0), np.float32(1.0))
     return kf, vf, qn, kn, vn
 
 

@@ -405,6 +405,33 @@ def test_prefill_matches_golden_and_sequential(tqk, port, cuda):
     assert ok, (max_abs, rel)
 
 
+PREFILL_TC = ["g4", "g4_at0_n1", "g4_at0", "g4_x30", "g4_outliers", "g8", "g2", "g1"]
+
+
+@pytest.mark.parametrize("name", PREFILL_TC)
+def test_prefill_tensor_core_golden(tqk, port, cuda, name):
+    """The tcgen05 prefill (head_dim 128, 1/2/4/8 q heads per kv head) against chunks the
+    reference's own attention_layer_batch produced (tests/golden/prefill_tc.npz): appended rows
+    bit-exact, attention within the 1e-3 tolerance -- including one token at position 0, a chunk
+    over an empty cache, the reference's x30 large-score scaling and x8 outlier blocks."""
+    import torch
+    from _cases import prefill_inputs
+    g = np.load(os.path.join(GOLDEN, "prefill_tc.npz"))
+    seed, nq, nkv, hd, mt, pos0, n, qs, of = (int(v) for v in g[f"{name}__params"])
+    kf, vf, qn, kn, vn = prefill_inputs(seed, nq, nkv, hd, mt, pos0, n, float(qs), of / 1e6)
+    kp = tqk.quantize_rows(torch.from_numpy(kf).to(cuda))
+    vp = tqk.quantize_rows(torch.from_numpy(vf).to(cuda))
+    out = torch.full((n, nq * hd), float("nan"), device=cuda)
+    tqk.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, torch.from_numpy(qn).to(cuda), torch.from_numpy(kn).to(cuda),
+                torch.from_numpy(vn).to(cuda), out)
+    assert np.array_equal(kp.cpu().numpy()[:, pos0:pos0 + n], g[f"{name}__kp"])
+    assert np.array_equal(vp.cpu().numpy()[:, pos0:pos0 + n], g[f"{name}__vp"])
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), g[f"{name}__out"])
+    print(f"prefill {name}: max abs {max_abs:.3g} rel {rel:.3g}")
+    assert ok, f"{name}: max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
 @pytest.mark.parametrize("nq,nkv,pos0,n,mt", [
     (8, 8, 0, 1, 64),        # one token, group 1
     (16, 8, 5, 77, 100),     # group 2, ragged last CTA
@@ -459,8 +486,9 @@ def test_config5_prefill_full(tqk, port, cuda):
     out = torch.empty(n, nq * hd, device=cuda)
     tqk.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, qn, kn, vn, out)
     kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
-    # the appended rows are the reference quantiser's
+    # the appended K and V rows are the reference quantiser's
     assert np.array_equal(kh[:, pos0:], port.quantize_rows(kn.cpu().numpy().reshape(n, nkv, hd).transpose(1, 0, 2)))
+    assert np.array_equal(vh[:, pos0:], port.quantize_rows(vn.cpu().numpy().reshape(n, nkv, hd).transpose(1, 0, 2)))
     got, qh = out.cpu().numpy(), qn.cpu().numpy()
     for i in (0, 1, 17, 511, 1024, 2046, 2047):
         ref = port.attend(kh, vh, nq, nkv, hd, mt, pos0 + i, qh[i])

@@ -347,3 +347,183 @@ def test_gather_wait_times_out_without_peer(cuda):
     finally:
         for b in boxes + [solo]:
             tqk.peer_buffer_free(b)
+
+
+def test_fused_gather_two_ranks_emulated_on_one_gpu(cuda):
+    """tqk_decode_q8_gather with two ranks emulated one after the other on one GPU (both
+    ranks' pair buffers are local, so nothing waits on another kernel): each rank's decode of
+    its kv heads writes its units' outputs into both buffers as {value, epoch} pairs; then
+    tqk_gather_collect of each buffer passes at once and gives the whole output, within the
+    attention tolerance of the oracle; then a second step of the other parity with different
+    q, k and v."""
+    import torch
+
+    import oracle
+    from _cases import tolerance_ok
+    from tailorquantkernel_b200 import shard, tqk
+    port_ = oracle.Oracle("port")
+    layers, nq, nkv, hd, pos, world = 4, 32, 8, 128, 500, 2
+    mt, per, group = pos + 2, nkv // world, nq // nkv
+    rng = np.random.default_rng(92)
+    kf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+    vf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+    kf[:, :, pos:] = 0.0
+    vf[:, :, pos:] = 0.0
+    kp_full, vp_full = port_.quantize_rows(kf), port_.quantize_rows(vf)
+    chunk = per * group
+    n = layers * world * chunk * hd
+    pair_bytes = (n * 8 + 255) // 256 * 256
+    boxes = [tqk.peer_buffer_alloc(2 * pair_bytes) for _ in range(world)]
+    try:
+        planes = []
+        for r in range(world):
+            lo = r * per
+            planes.append((torch.from_numpy(np.ascontiguousarray(kp_full[:, lo:lo + per])).cuda(),
+                           torch.from_numpy(np.ascontiguousarray(vp_full[:, lo:lo + per])).cuda()))
+        kout = torch.empty(layers, chunk * hd, device="cuda")
+        for step in range(2):
+            epoch = step + 1
+            off = (epoch & 1) * pair_bytes
+            q = rng.standard_normal((layers, nq * hd), dtype=np.float32)
+            k = rng.standard_normal((layers, nkv * hd), dtype=np.float32)
+            v = rng.standard_normal((layers, nkv * hd), dtype=np.float32)
+            for r in range(world):
+                ql = torch.from_numpy(shard.head_split_slice(q, layers, nq, hd, r, world)).cuda()
+                kn = torch.from_numpy(shard.head_split_slice(k, layers, nkv, hd, r, world)).cuda()
+                vn = torch.from_numpy(shard.head_split_slice(v, layers, nkv, hd, r, world)).cuda()
+                args = shard.head_split_args(tqk, planes[r][0], planes[r][1], layers, nq, nkv, hd, mt, world, ql, kout,
+                                             len0=pos + step + 1, k_new=kn, v_new=vn)
+                tqk.decode_gather(args, tqk.gather_dst(world, r, [b + off for b in boxes], chunk, epoch))
+                torch.cuda.synchronize()
+            ref = np.empty((layers, nq * hd), np.float32)
+            for layer in range(layers):
+                assert port_.store_kv(kp_full[layer], vp_full[layer], nkv, hd, mt, pos + step, k[layer], v[layer]) == 0
+                ref[layer] = port_.attend(kp_full[layer], vp_full[layer], nq, nkv, hd, mt, pos + step, q[layer])
+            for r in range(world):
+                out = torch.full((layers, nq * hd), float("nan"), device="cuda")
+                tqk.gather_collect(boxes[r] + off, n, epoch, out)
+                torch.cuda.synchronize()
+                ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), ref)
+                assert ok, f"step {step} buffer {r}: max abs {max_abs:.3g} rel {rel:.3g}"
+                ep = tqk.device_array(boxes[r] + off, (n, 2), "int32")[:, 1].cpu().numpy()
+                assert (ep == epoch).all()
+            for r in range(world):
+                lo = r * per
+                assert np.array_equal(planes[r][0].cpu().numpy(), kp_full[:, lo:lo + per])
+                assert np.array_equal(planes[r][1].cpu().numpy(), vp_full[:, lo:lo + per])
+        assert tqk.device_status() == 0
+    finally:
+        for b in boxes:
+            tqk.peer_buffer_free(b)
+
+
+def test_gather_collect_times_out_and_recovers(cuda):
+    """tqk_gather_collect on pairs that never show the epoch gives up after about a second,
+    records the timeout in the device error word and returns; on pairs that show it, it
+    writes their values."""
+    import time
+
+    import torch
+    from tailorquantkernel_b200 import tqk
+    n = 3000
+    box = tqk.peer_buffer_alloc(n * 8)
+    try:
+        assert tqk.device_status(clear=True) == 0
+        out = torch.empty(n, device="cuda")
+        t0 = time.time()
+        tqk.gather_collect(box, n, 1, out)  # zeroed pairs: epoch 1 never arrives
+        torch.cuda.synchronize()
+        assert 0.5 < time.time() - t0 < 30
+        assert tqk.device_status(clear=True) == 1
+        pairs = tqk.device_array(box, (n, 2), "int32")
+        vals = torch.arange(n, device="cuda", dtype=torch.float32) * 0.5
+        pairs[:, 0] = vals.view(torch.int32)
+        pairs[:, 1] = 7
+        tqk.gather_collect(box, n, 7, out)
+        torch.cuda.synchronize()
+        assert torch.equal(out, vals)
+        assert tqk.device_status() == 0
+        with pytest.raises(tqk.TQKError):
+            tqk.gather_collect(box + 4, n - 1, 7, out)  # not 8-byte aligned
+    finally:
+        tqk.peer_buffer_free(box)
+
+
+def _rank_main_fused(rank, world, port, result_dir):
+    """The fused kv-head-group split (shard.PeerHeadSplit) on `world` GPUs: three steps at
+    consecutive positions, so both parity buffers are used and one is reused."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    from tailorquantkernel_b200 import shard, tqk
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    hs = None
+    try:
+        port_ = oracle.Oracle("port")
+        layers, nq, nkv, hd, pos, steps = 3, 32, 8, 128, 700, 3
+        mt, per, group = pos + steps, nkv // world, nq // nkv
+        rng = np.random.default_rng(93)
+        kf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+        vf = rng.standard_normal((layers, nkv, mt, hd), dtype=np.float32)
+        kf[:, :, pos:] = 0.0
+        vf[:, :, pos:] = 0.0
+        kp_full, vp_full = port_.quantize_rows(kf), port_.quantize_rows(vf)
+        qs = rng.standard_normal((steps, layers, nq * hd), dtype=np.float32)
+        ks = rng.standard_normal((steps, layers, nkv * hd), dtype=np.float32)
+        vs = rng.standard_normal((steps, layers, nkv * hd), dtype=np.float32)
+        lo = rank * per
+        kl = torch.from_numpy(np.ascontiguousarray(kp_full[:, lo:lo + per])).cuda()
+        vl = torch.from_numpy(np.ascontiguousarray(vp_full[:, lo:lo + per])).cuda()
+        kout = torch.empty(layers, per * group * hd, device="cuda")
+        outs = []
+        for s in range(steps):
+            q = torch.from_numpy(shard.head_split_slice(qs[s], layers, nq, hd, rank, world)).cuda()
+            k = torch.from_numpy(shard.head_split_slice(ks[s], layers, nkv, hd, rank, world)).cuda()
+            v = torch.from_numpy(shard.head_split_slice(vs[s], layers, nkv, hd, rank, world)).cuda()
+            args = shard.head_split_args(tqk, kl, vl, layers, nq, nkv, hd, mt, world, q, kout, len0=pos + s + 1,
+                                         k_new=k, v_new=v)
+            if hs is None:
+                hs = shard.PeerHeadSplit(dist, tqk, layers, per * group, hd)
+            outs.append(hs.step(args).clone())
+        torch.cuda.synchronize()
+        refs = []
+        for s in range(steps):
+            ref = np.empty((layers, nq * hd), np.float32)
+            for layer in range(layers):
+                assert port_.store_kv(kp_full[layer], vp_full[layer], nkv, hd, mt, pos + s, ks[s, layer],
+                                      vs[s, layer]) == 0
+                ref[layer] = port_.attend(kp_full[layer], vp_full[layer], nq, nkv, hd, mt, pos + s, qs[s, layer])
+            refs.append(ref)
+        rows_ok = np.array_equal(kl.cpu().numpy(), kp_full[:, lo:lo + per]) and \
+            np.array_equal(vl.cpu().numpy(), vp_full[:, lo:lo + per])
+        np.save(os.path.join(result_dir, f"fused_rank{rank}.npy"),
+                np.stack([np.stack([o.cpu().numpy() for o in outs]), np.stack(refs)]))
+        with open(os.path.join(result_dir, f"fused_rank{rank}.txt"), "w") as f:
+            f.write(f"{int(rows_ok)} {tqk.device_status()}")
+    finally:
+        if hs is not None:
+            hs.close()
+        dist.destroy_process_group()
+
+
+def test_fused_head_split_two_gpus(cuda, tmp_path):
+    """The fused kv-head-group split over 2 GPUs against the oracle (three steps, both parities)."""
+    import torch
+    import torch.multiprocessing as mp
+    from _cases import tolerance_ok
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.spawn(_rank_main_fused, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        rows_ok, status = (int(x) for x in open(tmp_path / f"fused_rank{r}.txt").read().split())
+        assert rows_ok == 1 and status == 0, (r, rows_ok, status)
+        got, ref = np.load(tmp_path / f"fused_rank{r}.npy")
+        for s in range(got.shape[0]):
+            ok, max_abs, rel = tolerance_ok(got[s], ref[s])
+            assert ok, f"rank {r} step {s}: max abs {max_abs:.3g} rel {rel:.3g}"

@@ -63,6 +63,24 @@ def test_prefill_golden(port):
     assert np.array_equal(kp[:, pos0:pos0 + n], g["kp"]) and np.array_equal(vp[:, pos0:pos0 + n], g["vp"])
 
 
+def test_prefill_tc_golden(port):
+    """The restatement reproduces the reference's attention_layer_batch chunks on the tensor-core
+    prefill's shapes (head_dim 128, groups 1/2/4/8, a chunk at position 0, x30 scores, x8 outliers)
+    bit for bit."""
+    g = _load("prefill_tc.npz")
+    names = sorted({k.split("__")[0] for k in g.files})
+    assert len(names) == 8
+    for name in names:
+        seed, nq, nkv, hd, mt, pos0, n, qs, of = (int(v) for v in g[f"{name}__params"])
+        kf, vf, qn, kn, vn = prefill_inputs(seed, nq, nkv, hd, mt, pos0, n, float(qs), of / 1e6)
+        assert digest(kf, vf, qn, kn, vn) == str(g[f"{name}__in_sha"]), name
+        kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+        out = port.prefill(kp, vp, nq, nkv, hd, mt, pos0, n, qn, kn, vn).reshape(n, nq * hd)
+        assert np.array_equal(out, g[f"{name}__out"]), name
+        assert np.array_equal(kp[:, pos0:pos0 + n], g[f"{name}__kp"]), name
+        assert np.array_equal(vp[:, pos0:pos0 + n], g[f"{name}__vp"]), name
+
+
 def test_ops_sweep_golden(port):
     g = _load("ops_sweep.npz")
     keys = sorted({k.split("__")[0] for k in g.files})
