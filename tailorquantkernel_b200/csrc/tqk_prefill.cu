@@ -52,7 +52,24 @@ constexpr int PF_KT = 32;     // keys per step (one staged tile)
 constexpr int PF_HD = 128;
 constexpr int PF_NB = PF_HD / QK;            // 4 Q8 blocks per row
 constexpr int PF_ROW = PF_NB * BLOCK_BYTES;  // 144-byte cache row
-constexpr int PF_STAGES = 4;
+// V as an fp16 hi + lo pair (default) or in one fp16 plane (v*vd rounded to
+// nearest).  One plane saves half of the P*V MMAs and a third of their
+// shared-memory operand reads, but was measured at only 5% faster (254.7 vs
+// 268.4 us on config 5) while V's rounding alone then reaches 1e-3 absolute
+// error on ordinary chunks and 2.4e-3 with x8 outlier blocks: over the bar.
+#ifndef TQK_PF_VLO
+#define TQK_PF_VLO 1
+#endif
+constexpr bool PF_VLO = TQK_PF_VLO != 0;
+// P as an fp16 hi + lo pair: with fp16 P alone (about 11 bits) the output's
+// absolute error grows with |V| and passed 2e-3 on chunks with x8 outlier
+// blocks; P_hi * (V_hi + V_lo) + P_lo * V_hi carries about 21 bits.
+#ifndef TQK_PF_PLO
+#define TQK_PF_PLO 1
+#endif
+constexpr bool PF_PLO = TQK_PF_PLO != 0;
+constexpr int PF_PPLANES = PF_PLO ? 2 : 1;
+constexpr int PF_STAGES = PF_VLO ? 4 : 6;
 constexpr int PF_TPR = 2;                      // softmax threads per query row
 constexpr int PF_KH = PF_KT / PF_TPR;          // keys of a step per thread
 constexpr int PF_OH = PF_HD / PF_TPR;          // O columns per thread
@@ -71,17 +88,17 @@ constexpr uint64_t PF_DRAIN_NS = 20000000ull;
 constexpr int ST_K = 0;                               // int8 K, 4 blocks x [32 keys x 32 B], K-major
 constexpr int ST_KD = ST_K + PF_NB * PF_KT * 32;      // float kd [4 blocks][32 keys]
 constexpr int ST_VH = ST_KD + PF_NB * PF_KT * 4;      // fp16 (v*vd) hi [32 keys x 128 cols], MN-major
-constexpr int ST_VL = ST_VH + PF_KT * PF_HD * 2;      // fp16 lo
-constexpr int ST_BYTES = ST_VL + PF_KT * PF_HD * 2;   // 20992
+constexpr int ST_VL = ST_VH + PF_KT * PF_HD * 2;      // fp16 lo (with PF_VLO)
+constexpr int ST_BYTES = ST_VL + (PF_VLO ? PF_KT * PF_HD * 2 : 0);  // 20992 with the lo plane, 12800 without
 static_assert(ST_BYTES % 16 == 0 && ST_VH % 16 == 0 && ST_KD % 16 == 0, "bulk copy / operand alignment");
 
 // CTA shared memory.
 constexpr int OFF_RING = 0;                                   // [stage][tile image]
 constexpr int OFF_QC = OFF_RING + PF_STAGES * ST_BYTES;       // int8 Q: [tile][block][128 rows x 32 B]
 constexpr int QC_TILE = PF_NB * PF_M * 32;                    // 16 KB
-constexpr int OFF_PC = OFF_QC + PF_QT * QC_TILE;              // fp16 P: [tile][buf][128 rows x 32 keys], K-major
-constexpr int PC_BUF = PF_M * PF_KT * 2;                      // 8 KB
-constexpr int OFF_QD = OFF_PC + PF_QT * 2 * PC_BUF;           // float qd [tile][row][block]
+constexpr int OFF_PC = OFF_QC + PF_QT * QC_TILE;              // fp16 P: [tile][buf][hi, lo][128 rows x 32 keys], K-major
+constexpr int PC_BUF = PF_M * PF_KT * 2;                      // 8 KB per plane
+constexpr int OFF_QD = OFF_PC + PF_QT * 2 * PF_PPLANES * PC_BUF;  // float qd [tile][row][block]
 constexpr int OFF_MX = OFF_QD + PF_QT * PF_M * PF_NB * 4;     // float [step parity][tile][half][row]: row maxima
 constexpr int OFF_SL = OFF_MX + 2 * PF_QT * PF_TPR * PF_M * 4;  // float [tile][half][row]: row sums
 constexpr int OFF_BAR = OFF_SL + PF_QT * PF_TPR * PF_M * 4;
@@ -198,7 +215,8 @@ __global__ void __launch_bounds__(256) stage_kv_tiles_kernel(const uint8_t *k, c
             lo[e] = pack2_f16(__fsub_rn(a, f16_lo_to_f32(hi[e])), __fsub_rn(c, f16_hi_to_f32(hi[e])));
         }
         *reinterpret_cast<uint4 *>(dst + ST_VH + v_off(key, cg)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4 *>(dst + ST_VL + v_off(key, cg)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        if constexpr (PF_VLO)
+            *reinterpret_cast<uint4 *>(dst + ST_VL + v_off(key, cg)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -334,12 +352,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             };
             auto pv = [&](int t, int j) {
                 const uint64_t so = (uint64_t)(((j % PF_STAGES) * ST_BYTES) >> 4);
-                const uint64_t pa = d_p + (((2 * t + (j & 1)) * PC_BUF) >> 4);
+                const uint64_t pa = d_p + (((2 * t + (j & 1)) * PF_PPLANES * PC_BUF) >> 4);
                 const uint32_t o = tmem + TM_O + t * PF_HD;
                 umma_f16(o, pa, d_vh + so, id_pv, j > 0);
                 umma_f16(o, pa + (256 >> 4), d_vh + so + (256 >> 4), id_pv, true);
-                umma_f16(o, pa, d_vl + so, id_pv, true);
-                umma_f16(o, pa + (256 >> 4), d_vl + so + (256 >> 4), id_pv, true);
+                if constexpr (PF_VLO) {
+                    umma_f16(o, pa, d_vl + so, id_pv, true);
+                    umma_f16(o, pa + (256 >> 4), d_vl + so + (256 >> 4), id_pv, true);
+                }
+                if constexpr (PF_PLO) {
+                    const uint64_t pl = pa + (PC_BUF >> 4);
+                    umma_f16(o, pl, d_vh + so, id_pv, true);
+                    umma_f16(o, pl + (256 >> 4), d_vh + so + (256 >> 4), id_pv, true);
+                }
             };
             auto stage_ready = [&](int j) {  // staged tile j is in shared memory
                 if (!mbar_wait_bounded(&full[j % PF_STAGES], (uint32_t)((j / PF_STAGES) & 1),
@@ -461,7 +486,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
             l *= factor;
             m = m_new;
             const pf2 neg_m = pk(-m, -m), one2 = pk(1.0f, 1.0f);
-            uint32_t ph[PF_KH / 2];
+            uint32_t ph[PF_KH / 2], pl[PF_KH / 2];
             pf2 sum2 = pk(0.0f, 0.0f);
 #pragma unroll
             for (int i2 = 0; i2 < PF_KH / 2; i2++) {
@@ -472,15 +497,21 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_q8_tc_kernel(const Pref
                 float ea, ec;
                 upk(e2, ea, ec);
                 ph[i2] = pack2_f16(ea, ec);
+                if constexpr (PF_PLO)
+                    pl[i2] = pack2_f16(__fsub_rn(ea, f16_lo_to_f32(ph[i2])), __fsub_rn(ec, f16_hi_to_f32(ph[i2])));
             }
             float sa, sb;
             upk(sum2, sa, sb);
             l += sa + sb;
-            uint8_t *pb = pc + (2 * qt + (j & 1)) * PC_BUF;
+            uint8_t *pb = pc + (2 * qt + (j & 1)) * PF_PPLANES * PC_BUF;
 #pragma unroll
-            for (int kc = 0; kc < PF_KH / 8; kc++)
+            for (int kc = 0; kc < PF_KH / 8; kc++) {
                 *reinterpret_cast<uint4 *>(pb + p_off(r, hf * (PF_KH / 8) + kc)) =
                     make_uint4(ph[4 * kc], ph[4 * kc + 1], ph[4 * kc + 2], ph[4 * kc + 3]);
+                if constexpr (PF_PLO)
+                    *reinterpret_cast<uint4 *>(pb + PC_BUF + p_off(r, hf * (PF_KH / 8) + kc)) =
+                        make_uint4(pl[4 * kc], pl[4 * kc + 1], pl[4 * kc + 2], pl[4 * kc + 3]);
+            }
             fence_proxy_async();  // P -> the tensor core
             tc_fence_before();    // the O rescale is done
             __syncwarp();
