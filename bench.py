@@ -84,6 +84,7 @@ class Clocks:
         self.index = index
         self.rows = []
         self.stop = threading.Event()
+        self.first = threading.Event()
         self.thread = threading.Thread(target=self._run, daemon=True)
 
     def _sample(self):
@@ -100,10 +101,15 @@ class Clocks:
     def _run(self):
         while not self.stop.is_set():
             self._sample()
+            self.first.set()
             self.stop.wait(0.2)
 
     def __enter__(self):
+        # the first nvidia-smi query (its start-up holds the driver for a while) completes before the
+        # timed region starts, so that a short region is not stalled by it; later samples, every
+        # 200 ms, fall inside the region
         self.thread.start()
+        self.first.wait(15)
         return self
 
     def __exit__(self, *exc):
@@ -126,6 +132,43 @@ class Clocks:
         reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(self.rows[0][2]),
                 "reasons": reasons, "samples": len(self.rows)}
+
+
+class HostBuffer:
+    """Page-locked host memory from cudaHostAlloc (mapped into the device's address space: a kernel
+    may read or write it over PCIe) with raw cudaMemcpyAsync copies.  torch's pinned-tensor copy_
+    costs tens of microseconds of host time per call, which a synchronised step exposes in full."""
+
+    def __init__(self, nbytes: int):
+        from cuda.bindings import runtime as rt
+        self.rt, self.nbytes = rt, nbytes
+        err, self.ptr = rt.cudaHostAlloc(nbytes, 0)
+        if int(err) != 0:
+            raise RuntimeError(f"cudaHostAlloc({nbytes}): {err}")
+
+    def fill_from(self, t) -> None:
+        """Copies a CUDA tensor's bytes in (set-up, synchronous)."""
+        self._check(self.rt.cudaMemcpy(self.ptr, t.data_ptr(), t.numel() * t.element_size(),
+                                       self.rt.cudaMemcpyKind.cudaMemcpyDeviceToHost))
+
+    def to_device(self, dev_ptr: int, nbytes: int, stream: int, offset: int = 0) -> None:
+        self._check(self.rt.cudaMemcpyAsync(dev_ptr, self.ptr + offset, nbytes,
+                                            self.rt.cudaMemcpyKind.cudaMemcpyHostToDevice, stream))
+
+    def from_device(self, dev_ptr: int, nbytes: int, stream: int) -> None:
+        self._check(self.rt.cudaMemcpyAsync(self.ptr, dev_ptr, nbytes, self.rt.cudaMemcpyKind.cudaMemcpyDeviceToHost,
+                                            stream))
+
+    def _check(self, r):
+        err = r[0] if isinstance(r, tuple) else r
+        if int(err) != 0:
+            raise RuntimeError(f"CUDA runtime: {err}")
+
+    def __del__(self):
+        try:
+            self.rt.cudaFreeHost(self.ptr)
+        except Exception:  # noqa: BLE001  (interpreter shutdown)
+            pass
 
 
 # ---------------------------------------------------------------------------
@@ -235,25 +278,31 @@ class Config2:
         else:
             q = rope_np(q, hd, pos, 500000.0)
         q = q.reshape(layers, n_q, hd)[:, kvh0 * group:(kvh0 + per) * group].reshape(layers, per * group * hd)
-        # q, k_new and v_new are views of one device buffer, so the end-to-end leg moves a step's
-        # inputs with a single host-to-device copy
+        # q, k_new and v_new live in one device buffer, so the end-to-end leg moves a step's inputs
+        # with one host-to-device copy (per chunk of layers on one GPU: [layer][q | k_new | v_new])
         lq, lkv = per * group * hd, per * hd
         nq_f, nkv_f = layers * lq, layers * lkv
-        self.inbuf = torch.empty(nq_f + 2 * nkv_f, device="cuda")
-        self.q = self.inbuf[:nq_f].view(layers, lq)
-        self.q.copy_(torch.from_numpy(np.ascontiguousarray(q)))
-        self.k_new = self.inbuf[nq_f:nq_f + nkv_f].view(layers, lkv)
-        self.v_new = self.inbuf[nq_f + nkv_f:].view(layers, lkv)
-        self.k_new.copy_(torch.randn(layers, lkv, device="cuda", generator=g))
-        self.v_new.copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.lrow = lq + 2 * lkv
+        self.inbuf = torch.empty(layers, self.lrow, device="cuda")
+        self.inbuf[:, :lq].copy_(torch.from_numpy(np.ascontiguousarray(q)))
+        self.inbuf[:, lq:lq + lkv].copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.inbuf[:, lq + lkv:].copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.lq, self.lkv = lq, lkv
         self.out = torch.empty(layers, n_q * hd, device="cuda")  # the whole output, on every rank
         if world == 1:
             self.gather = None
-            self.args = tqk.decode_args(self.kp, self.vp, n_q, n_kv, hd, self.mt, self.q, self.out, n_items=layers,
-                                        item_stride_blocks=n_kv * self.mt * self.nb, len0=pos + 1,
-                                        q_item_stride=n_q * hd, out_item_stride=n_q * hd, k_new=self.k_new,
-                                        v_new=self.v_new, kv_new_item_stride=n_kv * hd, **pro)
+            self.pro = pro
+            self.args = self._layer_args(0, layers)
         else:
+            # q, k_new, v_new of this rank's heads as three packed arrays of one buffer
+            flat = torch.empty(nq_f + 2 * nkv_f, device="cuda")
+            self.q = flat[:nq_f].view(layers, lq)
+            self.k_new = flat[nq_f:nq_f + nkv_f].view(layers, lkv)
+            self.v_new = flat[nq_f + nkv_f:].view(layers, lkv)
+            self.q.copy_(self.inbuf[:, :lq])
+            self.k_new.copy_(self.inbuf[:, lq:lq + lkv])
+            self.v_new.copy_(self.inbuf[:, lq + lkv:])
+            self.inbuf = flat
             # the decode of this rank's heads pushes every unit's output into every rank's buffer
             # (tqk_decode_q8_gather); kout is the plain decode's output for the kernel-only timing
             self.kout = torch.empty(layers, lq, device="cuda")
@@ -268,17 +317,34 @@ class Config2:
         self.bytes_per_step = 2 * layers * per * (pos + 1) * self.nb * BB + 2 * layers * per * self.nb * BB
         self.tokens_per_step = 1
         self.launches_per_step = 1 if world == 1 else 2  # decode (+ the gather)
-        # pinned host buffers of the end-to-end leg: every rank copies its inputs in, rank 0 the
-        # whole output out (the job's bytes are the sums over ranks)
-        self.h_in = self.inbuf.cpu().pin_memory()
-        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
-        self.h2d = (nq_f + 2 * nkv_f) * 4 * world
-        self.d2h = self.h_out.numel() * 4
-        self.e2e_api = ("tqk_decode_q8 (C ABI) with pinned host q, k and v in and the attention output out, "
-                        "stream-synchronised every step; the step's host-to-device copy, the decode launch and the "
-                        "device-to-host copy are captured once as a CUDA graph and replayed per step" if world == 1 else
+        # page-locked host buffers of the end-to-end leg: every rank copies its inputs in, rank 0
+        # receives the whole output (the job's bytes are the sums over ranks)
+        self.in_bytes = (nq_f + 2 * nkv_f) * 4
+        self.h_in = HostBuffer(self.in_bytes)
+        self.h_in.fill_from(self.inbuf)
+        self.h_out = HostBuffer(self.out.numel() * 4)
+        self.h2d = self.in_bytes * world
+        self.d2h = self.out.numel() * 4
+        self.e2e_api = ("per step: q, k and v (786 KB) in from page-locked host memory with one cudaMemcpyAsync, "
+                        "then tqk_decode_q8 (C ABI) with its out in page-locked host memory (the kernel writes the "
+                        "512 KB output over PCIe), then a stream synchronisation" if world == 1 else
                         "per rank: its q/k/v slice in from pinned host memory, tqk_decode_q8_gather over its kv "
                         "heads + tqk_gather_collect; rank 0 copies the whole output out; stream-synchronised every step")
+
+    def _layer_args(self, first: int, count: int, out=None):
+        """One-GPU decode arguments of layers [first, first + count): raw addresses into the cache,
+        the interleaved input buffer and the output."""
+        base = self.inbuf.data_ptr() + first * self.lrow * 4
+        plane = self.nkv * self.mt * self.nb * BB  # bytes of one layer's plane
+        out = self.out[first:first + count] if out is None else out
+        return self.tqk.decode_args(self.kp.data_ptr() + first * plane, self.vp.data_ptr() + first * plane, self.nq,
+                                    self.nkv, self.hd, self.mt, base, out, n_items=count,
+                                    item_stride_blocks=self.nkv * self.mt * self.nb, len0=self.pos + 1,
+                                    q_item_stride=self.lrow, out_item_stride=self.nq * self.hd,
+                                    k_new=base + self.lq * 4, v_new=base + (self.lq + self.lkv) * 4,
+                                    kv_new_item_stride=self.lrow,
+                                    **{k: (v[first:first + count] if hasattr(v, "shape") else v)
+                                       for k, v in self.pro.items()})
 
     def step(self):
         if self.gather is None:
@@ -291,42 +357,27 @@ class Config2:
         self.kernel_count += 1
         self.tqk.decode(self.args_by[self.kernel_count % self.copies])
 
-    def _step_e2e_eager(self):
-        self.inbuf.copy_(self.h_in, non_blocking=True)  # q, k_new and v_new of the step
-        self.step()
-        if self.rank == 0:
-            self.h_out.copy_(self.out, non_blocking=True)
-
     def prepare_e2e(self):
-        """On one GPU the end-to-end step (pinned inputs in, the decode, the output out) is captured
-        once as a CUDA graph, as a serving loop would replay it; on several GPUs the gather's epoch
-        changes every step, so the step stays eager."""
+        """The end-to-end step: the inputs copied in from page-locked host memory with one
+        cudaMemcpyAsync, then the decode; on one GPU the decode writes its output straight into
+        page-locked host memory (the kernel's final stores cross PCIe while other units still
+        run), on several GPUs rank 0 copies the gathered output out."""
         import torch
-        self.e2e_graph = None
-        if self.world != 1:
-            return
-        ws = torch.zeros(self.tqk.decode_workspace_size(self.args) + 1024, dtype=torch.uint8, device="cuda")
-        self.tqk.workspace_init(ws)
-        self.e2e_ws = ws
-        cap = torch.cuda.Stream()
-        cap.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(cap):
-            self.tqk.decode(self.args, workspace=ws)  # outside capture: kernel set-up
-            self.e2e_graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.e2e_graph, stream=cap):
-                self.inbuf.copy_(self.h_in, non_blocking=True)
-                self.tqk.decode(self.args, workspace=ws)
-                self.h_out.copy_(self.out, non_blocking=True)
-        cap.synchronize()
+        self.stream_handle = torch.cuda.current_stream().cuda_stream
+        if self.world == 1:
+            self.e2e_args = self._layer_args(0, self.L, out=self.h_out.ptr)
 
     def step_e2e(self):
         import torch
-        s = torch.cuda.current_stream()
-        if getattr(self, "e2e_graph", None) is not None:
-            self.e2e_graph.replay()
+        st = self.stream_handle
+        self.h_in.to_device(self.inbuf.data_ptr(), self.in_bytes, st)
+        if self.world == 1:
+            self.tqk.decode(self.e2e_args, stream=st)
         else:
-            self._step_e2e_eager()
-        s.synchronize()
+            self.step()
+            if self.rank == 0:
+                self.h_out.from_device(self.out.data_ptr(), self.d2h, st)
+        torch.cuda.current_stream().synchronize()
 
     def describe(self):
         return describe_config2(self.L, self.nq, self.nkv, self.hd, self.pos, self.prologue)
@@ -351,8 +402,9 @@ class Config2:
     def host_planes(self):
         if self.world != 1:
             raise RuntimeError("the CPU baseline runs at N = 1")
-        return self.kp[0].cpu().numpy(), self.vp[0].cpu().numpy(), self.q.cpu().numpy(), \
-            self.k_new.cpu().numpy(), self.v_new.cpu().numpy()
+        x = self.inbuf.cpu().numpy()
+        return self.kp[0].cpu().numpy(), self.vp[0].cpu().numpy(), np.ascontiguousarray(x[:, :self.lq]), \
+            np.ascontiguousarray(x[:, self.lq:self.lq + self.lkv]), np.ascontiguousarray(x[:, self.lq + self.lkv:])
 
 
 def describe_config4(n_q, n_kv, hd, n):
@@ -409,10 +461,11 @@ class Config4:
         self.e2e_api = ("tqk_decode_q8 (C ABI, log-sum-exp partials of this rank's range) + tqk_exchange_merge "
                         if self.peer is not None else "tqk_decode_q8 (C ABI) ") + \
             "with pinned host q in and the attention output out, stream-synchronised every step"
-        self.h_q = self.q.cpu().pin_memory()
-        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
-        self.h2d = self.h_q.numel() * 4
-        self.d2h = self.h_out.numel() * 4
+        self.h_q = HostBuffer(self.q.numel() * 4)
+        self.h_q.fill_from(self.q)
+        self.h_out = HostBuffer(self.out.numel() * 4)
+        self.h2d = self.q.numel() * 4
+        self.d2h = self.out.numel() * 4
 
     def step(self):
         if self.world == 1:
@@ -438,9 +491,9 @@ class Config4:
     def step_e2e(self):
         import torch
         s = torch.cuda.current_stream()
-        self.q.copy_(self.h_q, non_blocking=True)
+        self.h_q.to_device(self.q.data_ptr(), self.h2d, s.cuda_stream)
         self.step()
-        self.h_out.copy_(self.out, non_blocking=True)
+        self.h_out.from_device(self.out.data_ptr(), self.d2h, s.cuda_stream)
         s.synchronize()
 
     def describe(self):
@@ -540,10 +593,11 @@ class Config3:
         self.launches_per_step = 1
         self.e2e_api = ("tqk_decode_q8 (C ABI, ragged device lengths) with the rank's sequences' pinned host q in "
                         "and their attention outputs out, stream-synchronised every step")
-        self.h_q = self.q.cpu().pin_memory()
-        self.h_out = torch.empty_like(self.out, device="cpu").pin_memory()
-        self.h2d = self.h_q.numel() * 4
-        self.d2h = self.h_out.numel() * 4
+        self.h_q = HostBuffer(self.q.numel() * 4)
+        self.h_q.fill_from(self.q)
+        self.h_out = HostBuffer(self.out.numel() * 4)
+        self.h2d = self.q.numel() * 4
+        self.d2h = self.out.numel() * 4
 
     def step(self):
         self.count += 1
@@ -552,9 +606,9 @@ class Config3:
     def step_e2e(self):
         import torch
         s = torch.cuda.current_stream()
-        self.q.copy_(self.h_q, non_blocking=True)
+        self.h_q.to_device(self.q.data_ptr(), self.h2d, s.cuda_stream)
         self.step()
-        self.h_out.copy_(self.out, non_blocking=True)
+        self.h_out.from_device(self.out.data_ptr(), self.d2h, s.cuda_stream)
         s.synchronize()
 
     def describe(self):
@@ -739,10 +793,11 @@ class Config6:
         self.bytes_per_step = wbytes + self.kv_bytes + 2 * layers * n_kv * self.nb * BB
         self.tokens_per_step = 1
         self.launches_per_step = 3 * layers
-        self.h_x = self.acts[0].cpu().pin_memory()
-        self.h_out = torch.empty(hidden).pin_memory()
-        self.h2d = self.h_x.numel() * 4
-        self.d2h = self.h_out.numel() * 4
+        self.h_x = HostBuffer(hidden * 4)
+        self.h_x.fill_from(self.acts[0])
+        self.h_out = HostBuffer(hidden * 4)
+        self.h2d = hidden * 4
+        self.d2h = hidden * 4
         self.e2e_api = ("tqk_attention_layer x 32 (C ABI) replayed as one CUDA graph, with the token's input "
                         "copied in from pinned host memory and the last layer's output copied out, "
                         "stream-synchronised every step")
@@ -751,9 +806,10 @@ class Config6:
         self.graph.replay()
 
     def step_e2e(self):
-        self.acts[0].copy_(self.h_x, non_blocking=True)
+        st = self.stream.cuda_stream
+        self.h_x.to_device(self.acts[0].data_ptr(), self.h2d, st)
         self.graph.replay()
-        self.h_out.copy_(self.acts[-1], non_blocking=True)
+        self.h_out.from_device(self.acts[-1].data_ptr(), self.d2h, st)
         self.stream.synchronize()
 
     def describe(self):
