@@ -820,6 +820,115 @@ class Config6:
         return "replicas: every GPU runs its own token" if world > 1 else "single GPU"
 
 
+def describe_config7(layers, n_q, n_kv, hd, hidden, inter, vocab, pos):
+    row = hd // QK * BB
+    q_dim, kv_dim = n_q * hd, n_kv * hd
+    per_layer = (q_dim * hidden + 2 * kv_dim * hidden + hidden * q_dim + 3 * inter * hidden) // QK * BB
+    wbytes = layers * per_layer + vocab * hidden // QK * BB
+    kv_bytes = 2 * layers * n_kv * (pos + 1) * row
+    return {"workload": f"config7: Llama-3-8B-shaped whole-token decode on the device (tq_forward_token): embedding, "
+                        f"{layers} layers of RMSNorm + attention (Q8 wq/wk/wv/wo, q/k RMSNorm + RoPE(500000), Q8 "
+                        f"cache append at {pos}, attention over {pos + 1} positions) + RMSNorm + Q8 MLP "
+                        f"({inter} wide, SiLU), final RMSNorm, tied Q8 lm_head over {vocab} tokens, greedy choice",
+            "layers": layers, "seq_len": pos + 1, "hidden": hidden, "intermediate": inter, "vocab": vocab,
+            "weight_bytes_per_token": wbytes, "kv_bytes_per_token": kv_bytes,
+            "l2": f"no flush: inputs larger than L2 ({(wbytes + kv_bytes) / 1e9:.2f} GB per step vs 126 MB L2)"}
+
+
+def random_q8_rows(rows: int, cols: int, g):
+    """Random packed Q8 rows made on the device (int8 uniform, scales uniform in [0.002, 0.02))."""
+    import torch
+    nb = cols // QK
+    w = torch.randint(0, 256, (rows, nb, BB), dtype=torch.uint8, device="cuda", generator=g)
+    d = torch.empty(rows, nb, device="cuda").uniform_(0.002, 0.02, generator=g)
+    w[:, :, :4] = d.view(torch.uint8).view(rows, nb, 4)
+    return w.view(rows, nb * BB)
+
+
+class Config7:
+    """A Llama-3-8B-shaped token through the whole decoder stack on the device (tqk_forward_token,
+    the reference's tq_forward_token of model/context.c:104-122): 8.7 GB of Q8 weights and 302 MB
+    of Q8 cache per token, the 260 launches captured once in a CUDA graph and replayed per step
+    (the position stays at 4096, so each step rewrites the same cache row)."""
+    name = "config7"
+    scaling = "weak"
+    e2e_steps = 200
+    data = ("synthetic: seeded random packed Q8 weights made on the device (int8 uniform, scales uniform in "
+            "[0.002, 0.02)), N(0,1) K/V quantised to Q8 on the device, RoPE tables of float32 numpy")
+
+    def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, inter=14336, vocab=128256,
+                 pos=4096):
+        import torch
+        from tailorquantkernel_b200 import tqk
+        self.tqk = tqk
+        self.L, self.nq, self.nkv, self.hd, self.hidden, self.inter, self.vocab, self.pos = \
+            layers, n_q, n_kv, hd, hidden, inter, vocab, pos
+        self.mt = pos + 1
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        q_dim, kv_dim = n_q * hd, n_kv * hd
+        norm = lambda n: 1 + 0.1 * torch.randn(n, device="cuda", generator=g)  # noqa: E731
+        self.layers = []
+        for _ in range(layers):
+            d = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(hd), "k_norm": norm(hd),
+                 "wq": random_q8_rows(q_dim, hidden, g), "wk": random_q8_rows(kv_dim, hidden, g),
+                 "wv": random_q8_rows(kv_dim, hidden, g), "wo": random_q8_rows(hidden, q_dim, g),
+                 "wgate": random_q8_rows(inter, hidden, g), "wup": random_q8_rows(inter, hidden, g),
+                 "wdown": random_q8_rows(hidden, inter, g)}
+            shape = (n_kv, self.mt, hd)
+            d["k_cache"] = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+            d["v_cache"] = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+            self.layers.append(d)
+        self.embed = random_q8_rows(vocab, hidden, g)
+        self.final_norm = norm(hidden)
+        inv = np.float32(500000.0) ** (-2.0 * np.arange(hd // 2, dtype=np.float32) / np.float32(hd))
+        ang = np.arange(self.mt, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
+        self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
+        self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).cuda()
+        cfg = {"n_layers": layers, "n_q_heads": n_q, "n_kv_heads": n_kv, "head_dim": hd, "hidden_size": hidden,
+               "intermediate_size": inter, "vocab_size": vocab, "max_tokens": self.mt, "rms_eps": 1e-5}
+        self.model = tqk.model_struct(cfg, self.layers, self.embed, self.final_norm, self.cos, self.sin, fmt=0)
+        self.scratch = torch.empty(tqk.forward_scratch_bytes(self.model) // 4, device="cuda")
+        self.logits = torch.empty(vocab, device="cuda")
+        self.next = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.ws = torch.zeros(1 << 22, dtype=torch.uint8, device="cuda")
+        self.token = 17
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            tqk.workspace_init(self.ws, cap)
+            tqk.forward_token(self.model, self.token, pos, self.scratch, self.logits, self.next, self.ws, cap)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=cap):
+                tqk.forward_token(self.model, self.token, pos, self.scratch, self.logits, self.next, self.ws, cap)
+        cap.synchronize()
+        self.stream = torch.cuda.current_stream()
+        d = describe_config7(layers, n_q, n_kv, hd, hidden, inter, vocab, pos)
+        self.weight_bytes, self.kv_bytes = d["weight_bytes_per_token"], d["kv_bytes_per_token"]
+        self.bytes_per_step = self.weight_bytes + self.kv_bytes + 2 * layers * n_kv * (hd // QK) * BB
+        self.tokens_per_step = 1
+        self.launches_per_step = 2 + 8 * layers + 2
+        self.h_out = HostBuffer(vocab * 4)
+        self.h2d = 0  # the token id is a host argument of the call
+        self.d2h = vocab * 4
+        self.e2e_api = ("tqk_forward_token x 1 (C ABI) replayed as one CUDA graph per token, the logits copied out to "
+                        "page-locked host memory, stream-synchronised every step")
+
+    def step(self):
+        self.graph.replay()
+
+    def step_e2e(self):
+        self.graph.replay()
+        self.h_out.from_device(self.logits.data_ptr(), self.d2h, self.stream.cuda_stream)
+        self.stream.synchronize()
+
+    def describe(self):
+        return describe_config7(self.L, self.nq, self.nkv, self.hd, self.hidden, self.inter, self.vocab, self.pos)
+
+    @staticmethod
+    def parallelism(world):
+        return "replicas: every GPU runs its own token" if world > 1 else "single GPU"
+
+
 class HostConfig6:
     """Config 6 on the host only, for the reference's attention_layer (CPU): the same shapes, random
     packed Q8 weights and a cache quantised by the reference's own quantiser."""
@@ -847,6 +956,60 @@ class HostConfig6:
 
     def describe(self):
         return describe_config6(self.L, self.nq, self.nkv, self.hd, self.hidden, self.pos)
+
+
+class HostConfig7:
+    """Config 7 on the host for the reference's own tq_forward_token (model/context.c:104-122): the
+    same shapes, random packed Q8 weights (int8 uniform, scales uniform in [0.002, 0.02)) and a Q8
+    cache of pos positions, quantised by the reference's quantiser, that the context starts from."""
+    name = "config7"
+
+    def __init__(self, orc, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, inter=14336, vocab=128256,
+                 pos=4096):
+        self.L, self.nq, self.nkv, self.hd, self.hidden, self.inter, self.vocab, self.pos = \
+            layers, n_q, n_kv, hd, hidden, inter, vocab, pos
+        self.mt = pos + 1
+        rng = np.random.default_rng(seed)
+        q_dim, kv_dim = n_q * hd, n_kv * hd
+        norm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
+        lay = []
+        self.planes = []
+        for _ in range(layers):
+            lay.append({"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(hd), "k_norm": norm(hd),
+                        "wq": q8_weight_rows_np(rng, q_dim, hidden), "wk": q8_weight_rows_np(rng, kv_dim, hidden),
+                        "wv": q8_weight_rows_np(rng, kv_dim, hidden), "wo": q8_weight_rows_np(rng, hidden, q_dim),
+                        "wgate": q8_weight_rows_np(rng, inter, hidden), "wup": q8_weight_rows_np(rng, inter, hidden),
+                        "wdown": q8_weight_rows_np(rng, hidden, inter)})
+            kf = rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32)
+            vf = rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32)
+            self.planes.append((orc.quantize_rows_bulk(kf), orc.quantize_rows_bulk(vf)))
+        self.model = {"cfg": {"n_q_heads": n_q, "n_kv_heads": n_kv, "head_dim": hd, "hidden_size": hidden,
+                              "rope_theta": 500000.0, "rms_eps": 1e-5, "n_layers": layers,
+                              "intermediate_size": inter, "vocab_size": vocab},
+                      "fmt": "8", "embed": q8_weight_rows_np(rng, vocab, hidden), "final_norm": norm(hidden),
+                      "layers": lay}
+        d = describe_config7(layers, n_q, n_kv, hd, hidden, inter, vocab, pos)
+        self.bytes_per_step = d["weight_bytes_per_token"] + d["kv_bytes_per_token"]
+
+    def describe(self):
+        return describe_config7(self.L, self.nq, self.nkv, self.hd, self.hidden, self.inter, self.vocab, self.pos)
+
+
+def reference_forward_seconds(orc, wl, tokens: int):
+    """Times the reference's tq_forward_token (all host threads: its matmuls and attention use
+    OpenMP) from position pos - tokens + 1 on: one context runs 1 token, another 1 + tokens, and the
+    difference over `tokens` is the per-token time (the context set-up and cache fill cancel).
+    Returns (seconds per token, tokens, threads)."""
+    threads = os.cpu_count() or 1
+    start = (wl.pos - tokens, wl.planes)
+    t0 = time.perf_counter()
+    _, rc1, _ = orc.forward_tokens(wl.model, [17], wl.mt, start_planes=start)
+    t1 = time.perf_counter()
+    _, rc2, _ = orc.forward_tokens(wl.model, [17] * (1 + tokens), wl.mt, start_planes=start)
+    t2 = time.perf_counter()
+    if rc1 != [0] or rc2 != [0] * (1 + tokens):
+        raise RuntimeError(f"the reference's tq_forward_token returned {rc1} / {rc2}")
+    return max((t2 - t1) - (t1 - t0), 1e-9) / tokens, tokens, threads
 
 
 def reference_layers_seconds(orc, wl, budget_s: float, max_tokens: int | None = None, min_tokens: int = 2):
@@ -1041,8 +1204,9 @@ def reference_prefill_token_seconds(orc, wl, budget_s: float, sample: int = 32, 
 # --tiny: shapes small enough for the CPU test of the reference arm (tests/test_bench_cpu.py);
 # never a benchmark line
 TINY = {2: dict(layers=2, pos=255), 3: dict(mt=256, lo=64), 4: dict(n=2048), 5: dict(pos0=64, n=64),
+        7: dict(layers=2, hidden=512, inter=1024, vocab=1000, pos=255),
         6: dict(layers=2, hidden=512, pos=255)}
-SCALING = {2: "strong", 3: "strong", 4: "strong", 5: "weak", 6: "weak"}
+SCALING = {2: "strong", 3: "strong", 4: "strong", 5: "weak", 6: "weak", 7: "weak"}
 
 
 def global_batch(config: int, world: int) -> int:
@@ -1057,7 +1221,12 @@ def run_reference(args):
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
     shape = TINY[args.config] if args.tiny else {}
-    if args.config == 6:
+    if args.config == 7:
+        wl = HostConfig7(orc, seed=7000, **shape)
+        sec, n, threads = reference_forward_seconds(orc, wl, max(1, min(args.steps, 3)))
+        sample = (f"{n} tokens through the reference's tq_forward_token ending at position {wl.pos} (a context "
+                  f"of 1 + {n} tokens minus one of 1 token, so set-up and cache fill cancel)")
+    elif args.config == 6:
         wl = HostConfig6(orc, seed=6000, **shape)
         reference_layers_seconds(orc, wl, 0.0, max_tokens=1, min_tokens=1)
         sec, n, threads = reference_layers_seconds(orc, wl, args.ref_seconds, max_tokens=args.steps,
@@ -1121,6 +1290,8 @@ def run_ours(args):
         wl = Config4(seed=4000, rank=rank, world=world, dist=dist, exchange=args.exchange, **shape)
     elif args.config == 6:
         wl = Config6(seed=6000 + rank, **shape)
+    elif args.config == 7:
+        wl = Config7(seed=7000 + rank, **shape)
     else:
         wl = Config5(seed=5000 + rank, **shape)
     stream = torch.cuda.current_stream()
@@ -1183,6 +1354,8 @@ def run_ours(args):
         cpu = {"value": 1.0 / sec, "unit": "tokens/s", "cores": threads, "kind": kind,
                "sample": f"{n} tokens: the first 32 tokens of the chunk through the reference's append + causal "
                          f"attention, repeated for ~{args.cpu_seconds:.0f} s, median per token"}
+    elif wl.name == "config7":
+        cpu = None  # the reference arm (--impl reference --config 7) times the reference's forward
     elif rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "config6":
         orc, kind = reference_oracle()
         sec, n, threads = reference_layers_seconds(orc, HostConfig6(orc, seed=6000), args.cpu_seconds)
@@ -1214,7 +1387,8 @@ def run_ours(args):
             roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                         "frac": achieved / peak, "peak_kind": peak_kind,
                         "algorithmic_bytes_per_launch": wl.bytes_per_step,
-                        "traffic": _traffic_from_profile(("layers_" if wl.name == "config6" else "decode_q8_")
+                        "traffic": _traffic_from_profile(("layers_" if wl.name in ("config6", "config7")
+                                                          else "decode_q8_")
                                                          + wl.name)}
         jobs = world if wl.scaling == "weak" else 1  # weak: every rank runs its own sequence
         if world > 1:
@@ -1256,7 +1430,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5, 6, 7])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0, help="CPU budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")

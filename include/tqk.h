@@ -309,6 +309,49 @@ typedef struct {
 TQK_API int tqk_attention_layer(const tqk_attn_layer_args *a, void *workspace, size_t workspace_bytes,
                                 tqk_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * One token through a whole decoder stack on the device: tq_forward_token
+ * (reference model/context.c:104-122) -- embed_lookup, then per layer
+ * rmsnorm + attention_layer + residual add, rmsnorm + mlp_layer + residual
+ * add (model/context.c:83-102, model/mlp.c:3-17), the final rmsnorm and the
+ * lm_head over the tied embedding (model/embedding.c:36-41) -- with weights,
+ * norms and Q8 caches in HBM.  Every matrix shares one format (TQK_FMT_Q8 or
+ * TQK_FMT_Q4; the reference's packed rows).  Every step is the reference's
+ * arithmetic except two: the decode's tolerance (within 1e-3, as everywhere),
+ * and the RMSNorms, which add their squares in a fixed tree rather than the
+ * reference's serial chain of hidden_size terms (which would cost about 8 us
+ * per norm at 4096).  Either can move an activation's Q8 rounding by one step
+ * now and then, so the logits and the appended cache rows agree with the
+ * reference's within tolerance rather than bit for bit.
+ */
+typedef struct {
+    const float *input_norm, *post_norm;   /* [hidden] (device) */
+    const void *wq, *wk, *wv, *wo;          /* attention projections (device) */
+    const float *q_norm, *k_norm;          /* [head_dim] (device) */
+    const void *wgate, *wup, *wdown;        /* MLP: [inter][hidden], [inter][hidden], [hidden][inter] */
+    tqk_block_q8 *k_cache, *v_cache;       /* the layer's Q8 planes [n_kv][max_tokens][head_dim/32] */
+} tqk_layer_weights;
+typedef struct {
+    int n_layers, n_q_heads, n_kv_heads, head_dim, hidden_size, intermediate_size, vocab_size, max_tokens;
+    float rms_eps;
+    int format;                            /* TQK_FMT_Q8 or TQK_FMT_Q4 */
+    const void *embed;                     /* [vocab][hidden] packed rows (device); also the lm_head */
+    const float *final_norm;               /* [hidden] (device) */
+    const float *rope_cos, *rope_sin;      /* rope_table (model/rope.c:4-12) of every position,
+                                              [max_tokens][head_dim/2] (device), as the host's libm gives it */
+    const tqk_layer_weights *layers;       /* HOST array of n_layers, device pointers inside */
+} tqk_model;
+/* Bytes of device scratch tqk_forward_token needs (the residual stream, its
+ * norm, the MLP's gate and up rows and one attention layer's scratch). */
+TQK_API size_t tqk_forward_scratch_bytes(const tqk_model *m);
+/* One token at position pos (the caches hold positions [0, pos)): logits
+ * [vocab_size] (device); next_token (device int, or NULL) receives the greedy
+ * choice of sample_greedy (model/sampler.c:3-13).  Returns -1 (TQK_EPOS), as
+ * the reference does, for pos outside [0, max_tokens) or a token outside
+ * [0, vocab_size), before touching anything.  workspace: as tqk_decode_q8's. */
+TQK_API int tqk_forward_token(const tqk_model *m, int token, int pos, void *scratch, float *logits,
+                              int32_t *next_token, void *workspace, size_t workspace_bytes, tqk_stream_t stream);
+
 /* attend_q8 for one layer of one sequence: n = pos + 1 positions
  * (reference model/attention_layer.c:125-150); TQK_EPOS if pos is out of range. */
 TQK_API int tqk_attend_q8(const tqk_block_q8 *k_plane, const tqk_block_q8 *v_plane, int n_q_heads, int n_kv_heads,
@@ -418,9 +461,9 @@ TQK_API int tqk_decode_unit_count(const tqk_decode_args *a, int *units);
  * (device memory, 8-byte aligned) shows `epoch`, and writes the values to
  * out[0..n).  Each thread waits at most 1 s in all, then records TQK_ETIMEOUT
  * in the device error word and leaves the value it has (out is then
- * undefined).  At its end it also waits for the kernel launched before it on
- * the stream to complete, so that the next launch may reuse that kernel's
- * workspace. */
+ * undefined).  It first waits for the kernel launched before it on the
+ * stream (the decode) to complete, so that it polls only for the peers' pairs
+ * and the next launch may reuse that kernel's workspace. */
 TQK_API int tqk_gather_collect(const void *pairs, size_t n, int epoch, float *out, tqk_stream_t stream);
 
 /* The kv-head-group split's gather over peer memory (the multi-GPU form of

@@ -95,6 +95,37 @@ class _TqKvCache(ctypes.Structure):
 
 
 
+class _TqMlpWeights(ctypes.Structure):
+    """tq_mlp_weights (model/model_ops.h)."""
+    _fields_ = [("wgate", _TqMatrix), ("wup", _TqMatrix), ("wdown", _TqMatrix)]
+
+
+class _TqLayerWeights(ctypes.Structure):
+    """tq_layer_weights (model/model_ops.h)."""
+    _fields_ = [("input_norm", ctypes.c_void_p), ("attn", _TqAttnWeights), ("post_norm", ctypes.c_void_p),
+                ("mlp", _TqMlpWeights)]
+
+
+class _TqModelConfig(ctypes.Structure):
+    """tq_model_config (model/model_ops.h)."""
+    _fields_ = [("attn", _TqAttnConfig), ("n_layers", ctypes.c_int), ("intermediate_size", ctypes.c_int),
+                ("vocab_size", ctypes.c_int)]
+
+
+class _TqModel(ctypes.Structure):
+    """tq_model = {tq_model_config cfg; tq_model_weights w = {embed, final_norm, layers}} (model/model_ops.h)."""
+    _fields_ = [("cfg", _TqModelConfig), ("embed", _TqMatrix), ("final_norm", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(_TqLayerWeights))]
+
+
+class _TqCtx(ctypes.Structure):
+    """tq_ctx (model/model_ops.h)."""
+    _fields_ = [("model", ctypes.c_void_p), ("caches", ctypes.POINTER(_TqKvCache)), ("pos", ctypes.c_int),
+                ("max_tokens", ctypes.c_int)] + \
+               [(n, ctypes.c_void_p) for n in ("x", "xn", "attn_out", "mlp_out", "gate", "up", "xq", "hq", "scores",
+                                               "logits")]
+
+
 class Oracle:
     def __init__(self, kind: str = "port"):
         path = _LIBS[kind]
@@ -298,6 +329,79 @@ class Oracle:
         if rc != 0:
             raise ValueError(f"attention_layer returned {rc}")
         return out
+
+    def forward_tokens(self, model: dict, tokens, max_tokens: int, start_planes=None):
+        """The reference's own tq_ctx_init + tq_forward_token (model/context.c:6-122) over `tokens`
+        with a Q8 KV cache (reference builds only).  model: cfg (n_q_heads, n_kv_heads, head_dim,
+        hidden_size, rope_theta, rms_eps, n_layers, intermediate_size, vocab_size), fmt ("8" / "4"),
+        embed (packed rows), final_norm, and layers: dicts with input_norm, post_norm, q_norm, k_norm
+        and the packed wq, wk, wv, wo, wgate, wup, wdown.  Returns (logits per token [n][vocab],
+        return codes, the K and V planes of every layer after the last token).  start_planes: (pos,
+        [(k, v) per layer]) to start from a cache that already holds positions [0, pos) (copied into
+        the context's planes) instead of an empty one."""
+        if self.kind == "port":
+            raise ValueError("forward_tokens runs the reference's own runtime: a reference build is needed")
+        c = model["cfg"]
+        f = 0 if model["fmt"] == "8" else 1
+        hidden, inter, vocab, hd = c["hidden_size"], c["intermediate_size"], c["vocab_size"], c["head_dim"]
+        q_dim, kv_dim = c["n_q_heads"] * hd, c["n_kv_heads"] * hd
+        keep = []
+
+        def mat(a, rows, cols):
+            a = np.ascontiguousarray(a)
+            keep.append(a)
+            return _TqMatrix(_vp(a), f, rows, cols)
+
+        def vec(a):
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            keep.append(a)
+            return _vp(a)
+
+        layers = (_TqLayerWeights * c["n_layers"])()
+        for i, lw in enumerate(model["layers"]):
+            attn = _TqAttnWeights(mat(lw["wq"], q_dim, hidden), mat(lw["wk"], kv_dim, hidden),
+                                  mat(lw["wv"], kv_dim, hidden), mat(lw["wo"], hidden, q_dim), vec(lw["q_norm"]),
+                                  vec(lw["k_norm"]))
+            mlp = _TqMlpWeights(mat(lw["wgate"], inter, hidden), mat(lw["wup"], inter, hidden),
+                                mat(lw["wdown"], hidden, inter))
+            layers[i] = _TqLayerWeights(vec(lw["input_norm"]), attn, vec(lw["post_norm"]), mlp)
+        cfg = _TqModelConfig(_TqAttnConfig(c["n_q_heads"], c["n_kv_heads"], hd, hidden, c["rope_theta"],
+                                           c["rms_eps"]), c["n_layers"], inter, vocab)
+        m = _TqModel(cfg, mat(model["embed"], vocab, hidden), vec(model["final_norm"]),
+                     ctypes.cast(layers, ctypes.POINTER(_TqLayerWeights)))
+        ctx = _TqCtx()
+        self.lib.tq_ctx_init.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        self.lib.tq_ctx_init.restype = ctypes.c_int
+        self.lib.tq_forward_token.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        self.lib.tq_forward_token.restype = ctypes.c_int
+        self.lib.tq_ctx_free.argtypes = [ctypes.c_void_p]
+        if self.lib.tq_ctx_init(ctypes.byref(ctx), ctypes.byref(m), 1, max_tokens) != 0:
+            raise ValueError("tq_ctx_init refused the model")
+        try:
+            if start_planes is not None:
+                pos0, planes0 = start_planes
+                for i, (kp, vp) in enumerate(planes0):
+                    cache = ctx.caches[i]
+                    ctypes.memmove(cache.k_q8, np.ascontiguousarray(kp).ctypes.data, kp.nbytes)
+                    ctypes.memmove(cache.v_q8, np.ascontiguousarray(vp).ctypes.data, vp.nbytes)
+                ctx.pos = pos0
+            logits, rcs = [], []
+            for t in tokens:
+                rcs.append(self.lib.tq_forward_token(ctypes.byref(ctx), int(t)))
+                logits.append(np.ctypeslib.as_array(ctypes.cast(ctx.logits, ctypes.POINTER(ctypes.c_float)),
+                                                    shape=(vocab,)).copy())
+            row = hd // QK * BLOCK_BYTES
+            planes = []
+            for i in range(c["n_layers"]):
+                cache = ctx.caches[i]
+                shape = (c["n_kv_heads"], max_tokens, row)
+                planes.append((np.ctypeslib.as_array(ctypes.cast(cache.k_q8, ctypes.POINTER(ctypes.c_uint8)),
+                                                     shape=shape).copy(),
+                               np.ctypeslib.as_array(ctypes.cast(cache.v_q8, ctypes.POINTER(ctypes.c_uint8)),
+                                                     shape=shape).copy()))
+            return np.stack(logits), rcs, planes
+        finally:
+            self.lib.tq_ctx_free(ctypes.byref(ctx))
 
     def max_threads(self) -> int:
         return self.lib.refdrv_max_threads() if self.kind != "port" else os.cpu_count() or 1

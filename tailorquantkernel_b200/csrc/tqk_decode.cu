@@ -83,7 +83,7 @@ struct DecodeParams {
     // fused gather of the kv-head-group split (tqk_decode_q8_gather; g_world == 0: off).  The
     // normalised output of local flat q head f = item * n_q_heads + qh goes to every rank r's
     // buffer g_out[r] at [f / g_chunk][g_rank][f % g_chunk][HD] as {value bits, g_epoch} pairs,
-    // each written by one 8-byte store, so a reader that sees the epoch sees the value.
+    // each written by one 64-bit store, so a reader that sees the epoch sees the value.
     int g_world, g_rank, g_chunk, g_epoch;
     uint2 *g_out[8];
 };
@@ -95,13 +95,15 @@ __device__ __forceinline__ void store_out(const DecodeParams &p, float *out_item
         out_item[(long long)qh * HD + c] = v;
         return;
     }
-    const long long f = (long long)item * (p.n_kv * p.group) + qh;
-    const long long grp = f / p.g_chunk, w = f - grp * p.g_chunk;
-    const long long off = ((grp * p.g_world + p.g_rank) * p.g_chunk + w) * HD + c;
-    for (int r = 0; r < p.g_world; r++)  // one 8-byte store per rank, over NVLink for the peers
-        asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p.g_out[r] + off), "r"(__float_as_uint(v)),
-                     "r"(p.g_epoch)
-                     : "memory");
+    // 32-bit index arithmetic (n_items * n_q_heads < 2^31): the division is by a runtime value
+    const unsigned f = (unsigned)item * (unsigned)(p.n_kv * p.group) + (unsigned)qh;
+    const unsigned grp = f / (unsigned)p.g_chunk, w = f - grp * (unsigned)p.g_chunk;
+    const size_t off = ((size_t)(grp * (unsigned)p.g_world + (unsigned)p.g_rank) * (unsigned)p.g_chunk + w) * HD + c;
+    // {value bits, epoch} as one 64-bit access: single-copy atomic, so a reader that sees the
+    // epoch sees the value
+    const unsigned long long pr = ((unsigned long long)(unsigned)p.g_epoch << 32) | __float_as_uint(v);
+    for (int r = 0; r < p.g_world; r++)  // one store per rank, over NVLink for the peers
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p.g_out[r] + off), "l"(pr) : "memory");
 }
 
 template <int NB>

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const ExchangeParam
 
     // launched with programmatic stream serialization: the records come from the decode grid before
     grid_dependency_wait();
+    grid_dependents_launch();  // the next kernel waits for this grid before it touches anything
     // this rank's records of the epoch are in its slot: tell every peer, then wait for theirs
     if (!raise_and_wait_flags(p.mbox, p.world, p.rank, p.epoch, p.flags_off, p.err)) return;
 
@@ -187,6 +188,7 @@ constexpr int GATHER_MAX_V4 = 8;  // float4 per thread: world * chunk <= 8192 fl
 
 __global__ void __launch_bounds__(GATHER_THREADS) exchange_gather_kernel(const GatherParams p) {
     grid_dependency_wait();
+    grid_dependents_launch();  // the next kernel waits for this grid before it touches anything
     if (!raise_and_wait_flags(p.mbox, p.world, p.rank, p.epoch, p.flags_off, p.err)) return;
     const int g = blockIdx.x, tid = threadIdx.x, par = p.epoch & 1;
     const int c4 = p.chunk >> 2, total = p.world * c4;
@@ -209,27 +211,35 @@ __global__ void __launch_bounds__(GATHER_THREADS) exchange_gather_kernel(const G
     }
 }
 
-__device__ __forceinline__ uint2 ld_relaxed_sys_v2(const uint2 *p) {
-    uint2 v;
-    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-    return v;
+// One {value bits, epoch} pair as a single 64-bit access (the writer's is one too).
+__device__ __forceinline__ uint2 ld_relaxed_sys_pair(const uint2 *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return make_uint2((uint32_t)v, (uint32_t)(v >> 32));
 }
 
-// tqk_gather_collect: every thread loads its {value, epoch} pairs, re-reads a
-// pair (bounded: 1 s in all) until it shows the step's epoch, and writes the
-// value.  Then the grid waits for the kernel before it on the stream (the
-// decode that wrote this rank's own pairs) to complete, so that the stream's
-// next kernel may reuse that decode's workspace.
+// tqk_gather_collect: launched with programmatic dependent launch behind the
+// decode, so its blocks are resident early; they first wait for that decode
+// grid to complete (this rank's own pairs are then written, and the stream's
+// next kernel may reuse the decode's workspace), and only then poll -- polling
+// during the decode would put every thread's re-reads on the memory system the
+// decode is streaming through.  Every thread loads its {value, epoch} pairs,
+// re-reads a pair (bounded: 1 s in all) until it shows the step's epoch, and
+// writes the value.
 constexpr int COLLECT_THREADS = 256, COLLECT_PER = 4;
 
 __global__ void __launch_bounds__(COLLECT_THREADS) gather_collect_kernel(const uint2 *pairs, long long n, int epoch,
                                                                         float *out, int *err) {
+    grid_dependency_wait();
+    // the next step's decode may launch now: it waits for this grid before it reads or writes
+    // anything, and its CTAs find the SMs the finished decode left
+    grid_dependents_launch();
     const long long base = (long long)blockIdx.x * COLLECT_THREADS * COLLECT_PER + threadIdx.x;
     uint2 v[COLLECT_PER];
 #pragma unroll
     for (int k = 0; k < COLLECT_PER; k++) {
         const long long i = base + (long long)k * COLLECT_THREADS;
-        if (i < n) v[k] = ld_relaxed_sys_v2(pairs + i);
+        if (i < n) v[k] = ld_relaxed_sys_pair(pairs + i);
     }
     bool ok = true;
     uint64_t t0 = 0;
@@ -245,11 +255,10 @@ __global__ void __launch_bounds__(COLLECT_THREADS) gather_collect_kernel(const u
                 break;
             }
             __nanosleep(64);
-            v[k] = ld_relaxed_sys_v2(pairs + i);
+            v[k] = ld_relaxed_sys_pair(pairs + i);
         }
         out[i] = __uint_as_float(v[k].x);
     }
-    grid_dependency_wait();
 }
 
 }  // namespace

@@ -130,6 +130,25 @@ class AttnLayerArgs(ctypes.Structure):
 
 
 tqk_attention_layer = _sig("tqk_attention_layer", [ctypes.POINTER(AttnLayerArgs), _vp, _sz, _vp])
+
+
+class LayerWeights(ctypes.Structure):
+    """Mirror of tqk_layer_weights (include/tqk.h)."""
+    _fields_ = [("input_norm", _vp), ("post_norm", _vp), ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp),
+                ("q_norm", _vp), ("k_norm", _vp), ("wgate", _vp), ("wup", _vp), ("wdown", _vp),
+                ("k_cache", _vp), ("v_cache", _vp)]
+
+
+class Model(ctypes.Structure):
+    """Mirror of tqk_model (include/tqk.h)."""
+    _fields_ = [("n_layers", _i), ("n_q_heads", _i), ("n_kv_heads", _i), ("head_dim", _i), ("hidden_size", _i),
+                ("intermediate_size", _i), ("vocab_size", _i), ("max_tokens", _i), ("rms_eps", _f), ("format", _i),
+                ("embed", _vp), ("final_norm", _vp), ("rope_cos", _vp), ("rope_sin", _vp),
+                ("layers", ctypes.POINTER(LayerWeights))]
+
+
+tqk_forward_scratch_bytes = _sig("tqk_forward_scratch_bytes", [ctypes.POINTER(Model)], _sz)
+tqk_forward_token = _sig("tqk_forward_token", [ctypes.POINTER(Model), _i, _i, _vp, _vp, _vp, _vp, _sz, _vp])
 tqk_attend_q8 = _sig("tqk_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp])
 tqk_append_attend_q8 = _sig("tqk_append_attend_q8", [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
 tqk_prefill_q8 = _sig("tqk_prefill_q8", [_vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp])
@@ -171,6 +190,7 @@ EXPORTED = [
     "tqk_ipc_open_handle", "tqk_ipc_close_handle", "tqk_exchange_merge",
     "tqk_gather_mailbox_bytes", "tqk_gather_slot_offset", "tqk_exchange_gather",
     "tqk_decode_q8_gather", "tqk_decode_unit_count", "tqk_gather_collect",
+    "tqk_forward_scratch_bytes", "tqk_forward_token",
 ]
 
 
@@ -363,6 +383,39 @@ def attention_layer(args: AttnLayerArgs, workspace=None, stream=None) -> None:
     ws = _ptr(workspace) if workspace is not None else None
     nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
     check(tqk_attention_layer(ctypes.byref(args), ws, nbytes, _stream(stream)), "tqk_attention_layer")
+
+
+def model_struct(cfg: dict, layers: list, embed, final_norm, rope_cos, rope_sin, fmt: int = 0) -> Model:
+    """tqk_model from device tensors.  cfg: n_layers, n_q_heads, n_kv_heads, head_dim, hidden_size,
+    intermediate_size, vocab_size, max_tokens, rms_eps; layers: one dict per layer with the keys of
+    tqk_layer_weights.  The returned struct keeps its layer array alive."""
+    arr = (LayerWeights * len(layers))()
+    for i, lw in enumerate(layers):
+        for k, _t in LayerWeights._fields_:
+            setattr(arr[i], k, _ptr(lw[k]))
+    m = Model()
+    for k in ("n_layers", "n_q_heads", "n_kv_heads", "head_dim", "hidden_size", "intermediate_size", "vocab_size",
+              "max_tokens"):
+        setattr(m, k, int(cfg[k]))
+    m.rms_eps = float(cfg["rms_eps"])
+    m.format = fmt
+    m.embed, m.final_norm, m.rope_cos, m.rope_sin = _ptr(embed), _ptr(final_norm), _ptr(rope_cos), _ptr(rope_sin)
+    m.layers = ctypes.cast(arr, ctypes.POINTER(LayerWeights))
+    m._keep = arr  # noqa: SLF001  (the layer array must outlive the struct)
+    return m
+
+
+def forward_scratch_bytes(model: Model) -> int:
+    return tqk_forward_scratch_bytes(ctypes.byref(model))
+
+
+def forward_token(model: Model, token: int, pos: int, scratch, logits, next_token=None, workspace=None,
+                  stream=None) -> None:
+    """tqk_forward_token: one token through the whole stack on the device."""
+    ws = _ptr(workspace) if workspace is not None else None
+    nbytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    check(tqk_forward_token(ctypes.byref(model), token, pos, _ptr(scratch), _ptr(logits), _ptr(next_token), ws,
+                            nbytes, _stream(stream)), "tqk_forward_token")
 
 
 def decode_static(args: DecodeArgs, stream=None) -> None:

@@ -180,3 +180,29 @@ def layer_inputs(seed: int, n_q: int, n_kv: int, hd: int, hidden: int, max_token
     vf[:, pos:] = 0.0
     xn = rng.standard_normal(hidden, dtype=np.float32)
     return w, qn, kn, port.quantize_rows(kf), port.quantize_rows(vf), xn
+
+
+def forward_model(seed: int, fmt: str, port, n_layers: int = 2, n_q: int = 8, n_kv: int = 2, hd: int = 128,
+                  hidden: int = 256, inter: int = 512, vocab: int = 96, theta: float = 500000.0,
+                  eps: float = 1e-5) -> dict:
+    """A small decoder stack for tq_forward_token (model/context.c:104-122): packed weights
+    (uniform in [-1, 1), packed by the pinned oracle packer; the embedding x0.5), norm weights
+    1 + 0.1 N(0,1), in the layout of Oracle.forward_tokens."""
+    rng = np.random.default_rng(seed)
+    q_dim, kv_dim = n_q * hd, n_kv * hd
+
+    def packed(rows, cols, scale=1.0):
+        return port.pack_matrix((rng.uniform(-1.0, 1.0, (rows, cols)) * scale).astype(np.float32), fmt)
+
+    def norm(n):
+        return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    layers = []
+    for _ in range(n_layers):
+        layers.append({"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(hd), "k_norm": norm(hd),
+                       "wq": packed(q_dim, hidden), "wk": packed(kv_dim, hidden), "wv": packed(kv_dim, hidden),
+                       "wo": packed(hidden, q_dim), "wgate": packed(inter, hidden), "wup": packed(inter, hidden),
+                       "wdown": packed(hidden, inter)})
+    cfg = {"n_q_heads": n_q, "n_kv_heads": n_kv, "head_dim": hd, "hidden_size": hidden, "rope_theta": theta,
+           "rms_eps": eps, "n_layers": n_layers, "intermediate_size": inter, "vocab_size": vocab}
+    return {"cfg": cfg, "fmt": fmt, "embed": packed(vocab, hidden, 0.5), "final_norm": norm(hidden), "layers": layers}

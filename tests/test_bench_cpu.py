@@ -26,7 +26,7 @@ def _run(*args, env_extra=None):
     return lines
 
 
-@pytest.mark.parametrize("config", [2, 3, 4, 5, 6])
+@pytest.mark.parametrize("config", [2, 3, 4, 5, 6, 7])
 def test_reference_arm_line(config):
     lines = _run("--impl", "reference", "--config", str(config), "--tiny", "--steps", "2", "--warmup", "3",
                  "--ref-seconds", "0.2")

@@ -1,0 +1,80 @@
+"""tqk_forward_token -- one token through a whole decoder stack on the device --
+against the reference's own runtime (tq_ctx_init + tq_forward_token,
+model/context.c:6-122, built from the reference's sources into oracle/_ref):
+the tokens of the reference's forward test (tools/test_model.c:1547) through a
+two-layer stack with Q8 or Q4 weights, the logits within the decode tolerance
+of the largest reference logit at every step, the same greedy choice
+(model/sampler.c:3-13), the caches' appended rows close to the reference's,
+and the reference's -1 guards."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOKENS = [3, 17, 17, 42, 0, 9]
+
+
+def _upload(model, mt, ref, fmt):
+    import torch
+    from tailorquantkernel_b200 import tqk
+    c = model["cfg"]
+    hd, nkv = c["head_dim"], c["n_kv_heads"]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    keep, layers = [], []
+    for lw in model["layers"]:
+        d = {k: dev(v) for k, v in lw.items()}
+        d["k_cache"] = torch.zeros(nkv, mt, hd // 32 * 36, dtype=torch.uint8, device="cuda")
+        d["v_cache"] = torch.zeros_like(d["k_cache"])
+        layers.append(d)
+        keep.append(d)
+    tabs = [ref.rope_table(hd, p, c["rope_theta"]) for p in range(mt)]
+    cos = dev(np.stack([t[0] for t in tabs]))
+    sin = dev(np.stack([t[1] for t in tabs]))
+    embed, final_norm = dev(model["embed"]), dev(model["final_norm"])
+    cfg = dict(c, max_tokens=mt)
+    m = tqk.model_struct(cfg, layers, embed, final_norm, cos, sin, fmt=0 if fmt == "8" else 1)
+    keep += [cos, sin, embed, final_norm]
+    return m, layers, keep
+
+
+@pytest.mark.parametrize("fmt", ["8", "4"])
+def test_forward_token_matches_the_reference_runtime(cuda, fmt):
+    import torch
+
+    import oracle
+    from _cases import forward_model
+    from tailorquantkernel_b200 import tqk
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree at build time)")
+    ref, port = oracle.Oracle("ref_scalar"), oracle.Oracle("port")
+    model = forward_model(72 if fmt == "8" else 73, fmt, port)
+    vocab, mt = model["cfg"]["vocab_size"], 8
+    ref_logits, rcs, ref_planes = ref.forward_tokens(model, TOKENS, mt)
+    assert rcs == [0] * len(TOKENS)
+    m, layers, _keep = _upload(model, mt, ref, fmt)
+    scratch = torch.empty(tqk.forward_scratch_bytes(m) // 4, device="cuda")
+    nxt = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    for pos, tok in enumerate(TOKENS):
+        logits = torch.full((vocab,), float("nan"), device="cuda")
+        tqk.forward_token(m, tok, pos, scratch, logits, next_token=nxt)
+        got = logits.cpu().numpy()
+        want = ref_logits[pos]
+        err = float(np.abs(got - want).max())
+        print(f"forward q{fmt} pos {pos}: max |diff| {err:.3g} of max |logit| {np.abs(want).max():.3g}")
+        assert np.isfinite(got).all() and err <= 1e-3 * float(np.abs(want).max()), (pos, err)
+        assert int(nxt.item()) == int(np.argmax(want)) == int(np.argmax(got)), pos
+    # the appended K / V rows of every layer: the same Q8 rows up to an occasional one-step rounding
+    row = model["cfg"]["head_dim"] // 32 * 36
+    for (kr, vr), d in zip(ref_planes, layers):
+        for want_plane, got_plane in ((kr, d["k_cache"]), (vr, d["v_cache"])):
+            a = oracle.dequantize(want_plane[:, :len(TOKENS)].reshape(-1, row))
+            b = oracle.dequantize(got_plane.cpu().numpy()[:, :len(TOKENS)].reshape(-1, row))
+            assert np.abs(a - b).max() <= 1e-2 * np.abs(a).max()
+    # the reference's guards: a token past the vocabulary, a full cache
+    with pytest.raises(tqk.TQKError) as e:
+        tqk.forward_token(m, vocab, len(TOKENS), scratch, logits)
+    assert e.value.status == -1
+    with pytest.raises(tqk.TQKError) as e:
+        tqk.forward_token(m, 0, mt, scratch, logits)
+    assert e.value.status == -1
+    assert tqk.device_status() == 0

@@ -512,15 +512,18 @@ def _rank_main_fused(rank, world, port, result_dir):
         dist.destroy_process_group()
 
 
-def test_fused_head_split_two_gpus(cuda, tmp_path):
-    """The fused kv-head-group split over 2 GPUs against the oracle (three steps, both parities)."""
+def test_fused_head_split_all_gpus(cuda, tmp_path):
+    """The fused kv-head-group split over every GPU of the box (2, 4 or 8 ranks; the 8 kv heads
+    must divide) against the oracle (three steps, both parities)."""
     import torch
     import torch.multiprocessing as mp
     from _cases import tolerance_ok
-    if torch.cuda.device_count() < 2:
+    n = torch.cuda.device_count()
+    world = 8 if n >= 8 else 4 if n >= 4 else 2
+    if n < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_rank_main_fused, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    for r in range(2):
+    mp.spawn(_rank_main_fused, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
         rows_ok, status = (int(x) for x in open(tmp_path / f"fused_rank{r}.txt").read().split())
         assert rows_ok == 1 and status == 0, (r, rows_ok, status)
         got, ref = np.load(tmp_path / f"fused_rank{r}.npy")

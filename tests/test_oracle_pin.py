@@ -293,3 +293,23 @@ def test_pack_edges_against_reference_build(port):
     ref = oracle.Oracle("ref_scalar")
     for fmt in "84":
         assert np.array_equal(port.pack_matrix(w, fmt), ref.pack_matrix(w, fmt))
+
+
+def test_reference_forward_runs_through_the_oracle_binding():
+    """Oracle.forward_tokens drives the reference's own tq_ctx_init / tq_forward_token
+    (model/context.c:6-122): finite logits, its guards (a token past the vocabulary and a full
+    cache both return -1) and a deterministic result."""
+    import oracle
+    from _cases import forward_model
+    if not oracle.available("ref_scalar"):
+        pytest.skip("oracle/_ref not built (needs the reference tree)")
+    ref, port = oracle.Oracle("ref_scalar"), oracle.Oracle("port")
+    model = forward_model(71, "8", port)
+    logits, rcs, planes = ref.forward_tokens(model, [3, 17, 17, 42], max_tokens=4)
+    assert rcs == [0, 0, 0, 0] and np.isfinite(logits).all()
+    again, _, planes2 = ref.forward_tokens(model, [3, 17, 17, 42], max_tokens=4)
+    assert np.array_equal(logits, again) and all(np.array_equal(a[0], b[0]) for a, b in zip(planes, planes2))
+    _, rcs, _ = ref.forward_tokens(model, [3, 96], max_tokens=4)
+    assert rcs == [0, -1]
+    _, rcs, _ = ref.forward_tokens(model, [1, 2, 3], max_tokens=2)
+    assert rcs == [0, 0, -1]
