@@ -41,6 +41,9 @@ typedef struct mirror {
     int n_kv, head_dim, max_tokens, device;
     tqk_block_q8 *dk, *dv;      /* device planes [n_kv][max_tokens][nb] */
     int synced;                 /* positions [0, synced) identical on host and device; -1 = unknown */
+    unsigned char *last_rows;   /* the K then V rows of every kv head this library last wrote to the
+                                   host planes, at position synced - 1: a caller who rewrites them
+                                   between calls is noticed (tq_b200_cache_invalidate covers the rest) */
     struct mirror *next;
 } mirror;
 
@@ -178,7 +181,31 @@ static void mirror_release(mirror *m) {
     if (!m) return;
     cudaFree(m->dk);
     cudaFree(m->dv);
+    free(m->last_rows);
     free(m);
+}
+
+/* The host rows at position pos of every kv head, K then V, into dst (or compared with it). */
+static int rows_at(const mirror *m, const tq_kv_cache *cache, int pos, unsigned char *dst, int compare) {
+    const size_t row = (size_t)(m->head_dim / QK) * sizeof(block_q8);
+    for (int plane = 0; plane < 2; plane++) {
+        const unsigned char *base = (const unsigned char *)(plane ? cache->v_q8 : cache->k_q8);
+        for (int h = 0; h < m->n_kv; h++) {
+            const unsigned char *src = base + ((size_t)h * m->max_tokens + pos) * row;
+            unsigned char *d = dst + ((size_t)plane * m->n_kv + h) * row;
+            if (compare) {
+                if (memcmp(d, src, row) != 0) return 1;
+            } else {
+                memcpy(d, src, row);
+            }
+        }
+    }
+    return 0;
+}
+
+/* After a call wrote rows [.., pos] into the host planes: remember row pos. */
+static void mirror_note_written(mirror *m, const tq_kv_cache *cache, int pos) {
+    if (m->last_rows) rows_at(m, cache, pos, m->last_rows, 0);
 }
 
 static mirror *mirror_find(const void *kk, const void *vv) {
@@ -223,6 +250,7 @@ static int mirror_get(const tq_kv_cache *cache, const tq_attn_config *cfg, mirro
         m->max_tokens = cache->max_tokens;
         m->device = G.device;
         m->synced = -1;
+        m->last_rows = (unsigned char *)malloc((size_t)2 * cfg->n_kv_heads * (cfg->head_dim / QK) * sizeof(block_q8));
         m->next = G.mirrors;
         G.mirrors = m;
     }
@@ -230,9 +258,11 @@ static int mirror_get(const tq_kv_cache *cache, const tq_attn_config *cfg, mirro
     return 0;
 }
 
-/* Makes device rows [0, pos) of every kv head equal to the host's. */
+/* Makes device rows [0, pos) of every kv head equal to the host's.  A mirror that
+ * holds [0, pos) already is trusted unless the host's row pos - 1 no longer holds
+ * what this library wrote there. */
 static int mirror_sync_prefix(mirror *m, const tq_kv_cache *cache, int pos) {
-    if (m->synced == pos) return 0;
+    if (m->synced == pos && (pos == 0 || !m->last_rows || !rows_at(m, cache, pos - 1, m->last_rows, 1))) return 0;
     const size_t row = (size_t)(m->head_dim / QK) * sizeof(block_q8);
     const size_t pitch = (size_t)m->max_tokens * row;
     if (pos > 0) {
@@ -304,6 +334,7 @@ static int q8_append_attend(tq_kv_cache *cache, const tq_attn_config *cfg, int p
         memcpy((unsigned char *)cache->v_q8 + dst, h + off_rv + (size_t)kvh * n * row, (size_t)n * row);
     }
     m->synced = pos0 + n;
+    mirror_note_written(m, cache, pos0 + n - 1);
     return set_status(0);
 }
 
@@ -561,6 +592,7 @@ static int device_layers(const wreg *r, tq_kv_cache *cache, const tq_attn_config
         memcpy((unsigned char *)cache->v_q8 + dst, h + h_rv + (size_t)kvh * n * row, (size_t)n * row);
     }
     m->synced = pos0 + n;
+    mirror_note_written(m, cache, pos0 + n - 1);
     return set_status(0);
 }
 

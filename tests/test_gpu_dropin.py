@@ -188,3 +188,63 @@ def test_device_error_word_reaches_the_dropin_caller(cuda):
             tqk.peer_buffer_free(b)
         lib.tq_kv_cache_free.argtypes = [ctypes.c_void_p]
         lib.tq_kv_cache_free(ctypes.byref(cache))
+
+
+@pytest.mark.parametrize("registered", [True, False])
+def test_rewritten_last_row_is_noticed_without_invalidate(cuda, registered):
+    """A caller that rewrites the cache row the previous call appended (here: K and V of
+    every kv head at that position replaced by rows ten times larger, so that this token
+    dominates the softmax) and calls again WITHOUT tq_b200_cache_invalidate: the drop-in
+    compares that row with the copy it wrote, re-uploads the planes, and the output follows
+    the rewritten cache (the reference reads the host planes on every call)."""
+    import ctypes
+
+    import numpy as np
+
+    import oracle
+    from _cases import layer_inputs
+    if not os.path.exists(HARNESS):
+        pytest.skip("oracle/_ref/libtqref_dropin.so not built (needs the reference tree at build time)")
+    lib = ctypes.CDLL(HARNESS)
+    port = oracle.Oracle("port")
+    seed, nq, nkv, hd, hidden, mt, pos, theta, eps = LAYER
+    fmt = "8"
+    w, qn, kn, kp, vp_, xn = layer_inputs(seed, nq, nkv, hd, hidden, mt, pos, fmt, port)
+    aw, cfg = _layer_structs(oracle, w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps)
+    cache = oracle._TqKvCache()
+    lib.tq_kv_cache_init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int]
+    assert lib.tq_kv_cache_init(ctypes.byref(cache), 1, ctypes.byref(cfg), mt) == 0
+    ctypes.memmove(cache.k_q8, kp.ctypes.data, kp.nbytes)
+    ctypes.memmove(cache.v_q8, vp_.ctypes.data, vp_.nbytes)
+    host_k = np.ctypeslib.as_array(ctypes.cast(cache.k_q8, ctypes.POINTER(ctypes.c_uint8)), shape=kp.shape)
+    host_v = np.ctypeslib.as_array(ctypes.cast(cache.v_q8, ctypes.POINTER(ctypes.c_uint8)), shape=vp_.shape)
+    if registered:
+        assert lib.tq_b200_register_attn_weights(ctypes.byref(aw), ctypes.byref(cfg)) == 0
+    fn = lib.attention_layer
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                   ctypes.c_void_p, ctypes.c_void_p]
+    scores = np.zeros(nq * mt, np.float32)
+    out = np.zeros(hidden, np.float32)
+    kp_ref, vp_ref = kp.copy(), vp_.copy()
+    try:
+        assert fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos, xn.ctypes.data, scores.ctypes.data,
+                  out.ctypes.data) == 0
+        port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp_ref, vp_ref, mt, pos, xn)
+        rng = np.random.default_rng(29)
+        new_k = port.quantize_rows(10.0 * rng.standard_normal((nkv, hd), dtype=np.float32))
+        new_v = port.quantize_rows(10.0 * rng.standard_normal((nkv, hd), dtype=np.float32))
+        host_k[:, pos] = new_k
+        host_v[:, pos] = new_v
+        kp_ref[:, pos] = new_k
+        vp_ref[:, pos] = new_v
+        x = rng.standard_normal(hidden, dtype=np.float32)
+        assert fn(ctypes.byref(aw), ctypes.byref(cfg), ctypes.byref(cache), pos + 1, x.ctypes.data,
+                  scores.ctypes.data, out.ctypes.data) == 0
+        want = port.attention_layer(w, fmt, qn, kn, nq, nkv, hd, hidden, theta, eps, kp_ref, vp_ref, mt, pos + 1, x)
+        assert np.array_equal(host_k[:, pos + 1], kp_ref[:, pos + 1])
+        assert np.abs(out - want).max() <= 1e-3 * np.abs(want).max()
+    finally:
+        if registered:
+            lib.tq_b200_unregister_attn_weights(ctypes.byref(aw))
+        lib.tq_kv_cache_free.argtypes = [ctypes.c_void_p]
+        lib.tq_kv_cache_free(ctypes.byref(cache))
