@@ -172,6 +172,121 @@ class HostBuffer:
 
 
 # ---------------------------------------------------------------------------
+# synthetic inputs: the reference benches' own generator
+# ---------------------------------------------------------------------------
+# Every config draws its K/V, q and appended rows (and norm weights, sequence lengths and outlier
+# picks) from the stream of the reference's benches: one xorshift64 generator from the seed
+# 88172645463325252 read through normal_sample / uniform_open (tools/bench_forward.c:82,199-210).
+# A config lays its inputs out as consecutive windows of that stream in a fixed order that does
+# not depend on the number of GPUs, so a rank fills its own share of the same global inputs.
+# Uniforms come from the same generator from step 2^62 on, which no normal sample reaches.
+UNIFORM_BASE = 1 << 62
+
+
+class LibGen:
+    """Our arm: tqk_fill_normal / tqk_fill_uniform (host threads, each jumping ahead to its
+    window; the same floats as the reference's sequential generator)."""
+    kind = "tqk_fill_normal"
+
+    def normal(self, first: int, n: int, scale: float = 1.0) -> np.ndarray:
+        from tailorquantkernel_b200 import tqk
+        return tqk.fill_normal(first, n, scale)
+
+    def uniform(self, first: int, n: int) -> np.ndarray:
+        from tailorquantkernel_b200 import tqk
+        return tqk.fill_uniform(UNIFORM_BASE + first, n)
+
+
+_XS_MASK = (1 << 64) - 1
+
+
+def _xs_step(x: int) -> int:
+    x ^= (x << 13) & _XS_MASK
+    x ^= x >> 7
+    return x ^ ((x << 17) & _XS_MASK)
+
+
+class RefGen:
+    """The reference arm: the reference's own normal_sample / uniform_open (oracle/_ref/libtqref_rng.so,
+    tools/bench_forward.c compiled in place; sequential), started at any window by jumping the
+    xorshift64 state: the step is linear over GF(2), so T^k is applied from its powers of two."""
+    kind = "reference normal_sample"
+    SEED = 88172645463325252
+
+    def __init__(self, path: str):
+        import ctypes
+        self._ct = ctypes
+        self.lib = ctypes.CDLL(path)
+        cols = [_xs_step(1 << i) for i in range(64)]
+        self.pows = [cols]
+        for _ in range(63):
+            m = self.pows[-1]
+            self.pows.append([self._apply(m, c) for c in m])
+
+    @staticmethod
+    def _apply(m, v: int) -> int:
+        r, i = 0, 0
+        while v:
+            if v & 1:
+                r ^= m[i]
+            v >>= 1
+            i += 1
+        return r
+
+    def _state(self, steps: int) -> int:
+        x, k = self.SEED, 0
+        while steps:
+            if steps & 1:
+                x = self._apply(self.pows[k], x)
+            steps >>= 1
+            k += 1
+        return x
+
+    def _fill(self, fn, steps: int, n: int) -> np.ndarray:
+        ct = self._ct
+        out = np.empty(n, np.float32)
+        st = ct.c_uint64(self._state(steps))
+        fn(ct.byref(st), ct.c_void_p(out.ctypes.data), ct.c_size_t(n))
+        return out
+
+    def normal(self, first: int, n: int, scale: float = 1.0) -> np.ndarray:
+        out = self._fill(self.lib.tqref_normal_fill, 2 * first, n)
+        return out if scale == 1.0 else out * np.float32(scale)
+
+    def uniform(self, first: int, n: int) -> np.ndarray:
+        return self._fill(self.lib.tqref_uniform_fill, UNIFORM_BASE + first, n)
+
+
+def reference_generator():
+    """The reference's own generator for the reference arm, else (no reference build here) the
+    library's, which gives the same floats."""
+    path = os.path.join(ROOT, "oracle", "_ref", "libtqref_rng.so")
+    return RefGen(path) if os.path.exists(path) else LibGen()
+
+
+def outliers(gen, first_u: int, x: np.ndarray) -> np.ndarray:
+    """1% of the entries times 8 (config 3): entry i is picked when uniform #(first_u + i) < 0.01."""
+    u = gen.uniform(first_u, x.size).reshape(x.shape)
+    return np.where(u < np.float32(0.01), x * np.float32(8), x)
+
+
+def ragged_lengths(gen, count: int, lo: int, hi: int) -> np.ndarray:
+    """count lengths uniform on [lo, hi] from uniforms #0.. (u in (0, 1] -> lo + floor(u * (hi - lo + 1)),
+    u = 1 clamped to hi)."""
+    u = gen.uniform(0, count).astype(np.float64)
+    return np.minimum(lo + np.floor(u * (hi - lo + 1)), hi).astype(np.int32)
+
+
+def device_q8_rows(gen, first: int, rows: int, hd: int, out=None):
+    """rows x hd normal samples from `first`, quantised on the device into Q8 rows (the bit-exact
+    quantiser): written into `out` ([rows, hd/32*36] uint8, contiguous) or returned."""
+    import torch
+    from tailorquantkernel_b200 import tqk
+    x = torch.from_numpy(gen.normal(first, rows * hd)).cuda().view(rows, hd)
+    return tqk.quantize_rows(x, out=out)
+
+
+# ---------------------------------------------------------------------------
 # distributed plumbing
 # ---------------------------------------------------------------------------
 def dist_init(n_gpus: int):
@@ -212,6 +327,16 @@ def barrier(dist):
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
+def config2_stream(layers, n_q, n_kv, hd, mt):
+    """Config 2's inputs in the reference stream, in this order: for every layer, K then V, every kv
+    head's mt rows of hd values; then for every layer that step's q [n_q*hd], k [n_kv*hd] and
+    v [n_kv*hd]; then the q and k RMSNorm weights [layers][hd] each (as 1 + 0.1 x, --prologue)."""
+    rows = mt * hd
+    step = layers * 2 * n_kv * rows
+    return {"kv": lambda layer, p, h: ((layer * 2 + p) * n_kv + h) * rows, "step": step,
+            "norms": step + layers * (n_q + 2 * n_kv) * hd}
+
+
 def describe_config2(layers, n_q, n_kv, hd, pos, prologue=False):
     """config entry of config 2 (shared by our arm and the reference arm)."""
     row = hd // QK * BB
@@ -256,13 +381,21 @@ class Config2:
         # on N GPUs each rank holds 1/N of the cache, less than L2 for N >= 4: it rotates over N
         # copies of its slice, one per step, so that its working set stays the whole cache's size
         self.copies = world
-        g = torch.Generator(device="cuda").manual_seed(seed + rank)
-        shape = (self.copies, layers, per, self.mt, hd)
-        # setup (untimed): N(0,1) K/V quantised by the device quantiser into the cache
-        self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
-        self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
-        rng = np.random.default_rng(seed)
-        q = rng.standard_normal((layers, n_q * hd), dtype=np.float32)  # the same q at every N
+        gen = LibGen()
+        off = config2_stream(layers, n_q, n_kv, hd, self.mt)
+        row = self.nb * BB
+        # setup (untimed): this rank's kv heads of the global N(0,1) K/V, quantised on the device
+        self.kp = torch.empty(self.copies, layers, per, self.mt, row, dtype=torch.uint8, device="cuda")
+        self.vp = torch.empty_like(self.kp)
+        for layer in range(layers):
+            for p, plane in enumerate((self.kp, self.vp)):
+                device_q8_rows(gen, off["kv"](layer, p, kvh0), per * self.mt, hd,
+                               out=plane[0, layer].view(per * self.mt, row))
+        for c in range(1, self.copies):
+            self.kp[c].copy_(self.kp[0])
+            self.vp[c].copy_(self.vp[0])
+        qkv = gen.normal(off["step"], layers * (n_q + 2 * n_kv) * hd).reshape(layers, n_q + 2 * n_kv, hd)
+        q = np.ascontiguousarray(qkv[:, :n_q]).reshape(layers, n_q * hd)  # the same q at every N
         pro = {}
         if prologue:
             # Qwen3-style layer: per-layer q/k RMSNorm weights and the RoPE table of position pos,
@@ -271,13 +404,16 @@ class Config2:
             ang = np.float32(pos) * inv.astype(np.float32)
             self.rope_cos = torch.from_numpy(np.tile(np.cos(ang).astype(np.float32), (layers, 1))).cuda()
             self.rope_sin = torch.from_numpy(np.tile(np.sin(ang).astype(np.float32), (layers, 1))).cuda()
-            self.q_norm = torch.from_numpy(1 + 0.1 * rng.standard_normal((layers, hd), dtype=np.float32)).cuda()
-            self.k_norm = torch.from_numpy(1 + 0.1 * rng.standard_normal((layers, hd), dtype=np.float32)).cuda()
+            norms = 1 + np.float32(0.1) * gen.normal(off["norms"], 2 * layers * hd).reshape(2, layers, hd)
+            self.q_norm = torch.from_numpy(np.ascontiguousarray(norms[0])).cuda()
+            self.k_norm = torch.from_numpy(np.ascontiguousarray(norms[1])).cuda()
             pro = dict(q_norm=self.q_norm, k_norm=self.k_norm, norm_item_stride=hd, norm_eps=1e-6,
                        rope_cos=self.rope_cos, rope_sin=self.rope_sin, rope_item_stride=hd // 2)
         else:
             q = rope_np(q, hd, pos, 500000.0)
         q = q.reshape(layers, n_q, hd)[:, kvh0 * group:(kvh0 + per) * group].reshape(layers, per * group * hd)
+        k_new = np.ascontiguousarray(qkv[:, n_q + kvh0:n_q + kvh0 + per]).reshape(layers, per * hd)
+        v_new = np.ascontiguousarray(qkv[:, n_q + n_kv + kvh0:n_q + n_kv + kvh0 + per]).reshape(layers, per * hd)
         # q, k_new and v_new live in one device buffer, so the end-to-end leg moves a step's inputs
         # with one host-to-device copy (per chunk of layers on one GPU: [layer][q | k_new | v_new])
         lq, lkv = per * group * hd, per * hd
@@ -285,8 +421,8 @@ class Config2:
         self.lrow = lq + 2 * lkv
         self.inbuf = torch.empty(layers, self.lrow, device="cuda")
         self.inbuf[:, :lq].copy_(torch.from_numpy(np.ascontiguousarray(q)))
-        self.inbuf[:, lq:lq + lkv].copy_(torch.randn(layers, lkv, device="cuda", generator=g))
-        self.inbuf[:, lq + lkv:].copy_(torch.randn(layers, lkv, device="cuda", generator=g))
+        self.inbuf[:, lq:lq + lkv].copy_(torch.from_numpy(k_new))
+        self.inbuf[:, lq + lkv:].copy_(torch.from_numpy(v_new))
         self.lq, self.lkv = lq, lkv
         self.out = torch.empty(layers, n_q * hd, device="cuda")  # the whole output, on every rank
         if world == 1:
@@ -407,6 +543,12 @@ class Config2:
             np.ascontiguousarray(x[:, self.lq:self.lq + self.lkv]), np.ascontiguousarray(x[:, self.lq + self.lkv:])
 
 
+def config4_stream(n_kv, n, hd, p, h):
+    """Config 4's inputs in the reference stream: K then V (p = 0, 1), every kv head's n rows of hd
+    values, then q (p = 2)."""
+    return (p * n_kv + h) * n * hd
+
+
 def describe_config4(n_q, n_kv, hd, n):
     kv_bytes = 2 * n_kv * n * (hd // QK) * BB
     return {"workload": f"config4: Llama-3-70B-shaped Q8 GQA long-context decode, 1 layer, {n_q} q / {n_kv} kv "
@@ -441,12 +583,19 @@ class Config4:
         # that its working set stays the whole cache's size (larger than L2)
         self.copies = world
         self.count = 0
-        g = torch.Generator(device="cuda").manual_seed(seed + rank)
-        shape = (self.copies, n_kv, max(self.n_local, 1), hd)
-        self.kp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
-        self.vp = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
-        gq = torch.Generator(device="cuda").manual_seed(seed)  # the same q on every rank
-        self.q = torch.randn(n_q * hd, device="cuda", generator=gq)
+        gen = LibGen()
+        rows = max(self.n_local, 1)
+        self.kp = torch.zeros(self.copies, n_kv, rows, self.nb * BB, dtype=torch.uint8, device="cuda")
+        self.vp = torch.zeros_like(self.kp)
+        for p, plane in enumerate((self.kp, self.vp)):  # this rank's positions of the global K/V
+            for h in range(n_kv):
+                if self.n_local:
+                    device_q8_rows(gen, config4_stream(n_kv, n, hd, p, h) + self.start * hd, self.n_local, hd,
+                                   out=plane[0, h])
+        for c in range(1, self.copies):
+            self.kp[c].copy_(self.kp[0])
+            self.vp[c].copy_(self.vp[0])
+        self.q = torch.from_numpy(gen.normal(config4_stream(n_kv, n, hd, 2, 0), n_q * hd)).cuda()  # on every rank
         self.out = torch.empty(n_q * hd, device="cuda")
         self.partial = torch.empty(n_q * (hd + 2), device="cuda")
         self.gathered = torch.empty(world, n_q * (hd + 2), device="cuda")
@@ -531,6 +680,16 @@ def rope_np(x, hd, pos, theta):
     return h.astype(np.float32).reshape(x.shape)
 
 
+def config3_stream(all_lens, n_q, n_kv, hd):
+    """Config 3's inputs in the reference stream: the 64 lengths are uniforms #0..63; then for every
+    sequence b, K then V, every kv head's len_b rows of hd values; then every sequence's q [n_q*hd].
+    The outlier pick of normal sample i is uniform #(64 + i)."""
+    starts = np.concatenate([[0], np.cumsum(all_lens.astype(np.int64))]) * (2 * n_kv * hd)
+    q0 = int(starts[-1])
+    return {"kv": lambda b, p: int(starts[b]) + p * n_kv * int(all_lens[b]) * hd,
+            "q": lambda b: q0 + b * n_q * hd, "u": lambda i: len(all_lens) + i}
+
+
 def describe_config3(all_lens, lo, mt, n_q, n_kv, hd):
     kv_bytes = 2 * n_kv * int(np.sum(all_lens)) * (hd // QK) * BB
     return {"workload": f"config3: ragged batched Q8 GQA decode, {len(all_lens)} sequences, lengths U[{lo}, {mt}] "
@@ -557,21 +716,23 @@ class Config3:
         self.tqk = tqk
         self.L, self.nq, self.nkv, self.hd, self.mt, self.lo = 1, n_q, n_kv, hd, mt, lo
         self.nb = hd // QK
-        rng = np.random.default_rng(seed)
-        self.all_lens = rng.integers(lo, mt + 1, self.B).astype(np.int32)
+        gen = LibGen()
+        self.all_lens = ragged_lengths(gen, self.B, lo, mt)
+        off = config3_stream(self.all_lens, n_q, n_kv, hd)
         self.mine = shard.batch_shard(self.all_lens, world)[rank]
         lens = self.all_lens[self.mine]
         nloc = len(self.mine)
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        self.kp = torch.empty(nloc, n_kv, mt, self.nb * BB, dtype=torch.uint8, device="cuda")
-        self.vp = torch.empty_like(self.kp)
-        for i in range(nloc):  # one sequence at a time: bounded fp32 scratch
-            for plane in (self.kp, self.vp):
-                x = torch.randn(n_kv, mt, hd, device="cuda", generator=g)
-                x = torch.where(torch.rand(n_kv, mt, hd, device="cuda", generator=g) < 0.01, x * 8, x)
-                plane[i] = tqk.quantize_rows(x).view(n_kv, mt, self.nb * BB)
+        self.kp = torch.zeros(nloc, n_kv, mt, self.nb * BB, dtype=torch.uint8, device="cuda")
+        self.vp = torch.zeros_like(self.kp)
+        for i, b in enumerate(self.mine):  # one sequence at a time: bounded fp32 scratch
+            n = int(self.all_lens[b])
+            for p, plane in enumerate((self.kp, self.vp)):
+                x = outliers(gen, off["u"](off["kv"](b, p)), gen.normal(off["kv"](b, p), n_kv * n * hd))
+                x = torch.from_numpy(x).cuda().view(n_kv, n, hd)
+                for h in range(n_kv):
+                    tqk.quantize_rows(x[h], out=plane[i, h, :n])
         self.lens = torch.from_numpy(lens).cuda()
-        self.q = torch.randn(nloc, n_q * hd, device="cuda", generator=g)
+        self.q = torch.from_numpy(np.stack([gen.normal(off["q"](b), n_q * hd) for b in self.mine])).cuda()
         self.out = torch.empty(nloc, n_q * hd, device="cuda")
         self.kv_bytes = 2 * n_kv * int(self.all_lens.sum()) * self.nb * BB  # the whole batch
         self.bytes_per_step = 2 * n_kv * int(lens.sum()) * self.nb * BB   # this rank's decode kernel
@@ -631,6 +792,14 @@ def prefill_flops(n_q, hd, pos0, n):
     return n_q * pairs * 2 * 2 * hd
 
 
+def config5_stream(n_q, n_kv, hd, pos0, n):
+    """Config 5's inputs in the reference stream: K then V of the cached prefix, every kv head's pos0
+    rows of hd values; then the chunk's q [n][n_q*hd], k [n][n_kv*hd] and v [n][n_kv*hd]."""
+    kv = 2 * n_kv * pos0 * hd
+    return {"kv": lambda p, h: (p * n_kv + h) * pos0 * hd, "q": kv, "k": kv + n * n_q * hd,
+            "v": kv + n * (n_q + n_kv) * hd}
+
+
 def describe_config5(n_q, n_kv, hd, pos0, n):
     return {"workload": f"config5: chunked causal prefill, {n} new tokens at positions {pos0}..{pos0 + n - 1} over a "
                         f"{pos0}-position Q8 cache, {n_q} q / {n_kv} kv heads, head_dim {hd}",
@@ -657,16 +826,15 @@ class Config5:
         self.FLOPS = prefill_flops(n_q, hd, pos0, n)  # 103,095,992,320 at the default shape
         self.mt = pos0 + n
         self.nb = hd // QK
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        kf = torch.zeros(n_kv, self.mt, hd, device="cuda")
-        vf = torch.zeros(n_kv, self.mt, hd, device="cuda")
-        kf[:, :pos0] = torch.randn(n_kv, pos0, hd, device="cuda", generator=g)
-        vf[:, :pos0] = torch.randn(n_kv, pos0, hd, device="cuda", generator=g)
-        self.kp, self.vp = tqk.quantize_rows(kf), tqk.quantize_rows(vf)
-        del kf, vf
-        self.q = torch.randn(n, n_q * hd, device="cuda", generator=g)
-        self.k_new = torch.randn(n, n_kv * hd, device="cuda", generator=g)
-        self.v_new = torch.randn(n, n_kv * hd, device="cuda", generator=g)
+        gen = LibGen()
+        off = config5_stream(n_q, n_kv, hd, pos0, n)
+        self.kp = torch.zeros(n_kv, self.mt, self.nb * BB, dtype=torch.uint8, device="cuda")
+        self.vp = torch.zeros_like(self.kp)
+        for p, plane in enumerate((self.kp, self.vp)):
+            for h in range(n_kv):
+                device_q8_rows(gen, off["kv"](p, h), pos0, hd, out=plane[h, :pos0])
+        dev = lambda key, w: torch.from_numpy(gen.normal(off[key], n * w * hd)).cuda().view(n, w * hd)  # noqa: E731
+        self.q, self.k_new, self.v_new = dev("q", n_q), dev("k", n_kv), dev("v", n_kv)
         self.out = torch.empty(n, n_q * hd, device="cuda")
         self.tokens_per_step = n
         self.launches_per_step = 3  # the append, the K/V tile staging and the attention
@@ -716,6 +884,15 @@ def q8_weight_rows_np(rng, rows: int, cols: int) -> np.ndarray:
     return w.reshape(rows, nb * BB)
 
 
+def config6_stream(layers, n_kv, hd, mt, hidden):
+    """Config 6's inputs in the reference stream: K/V as config 2's (every layer, K then V, every kv
+    head's mt rows), then the input activation [hidden], then the q and k RMSNorm weights
+    [layers][hd] each (as 1 + 0.1 x).  The weight matrices are random packed Q8 rows (numpy, the
+    same bytes in both arms)."""
+    x = layers * 2 * n_kv * mt * hd
+    return {"kv": lambda layer, p, h: ((layer * 2 + p) * n_kv + h) * mt * hd, "x": x, "norms": x + hidden}
+
+
 def describe_config6(layers, n_q, n_kv, hd, hidden, pos):
     row = hd // QK * BB
     q_dim, kv_dim = n_q * hd, n_kv * hd
@@ -739,8 +916,9 @@ class Config6:
     name = "config6"
     scaling = "weak"
     e2e_steps = 2000
-    data = ("synthetic: seeded random packed Q8 weights (int8 uniform, scales uniform in [0.002, 0.02)), "
-            "N(0,1) K/V quantised to Q8 on the device, N(0,1) input")
+    data = ("synthetic: K/V, input and norm weights from the reference benches' generator (xorshift64 + "
+            "Box-Muller, seed 88172645463325252), K/V quantised to Q8 on the device; seeded random packed Q8 "
+            "weights (int8 uniform, scales uniform in [0.002, 0.02))")
 
     def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, pos=4096):
         import torch
@@ -750,23 +928,24 @@ class Config6:
         self.mt = pos + 1
         self.nb = hd // QK
         rng = np.random.default_rng(seed)
-        g = torch.Generator(device="cuda").manual_seed(seed)
         q_dim, kv_dim = n_q * hd, n_kv * hd
         shapes = {"wq": (q_dim, hidden), "wk": (kv_dim, hidden), "wv": (kv_dim, hidden), "wo": (hidden, q_dim)}
         self.w = [{n: torch.from_numpy(q8_weight_rows_np(rng, *sh)).cuda() for n, sh in shapes.items()}
                   for _ in range(layers)]
-        self.qn = [torch.from_numpy((1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)).cuda()
-                   for _ in range(layers)]
-        self.kn = [torch.from_numpy((1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)).cuda()
-                   for _ in range(layers)]
-        shape = (n_kv, self.mt, hd)
-        self.kp = [tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g)) for _ in range(layers)]
-        self.vp = [tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g)) for _ in range(layers)]
+        gen = LibGen()
+        off = config6_stream(layers, n_kv, hd, self.mt, hidden)
+        norms = 1 + np.float32(0.1) * gen.normal(off["norms"], 2 * layers * hd).reshape(2, layers, hd)
+        self.qn = [torch.from_numpy(norms[0, l].copy()).cuda() for l in range(layers)]
+        self.kn = [torch.from_numpy(norms[1, l].copy()).cuda() for l in range(layers)]
+        self.kp = [device_q8_rows(gen, off["kv"](l, 0, 0), n_kv * self.mt, hd).view(n_kv, self.mt, -1)
+                   for l in range(layers)]
+        self.vp = [device_q8_rows(gen, off["kv"](l, 1, 0), n_kv * self.mt, hd).view(n_kv, self.mt, -1)
+                   for l in range(layers)]
         inv = np.float32(500000.0) ** (-2.0 * np.arange(hd // 2, dtype=np.float32) / np.float32(hd))
         ang = np.float32(pos) * inv.astype(np.float32)
         self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
         self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).cuda()
-        self.acts = [torch.from_numpy(rng.standard_normal(hidden, dtype=np.float32)).cuda()]
+        self.acts = [torch.from_numpy(gen.normal(off["x"], hidden)).cuda()]
         self.acts += [torch.empty(hidden, device="cuda") for _ in range(layers)]
         self.scratch = torch.empty(tqk.layer_scratch_floats(n_q, n_kv, hd), device="cuda")
         self.ws = torch.zeros(1 << 22, dtype=torch.uint8, device="cuda")
@@ -820,6 +999,16 @@ class Config6:
         return "replicas: every GPU runs its own token" if world > 1 else "single GPU"
 
 
+def config7_stream(layers, n_kv, hd, mt, hidden):
+    """Config 7's cache and norm weights in the reference stream: K/V as config 2's, then for every
+    layer its input and post-attention RMSNorm weights [hidden] and q / k norm weights [hd] (as
+    1 + 0.1 x), then the final norm [hidden].  The weight matrices are random packed Q8 rows."""
+    kv = layers * 2 * n_kv * mt * hd
+    per = 2 * hidden + 2 * hd
+    return {"kv": lambda layer, p, h: ((layer * 2 + p) * n_kv + h) * mt * hd,
+            "norms": lambda layer: kv + layer * per, "final_norm": kv + layers * per}
+
+
 def describe_config7(layers, n_q, n_kv, hd, hidden, inter, vocab, pos):
     row = hd // QK * BB
     q_dim, kv_dim = n_q * hd, n_kv * hd
@@ -853,8 +1042,9 @@ class Config7:
     name = "config7"
     scaling = "weak"
     e2e_steps = 200
-    data = ("synthetic: seeded random packed Q8 weights made on the device (int8 uniform, scales uniform in "
-            "[0.002, 0.02)), N(0,1) K/V quantised to Q8 on the device, RoPE tables of float32 numpy")
+    data = ("synthetic: K/V and norm weights from the reference benches' generator (xorshift64 + Box-Muller, "
+            "seed 88172645463325252), K/V quantised to Q8 on the device; seeded random packed Q8 weights made "
+            "on the device (int8 uniform, scales uniform in [0.002, 0.02)); RoPE tables of float32 numpy")
 
     def __init__(self, seed: int, layers=32, n_q=32, n_kv=8, hd=128, hidden=4096, inter=14336, vocab=128256,
                  pos=4096):
@@ -865,21 +1055,24 @@ class Config7:
             layers, n_q, n_kv, hd, hidden, inter, vocab, pos
         self.mt = pos + 1
         g = torch.Generator(device="cuda").manual_seed(seed)
+        gen = LibGen()
         q_dim, kv_dim = n_q * hd, n_kv * hd
-        norm = lambda n: 1 + 0.1 * torch.randn(n, device="cuda", generator=g)  # noqa: E731
+        off = config7_stream(layers, n_kv, hd, self.mt, hidden)
+        norm = lambda first, n: torch.from_numpy(1 + np.float32(0.1) * gen.normal(first, n)).cuda()  # noqa: E731
         self.layers = []
-        for _ in range(layers):
-            d = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(hd), "k_norm": norm(hd),
+        for layer in range(layers):
+            nrm = off["norms"](layer)
+            d = {"input_norm": norm(nrm, hidden), "post_norm": norm(nrm + hidden, hidden),
+                 "q_norm": norm(nrm + 2 * hidden, hd), "k_norm": norm(nrm + 2 * hidden + hd, hd),
                  "wq": random_q8_rows(q_dim, hidden, g), "wk": random_q8_rows(kv_dim, hidden, g),
                  "wv": random_q8_rows(kv_dim, hidden, g), "wo": random_q8_rows(hidden, q_dim, g),
                  "wgate": random_q8_rows(inter, hidden, g), "wup": random_q8_rows(inter, hidden, g),
                  "wdown": random_q8_rows(hidden, inter, g)}
-            shape = (n_kv, self.mt, hd)
-            d["k_cache"] = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
-            d["v_cache"] = tqk.quantize_rows(torch.randn(shape, device="cuda", generator=g))
+            for p, key in enumerate(("k_cache", "v_cache")):
+                d[key] = device_q8_rows(gen, off["kv"](layer, p, 0), n_kv * self.mt, hd).view(n_kv, self.mt, -1)
             self.layers.append(d)
         self.embed = random_q8_rows(vocab, hidden, g)
-        self.final_norm = norm(hidden)
+        self.final_norm = norm(off["final_norm"], hidden)
         inv = np.float32(500000.0) ** (-2.0 * np.arange(hd // 2, dtype=np.float32) / np.float32(hd))
         ang = np.arange(self.mt, dtype=np.float32)[:, None] * inv[None, :].astype(np.float32)
         self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
@@ -942,14 +1135,16 @@ class HostConfig6:
         q_dim, kv_dim = n_q * hd, n_kv * hd
         shapes = {"wq": (q_dim, hidden), "wk": (kv_dim, hidden), "wv": (kv_dim, hidden), "wo": (hidden, q_dim)}
         self.w = [{n: q8_weight_rows_np(rng, *sh) for n, sh in shapes.items()} for _ in range(layers)]
-        self.qn = [(1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) for _ in range(layers)]
-        self.kn = [(1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) for _ in range(layers)]
+        gen = reference_generator()
+        off = config6_stream(layers, n_kv, hd, self.mt, hidden)
+        norms = 1 + np.float32(0.1) * gen.normal(off["norms"], 2 * layers * hd).reshape(2, layers, hd)
+        self.qn = [norms[0, l].copy() for l in range(layers)]
+        self.kn = [norms[1, l].copy() for l in range(layers)]
         row = self.nb * BB
-        self.kp = [orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
-                   for _ in range(layers)]
-        self.vp = [orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
-                   for _ in range(layers)]
-        self.x = rng.standard_normal(hidden, dtype=np.float32)
+        self.kp, self.vp = ([orc.quantize_rows_bulk(gen.normal(off["kv"](l, p, 0), n_kv * self.mt * hd)
+                                                    .reshape(n_kv, self.mt, hd)) for l in range(layers)]
+                            for p in (0, 1))
+        self.x = gen.normal(off["x"], hidden)
         wbytes = sum(a.size for a in self.w[0].values()) * layers
         self.kv_bytes = 2 * layers * n_kv * (pos + 1) * row
         self.bytes_per_step = wbytes + self.kv_bytes + 2 * layers * n_kv * row
@@ -970,24 +1165,27 @@ class HostConfig7:
             layers, n_q, n_kv, hd, hidden, inter, vocab, pos
         self.mt = pos + 1
         rng = np.random.default_rng(seed)
+        gen = reference_generator()
+        off = config7_stream(layers, n_kv, hd, self.mt, hidden)
         q_dim, kv_dim = n_q * hd, n_kv * hd
-        norm = lambda n: (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)  # noqa: E731
+        norm = lambda first, n: 1 + np.float32(0.1) * gen.normal(first, n)  # noqa: E731
         lay = []
         self.planes = []
-        for _ in range(layers):
-            lay.append({"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(hd), "k_norm": norm(hd),
+        for layer in range(layers):
+            nrm = off["norms"](layer)
+            lay.append({"input_norm": norm(nrm, hidden), "post_norm": norm(nrm + hidden, hidden),
+                        "q_norm": norm(nrm + 2 * hidden, hd), "k_norm": norm(nrm + 2 * hidden + hd, hd),
                         "wq": q8_weight_rows_np(rng, q_dim, hidden), "wk": q8_weight_rows_np(rng, kv_dim, hidden),
                         "wv": q8_weight_rows_np(rng, kv_dim, hidden), "wo": q8_weight_rows_np(rng, hidden, q_dim),
                         "wgate": q8_weight_rows_np(rng, inter, hidden), "wup": q8_weight_rows_np(rng, inter, hidden),
                         "wdown": q8_weight_rows_np(rng, hidden, inter)})
-            kf = rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32)
-            vf = rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32)
-            self.planes.append((orc.quantize_rows_bulk(kf), orc.quantize_rows_bulk(vf)))
+            self.planes.append(tuple(orc.quantize_rows_bulk(gen.normal(off["kv"](layer, p, 0), n_kv * self.mt * hd)
+                                                            .reshape(n_kv, self.mt, hd)) for p in (0, 1)))
         self.model = {"cfg": {"n_q_heads": n_q, "n_kv_heads": n_kv, "head_dim": hd, "hidden_size": hidden,
                               "rope_theta": 500000.0, "rms_eps": 1e-5, "n_layers": layers,
                               "intermediate_size": inter, "vocab_size": vocab},
-                      "fmt": "8", "embed": q8_weight_rows_np(rng, vocab, hidden), "final_norm": norm(hidden),
-                      "layers": lay}
+                      "fmt": "8", "embed": q8_weight_rows_np(rng, vocab, hidden),
+                      "final_norm": norm(off["final_norm"], hidden), "layers": lay}
         d = describe_config7(layers, n_q, n_kv, hd, hidden, inter, vocab, pos)
         self.bytes_per_step = d["weight_bytes_per_token"] + d["kv_bytes_per_token"]
 
@@ -998,8 +1196,9 @@ class HostConfig7:
 def reference_forward_seconds(orc, wl, tokens: int):
     """Times the reference's tq_forward_token (all host threads: its matmuls and attention use
     OpenMP) from position pos - tokens + 1 on: one context runs 1 token, another 1 + tokens, and the
-    difference over `tokens` is the per-token time (the context set-up and cache fill cancel).
-    Returns (seconds per token, tokens, threads)."""
+    difference over `tokens` is the per-token time (the context set-up and cache fill cancel).  When
+    that difference is under a tenth of the longer run (shapes so small that set-up noise dominates),
+    the longer run's time per token is returned instead.  Returns (seconds per token, tokens, threads)."""
     threads = os.cpu_count() or 1
     start = (wl.pos - tokens, wl.planes)
     t0 = time.perf_counter()
@@ -1009,7 +1208,10 @@ def reference_forward_seconds(orc, wl, tokens: int):
     t2 = time.perf_counter()
     if rc1 != [0] or rc2 != [0] * (1 + tokens):
         raise RuntimeError(f"the reference's tq_forward_token returned {rc1} / {rc2}")
-    return max((t2 - t1) - (t1 - t0), 1e-9) / tokens, tokens, threads
+    diff = (t2 - t1) - (t1 - t0)
+    if diff < 0.1 * (t2 - t1):  # set-up noise swamps the tokens (tiny shapes): the whole second run per token
+        return (t2 - t1) / (1 + tokens), tokens, threads
+    return diff / tokens, tokens, threads
 
 
 def reference_layers_seconds(orc, wl, budget_s: float, max_tokens: int | None = None, min_tokens: int = 2):
@@ -1038,16 +1240,19 @@ class HostConfig2:
         self.L, self.nq, self.nkv, self.hd, self.pos = layers, n_q, n_kv, hd, pos
         self.mt = pos + 1
         self.nb = hd // QK
-        rng = np.random.default_rng(seed)
+        gen = reference_generator()
+        off = config2_stream(layers, n_q, n_kv, hd, self.mt)
         row = self.nb * BB
         self.kp = np.empty((layers, n_kv, self.mt, row), np.uint8)
         self.vp = np.empty((layers, n_kv, self.mt, row), np.uint8)
         for layer in range(layers):
-            self.kp[layer] = orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
-            self.vp[layer] = orc.quantize_rows_bulk(rng.standard_normal((n_kv, self.mt, hd), dtype=np.float32))
-        self.q = rope_np(rng.standard_normal((layers, n_q * hd), dtype=np.float32), hd, pos, 500000.0)
-        self.k_new = rng.standard_normal((layers, n_kv * hd), dtype=np.float32)
-        self.v_new = rng.standard_normal((layers, n_kv * hd), dtype=np.float32)
+            for p, plane in enumerate((self.kp, self.vp)):
+                x = gen.normal(off["kv"](layer, p, 0), n_kv * self.mt * hd).reshape(n_kv, self.mt, hd)
+                plane[layer] = orc.quantize_rows_bulk(x)
+        qkv = gen.normal(off["step"], layers * (n_q + 2 * n_kv) * hd).reshape(layers, n_q + 2 * n_kv, hd)
+        self.q = rope_np(np.ascontiguousarray(qkv[:, :n_q]).reshape(layers, n_q * hd), hd, pos, 500000.0)
+        self.k_new = np.ascontiguousarray(qkv[:, n_q:n_q + n_kv]).reshape(layers, n_kv * hd)
+        self.v_new = np.ascontiguousarray(qkv[:, n_q + n_kv:]).reshape(layers, n_kv * hd)
         self.kv_bytes = 2 * layers * n_kv * (pos + 1) * row
         self.bytes_per_step = self.kv_bytes + 2 * layers * n_kv * row
 
@@ -1066,20 +1271,21 @@ class HostConfig3:
 
     def __init__(self, orc, seed: int, n_q=32, n_kv=8, hd=128, mt=8192, lo=512, sample=4):
         self.L, self.nq, self.nkv, self.hd, self.mt, self.lo = 1, n_q, n_kv, hd, mt, lo
-        rng = np.random.default_rng(seed)
-        self.all_lens = rng.integers(lo, mt + 1, Config3.B).astype(np.int32)
+        gen = reference_generator()
+        self.all_lens = ragged_lengths(gen, Config3.B, lo, mt)
+        off = config3_stream(self.all_lens, n_q, n_kv, hd)
         self.sample = list(range(sample))
         self.sample_lens = self.all_lens[:sample]
         row = hd // QK * BB
         self.kp, self.vp = [], []
-        for i in self.sample:
-            n = int(self.sample_lens[i])
-            for planes in (self.kp, self.vp):
-                x = rng.standard_normal((n_kv, mt, hd), dtype=np.float32)
-                x[:, n:] = 0.0
-                x = np.where(rng.random((n_kv, mt, hd), dtype=np.float32) < 0.01, x * 8, x)
+        for b in self.sample:
+            n = int(self.sample_lens[b])
+            for p, planes in enumerate((self.kp, self.vp)):
+                x = np.zeros((n_kv, mt, hd), np.float32)
+                x[:, :n] = outliers(gen, off["u"](off["kv"](b, p)),
+                                    gen.normal(off["kv"](b, p), n_kv * n * hd)).reshape(n_kv, n, hd)
                 planes.append(orc.quantize_rows_bulk(x).reshape(n_kv, mt, row))
-        self.q = rng.standard_normal((sample, n_q * hd), dtype=np.float32)
+        self.q = np.stack([gen.normal(off["q"](b), n_q * hd) for b in self.sample])
         self.bytes_per_step = 2 * n_kv * int(self.all_lens.sum()) * row
         self.n = 1
 
@@ -1096,11 +1302,11 @@ class HostConfig4:
         self.L, self.nq, self.nkv, self.hd, self.n = 1, n_q, n_kv, hd, n
         self.mt, self.pos = n, n - 1
         self.nb = hd // QK
-        rng = np.random.default_rng(seed)
+        gen = reference_generator()
         row = self.nb * BB
-        self.kp = orc.quantize_rows_bulk(rng.standard_normal((n_kv, n, hd), dtype=np.float32)).reshape(1, n_kv, n, row)
-        self.vp = orc.quantize_rows_bulk(rng.standard_normal((n_kv, n, hd), dtype=np.float32)).reshape(1, n_kv, n, row)
-        self.q = rng.standard_normal((1, n_q * hd), dtype=np.float32)
+        self.kp, self.vp = (orc.quantize_rows_bulk(gen.normal(config4_stream(n_kv, n, hd, p, 0), n_kv * n * hd)
+                                                   .reshape(n_kv, n, hd)).reshape(1, n_kv, n, row) for p in (0, 1))
+        self.q = gen.normal(config4_stream(n_kv, n, hd, 2, 0), n_q * hd).reshape(1, n_q * hd)
         self.kv_bytes = 2 * n_kv * n * row
         self.bytes_per_step = self.kv_bytes
 
@@ -1119,17 +1325,18 @@ class HostConfig5:
         self.L, self.nq, self.nkv, self.hd, self.pos0, self.n = 1, n_q, n_kv, hd, pos0, n
         self.FLOPS = prefill_flops(n_q, hd, pos0, n)
         self.mt = pos0 + n
-        rng = np.random.default_rng(seed)
+        gen = reference_generator()
+        off = config5_stream(n_q, n_kv, hd, pos0, n)
         row = hd // QK * BB
-        kf = np.zeros((n_kv, self.mt, hd), np.float32)
-        vf = np.zeros((n_kv, self.mt, hd), np.float32)
-        kf[:, :pos0] = rng.standard_normal((n_kv, pos0, hd), dtype=np.float32)
-        vf[:, :pos0] = rng.standard_normal((n_kv, pos0, hd), dtype=np.float32)
-        self.kp = orc.quantize_rows_bulk(kf).reshape(n_kv, self.mt, row)
-        self.vp = orc.quantize_rows_bulk(vf).reshape(n_kv, self.mt, row)
-        self.q = rng.standard_normal((n, n_q * hd), dtype=np.float32)
-        self.k_new = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
-        self.v_new = rng.standard_normal((n, n_kv * hd), dtype=np.float32)
+        planes = []
+        for p in (0, 1):
+            x = np.zeros((n_kv, self.mt, hd), np.float32)
+            x[:, :pos0] = gen.normal(off["kv"](p, 0), n_kv * pos0 * hd).reshape(n_kv, pos0, hd)
+            planes.append(orc.quantize_rows_bulk(x).reshape(n_kv, self.mt, row))
+        self.kp, self.vp = planes
+        self.q = gen.normal(off["q"], n * n_q * hd).reshape(n, n_q * hd)
+        self.k_new = gen.normal(off["k"], n * n_kv * hd).reshape(n, n_kv * hd)
+        self.v_new = gen.normal(off["v"], n * n_kv * hd).reshape(n, n_kv * hd)
         self.bytes_per_step = 2 * n_kv * self.mt * row
 
     def host_planes(self):
@@ -1220,6 +1427,7 @@ def run_reference(args):
     if rank != 0:
         return 0  # the reference is a single-process CPU library: rank 0 alone runs it
     orc, kind = reference_oracle()
+    gen_kind = reference_generator().kind
     shape = TINY[args.config] if args.tiny else {}
     if args.config == 7:
         wl = HostConfig7(orc, seed=7000, **shape)
@@ -1257,7 +1465,8 @@ def run_reference(args):
     per_step = sec * (Config3.B if args.config == 3 else wl.n if args.config == 5 else 1)
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": n,
             "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
-            "scaling": SCALING[args.config], "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
+            "scaling": SCALING[args.config], "vs_baseline": None, "dtype": "int8+fp32",
+            "data": f"synthetic, from the reference benches' generator ({gen_kind})",
             "impl": "reference",
             "config": {**wl.describe(), "global_batch": global_batch(args.config, 1),
                        "parallelism": "reference CPU (its OpenMP over kv heads, all host threads)"},
@@ -1402,7 +1611,9 @@ def run_ours(args):
             "ms_per_step": t / args.steps * 1e3,
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
             "dtype": "int8+fp32",
-            "data": getattr(wl, "data", "synthetic: seeded N(0,1) K/V quantised to Q8 on the device, RoPE'd N(0,1) q"),
+            "data": getattr(wl, "data", "synthetic: N(0,1) from the reference benches' generator (xorshift64 + "
+                                        "Box-Muller, seed 88172645463325252; tqk_fill_normal), K/V quantised to Q8 "
+                                        "on the device, q RoPE'd"),
             "config": {**wl.describe(), "global_batch": global_batch(args.config, world),
                        "parallelism": wl.parallelism(world)},
             **({"per_gpu": wl.per_rank()} if hasattr(wl, "per_rank") else {}),

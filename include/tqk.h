@@ -484,6 +484,23 @@ TQK_API size_t tqk_gather_slot_offset(int n_groups, int chunk_floats, int epoch)
 TQK_API int tqk_exchange_gather(int n_groups, int chunk_floats, int world, int rank, void *const *mailboxes,
                                 int epoch, float *out, tqk_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Synthetic inputs (host).  The reference's benches draw every input from one
+ * xorshift64 generator through uniform_open / normal_sample, seeded with
+ * TQK_REF_SEED (tools/bench_forward.c:82,199-210; tools/bench.c:102,119-130).
+ * These fill host memory with the same values, bit for bit on the same C
+ * library, from any position of that stream, on `threads` host threads (<= 0:
+ * all cores); the values do not depend on the thread count.
+ *   tqk_fill_normal:  out[i] = normal_sample #(first + i) * scale
+ *                     (normal sample k takes generator steps 2k+1 and 2k+2);
+ *   tqk_fill_uniform: out[i] = uniform_open #(first + i), in (0, 1];
+ *   tqk_xorshift_jump: the generator state `steps` steps after `state`.
+ * The seed must be non-zero. */
+#define TQK_REF_SEED 88172645463325252ull
+TQK_API int tqk_fill_normal(uint64_t seed, uint64_t first, float *out, size_t n, float scale, int threads);
+TQK_API int tqk_fill_uniform(uint64_t seed, uint64_t first, float *out, size_t n, int threads);
+TQK_API uint64_t tqk_xorshift_jump(uint64_t state, uint64_t steps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,7 +23,7 @@ INCLUDE = os.path.join(ROOT, "include")
 
 CUDA_SOURCES = ["tqk_runtime.cu", "tqk_quant.cu", "tqk_decode.cu", "tqk_prefill.cu", "tqk_prologue.cu",
                 "tqk_matvec.cu", "tqk_layer.cu", "tqk_pack.cu", "tqk_ref_ops.cu", "tqk_exchange.cu",
-                "tqk_forward.cu"]
+                "tqk_forward.cu", "tqk_inputs.cu"]
 DROPIN_SOURCES = ["dropin/tq_attn_b200.c"]
 
 NVCC_FLAGS = [

@@ -173,7 +173,11 @@ tqk_gather_collect = _sig("tqk_gather_collect", [_vp, _sz, _i, _vp, _vp])
 tqk_gather_mailbox_bytes = _sig("tqk_gather_mailbox_bytes", [_i, _i, _i], _sz)
 tqk_gather_slot_offset = _sig("tqk_gather_slot_offset", [_i, _i, _i], _sz)
 tqk_exchange_gather = _sig("tqk_exchange_gather", [_i, _i, _i, _i, ctypes.POINTER(_vp), _i, _vp, _vp])
+tqk_fill_normal = _sig("tqk_fill_normal", [ctypes.c_uint64, ctypes.c_uint64, _vp, _sz, _f, _i])
+tqk_fill_uniform = _sig("tqk_fill_uniform", [ctypes.c_uint64, ctypes.c_uint64, _vp, _sz, _i])
+tqk_xorshift_jump = _sig("tqk_xorshift_jump", [ctypes.c_uint64, ctypes.c_uint64], ctypes.c_uint64)
 IPC_HANDLE_BYTES = 64
+REF_SEED = 88172645463325252  # TQK_REF_SEED: the reference benches' generator seed
 
 EXPORTED = [
     "tqk_status_string", "tqk_last_error", "tqk_version", "tqk_device_status", "tqk_device_status_async",
@@ -191,6 +195,7 @@ EXPORTED = [
     "tqk_gather_mailbox_bytes", "tqk_gather_slot_offset", "tqk_exchange_gather",
     "tqk_decode_q8_gather", "tqk_decode_unit_count", "tqk_gather_collect",
     "tqk_forward_scratch_bytes", "tqk_forward_token",
+    "tqk_fill_normal", "tqk_fill_uniform", "tqk_xorshift_jump",
 ]
 
 
@@ -542,3 +547,25 @@ def device_status(clear: bool = False) -> int:
     v = _i(0)
     check(tqk_device_status(ctypes.byref(v), int(clear)), "tqk_device_status")
     return v.value
+
+
+def fill_normal(first: int, n: int, scale: float = 1.0, seed: int = REF_SEED, threads: int = 0, out=None):
+    """tqk_fill_normal: samples first .. first + n - 1 of the reference benches' N(0,1)
+    stream (xorshift64 + Box-Muller), times scale, as a float32 numpy array (or into
+    `out`, a C-contiguous float32 numpy array of n values)."""
+    import numpy as np
+    if out is None:
+        out = np.empty(n, np.float32)
+    assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == n
+    check(tqk_fill_normal(seed, first, out.ctypes.data, n, scale, threads), "tqk_fill_normal")
+    return out
+
+
+def fill_uniform(first: int, n: int, seed: int = REF_SEED, threads: int = 0, out=None):
+    """tqk_fill_uniform: uniforms first .. first + n - 1 of the same generator, in (0, 1]."""
+    import numpy as np
+    if out is None:
+        out = np.empty(n, np.float32)
+    assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == n
+    check(tqk_fill_uniform(seed, first, out.ctypes.data, n, threads), "tqk_fill_uniform")
+    return out

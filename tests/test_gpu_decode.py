@@ -119,6 +119,28 @@ def test_config2_all_layers_fused_append(tqk, port, cuda):
     assert tqk.device_status() == 0
 
 
+def test_config1_on_the_reference_generator(tqk, port, cuda):
+    """Config 1 (one layer, 32 q / 8 kv heads, n = 1024) on inputs drawn the way the reference's
+    benches draw theirs: the xorshift64 + Box-Muller stream from 88172645463325252
+    (tools/bench_forward.c:82,199-210), here through tqk_fill_normal, which
+    tests/test_inputs_cpu.py pins bit for bit to the reference's own normal_sample.  K then V
+    ([kv head][position][head_dim]), then q; K/V quantised by the oracle's reference quantiser."""
+    import torch
+    nq, nkv, hd, n = 32, 8, 128, 1024
+    kf = tqk.fill_normal(0, nkv * n * hd).reshape(nkv, n, hd)
+    vf = tqk.fill_normal(nkv * n * hd, nkv * n * hd).reshape(nkv, n, hd)
+    q = tqk.fill_normal(2 * nkv * n * hd, nq * hd)
+    kp, vp = port.quantize_rows(kf), port.quantize_rows(vf)
+    out = torch.empty(nq * hd, device=cuda)
+    args = tqk.decode_args(torch.from_numpy(kp).to(cuda), torch.from_numpy(vp).to(cuda), nq, nkv, hd, n,
+                           torch.from_numpy(q).to(cuda), out, len0=n)
+    tqk.decode(args)
+    ref = port.attend(kp, vp, nq, nkv, hd, n, n - 1, q)
+    ok, max_abs, rel = tolerance_ok(out.cpu().numpy(), ref)
+    assert ok, f"max abs {max_abs:.3g} rel {rel:.3g}"
+    assert tqk.device_status() == 0
+
+
 def test_config3_ragged_batch_device_lens(tqk, port, cuda):
     """Config 3: batch 64, lengths ~U[512, 8192], 1% x8 outliers, device lens array."""
     import torch
