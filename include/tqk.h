@@ -155,6 +155,7 @@ TQK_API int tqk_softmax_rows(float *x, int rows, int n, size_t stride, tqk_strea
  * (layout: out + i*out_item_stride + h*(head_dim+2)) for a cross-device
  * log-sum-exp merge with tqk_merge_partials().
  */
+#define TQK_SPLIT_BALANCED  -1  /* tqk_decode_args.split_tokens: see there */
 #define TQK_OUT_NORMALIZED 0
 #define TQK_OUT_PARTIAL    1
 
@@ -171,7 +172,10 @@ typedef struct {
     const float *k_new, *v_new;   /* optional fused append (device), or NULL */
     int64_t kv_new_item_stride;
     int out_mode;                 /* TQK_OUT_NORMALIZED or TQK_OUT_PARTIAL */
-    int split_tokens;             /* tokens per split (multiple of 64); 0 = choose automatically */
+    int split_tokens;             /* tokens per split (multiple of 64); 0 = choose automatically;
+                                     TQK_SPLIT_BALANCED = the balanced schedule (equal runs of tiles
+                                     per CTA across items) whenever the call qualifies for it, else
+                                     as 0 (tqk_decode_q8_static always treats it as 0) */
     /* Optional fused prologue (attention_layer.c:183-189, norm_heads + rope_heads): each q head
      * of item i, and each appended k_new head, is first RMS-normalised with q_norm / k_norm +
      * i*norm_item_stride ([head_dim] floats, shared by the heads; both NULL = no norm) and then

@@ -910,6 +910,29 @@ size_t counters_region(int n_items, int units) {
     return b;
 }
 
+// K/V bytes a call streams with every item at max_len.
+long long kv_bytes_of(const tqk_decode_args *a, int max_len) {
+    return 2LL * a->n_items * a->n_kv_heads * max_len * (a->head_dim / QK) * BLOCK_BYTES;
+}
+
+// Splits per (item, head unit) of the automatic fixed split.  Measured on B200:
+//  * equal lengths: as many as keep every CTA in one wave of the resident slots
+//    (a second, partly filled wave costs more than the shorter splits save:
+//    76 us in one wave against 101 us in 1.15 waves); but a call that streams
+//    less than LATENCY_BYTES is bound by its fixed costs, not by bandwidth, and
+//    then at most MERGE_GROUP splits (one merge level) win: a Llama-3-8B layer
+//    at n = 4097 took 16.4 us with 13 splits against 17.6 us with 64;
+//  * unequal lengths (device lengths unknown to the host): about 0.9 waves if
+//    the lengths spread evenly up to max_len, and one merge level: ragged
+//    config-3 shares of 8 and 16 sequences took 24.6 and 40.5 us that way
+//    against 35.2 and 51.5 us with two CTAs per slot (1.1 waves, two levels).
+constexpr long long LATENCY_BYTES = 16LL << 20;
+long long auto_splits(bool uniform, long long slots, long long units, long long kv_bytes) {
+    long long want = uniform ? slots / units : (9 * slots) / (5 * units);
+    if ((!uniform || kv_bytes < LATENCY_BYTES) && want > MERGE_GROUP) want = MERGE_GROUP;
+    return want < 1 ? 1 : want;
+}
+
 int make_plan(const tqk_decode_args *a, Plan *pl, bool gather = false) {
     if (!a) return fail(TQK_EINVAL, "decode: NULL args");
     if (a->n_items <= 0 || a->n_q_heads <= 0 || a->n_kv_heads <= 0 || a->head_dim <= 0 || a->max_tokens <= 0)
@@ -961,18 +984,30 @@ int make_plan(const tqk_decode_args *a, Plan *pl, bool gather = false) {
         const int rc = ensure_device();
         if (rc) return rc;
         const DeviceInfo *d = device_info();
-        // the balanced schedule pays a segment switch mid-run; it wins where the
-        // fixed split cannot even out the work: unequal lengths across items
+        // the balanced schedule pays a segment switch mid-run (about 7 us of a
+        // CTA's time); it wins where the fixed split cannot even out the work --
+        // unequal lengths across items -- and every CTA's run is long enough to
+        // absorb its switches: at least BAL_MIN_TILES tiles per resident slot,
+        // counted with every unit at max_len (the host does not see device
+        // lengths).  TQK_SPLIT_BALANCED asks for it whenever the call qualifies.
         const bool ragged = a->n_items > 1 && (a->lens != nullptr || a->len_step != 0);
-        const bool balanced = !gather && pl->pack && ragged && a->n_items <= BAL_MAX_ITEMS;
+        const bool can_balance = !gather && pl->pack && a->n_items <= BAL_MAX_ITEMS;
+        const long long pairs_total = (long long)a->n_items * pl->pairs;
+        bool balanced = can_balance && (split == TQK_SPLIT_BALANCED || ragged);
         int occ = 0;
         DecodeParams dummy{};
-        const int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ, balanced)
-                        : pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
-                                  : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
+        int orc = pl->pack  ? dispatch_pack(nb, dummy, dim3(1), nullptr, &occ, balanced)
+                  : pl->mma ? dispatch_mma(nb, pl->gmax, dummy, dim3(1), nullptr, &occ)
+                            : dispatch(nb, pl->gmax, dummy, dim3(1), nullptr, &occ);
         if (orc) return orc;
-        const long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
-        const long long pairs_total = (long long)a->n_items * pl->pairs;
+        long long slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
+        if (balanced && split != TQK_SPLIT_BALANCED &&
+            pairs_total * ((max_len + PK_T - 1) / PK_T) < (long long)BAL_MIN_TILES * slots) {
+            balanced = false;
+            orc = dispatch_pack(nb, dummy, dim3(1), nullptr, &occ, false);
+            if (orc) return orc;
+            slots = (long long)(d ? d->sm_count : 148) * (occ > 0 ? occ : 1);
+        }
         if (balanced) {
             // one CTA per resident slot (never more than there are tiles), each
             // streaming an equal run of the units' tiles
@@ -993,12 +1028,8 @@ int make_plan(const tqk_decode_args *a, Plan *pl, bool gather = false) {
             pl->part_bytes = (size_t)(ctas + pairs_total) * 8 * (a->head_dim + 2) * sizeof(float);
             return TQK_OK;
         }
-        // equal lengths: as many splits as keep every CTA in one wave (a second,
-        // partly filled wave costs more than the shorter splits save); unequal
-        // lengths: about two CTAs per slot, so short and long items even out
         const bool uniform = !a->lens && a->len_step == 0;
-        long long want = uniform ? slots / pairs_total : (2 * slots + pairs_total - 1) / pairs_total;
-        if (want < 1) want = 1;
+        const long long want = auto_splits(uniform, slots, pairs_total, kv_bytes_of(a, max_len));
         split = (int)((max_len + want - 1) / want);
     }
     split = ((split + DEC_T - 1) / DEC_T) * DEC_T;
@@ -1218,8 +1249,7 @@ extern "C" int tqk_decode_q8_static(const tqk_decode_args *args, tqk_stream_t st
         const long long slots = (long long)sms * (occ > 0 ? occ : 1);
         const long long units = (long long)a.n_items * pl.pairs;
         const bool uniform = !a.lens && a.len_step == 0;
-        long long want = uniform ? slots / units : (2 * slots + units - 1) / units;
-        if (want < 1) want = 1;
+        const long long want = auto_splits(uniform, slots, units, kv_bytes_of(&a, pl.max_len));
         a.split_tokens = (int)((pl.max_len + want - 1) / want);
         if (a.split_tokens < 1) a.split_tokens = 1;
         rc = make_plan(&a, &pl);

@@ -596,6 +596,12 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
 // ---------------------------------------------------------------------------
 constexpr int BAL_MAX_ITEMS = 256;  // items whose lengths and tile prefix fit in shared memory
 constexpr int BAL_MAX_CTAS = 1024;
+// The automatic choice takes the balanced schedule for ragged batches only from
+// this many tiles per resident CTA slot on (every unit counted at max_len).
+// Measured on B200, ragged batches of 64 / 32 / 16 / 8 config-3 sequences
+// (about 110 / 55 / 27 / 14 such tiles per slot): balanced 124.1 / 70.8 / 47.1 /
+// 43.7 us against the best fixed split tried 130.5 / 70.0 / 40.5 / 24.6 us.
+constexpr int BAL_MIN_TILES = 40;
 
 template <int NB>
 struct PackBalLayout {

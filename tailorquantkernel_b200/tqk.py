@@ -35,6 +35,7 @@ ETIMEOUT = -25
 EUNSUPPORTED = -26
 EDEVLEN = -27
 
+SPLIT_BALANCED = -1  # TQK_SPLIT_BALANCED
 OUT_NORMALIZED = 0
 OUT_PARTIAL = 1
 

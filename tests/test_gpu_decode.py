@@ -244,10 +244,11 @@ def test_zero_length_items_and_partial_output(tqk, port, cuda):
 
 
 @pytest.mark.parametrize("out_mode", [0, 1])
-def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
-    """The automatic split for 4 q heads per kv head (the packed kernel):
-    ragged device lengths with empty items, tile-edge lengths, a fused append,
-    both output modes, and a single short sequence."""
+@pytest.mark.parametrize("split", [0, -1])
+def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode, split):
+    """The automatic split (0) and the balanced schedule (-1, TQK_SPLIT_BALANCED) for 4 q heads
+    per kv head (the packed kernel): ragged device lengths with empty items, tile-edge lengths, a
+    fused append, both output modes, and a single short sequence."""
     import torch
     nq, nkv, hd, mt = 16, 4, 128, 4200
     lens = np.array([0, 1, 31, 32, 33, 4097, 0, 2048, 100, 4200, 64, 7], dtype=np.int32)
@@ -266,7 +267,7 @@ def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
     args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=B,
                            item_stride_blocks=nkv * mt * (hd // 32), lens=nonzero, max_len=int(lens.max()),
                            q_item_stride=nq * hd, out_item_stride=nq * width, k_new=torch.from_numpy(k_new).to(cuda),
-                           v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd, out_mode=out_mode)
+                           v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd, out_mode=out_mode, split_tokens=split)
     tqk.decode(args)
     got = out.cpu().numpy()
     kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
@@ -287,7 +288,7 @@ def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
     out = torch.full((B, nq * hd), 7.0, device=cuda)
     args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, torch.from_numpy(q).to(cuda), out, n_items=B,
                            item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
-                           q_item_stride=nq * hd, out_item_stride=nq * hd)
+                           q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=split)
     tqk.decode(args)
     got = out.cpu().numpy()
     for b in range(B):
@@ -305,9 +306,9 @@ def test_auto_schedule_ragged_append(tqk, port, cuda, out_mode):
 
 @pytest.mark.parametrize("n_items", [256, 300])
 def test_balanced_schedule_items_and_workspace_reuse(tqk, port, cuda, n_items):
-    """The packed kernel's automatic schedule: up to 256 items the units' tiles are cut into
-    equal per-CTA runs that cross unit boundaries (256 here, with empty and one-token items);
-    above that it falls back to the fixed split (300).  Checked against the oracle on a sample
+    """The packed kernel's balanced schedule (TQK_SPLIT_BALANCED): up to 256 items the units'
+    tiles are cut into equal per-CTA runs that cross unit boundaries (256 here, with empty and
+    one-token items); above that it falls back to the fixed split (300).  Checked against the oracle on a sample
     of items; repeated calls through one caller workspace give identical bytes (the tickets
     are left at zero), and so does a fixed-split call in between."""
     import torch
@@ -331,12 +332,14 @@ def test_balanced_schedule_items_and_workspace_reuse(tqk, port, cuda, n_items):
         tqk.decode(a, workspace=ws)
         return out.cpu().numpy(), a
 
-    first, a = call(0)
+    bal = tqk.SPLIT_BALANCED
+    first, a = call(bal)
     ws = torch.empty(max(tqk.decode_workspace_size(a), 1 << 24), dtype=torch.uint8, device=cuda)
     tqk.workspace_init(ws)
-    assert np.array_equal(call(0, ws)[0], first)
+    assert np.array_equal(call(bal, ws)[0], first)
     fixed = call(64, ws)[0]
-    assert np.array_equal(call(0, ws)[0], first)
+    assert np.array_equal(call(bal, ws)[0], first)
+    assert np.abs(call(0, ws)[0] - first).max() <= 2e-6 * max(1.0, np.abs(first).max())  # the automatic choice
     assert np.abs(fixed - first).max() <= 2e-6 * max(1.0, np.abs(first).max())
     kh, vh, qh = kp.cpu().numpy(), vp.cpu().numpy(), q.cpu().numpy()
     for b in (0, 5, 6, 37, 100, n_items - 1):
@@ -368,7 +371,7 @@ def test_balanced_schedule_long_ragged_two_level_merge(tqk, port, cuda):
                            item_stride_blocks=nkv * mt * (hd // 32), lens=torch.from_numpy(lens).to(cuda),
                            max_len=int(lens.max()), q_item_stride=nq * hd, out_item_stride=nq * hd,
                            k_new=torch.from_numpy(k_new).to(cuda), v_new=torch.from_numpy(v_new).to(cuda),
-                           kv_new_item_stride=nkv * hd)
+                           kv_new_item_stride=nkv * hd, split_tokens=tqk.SPLIT_BALANCED)
     tqk.decode(args)
     got = out.cpu().numpy()
     kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
@@ -395,14 +398,15 @@ def test_config3_auto_schedule(tqk, port, cuda):
     q = torch.from_numpy(rng.standard_normal((B, nq * hd), dtype=np.float32)).to(cuda)
     lens_d = torch.from_numpy(lens).to(cuda)
     outs = []
-    for split in (0, 1024):
+    for split in (0, tqk.SPLIT_BALANCED, 1024):
         out = torch.empty(B, nq * hd, device=cuda)
         tqk.decode(tqk.decode_args(kp, vp, nq, nkv, hd, mt, q, out, n_items=B,
                                    item_stride_blocks=nkv * mt * (hd // 32), lens=lens_d, max_len=int(lens.max()),
                                    q_item_stride=nq * hd, out_item_stride=nq * hd, split_tokens=split))
         outs.append(out.cpu().numpy())
     # schedules differ only in where fp32 partials are merged
-    assert np.abs(outs[0] - outs[1]).max() <= 1e-5 * max(1.0, np.abs(outs[1]).max())
+    for o in outs[:2]:
+        assert np.abs(o - outs[2]).max() <= 1e-5 * max(1.0, np.abs(outs[2]).max())
     kh, vh, qh = kp.cpu().numpy(), vp.cpu().numpy(), q.cpu().numpy()
     for b in (0, 17, 63):
         ok, max_abs, rel = tolerance_ok(outs[0][b], port.attend(kh[b], vh[b], nq, nkv, hd, mt, int(lens[b]) - 1, qh[b]))
