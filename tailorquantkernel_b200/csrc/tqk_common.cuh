@@ -294,6 +294,56 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+// ----------------------------------------------------------------------------
+// Thread-block cluster helpers (sm_90+): distributed shared memory and
+// mbarriers that other CTAs of the cluster arrive on.
+// ----------------------------------------------------------------------------
+// Cluster-wide barrier of every thread of every CTA.  Only for code that every
+// thread reaches unconditionally (kernel entry): it has no time bound.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of this CTA's shared-memory location `p` in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t cluster_map(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+// Arrive (count 1, release at cluster scope) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Bounded wait with acquire at cluster scope (arrivals from other CTAs of the cluster).
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns,
+                                                          int *err) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            record_error(err, DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // 1-D TMA bulk copy (non-multicast).  dst/src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_copy_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
     asm volatile(

@@ -21,6 +21,7 @@
 #include "tqk_internal.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <mutex>
 
@@ -31,6 +32,7 @@ constexpr int DEC_WARPS = DEC_THREADS / 32;
 constexpr int DEC_T = 64;          // tokens per tile
 constexpr int MAX_SPLITS = 128;    // bound on splits per (item, kv head)
 constexpr int MERGE_GROUP = 16;    // up to 16 splits merge in one level; more in groups of 16
+constexpr int CL_MAX = 16;         // largest cluster of the cluster merge (non-portable above 8)
 // ints per (item, head unit) in the ticket region: the final ticket and one per
 // group; the stride is kept at 17 so that caller workspaces keep their layout
 constexpr int TICKETS_PER_UNIT = 17;
@@ -86,6 +88,9 @@ struct DecodeParams {
     // each written by one 64-bit store, so a reader that sees the epoch sees the value.
     int g_world, g_rank, g_chunk, g_epoch;
     uint2 *g_out[8];
+    // the packed kernel's split merge through a thread-block cluster (the max_splits CTAs of one
+    // unit, cluster dims (cluster, 1, 1)); 0 = tickets and partials in global memory
+    int cluster;
 };
 
 // One element of the call's normalised output: head qh (of the item) column c.
@@ -770,6 +775,43 @@ int launch_mma(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_
 }
 
 // Two-kv-heads-per-CTA kernel for 4 q heads per kv head.
+// Whether clusters of grid.x CTAs of `kernel` can be placed on device `dev` (cached per device and
+// cluster size; sizes above 8 are opted in as non-portable).  Off with TQK_DECODE_CLUSTER=0.
+template <typename K>
+bool cluster_merge_ok(K kernel, int dev, dim3 grid, int threads, int smem) {
+    static std::mutex mu;
+    static signed char ok_by[64][CL_MAX + 1];  // 0 = unknown, 1 = yes, -1 = no
+    static const bool enabled = [] {
+        const char *e = getenv("TQK_DECODE_CLUSTER");
+        return !(e && e[0] == '0');
+    }();
+    if (!enabled || dev < 0 || dev >= 64 || grid.x > (unsigned)CL_MAX) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    signed char &ok = ok_by[dev][grid.x];
+    if (ok == 0) {
+        cudaError_t e = cudaSuccess;
+        if (grid.x > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        int n = 0;
+        if (e == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(grid.x, 1, 1);
+            cfg.blockDim = dim3(threads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = grid.x;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+        }
+        if (e != cudaSuccess) (void)cudaGetLastError();  // not an error of the call: no clusters
+        ok = (e == cudaSuccess && n > 0) ? 1 : -1;
+    }
+    return ok > 0;
+}
+
 template <int NB>
 int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_per_sm) {
     using L = PackLayout<NB>;
@@ -794,6 +836,14 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
     if (ctas_per_sm) {
         *ctas_per_sm = occ;
         return TQK_OK;
+    }
+    // the splits of a unit (grid.x of them) merge through a thread-block cluster when they fit one
+    // and the device can place such clusters; TQK_DECODE_CLUSTER=0 in the environment turns it off
+    if (grid.x >= 2 && grid.x <= (unsigned)CL_MAX && cluster_merge_ok(decode_q8_pack_kernel<NB>, dev, grid,
+                                                                        PK_THREADS, L::BYTES)) {
+        DecodeParams pc = p;
+        pc.cluster = (int)grid.x;
+        return launch_pdl_cluster(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, grid.x, pc);
     }
     return launch_pdl(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, p);
 }

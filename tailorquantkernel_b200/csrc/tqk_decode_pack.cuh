@@ -54,11 +54,19 @@ struct PackLayout {
     static constexpr int OFF_NEW = OFF_QD + ((8 * NB * 4 + 15) / 16) * 16;     // appended rows [head][K,V][ROW]
     static constexpr int OFF_PRO = OFF_NEW + ((4 * ROW + 15) / 16) * 16;       // prologue rows [warp][PK_QR + PK_NJ]
     static constexpr int OFF_FLAG = OFF_PRO + PK_WARPS * (PK_QR + PK_NJ) * pro_stride<NB>() * 4;
-    static constexpr int BYTES = OFF_FLAG + 16;
+    // cluster merge (p.cluster > 1): two mbarriers; this CTA's partial, acc [8][HD] then m [8], l [8];
+    // every cluster CTA's m and l [2][CL_MAX][8]; the final M and L [2][8] and a flag
+    static constexpr int OFF_CBAR = OFF_FLAG + 16;
+    static constexpr int OFF_CPART = OFF_CBAR + 16;
+    static constexpr int OFF_CML = OFF_CPART + (8 * HD + 16) * 4;
+    static constexpr int BYTES = OFF_CML + (2 * CL_MAX * 8 + 16 + 4) * 4;
     static constexpr int RED_STRIDE = HD + 1;  // reduction rows padded: the 32 lanes' stores hit 32 banks
     static constexpr int RED_FLOATS = PK_WARPS * 8 * RED_STRIDE;
     static constexpr int SCRATCH_FLOATS = RED_FLOATS + 3 * PK_WARPS * 8 + 2 * 8 + 2 * MAX_SPLITS * 8;
     static_assert(SCRATCH_FLOATS * 4 <= OFF_BAR, "stage ring too small for the epilogue scratch");
+    static_assert(OFF_CBAR % 8 == 0 && OFF_CPART % 16 == 0, "cluster merge alignment");
+    // the cluster merge gathers every rank's values of this CTA's share into the reduction rows
+    static_assert(8 * HD + CL_MAX <= RED_FLOATS, "reduction rows too small for the cluster merge");
 };
 
 // D(rows 0-7) += A(16x32 s8, rows 8-15 zero) * B(32x8 s8), int32.
@@ -427,6 +435,102 @@ __device__ __forceinline__ void pack_reduce(const PackState<NB> &st, const PackR
     cta_sync<1, PK_WARPS * 32>();
 }
 
+// The split merge through the thread-block cluster of a unit's splits
+// (p.cluster > 1, cluster dims (p.cluster, 1, 1) over the split axis), in
+// place of the tickets and the partials in global memory.  Every CTA puts its
+// partial (acc [8][HD], m, l) into its own shared memory and arrives on every
+// other CTA's cbar[0]; once its own cbar[0] completes, it merges its share of
+// the 8 x HD output elements from every CTA's partial by log-sum-exp -- the
+// values read over distributed shared memory, all in flight at once, folded in
+// rank order -- and writes them; then it arrives on every other CTA's cbar[1]
+// and leaves only when its own cbar[1] completes, i.e. when no CTA reads its
+// shared memory any more.  Every wait is bounded (the error word records a
+// timeout).  empty: this CTA holds no keys, or gave up on a wait.  Run by the
+// consumer threads only.
+constexpr uint64_t CL_WAIT_NS = 2000000000ull;  // above the 1 s bound of every wait before the merge
+template <int NB>
+__device__ __forceinline__ void pack_cluster_merge(const DecodeParams &p, uint8_t *smem, const PackRed &r, bool empty,
+                                                   int tid, int item, int qh0, float *out_item) {
+    using L = PackLayout<NB>;
+    constexpr int HD = L::HD, NT = PK_WARPS * 32, E = 8 * HD;
+    constexpr int KV = (E + CL_MAX + NT - 1) / NT;  // (element, rank) values per thread
+    uint64_t *cbar = reinterpret_cast<uint64_t *>(smem + L::OFF_CBAR);
+    float *cp = reinterpret_cast<float *>(smem + L::OFF_CPART);
+    float *cm = reinterpret_cast<float *>(smem + L::OFF_CML);  // m, then the weights, [CL_MAX][8]
+    float *cl = cm + CL_MAX * 8;                                // l [CL_MAX][8]
+    float *fin = cl + CL_MAX * 8;                               // M [8], L [8]
+    int *okf = reinterpret_cast<int *>(fin + 16);
+    float *vals = r.red;                                        // [share][rank], free after the partial is out
+    const int C = p.cluster;
+    const int rank = (int)cluster_ctarank();
+    for (int i = tid; i < E; i += NT) cp[i] = empty ? 0.0f : r.acc<L::RED_STRIDE>(i / HD, i % HD);
+    if (tid < 8) {
+        cp[E + tid] = empty ? -INFINITY : r.fm()[tid];
+        cp[E + 8 + tid] = empty ? 0.0f : r.fl()[tid];
+    }
+    if (tid == 0) *okf = 1;
+    cta_sync<1, NT>();  // the partial is complete (and the reduction rows are free)
+    if (tid < C && tid != rank) mbar_arrive_remote(cluster_map(&cbar[0], (uint32_t)tid));
+    if (!mbar_wait_cluster_bounded(&cbar[0], 0, CL_WAIT_NS, p.err)) *okf = 0;
+    cta_sync<1, NT>();
+    const int S = (E + C - 1) / C, i0 = rank * S, n_share = max(0, min(E, i0 + S) - i0);
+    if (*okf) {
+        // every load first (the (m, l) pairs and this thread's values), then the folds
+        float mv = 0.0f, lv = 0.0f, v[KV];
+        if (tid < C * 8) {
+            mv = ld_cluster_f32(cluster_map(cp + E + (tid & 7), (uint32_t)(tid >> 3)));
+            lv = ld_cluster_f32(cluster_map(cp + E + 8 + (tid & 7), (uint32_t)(tid >> 3)));
+        }
+#pragma unroll
+        for (int k = 0; k < KV; k++) {
+            const int q = tid + k * NT, e = q / C, rr = q - e * C;
+            v[k] = e < n_share ? ld_cluster_f32(cluster_map(cp + i0 + e, (uint32_t)rr)) : 0.0f;
+        }
+        if (tid < C * 8) {
+            cm[tid] = mv;
+            cl[tid] = lv;
+        }
+#pragma unroll
+        for (int k = 0; k < KV; k++) {
+            const int q = tid + k * NT;
+            if (q / C < n_share) vals[q] = v[k];
+        }
+        cta_sync<1, NT>();
+        if (tid < 8) {
+            float M = -INFINITY;
+            for (int rr = 0; rr < C; rr++) M = fmaxf(M, cm[rr * 8 + tid]);
+            float Ls = 0.0f;
+            for (int rr = 0; rr < C; rr++) {
+                const float m = cm[rr * 8 + tid];
+                const float w = m == -INFINITY ? 0.0f : expf(m - M);
+                cm[rr * 8 + tid] = w;
+                Ls += cl[rr * 8 + tid] * w;
+            }
+            fin[tid] = M;
+            fin[8 + tid] = Ls;
+        }
+        cta_sync<1, NT>();
+        for (int e = tid; e < n_share; e += NT) {
+            const int i = i0 + e, g = i / HD, c = i - g * HD;
+            float a = 0.0f;
+            for (int rr = 0; rr < C; rr++) {
+                const float w = cm[rr * 8 + g];
+                if (w != 0.0f) a = fmaf(w, vals[e * C + rr], a);
+            }
+            if (p.out_mode == TQK_OUT_NORMALIZED) {
+                store_out<HD>(p, out_item, item, qh0 + g, c, a / fin[8 + g]);
+            } else {
+                float *o = out_item + (long long)(qh0 + g) * (HD + 2);
+                o[c] = a;
+                if (c == 0) { o[HD] = fin[g]; o[HD + 1] = fin[8 + g]; }
+            }
+        }
+    }
+    cta_sync<1, NT>();  // this CTA's reads of the other CTAs' shared memory are done
+    if (tid < C && tid != rank) mbar_arrive_remote(cluster_map(&cbar[1], (uint32_t)tid));
+    if (tid == 0) mbar_wait_cluster_bounded(&cbar[1], 0, CL_WAIT_NS, p.err);
+}
+
 template <int NB>
 __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel(const DecodeParams p) {
     using L = PackLayout<NB>;
@@ -434,6 +538,19 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool clustered = p.cluster > 1;
+    if (clustered) {
+        // the cluster merge's barriers, initialised and made visible to the whole cluster before
+        // any CTA can arrive on them; every thread passes here unconditionally
+        uint64_t *cbar = reinterpret_cast<uint64_t *>(smem + PackLayout<NB>::OFF_CBAR);
+        if (tid == 0) {
+            mbar_init(&cbar[0], (uint32_t)(p.cluster - 1));
+            mbar_init(&cbar[1], (uint32_t)(p.cluster - 1));
+            fence_barrier_init();
+        }
+        __syncwarp();
+        cluster_sync_all();
+    }
     // programmatic dependent launch: everything this kernel reads (q, new rows,
     // lengths, cache rows) may come from earlier kernels of the stream, so wait
     // for them first; then the next kernel may start its own prefetch
@@ -455,9 +572,17 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
         n_splits = p.max_splits;    // the last split then runs to len (<= max_tokens)
     }
     const int s = blockIdx.x;
-    if (s >= (n_splits > 0 ? n_splits : 1)) return;
     const int qh0 = kvh_a * p.group;  // q heads qh0..qh0+7 are contiguous (group == 4)
     float *out_item = p.out + (long long)item * p.out_item_stride;
+    if (s >= (n_splits > 0 ? n_splits : 1)) {
+        // a split past this item's length: in a cluster it still takes part in the merge (an empty
+        // partial); with len == 0 every CTA of the cluster (one item) leaves here or just below
+        if (clustered && len > 0 && warp < PK_WARPS) {
+            float *red = reinterpret_cast<float *>(smem);
+            pack_cluster_merge<NB>(p, smem, PackRed{red, red + L::RED_FLOATS}, true, tid, item, qh0, out_item);
+        }
+        return;
+    }
 
     if (len == 0) {
         for (int i = tid; i < G * HD; i += PK_THREADS) {
@@ -572,11 +697,18 @@ __global__ void __launch_bounds__(PK_THREADS, TQK_PK_MINB) decode_q8_pack_kernel
     // ------------------------------------------------------------------ epilogue
     if (timed_out) *timeout = 1;
     cta_sync<1, PK_WARPS * 32>();
-    if (*timeout) return;
-
     float *red = reinterpret_cast<float *>(smem);  // [W][8][RED_STRIDE]
     PackRed r{red, red + L::RED_FLOATS};
+    if (*timeout) {
+        if (clustered) pack_cluster_merge<NB>(p, smem, r, true, tid, item, qh0, out_item);
+        return;
+    }
+
     pack_reduce<NB, L::RED_STRIDE>(st, r, warp, g, t, tid);
+    if (clustered) {
+        pack_cluster_merge<NB>(p, smem, r, false, tid, item, qh0, out_item);
+        return;
+    }
     float *wts = r.fl() + 8;                       // [2][MAX_SPLITS][8]
     auto acc_of = [&](int gg, int c) { return r.acc<L::RED_STRIDE>(gg, c); };
     finish_split<HD, 8, PK_WARPS * 32, 1>(p, tid, item, pair, s, n_splits, qh0, G, out_item, acc_of, r.fm(), r.fl(),

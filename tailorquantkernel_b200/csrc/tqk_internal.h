@@ -62,6 +62,29 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     return check_launch("kernel launch");
 }
 
+// launch_pdl with thread-block clusters of (cluster_x, 1, 1) CTAs.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       unsigned cluster_x, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+    if (e != cudaSuccess) return fail_cuda(e, "kernel launch (cluster)");
+    return check_launch("kernel launch (cluster)");
+}
+
 // Tensor-core prefill attention over the chunk [pos0, pos0 + n) whose K/V rows
 // are already in the planes (tqk_prefill.cu).  TQK_EUNSUPPORTED for shapes it
 // does not cover (the caller then uses the decode kernel).

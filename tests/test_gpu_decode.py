@@ -141,6 +141,75 @@ def test_config1_on_the_reference_generator(tqk, port, cuda):
     assert tqk.device_status() == 0
 
 
+@pytest.mark.parametrize("out_mode", [0, 1])
+def test_cluster_merge_every_size(tqk, port, cuda, out_mode):
+    """The packed kernel's split merge through a thread-block cluster, for every cluster size from
+    2 to 16 splits of a unit: a long item with a fused append, a 300-token item and a one-token
+    item whose later splits are empty (they take part with empty partials), through device
+    lengths, in both output modes; then an empty item without an append (its cluster leaves
+    without merging).  The appended rows bit-exact, the outputs within the tolerance."""
+    import torch
+    nq, nkv, hd, mt = 32, 8, 128, 4097
+    rng = np.random.default_rng(31)
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    B = 3
+    kp0 = _gpu_planes(gen, (B, nkv, mt, hd), tqk)
+    vp0 = _gpu_planes(gen, (B, nkv, mt, hd), tqk)
+    q = rng.standard_normal((B, nq * hd), dtype=np.float32)
+    k_new = rng.standard_normal((B, nkv * hd), dtype=np.float32)
+    v_new = rng.standard_normal((B, nkv * hd), dtype=np.float32)
+    kh0, vh0 = kp0.cpu().numpy(), vp0.cpu().numpy()
+    width = hd + 2 if out_mode == 1 else hd
+    qd = torch.from_numpy(q).to(cuda)
+
+    def n_splits_of(n, split):
+        return n // split + (1 if n % split > split // 4 else 0)
+
+    cases = [(4097, 2048), (4097, 1408), (4097, 1024), (4097, 832), (4097, 704), (4097, 640), (4097, 512),
+             (4097, 448), (2560, 256), (4097, 384), (3072, 256), (4097, 320), (3584, 256), (3840, 256), (4097, 256)]
+    assert [n_splits_of(n, sp) for n, sp in cases] == list(range(2, 17))
+    for n0, split in cases:
+        lens = np.array([n0, 300, 1], dtype=np.int32)
+        kp, vp = kp0.clone(), vp0.clone()
+        out = torch.full((B, nq * width), 7.0, device=cuda)
+        args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, qd, out, n_items=B, item_stride_blocks=nkv * mt * (hd // 32),
+                               lens=torch.from_numpy(lens).to(cuda), max_len=n0, q_item_stride=nq * hd,
+                               out_item_stride=nq * width, out_mode=out_mode, k_new=torch.from_numpy(k_new).to(cuda),
+                               v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd, split_tokens=split)
+        tqk.decode(args)
+        got = out.cpu().numpy()
+        kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
+        for b in range(B):
+            n = int(lens[b])
+            kref, vref = kh0[b].copy(), vh0[b].copy()
+            assert port.store_kv(kref, vref, nkv, hd, mt, n - 1, k_new[b], v_new[b]) == 0
+            assert np.array_equal(kref, kh[b]) and np.array_equal(vref, vh[b]), (n0, split, b)
+            g = got[b].reshape(nq, width)
+            if out_mode == 1:
+                g = g[:, :hd] / g[:, hd + 1:hd + 2]
+            ok, max_abs, rel = tolerance_ok(g.reshape(-1), port.attend(kref, vref, nq, nkv, hd, mt, n - 1, q[b]))
+            assert ok, f"{n_splits_of(n0, split)} splits, item {b}: max abs {max_abs:.3g} rel {rel:.3g}"
+    # an empty item next to full ones, no append
+    lens = np.array([4097, 0, 300], dtype=np.int32)
+    out = torch.full((B, nq * width), 7.0, device=cuda)
+    tqk.decode(tqk.decode_args(kp0, vp0, nq, nkv, hd, mt, qd, out, n_items=B, item_stride_blocks=nkv * mt * (hd // 32),
+                               lens=torch.from_numpy(lens).to(cuda), max_len=4097, q_item_stride=nq * hd,
+                               out_item_stride=nq * width, out_mode=out_mode, split_tokens=256))
+    got = out.cpu().numpy()
+    for b in (0, 2):
+        g = got[b].reshape(nq, width)
+        if out_mode == 1:
+            g = g[:, :hd] / g[:, hd + 1:hd + 2]
+        ref = port.attend(kh0[b], vh0[b], nq, nkv, hd, mt, int(lens[b]) - 1, q[b])
+        ok, max_abs, rel = tolerance_ok(g.reshape(-1), ref)
+        assert ok, f"item {b}: max abs {max_abs:.3g} rel {rel:.3g}"
+    e = got[1].reshape(nq, width)
+    assert (e[:, :hd] == 0).all()
+    if out_mode == 1:
+        assert (e[:, hd] == -np.inf).all() and (e[:, hd + 1] == 0).all()
+    assert tqk.device_status() == 0
+
+
 def test_config3_ragged_batch_device_lens(tqk, port, cuda):
     """Config 3: batch 64, lengths ~U[512, 8192], 1% x8 outliers, device lens array."""
     import torch
