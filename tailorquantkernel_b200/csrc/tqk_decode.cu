@@ -837,10 +837,13 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
         *ctas_per_sm = occ;
         return TQK_OK;
     }
-    // the splits of a unit (grid.x of them) merge through a thread-block cluster when they fit one
-    // and the device can place such clusters; TQK_DECODE_CLUSTER=0 in the environment turns it off
-    if (grid.x >= 2 && grid.x <= (unsigned)CL_MAX && cluster_merge_ok(decode_q8_pack_kernel<NB>, dev, grid,
-                                                                        PK_THREADS, L::BYTES)) {
+    // the splits of a unit (grid.x of them) merge through a thread-block cluster when they fit one,
+    // every item has the same length (with ragged lengths the idle splits of short items would stay
+    // resident until their cluster's merge) and the device can place such clusters;
+    // TQK_DECODE_CLUSTER=0 in the environment turns it off
+    const bool equal_lengths = p.lens == nullptr && p.len_step == 0;
+    if (equal_lengths && grid.x >= 2 && grid.x <= (unsigned)CL_MAX &&
+        cluster_merge_ok(decode_q8_pack_kernel<NB>, dev, grid, PK_THREADS, L::BYTES)) {
         DecodeParams pc = p;
         pc.cluster = (int)grid.x;
         return launch_pdl_cluster(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, grid.x, pc);

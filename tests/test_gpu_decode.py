@@ -143,11 +143,12 @@ def test_config1_on_the_reference_generator(tqk, port, cuda):
 
 @pytest.mark.parametrize("out_mode", [0, 1])
 def test_cluster_merge_every_size(tqk, port, cuda, out_mode):
-    """The packed kernel's split merge through a thread-block cluster, for every cluster size from
-    2 to 16 splits of a unit: a long item with a fused append, a 300-token item and a one-token
-    item whose later splits are empty (they take part with empty partials), through device
-    lengths, in both output modes; then an empty item without an append (its cluster leaves
-    without merging).  The appended rows bit-exact, the outputs within the tolerance."""
+    """The packed kernel's split merge for every split count from 2 to 16: with equal lengths
+    (len_step 0) it runs through a thread-block cluster of the unit's splits -- three items of the
+    same length with a fused append, in both output modes; with device lengths (a long item, a
+    300-token and a one-token item whose later splits are empty) it runs through the tickets;
+    then an empty item without an append.  The appended rows bit-exact, the outputs within the
+    tolerance."""
     import torch
     nq, nkv, hd, mt = 32, 8, 128, 4097
     rng = np.random.default_rng(31)
@@ -168,14 +169,15 @@ def test_cluster_merge_every_size(tqk, port, cuda, out_mode):
     cases = [(4097, 2048), (4097, 1408), (4097, 1024), (4097, 832), (4097, 704), (4097, 640), (4097, 512),
              (4097, 448), (2560, 256), (4097, 384), (3072, 256), (4097, 320), (3584, 256), (3840, 256), (4097, 256)]
     assert [n_splits_of(n, sp) for n, sp in cases] == list(range(2, 17))
-    for n0, split in cases:
-        lens = np.array([n0, 300, 1], dtype=np.int32)
+    for (n0, split), device_lens in [(c, dl) for c in cases for dl in (False, True)]:
+        lens = np.array([n0, 300, 1] if device_lens else [n0] * B, dtype=np.int32)
         kp, vp = kp0.clone(), vp0.clone()
         out = torch.full((B, nq * width), 7.0, device=cuda)
+        length = dict(lens=torch.from_numpy(lens).to(cuda), max_len=n0) if device_lens else dict(len0=n0)
         args = tqk.decode_args(kp, vp, nq, nkv, hd, mt, qd, out, n_items=B, item_stride_blocks=nkv * mt * (hd // 32),
-                               lens=torch.from_numpy(lens).to(cuda), max_len=n0, q_item_stride=nq * hd,
-                               out_item_stride=nq * width, out_mode=out_mode, k_new=torch.from_numpy(k_new).to(cuda),
-                               v_new=torch.from_numpy(v_new).to(cuda), kv_new_item_stride=nkv * hd, split_tokens=split)
+                               q_item_stride=nq * hd, out_item_stride=nq * width, out_mode=out_mode,
+                               k_new=torch.from_numpy(k_new).to(cuda), v_new=torch.from_numpy(v_new).to(cuda),
+                               kv_new_item_stride=nkv * hd, split_tokens=split, **length)
         tqk.decode(args)
         got = out.cpu().numpy()
         kh, vh = kp.cpu().numpy(), vp.cpu().numpy()
