@@ -775,31 +775,32 @@ int launch_mma(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas_
 }
 
 // Two-kv-heads-per-CTA kernel for 4 q heads per kv head.
-// Whether clusters of grid.x CTAs of `kernel` can be placed on device `dev` (cached per device and
-// cluster size; sizes above 8 are opted in as non-portable).  Off with TQK_DECODE_CLUSTER=0.
+// How many clusters of cx CTAs of `kernel` the device `dev` holds at once (cached per device and
+// cluster size; sizes above 8 are opted in as non-portable); 0 when it holds none, or with
+// TQK_DECODE_CLUSTER=0 in the environment.
 template <typename K>
-bool cluster_merge_ok(K kernel, int dev, dim3 grid, int threads, int smem) {
+int max_active_clusters(K kernel, int dev, unsigned cx, int threads, int smem) {
     static std::mutex mu;
-    static signed char ok_by[64][CL_MAX + 1];  // 0 = unknown, 1 = yes, -1 = no
+    static int count_by[64][CL_MAX + 1];  // 0 = unknown, -1 = none, n = n clusters
     static const bool enabled = [] {
         const char *e = getenv("TQK_DECODE_CLUSTER");
         return !(e && e[0] == '0');
     }();
-    if (!enabled || dev < 0 || dev >= 64 || grid.x > (unsigned)CL_MAX) return false;
+    if (!enabled || dev < 0 || dev >= 64 || cx > (unsigned)CL_MAX) return 0;
     std::lock_guard<std::mutex> lock(mu);
-    signed char &ok = ok_by[dev][grid.x];
-    if (ok == 0) {
+    int &count = count_by[dev][cx];
+    if (count == 0) {
         cudaError_t e = cudaSuccess;
-        if (grid.x > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (cx > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         int n = 0;
         if (e == cudaSuccess) {
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(grid.x, 1, 1);
+            cfg.gridDim = dim3(cx, 1, 1);
             cfg.blockDim = dim3(threads);
             cfg.dynamicSmemBytes = smem;
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = grid.x;
+            attr[0].val.clusterDim.x = cx;
             attr[0].val.clusterDim.y = 1;
             attr[0].val.clusterDim.z = 1;
             cfg.attrs = attr;
@@ -807,9 +808,9 @@ bool cluster_merge_ok(K kernel, int dev, dim3 grid, int threads, int smem) {
             e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
         }
         if (e != cudaSuccess) (void)cudaGetLastError();  // not an error of the call: no clusters
-        ok = (e == cudaSuccess && n > 0) ? 1 : -1;
+        count = (e == cudaSuccess && n > 0) ? n : -1;
     }
-    return ok > 0;
+    return count > 0 ? count : 0;
 }
 
 template <int NB>
@@ -839,11 +840,14 @@ int launch_pack(const DecodeParams &p, dim3 grid, cudaStream_t stream, int *ctas
     }
     // the splits of a unit (grid.x of them) merge through a thread-block cluster when they fit one,
     // every item has the same length (with ragged lengths the idle splits of short items would stay
-    // resident until their cluster's merge) and the device can place such clusters;
+    // resident until their cluster's merge), and the device holds every cluster of the grid at once:
+    // a cluster is placed whole within one GPC, so a grid of more clusters than fit runs in two
+    // waves (measured on B200: 16 clusters of 16 CTAs took 29 us where the ticket merge took 19 us).
     // TQK_DECODE_CLUSTER=0 in the environment turns it off
     const bool equal_lengths = p.lens == nullptr && p.len_step == 0;
     if (equal_lengths && grid.x >= 2 && grid.x <= (unsigned)CL_MAX &&
-        cluster_merge_ok(decode_q8_pack_kernel<NB>, dev, grid, PK_THREADS, L::BYTES)) {
+        (long long)grid.y * grid.z <=
+            max_active_clusters(decode_q8_pack_kernel<NB>, dev, grid.x, PK_THREADS, L::BYTES)) {
         DecodeParams pc = p;
         pc.cluster = (int)grid.x;
         return launch_pdl_cluster(decode_q8_pack_kernel<NB>, grid, dim3(PK_THREADS), L::BYTES, stream, grid.x, pc);
@@ -976,12 +980,14 @@ long long kv_bytes_of(const tqk_decode_args *a, int max_len) {
 //    then at most MERGE_GROUP splits (one merge level) win: a Llama-3-8B layer
 //    at n = 4097 took 16.4 us with 13 splits against 17.6 us with 64;
 //  * unequal lengths (device lengths unknown to the host): about 0.9 waves if
-//    the lengths spread evenly up to max_len, and one merge level: ragged
-//    config-3 shares of 8 and 16 sequences took 24.6 and 40.5 us that way
-//    against 35.2 and 51.5 us with two CTAs per slot (1.1 waves, two levels).
+//    the lengths spread evenly up to max_len -- each unit then takes about
+//    want / 2 + 1/2 splits, the half for its last, partial split -- and one
+//    merge level: ragged config-3 shares of 8 and 16 sequences took 24.6 and
+//    40.5 us with splits near that choice against 35.2 and 51.5 us with two
+//    CTAs per slot (1.1 waves, two levels).
 constexpr long long LATENCY_BYTES = 16LL << 20;
 long long auto_splits(bool uniform, long long slots, long long units, long long kv_bytes) {
-    long long want = uniform ? slots / units : (9 * slots) / (5 * units);
+    long long want = uniform ? slots / units : (9 * slots - 5 * units) / (5 * units);
     if ((!uniform || kv_bytes < LATENCY_BYTES) && want > MERGE_GROUP) want = MERGE_GROUP;
     return want < 1 ? 1 : want;
 }
