@@ -71,3 +71,57 @@ def test_default_shapes_describe_the_baseline_configs():
     assert bench.describe_config4(64, 8, 128, 131072)["kv_bytes_per_token"] == 301_989_888
     assert bench.prefill_flops(32, 128, 2048, 2048) == 103_095_992_320
     assert "n=4097" in bench.describe_config2(32, 32, 8, 128, 4096)["workload"]
+
+
+def test_both_arms_draw_the_same_inputs():
+    """The reference arm draws its inputs with the reference's own normal_sample (oracle/_ref,
+    sequential, state jumped in Python), our arm with tqk_fill_normal: the same floats for the
+    same windows of the stream, and the same uniforms (config 3's lengths and outlier picks)."""
+    import numpy as np
+    import bench
+    ref, lib = bench.reference_generator(), bench.LibGen()
+    if not isinstance(ref, bench.RefGen):
+        pytest.skip("oracle/_ref/libtqref_rng.so not built (needs the reference tree at build time)")
+    for first, n in ((0, 1000), (123_456_789, 513), (2 * 8 * 4097 * 128 * 32, 4096)):
+        assert np.array_equal(ref.normal(first, n).view(np.uint32), lib.normal(first, n).view(np.uint32))
+        assert np.array_equal(ref.uniform(first, n).view(np.uint32), lib.uniform(first, n).view(np.uint32))
+    assert np.array_equal(bench.ragged_lengths(ref, 64, 512, 8192), bench.ragged_lengths(lib, 64, 512, 8192))
+
+
+def test_config_streams_tile_without_overlap():
+    """Every config's input windows are disjoint and leave no gap: each input is its own part of
+    the stream, and a rank's share of a partitioned config is the same floats as at N = 1."""
+    import numpy as np
+    import bench
+
+    def check(windows):
+        windows = sorted(windows)
+        for (a0, n0), (a1, _) in zip(windows, windows[1:]):
+            assert a0 + n0 == a1, (a0, n0, a1)
+        assert windows[0][0] == 0
+
+    L, nq, nkv, hd, mt = 3, 8, 4, 64, 37
+    o = bench.config2_stream(L, nq, nkv, hd, mt)
+    w = [(o["kv"](l, p, h), mt * hd) for l in range(L) for p in (0, 1) for h in range(nkv)]
+    w += [(o["step"] + l * (nq + 2 * nkv) * hd, (nq + 2 * nkv) * hd) for l in range(L)]
+    w += [(o["norms"], 2 * L * hd)]
+    check(w)
+    n = 50
+    check([(bench.config4_stream(nkv, n, hd, p, h), n * hd) for p in (0, 1) for h in range(nkv)] +
+          [(bench.config4_stream(nkv, n, hd, 2, 0), 16 * hd)])
+    lens = np.array([5, 9, 1], np.int32)
+    o = bench.config3_stream(lens, nq, nkv, hd)
+    w = [(o["kv"](b, p), nkv * int(lens[b]) * hd) for b in range(3) for p in (0, 1)]
+    w += [(o["q"](b), nq * hd) for b in range(3)]
+    check(w)
+    pos0, nn = 6, 4
+    o = bench.config5_stream(nq, nkv, hd, pos0, nn)
+    check([(o["kv"](p, h), pos0 * hd) for p in (0, 1) for h in range(nkv)] +
+          [(o["q"], nn * nq * hd), (o["k"], nn * nkv * hd), (o["v"], nn * nkv * hd)])
+    hidden = 96
+    o = bench.config6_stream(L, nkv, hd, mt, hidden)
+    check([(o["kv"](l, p, h), mt * hd) for l in range(L) for p in (0, 1) for h in range(nkv)] +
+          [(o["x"], hidden), (o["norms"], 2 * L * hd)])
+    o = bench.config7_stream(L, nkv, hd, mt, hidden)
+    check([(o["kv"](l, p, h), mt * hd) for l in range(L) for p in (0, 1) for h in range(nkv)] +
+          [(o["norms"](l), 2 * hidden + 2 * hd) for l in range(L)] + [(o["final_norm"], hidden)])
