@@ -7,7 +7,7 @@
 //     attention_layer                tqk_attention_layer (3 launches: q/k/v projection, the decode
 //                                    with the fused norm + RoPE + Q8 append, output projection)
 //     x += attn; rmsnorm(x, post_norm)  residual_rmsnorm_kernel      (model/vec.c:3-7, context.c:96-98)
-//     mlp_layer                      tqk_project (gate, up) -> silu_mul_kernel -> tqk_project (down)
+//     mlp_layer                      tqk_project (gate, up) -> silu_mul_q8_kernel -> tqk_matmul (down)
 //                                    (model/mlp.c:3-17, model/silu.c:6-20)
 //     x += mlp                       folded into the next layer's (or the final) rmsnorm launch
 //   rmsnorm(x, final_norm) + lm_head  residual_rmsnorm_kernel + tqk_project over the tied embedding
@@ -84,15 +84,24 @@ __global__ void __launch_bounds__(FW_THREADS) residual_rmsnorm_kernel(float *x, 
         out[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
 }
 
-// out = silu(gate) * up, silu(g) = g * (1 / (1 + expf(-g))) (model/silu.c:6-20).
-__global__ void __launch_bounds__(256) silu_mul_kernel(const float *gate, const float *up, float *out, int n) {
+// silu(gate) * up, silu(g) = g * (1 / (1 + expf(-g))) (model/silu.c:6-20), fused with the Q8
+// quantisation of the result, which is the down projection's input (model/mlp.c:12-14 quantises
+// the silu * up row before that matmul): one warp per 32-element block, every step rounded as the
+// reference's separate silu_mul and quantize_row_q8, so the blocks are bit-identical to those two
+// steps and one launch shorter.
+__global__ void __launch_bounds__(256) silu_mul_q8_kernel(const float *gate, const float *up, uint8_t *xq, int n) {
     grid_dependency_wait();
     grid_dependents_launch();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+    const int blk = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (blk >= n / QK) return;  // whole warps: blockDim is a multiple of 32
+    const int i = blk * QK + lane;
     const float g = gate[i];
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-    out[i] = __fmul_rn(__fmul_rn(g, sig), up[i]);
+    float d;
+    const int8_t q = warp_quantize_block(__fmul_rn(__fmul_rn(g, sig), up[i]), &d);
+    uint8_t *o = xq + (long long)blk * BLOCK_BYTES;
+    o[4 + lane] = (uint8_t)q;
+    if (lane == 0) *reinterpret_cast<float *>(o) = d;
 }
 
 // sample_greedy: the index of the first maximum of logits[0..n), scanning as the
@@ -132,7 +141,13 @@ __global__ void __launch_bounds__(FW_THREADS) argmax_kernel(const float *logits,
 
 struct ScratchLayout {
     float *x, *xn, *attn, *mlp, *gate, *up, *layer;
+    uint8_t *xq;  // the down projection's Q8 input, [inter / 32] blocks
 };
+
+// Floats of the attention layer's scratch region.
+size_t layer_floats(const tqk_model *m) {
+    return 2 * (size_t)m->n_q_heads * m->head_dim + 2 * (size_t)m->n_kv_heads * m->head_dim;
+}
 
 ScratchLayout scratch_layout(const tqk_model *m, void *scratch) {
     ScratchLayout s{};
@@ -145,6 +160,7 @@ ScratchLayout scratch_layout(const tqk_model *m, void *scratch) {
     s.gate = s.mlp + hidden;
     s.up = s.gate + inter;
     s.layer = s.up + inter;
+    s.xq = reinterpret_cast<uint8_t *>(s.layer + ((layer_floats(m) + 3) / 4) * 4);  // 16-byte aligned
     return s;
 }
 
@@ -161,9 +177,9 @@ extern "C" size_t tqk_forward_scratch_bytes(const tqk_model *m) {
     if (!m || m->hidden_size <= 0 || m->intermediate_size <= 0 || m->n_q_heads <= 0 || m->n_kv_heads <= 0 ||
         m->head_dim <= 0)
         return 0;
-    const size_t floats = 4 * (size_t)m->hidden_size + 2 * (size_t)m->intermediate_size +
-                          2 * (size_t)m->n_q_heads * m->head_dim + 2 * (size_t)m->n_kv_heads * m->head_dim;
-    return floats * sizeof(float);
+    const size_t floats =
+        4 * (size_t)m->hidden_size + 2 * (size_t)m->intermediate_size + ((layer_floats(m) + 3) / 4) * 4;
+    return floats * sizeof(float) + (size_t)(m->intermediate_size / QK) * BLOCK_BYTES;
 }
 
 extern "C" int tqk_forward_token(const tqk_model *m, int token, int pos, void *scratch, float *logits,
@@ -227,11 +243,14 @@ extern "C" int tqk_forward_token(const tqk_model *m, int token, int pos, void *s
         const tqk_proj_job gu[2] = {{w.wgate, s.gate, inter}, {w.wup, s.up, inter}};
         rc = tqk_project(gu, 2, m->format, s.xn, hidden, 1, stream);
         if (rc) return rc;
-        rc = launch_pdl(silu_mul_kernel, dim3((inter + 255) / 256), dim3(256), 0, st, (const float *)s.gate,
-                        (const float *)s.up, s.gate, inter);
+        const int blocks = inter / QK;
+        rc = launch_pdl(silu_mul_q8_kernel, dim3((blocks + 7) / 8), dim3(256), 0, st, (const float *)s.gate,
+                        (const float *)s.up, s.xq, inter);
         if (rc) return rc;
-        const tqk_proj_job dn = {w.wdown, s.mlp, hidden};
-        rc = tqk_project(&dn, 1, m->format, s.gate, inter, 1, stream);
+        const tqk_block_q8 *xq = reinterpret_cast<const tqk_block_q8 *>(s.xq);
+        rc = m->format == TQK_FMT_Q8
+                 ? tqk_matmul_q8(static_cast<const tqk_block_q8 *>(w.wdown), xq, s.mlp, hidden, inter, stream)
+                 : tqk_matmul_q4(static_cast<const tqk_block_q4 *>(w.wdown), xq, s.mlp, hidden, inter, stream);
         if (rc) return rc;
         const float *next_norm = l + 1 < m->n_layers ? m->layers[l + 1].input_norm : m->final_norm;
         rc = residual_rmsnorm(s.x, s.mlp, next_norm, s.xn, hidden, m->rms_eps, st);
